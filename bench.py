@@ -1,0 +1,420 @@
+"""Benchmark of the sparse KV-cache miss-stream decode path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ferry|reference]
+
+A step is one decode tick of the job: every active request of the workload runs
+select -> miss detect -> miss gather (pinned host -> HBM) -> sparse attention for
+all its layers and kv heads. At N=1 the workload is configs[0] of the benchmark
+("cfg1": 16 requests x 4096 tokens, 32/32 heads, 1 layer, top-64 pages, 25%
+LRU cache, Poisson 50 req/s, 200 decode steps). configs[1] (64 x 32768 tokens,
+32 layers, 30% cache = 300 GiB) does not fit one GPU's HBM.
+
+value  decode tokens/s, device-timed (CUDA events on the launching stream,
+       barrier + synchronize on both sides, max over ranks), KV pool resident in
+       pinned host memory (the workload serves misses from it), queries resident
+       in HBM. Multi-GPU: independent replicas per rank (weak scaling).
+e2e    the same through the fused public call ferry_decode_step with host
+       buffers: per step H2D of queries + request ids from pinned memory and D2H
+       of the attention output inside the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tokens/s (sparse KV miss-stream decode: select+miss-detect+gather+attention)"
+UNIT = "tokens/s"
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def _ncu_traffic():
+    """dram bytes per attention launch from the committed ncu summary, if any."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+class Clocks:
+    """Sample SM clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        rows = [r.split(",") for r in (self.out or "").strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i]})
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def cpu_baseline(w, seconds: float = 15.0, threads: int | None = None, ticks: int | None = None):
+    """The reference path restated on host cores (oracle pipeline: select ->
+    LRU -> memcpy gather -> fp32 attention), all host threads, over a bounded
+    sample of the job's ticks. Returns (tokens/s, threads, sample text,
+    per-tick [(ms, tokens)])."""
+    import oracle
+    from ferry_b200.workload import Schedule, q_stream
+
+    oracle.build()
+    threads = threads or os.cpu_count() or 1
+    LH = w.lanes_per_req
+    pool = oracle.kv_gen(w.seed, 0, w.pool_units, threads=threads)
+    summ = oracle.page_summary(pool)
+    pipe = oracle.CpuPipeline(w.num_requests * LH, w.max_pages, w.cache_pages, w.top_k, w.group,
+                              pool, summ, threads)
+    sch = Schedule(w)
+    qs = [q_stream(w, r) for r in range(w.num_requests)]
+    tok, t_used, i, per_tick = 0, 0.0, 0, []
+    limit = sch.length if ticks is None else ticks
+    while i < limit and (ticks is not None or t_used < seconds):
+        active, steps, job = sch.tick(i)
+        i += 1
+        if len(active) == 0:
+            per_tick.append((0.0, 0))
+            continue
+        if job:
+            qs = [q_stream(w, r, job=job) for r in range(w.num_requests)]
+        lanes = (active[:, None] * LH + np.arange(LH)[None]).ravel().astype(np.int32)
+        reset = np.repeat((steps == 0).astype(np.uint8), LH)
+        q = np.stack([qs[r][s] for r, s in zip(active, steps)]).view(np.uint16)
+        t0 = time.perf_counter()
+        pipe.step(lanes, q.reshape(len(lanes), w.group, 128), reset=reset)
+        dt = time.perf_counter() - t0
+        t_used += dt
+        per_tick.append((dt * 1e3, len(active)))
+        tok += len(active)
+    return tok / t_used, threads, f"first {i} ticks of the {w.name} job ({tok} tokens)", per_tick
+
+
+def run_reference(args, w):
+    """--impl reference: the path's CPU implementation on the box's host cores."""
+    ws, rank, _ = _dist()
+    if rank != 0:
+        return
+    _, threads, _, per_tick = cpu_baseline(w, ticks=args.warmup + args.steps)
+    timed = per_tick[args.warmup:]
+    t_ms = sum(m for m, _ in timed)
+    tok = sum(n for _, n in timed)
+    v = tok / (t_ms / 1e3) if t_ms > 0 else 0.0
+    sample = f"ticks {args.warmup}..{args.warmup + args.steps - 1} of the {w.name} job ({tok} tokens)"
+    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_ms / max(1, args.steps),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp16-kv/fp32-acc", "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"{w.name} (configs[0])", "requests": w.num_requests,
+                       "ctx_tokens": w.ctx_tokens, "layers": w.num_layers,
+                       "heads": [w.q_heads, w.kv_heads], "top_k": w.top_k,
+                       "cache_pages": w.cache_pages, "parallelism": "host threads"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ferry(args, w):
+    import torch
+    import torch.distributed as dist
+
+    from ferry_b200.engine import Decoder
+    from ferry_b200.workload import Schedule, Workload, q_stream
+    import dataclasses
+
+    ws, rank, local = _dist()
+    if ws > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    # replicas: same shape, per-rank seed
+    w = dataclasses.replace(w, seed=w.seed + 1000 * rank)
+    dec = Decoder(w, local)
+    dec.register_pool()
+    sch = Schedule(w)
+    LH = w.lanes_per_req
+    n_ticks = args.warmup + args.steps
+
+    # per-tick device inputs, built before timing
+    qs = [torch.from_numpy(q_stream(w, r)) for r in range(w.num_requests)]
+    ticks = []
+    for i in range(n_ticks):
+        active, steps, job = sch.tick(i)
+        if job:
+            # a repeated job restarts every request with fresh queries
+            qj = [torch.from_numpy(q_stream(w, r, job=job)) for r in range(w.num_requests)]
+        else:
+            qj = qs
+        q = torch.stack([qj[r][s] for r, s in zip(active, steps)]) if len(active) else None
+        new = active[steps == 0]
+        ticks.append(dict(active=active, steps=steps, q=q,
+                          ids=torch.from_numpy(active).to(dev),
+                          qd=None if q is None else q.to(dev),
+                          new=None if len(new) == 0 else torch.from_numpy(new).to(dev)))
+    n_pages = torch.full((w.num_requests,), w.max_pages, dtype=torch.int32, device=dev)
+    out = torch.empty((w.num_requests, w.num_layers, w.q_heads, 128), dtype=torch.float32, device=dev)
+    st = torch.cuda.current_stream(dev)
+
+    def tick_run(tk, evs=None):
+        if tk["new"] is not None:
+            dec.begin(tk["new"], n_pages[: len(tk["new"])], stream=st)
+        if tk["qd"] is None:
+            return 0
+        n = len(tk["active"])
+        if evs is None:
+            dec.step(tk["qd"], tk["ids"], out[:n], stream=st)
+            return n
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        e[0].record(st)
+        dec.select(tk["qd"], tk["ids"], stream=st)
+        e[1].record(st)
+        dec.detect(tk["ids"], stream=st)
+        e[2].record(st)
+        dec.gather(tk["ids"], stream=st)
+        e[3].record(st)
+        dec.attention(tk["qd"], tk["ids"], out[:n], stream=st)
+        e[4].record(st)
+        evs.append((e, n))
+        return n
+
+    # ---------------------------------------------------------------- device-timed value
+    for i in range(args.warmup):
+        tick_run(ticks[i], [])
+    torch.cuda.synchronize(dev)
+    dec.stats(reset=True)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    evs = []
+    tokens = 0
+    with Clocks(local) as clk:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(st)
+        for i in range(args.warmup, n_ticks):
+            tokens += tick_run(ticks[i], evs)
+        t1.record(st)
+        torch.cuda.synchronize(dev)
+    elapsed_ms = t0.elapsed_time(t1)
+    dec.check()
+    units, gbytes = dec.stats(reset=True)
+    launches = len(evs) * 4 + sum(1 for i in range(args.warmup, n_ticks) if ticks[i]["new"] is not None)
+    k_ms = np.zeros(4)
+    step_ms = []
+    for e, n in evs:
+        d = [e[j].elapsed_time(e[j + 1]) for j in range(4)]
+        k_ms += d
+        step_ms.append(sum(d))
+    if ws > 1:
+        t = torch.tensor([elapsed_ms, float(tokens), float(gbytes)], dtype=torch.float64, device=dev)
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = t.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        elapsed_max, tokens_all, gbytes_all = float(mx[0]), float(sm[1]), float(sm[2])
+    else:
+        elapsed_max, tokens_all, gbytes_all = elapsed_ms, float(tokens), float(gbytes)
+    value = tokens_all / (elapsed_max / 1e3)
+
+    # ---------------------------------------------------------------- e2e through the public call
+    # fresh job state so the e2e pass decodes the same ticks again
+    dec.close()
+    dec = Decoder(w, local)
+    dec.register_pool()
+    pin_q = [None if tk["q"] is None else tk["q"].pin_memory() for tk in ticks]
+    pin_ids = [torch.from_numpy(tk["active"]).pin_memory() for tk in ticks]
+    host_out = torch.empty_like(out, device="cpu").pin_memory()
+    qbuf = torch.empty((w.num_requests, w.num_layers, w.q_heads, 128), dtype=torch.float16, device=dev)
+    ibuf = torch.empty(w.num_requests, dtype=torch.int32, device=dev)
+    h2d = d2h = 0
+
+    def e2e_tick(i):
+        nonlocal h2d, d2h
+        tk = ticks[i]
+        if tk["new"] is not None:
+            dec.begin(tk["new"], n_pages[: len(tk["new"])], stream=st)
+        if pin_q[i] is None:
+            return 0
+        n = len(tk["active"])
+        qbuf[:n].copy_(pin_q[i], non_blocking=True)
+        ibuf[:n].copy_(pin_ids[i], non_blocking=True)
+        dec.step(qbuf[:n], ibuf[:n], out[:n], stream=st)
+        host_out[:n].copy_(out[:n], non_blocking=True)
+        h2d += pin_q[i].numel() * 2 + n * 4
+        d2h += n * w.num_layers * w.q_heads * 128 * 4
+        return n
+
+    for i in range(args.warmup):
+        e2e_tick(i)
+    torch.cuda.synchronize(dev)
+    h2d = d2h = 0
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(st)
+    e2e_tokens = sum(e2e_tick(i) for i in range(args.warmup, n_ticks))
+    t1.record(st)
+    torch.cuda.synchronize(dev)
+    e2e_ms = t0.elapsed_time(t1)
+    dec.check()
+    if ws > 1:
+        t = torch.tensor([e2e_ms, float(e2e_tokens)], dtype=torch.float64, device=dev)
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = t.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        e2e_ms, e2e_tokens = float(mx[0]), float(sm[1])
+    e2e_value = e2e_tokens / (e2e_ms / 1e3)
+
+    # ---------------------------------------------------------------- link peak (H2D from pinned)
+    src = torch.empty(512 << 20, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    best = 0.0
+    for _ in range(4):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        dst.copy_(src, non_blocking=True)
+        b.record(st)
+        torch.cuda.synchronize(dev)
+        best = max(best, src.numel() / (a.elapsed_time(b) / 1e3) / 1e9)
+    del src, dst
+    dec.close()
+
+    if rank == 0:
+        hbm_peak, peak_kind = _peaks()
+        nl = tokens * LH  # lanes processed by this rank
+        attn_bytes = tokens * w.attn_bytes_per_token() + tokens * w.qo_bytes_per_token()
+        sel_bytes = tokens * w.select_bytes_per_token()
+        n_launch = len(evs)
+        attn_ms = k_ms[3] / max(1, n_launch)
+        achieved = (attn_bytes / max(1, n_launch)) / (attn_ms / 1e3) / 1e9
+        sel_ach = (sel_bytes / max(1, n_launch)) / (k_ms[0] / max(1, n_launch) / 1e3) / 1e9
+        gather_gbs = gbytes / (k_ms[2] / 1e3) / 1e9 if k_ms[2] > 0 else 0.0
+        traffic = _ncu_traffic()
+        shares = {k: round(float(v / k_ms.sum()), 4) for k, v in
+                  zip(["select", "detect", "gather", "attention"], k_ms)}
+        srt = np.sort(step_ms)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": elapsed_max / args.steps,
+            "p50_step_ms": float(srt[len(srt) // 2]) if len(srt) else None,
+            "p99_step_ms": float(srt[int(0.99 * (len(srt) - 1))]) if len(srt) else None,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp16-kv/fp32-acc", "data": "synthetic (procedural KV, AR(1) queries, seeded)",
+            "config": {"workload": f"{w.name} (configs[0])", "requests": w.num_requests,
+                       "ctx_tokens": w.ctx_tokens, "layers": w.num_layers,
+                       "heads": [w.q_heads, w.kv_heads], "head_dim": 128, "page_tokens": 16,
+                       "top_k": w.top_k, "cache_pages": w.cache_pages,
+                       "arrivals": f"poisson {w.arrival_rate} req/s on a {w.tick_ms} ms tick",
+                       "l2": "inputs larger than L2 (selected KV 256 MiB + summaries 64 MiB per full step)",
+                       "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU"},
+            "miss_gather": {"GB_s": gather_gbs, "bytes": gbytes_all, "units": units,
+                            "link_peak_GB_s": best, "frac": gather_gbs / best if best else None,
+                            "peak_kind": "measured H2D copy from pinned host, this run"},
+            "roofline": {"bound": "hbm", "kernel": "attn_kernel", "achieved": achieved,
+                         "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                         "peak_kind": peak_kind,
+                         "traffic": (traffic or {}).get("attn_bytes_per_launch"),
+                         "bytes_per_launch": attn_bytes / max(1, n_launch)},
+            "roofline_select": {"bound": "hbm", "achieved": sel_ach, "peak": hbm_peak,
+                                "unit": "GB/s", "frac": sel_ach / hbm_peak},
+            "kernel_ms_per_step": {k: float(v / max(1, n_launch)) for k, v in
+                                   zip(["select", "detect", "gather", "attention"], k_ms)},
+            "kernel_time_share": shares,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d / args.steps,
+                    "d2h_bytes_per_step": d2h / args.steps, "api": "ferry_decode_step"},
+            "gpu_launches": launches,
+        }
+        line["clocks"] = clk.summary()
+        if ws == 1 and not args.no_cpu_baseline:
+            v, threads, sample, _ = cpu_baseline(w, seconds=args.cpu_seconds)
+            line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                                    "sample": sample}
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ferry", "reference"], default="ferry")
+    ap.add_argument("--workload", default="cfg1")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    from ferry_b200.workload import WORKLOADS
+
+    w = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, w)
+    else:
+        run_ferry(args, w)
+
+
+if __name__ == "__main__":
+    main()

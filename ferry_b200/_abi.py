@@ -1,0 +1,96 @@
+"""ctypes binding of libferry_cuda.so (the C ABI declared in include/ferry_cuda.h).
+
+The library is required: importing this module on a machine where it was not
+built raises immediately -- there is no CPU fallback for the decode path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libferry_cuda.so")
+
+OK, E_INVAL, E_OOM, E_TIMEOUT, E_CUDA, E_STATE, E_RANGE = range(7)
+_NAMES = {E_INVAL: "FERRY_E_INVAL", E_OOM: "FERRY_E_OOM", E_TIMEOUT: "FERRY_E_TIMEOUT",
+          E_CUDA: "FERRY_E_CUDA", E_STATE: "FERRY_E_STATE", E_RANGE: "FERRY_E_RANGE"}
+KV_F16 = 0
+LRU_DISTINCT = 1
+
+# every symbol include/ferry_cuda.h declares
+EXPORTS = [
+    "ferry_last_error", "ferry_version", "ferry_ctx_create", "ferry_ctx_destroy",
+    "ferry_ctx_check", "ferry_host_alloc", "ferry_host_free", "ferry_kv_register",
+    "ferry_kv_generate", "ferry_page_summary_update", "ferry_requests_begin",
+    "ferry_select_topk", "ferry_detect_misses", "ferry_gather_misses", "ferry_sparse_decode",
+    "ferry_decode_step", "ferry_stats_read", "ferry_debug_read", "ferry_lru_create",
+    "ferry_lru_destroy", "ferry_lru_touch", "ferry_lru_read",
+]
+
+
+class FerryError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{_NAMES.get(code, code)}: {msg}")
+        self.code = code
+
+
+class Cfg(C.Structure):
+    _fields_ = [("num_requests", C.c_int), ("num_layers", C.c_int), ("q_heads", C.c_int),
+                ("kv_heads", C.c_int), ("head_dim", C.c_int), ("page_tokens", C.c_int),
+                ("max_pages", C.c_int), ("cache_pages", C.c_int), ("top_k", C.c_int),
+                ("kv_dtype", C.c_int)]
+
+
+_lib = None
+
+V = C.c_void_p
+I = C.c_int
+_SIGS = {
+    "ferry_last_error": (C.c_char_p, []),
+    "ferry_version": (I, []),
+    "ferry_ctx_create": (I, [I, C.POINTER(Cfg), C.POINTER(V)]),
+    "ferry_ctx_destroy": (I, [V]),
+    "ferry_ctx_check": (I, [V]),
+    "ferry_host_alloc": (I, [C.c_size_t, C.POINTER(V)]),
+    "ferry_host_free": (I, [V]),
+    "ferry_kv_register": (I, [V, V, C.c_size_t]),
+    "ferry_kv_generate": (I, [V, C.c_uint64, C.c_uint64, C.c_int64, V]),
+    "ferry_page_summary_update": (I, [V, V, C.c_int64, C.c_int64]),
+    "ferry_requests_begin": (I, [V, V, V, V, I]),
+    "ferry_select_topk": (I, [V, V, V, V, I, V, V]),
+    "ferry_detect_misses": (I, [V, V, V, I, V, V, V, V, V, V, V]),
+    "ferry_gather_misses": (I, [V, V, V, I, V, V, V]),
+    "ferry_sparse_decode": (I, [V, V, V, V, I, V, V, V]),
+    "ferry_decode_step": (I, [V, V, V, V, I, V]),
+    "ferry_stats_read": (I, [V, V, I]),
+    "ferry_debug_read": (I, [V, I, C.c_size_t, C.c_size_t, V]),
+    "ferry_lru_create": (I, [I, I, I, I, C.POINTER(V)]),
+    "ferry_lru_destroy": (I, [V]),
+    "ferry_lru_touch": (I, [V, V, V, V, I, V, I, V, I, V, V, V, V, V]),
+    "ferry_lru_read": (I, [V, I, V, V, V]),
+}
+
+
+def lib() -> C.CDLL:
+    """Load libferry_cuda.so; raise if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: run `python -m ferry_b200.build` "
+                              "(there is no CPU fallback)")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(rc: int) -> None:
+    if rc != OK:
+        raise FerryError(rc, lib().ferry_last_error().decode())
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args))

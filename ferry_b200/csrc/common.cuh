@@ -1,0 +1,199 @@
+// common.cuh -- shared definitions of libferry_cuda.so (sm_100a only).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "ferry_cuda.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "libferry_cuda is built for sm_100a (B200) only"
+#endif
+
+namespace ferry {
+
+constexpr int kHeadDim = 128;
+constexpr int kPageTokens = 16;
+constexpr int kUnitElems = 2 * kPageTokens * kHeadDim;  // K[16][128] then V[16][128]
+constexpr int kUnitBytes = kUnitElems * 2;              // fp16: 8192 bytes
+constexpr int kMaxGroup = 8;
+constexpr int kMaxPages = 16384;
+
+// Device-side error record bits (ctx->d_err); read by ferry_ctx_check.
+enum : uint32_t { kErrTimeout = 1u, kErrRange = 2u };
+
+// Every spin on an mbarrier or flag gives up after this many polls, records
+// kErrTimeout and lets the kernel return.
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+// ---------------------------------------------------------------- host errors
+void set_error(const char* fmt, ...);
+int cuda_status(cudaError_t e, const char* what);
+
+#define FERRY_TRY(call)                                        \
+  do {                                                         \
+    cudaError_t e__ = (call);                                  \
+    if (e__ != cudaSuccess) return ferry::cuda_status(e__, #call); \
+  } while (0)
+
+// ---------------------------------------------------------------- device helpers
+__device__ __forceinline__ void record_error(uint32_t* err, uint32_t bit) {
+  if (err) atomicOr(err, bit);
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+// Make mbarrier initialisation visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Order this thread's earlier generic-proxy shared-memory accesses before
+// subsequent async-proxy (bulk copy) accesses.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase: true when the phase completed, false
+// (after recording kErrTimeout) when the poll budget ran out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  record_error(err, kErrTimeout);
+  return false;
+}
+
+// 1-D bulk async copy global -> shared (TMA engine), completion signalled on
+// the mbarrier as transaction bytes. dst, src 16-byte aligned; bytes % 16 == 0.
+__device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst_smem)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void st_v4(void* p, uint4 v) {
+  asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// splitmix64 finaliser (Steele, Lea, Flood 2014).
+__host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+}  // namespace ferry
+
+// ---------------------------------------------------------------- ctx
+struct ferry_lru {
+  int device = -1;
+  int lanes = 0, cap = 0, ids = 0;
+  int32_t* page_slot = nullptr;  // lanes * ids, -1 = absent
+  int32_t* slot_page = nullptr;  // lanes * cap
+  int32_t* order = nullptr;      // lanes * cap, LRU order as slots (front first)
+  int32_t* size = nullptr;       // lanes
+  uint32_t* err = nullptr;       // device error record
+};
+
+struct ferry_ctx {
+  int device = -1;
+  ferry_cfg cfg{};
+  int group = 1;          // q heads per kv head
+  int lanes_per_req = 0;  // L * Hkv
+  int64_t lanes = 0;      // R * L * Hkv
+  int chunk_pages = 8;    // attention split size (pages per work chunk)
+  int chunks_per_lane = 0;
+
+  uint8_t* cache = nullptr;  // lanes * C units
+  ferry_lru lru;             // page tables + LRU order, lanes x (C, N)
+  int32_t* ctx_pages = nullptr;  // R
+
+  // host pool
+  uint8_t* pool_dev = nullptr;  // device-visible address of the pinned pool
+  uint64_t pool_units = 0;
+  float* summ = nullptr;  // pool_units * 128
+
+  // decode-step workspace (sized for R requests)
+  int32_t* ws = nullptr;
+  int32_t *ws_sel = nullptr, *ws_nsel = nullptr, *ws_islot = nullptr, *ws_mpage = nullptr,
+          *ws_mslot = nullptr, *ws_nmiss = nullptr;
+
+  // attention scratch
+  float* part = nullptr;          // lanes * chunks_per_lane * group * kPartStride
+  uint32_t* lane_done = nullptr;  // lanes
+  uint32_t* grid_done = nullptr;  // 1
+
+  uint32_t* err = nullptr;                // device error record
+  unsigned long long* stats = nullptr;    // [0] units gathered, [1] bytes
+  int num_sms = 148;
+};
+
+namespace ferry {
+constexpr int kPartStride = 132;  // o[128], m, l, pad -> 16-byte rows
+
+// kernels' launchers (one per .cu)
+int launch_kv_generate(cudaStream_t st, uint64_t seed, uint64_t unit0, int64_t n_units, void* dst);
+int launch_summary(cudaStream_t st, const uint8_t* pool, int64_t unit0, int64_t n_units,
+                   float* summ);
+int launch_select(const ferry_ctx* c, cudaStream_t st, const uint16_t* q, const int32_t* req_ids,
+                  int n_req, int32_t* sel, int32_t* n_sel);
+int launch_lru(const ferry_lru* L, cudaStream_t st, const int32_t* lane_ids, const int32_t* req_ids,
+               int lanes_per_req, const uint8_t* reset, int n, const int32_t* sel, int k,
+               const int32_t* n_sel, int distinct, uint8_t* is_miss, int32_t* item_slot,
+               int32_t* miss_page, int32_t* miss_slot, int32_t* n_miss);
+int launch_lru_reset(const ferry_lru* L, cudaStream_t st, const int32_t* req_ids, int n,
+                     int lanes_per_req, const int32_t* n_pages, int32_t* ctx_pages);
+int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, int n_req,
+                  const int32_t* miss_page, const int32_t* miss_slot, const int32_t* n_miss);
+int launch_attention(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,
+                     const int32_t* req_ids, int n_req, const int32_t* item_slot,
+                     const int32_t* n_sel, float* out);
+}  // namespace ferry

@@ -1,0 +1,416 @@
+// ctx.cu -- C ABI of libferry_cuda.so: context lifecycle, host pool
+// registration and the per-step entry points (ferry_cuda.h).
+#include <cstdarg>
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+
+namespace ferry {
+
+static thread_local std::string g_last_error;
+
+void set_error(const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  set_error("%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+  return e == cudaErrorMemoryAllocation ? FERRY_E_OOM : FERRY_E_CUDA;
+}
+
+namespace {
+
+// Switch to a device for the duration of a call and restore the caller's.
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = false;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    ok = cudaSetDevice(dev) == cudaSuccess;
+    if (!ok) set_error("cudaSetDevice(%d) failed", dev);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+template <typename T>
+int dev_alloc(T** p, size_t count, int fill_byte) {
+  *p = nullptr;
+  if (count == 0) return FERRY_OK;
+  cudaError_t e = cudaMalloc((void**)p, count * sizeof(T));
+  if (e != cudaSuccess) {
+    *p = nullptr;
+    return cuda_status(e, "cudaMalloc");
+  }
+  FERRY_TRY(cudaMemset(*p, fill_byte, count * sizeof(T)));
+  return FERRY_OK;
+}
+
+void free_lru_state(ferry_lru* L) {
+  cudaFree(L->page_slot);
+  cudaFree(L->slot_page);
+  cudaFree(L->order);
+  cudaFree(L->size);
+  L->page_slot = L->slot_page = L->order = L->size = nullptr;
+}
+
+int alloc_lru_state(ferry_lru* L, int64_t lanes, int cap, int ids, uint32_t* err) {
+  L->lanes = (int)lanes;
+  L->cap = cap;
+  L->ids = ids;
+  L->err = err;
+  int rc;
+  if ((rc = dev_alloc(&L->page_slot, (size_t)lanes * ids, 0xFF))) return rc;
+  if ((rc = dev_alloc(&L->slot_page, (size_t)lanes * cap, 0xFF))) return rc;
+  if ((rc = dev_alloc(&L->order, (size_t)lanes * cap, 0))) return rc;
+  if ((rc = dev_alloc(&L->size, (size_t)lanes, 0))) return rc;
+  return FERRY_OK;
+}
+
+void destroy_ctx(ferry_ctx* c) {
+  if (!c) return;
+  free_lru_state(&c->lru);
+  cudaFree(c->cache);
+  cudaFree(c->ctx_pages);
+  cudaFree(c->summ);
+  cudaFree(c->ws);
+  cudaFree(c->part);
+  cudaFree(c->lane_done);
+  cudaFree(c->err);
+  cudaFree(c->stats);
+  delete c;
+}
+
+int validate_cfg(const ferry_cfg* cfg) {
+  if (!cfg) return set_error("cfg is NULL"), FERRY_E_INVAL;
+  if (cfg->head_dim != kHeadDim) return set_error("head_dim must be 128"), FERRY_E_INVAL;
+  if (cfg->page_tokens != kPageTokens) return set_error("page_tokens must be 16"), FERRY_E_INVAL;
+  if (cfg->kv_dtype != FERRY_KV_F16) return set_error("kv_dtype must be FERRY_KV_F16"), FERRY_E_INVAL;
+  if (cfg->num_requests < 1 || cfg->num_layers < 1 || cfg->kv_heads < 1 || cfg->q_heads < 1)
+    return set_error("num_requests, num_layers, q_heads, kv_heads must be >= 1"), FERRY_E_INVAL;
+  if (cfg->q_heads % cfg->kv_heads)
+    return set_error("q_heads %% kv_heads != 0"), FERRY_E_INVAL;
+  const int g = cfg->q_heads / cfg->kv_heads;
+  if (g != 1 && g != 2 && g != 4 && g != 8)
+    return set_error("GQA group %d not in {1,2,4,8}", g), FERRY_E_INVAL;
+  if (cfg->max_pages < 1 || cfg->max_pages > kMaxPages)
+    return set_error("max_pages must be in [1, %d]", kMaxPages), FERRY_E_INVAL;
+  if (cfg->cache_pages < 1 || cfg->top_k < 1 || cfg->top_k > cfg->cache_pages)
+    return set_error("need 1 <= top_k <= cache_pages"), FERRY_E_INVAL;
+  return FERRY_OK;
+}
+
+}  // namespace
+}  // namespace ferry
+
+using namespace ferry;
+
+extern "C" {
+
+const char* ferry_last_error(void) { return g_last_error.c_str(); }
+int ferry_version(void) { return 100; }
+
+int ferry_ctx_create(int device, const ferry_cfg* cfg, ferry_ctx** out) {
+  if (!out) return set_error("out is NULL"), FERRY_E_INVAL;
+  *out = nullptr;
+  int rc = validate_cfg(cfg);
+  if (rc) return rc;
+  int ndev = 0;
+  FERRY_TRY(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return set_error("device %d out of range", device), FERRY_E_INVAL;
+  DeviceGuard guard(device);
+  if (!guard.ok) return FERRY_E_CUDA;
+  auto* c = new ferry_ctx;
+  c->device = device;
+  c->cfg = *cfg;
+  c->group = cfg->q_heads / cfg->kv_heads;
+  c->lanes_per_req = cfg->num_layers * cfg->kv_heads;
+  c->lanes = (int64_t)cfg->num_requests * c->lanes_per_req;
+  cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
+  // attention chunking: smallest power-of-two chunk (>= 2 pages) that still
+  // gives every warp of the persistent grid ~4 chunks at a full batch
+  const int64_t warps = (int64_t)c->num_sms * 2 * 4;
+  int pc = 16;
+  while (pc > 2 && c->lanes * ((cfg->top_k + pc - 1) / pc) < 4 * warps) pc >>= 1;
+  c->chunk_pages = pc;
+  c->chunks_per_lane = (cfg->top_k + pc - 1) / pc;
+
+  const size_t R = cfg->num_requests, k = cfg->top_k;
+  const size_t LH = c->lanes_per_req;
+#define FERRY_CK(x)        \
+  if ((rc = (x))) {        \
+    destroy_ctx(c);        \
+    return rc;             \
+  }
+  FERRY_CK(dev_alloc(&c->err, 1, 0));
+  FERRY_CK(dev_alloc(&c->stats, 2, 0));
+  FERRY_CK(dev_alloc(&c->cache, (size_t)c->lanes * cfg->cache_pages * kUnitBytes, 0));
+  FERRY_CK(alloc_lru_state(&c->lru, c->lanes, cfg->cache_pages, cfg->max_pages, c->err));
+  c->lru.device = device;
+  FERRY_CK(dev_alloc(&c->ctx_pages, R, 0));
+  const size_t ws_ints = R * LH * (4 * k + 2);
+  FERRY_CK(dev_alloc(&c->ws, ws_ints, 0));
+  c->ws_sel = c->ws;
+  c->ws_islot = c->ws_sel + R * LH * k;
+  c->ws_mpage = c->ws_islot + R * LH * k;
+  c->ws_mslot = c->ws_mpage + R * LH * k;
+  c->ws_nsel = c->ws_mslot + R * LH * k;
+  c->ws_nmiss = c->ws_nsel + R * LH;
+  FERRY_CK(dev_alloc(&c->part, (size_t)c->lanes * c->chunks_per_lane * c->group * kPartStride, 0));
+  FERRY_CK(dev_alloc(&c->lane_done, (size_t)c->lanes, 0));
+#undef FERRY_CK
+  FERRY_TRY(cudaDeviceSynchronize());
+  *out = c;
+  return FERRY_OK;
+}
+
+int ferry_ctx_destroy(ferry_ctx* c) {
+  if (!c) return FERRY_OK;
+  DeviceGuard guard(c->device);
+  cudaDeviceSynchronize();
+  destroy_ctx(c);
+  return FERRY_OK;
+}
+
+int ferry_ctx_check(ferry_ctx* c) {
+  if (!c) return set_error("ctx is NULL"), FERRY_E_INVAL;
+  DeviceGuard guard(c->device);
+  FERRY_TRY(cudaDeviceSynchronize());
+  uint32_t e = 0;
+  FERRY_TRY(cudaMemcpy(&e, c->err, 4, cudaMemcpyDeviceToHost));
+  if (!e) return FERRY_OK;
+  FERRY_TRY(cudaMemset(c->err, 0, 4));
+  FERRY_TRY(cudaMemset(c->lane_done, 0, (size_t)c->lanes * 4));
+  if (e & kErrTimeout) return set_error("a device wait timed out"), FERRY_E_TIMEOUT;
+  return set_error("a kernel saw an out-of-range index"), FERRY_E_RANGE;
+}
+
+int ferry_host_alloc(size_t bytes, void** out) {
+  if (!out || bytes == 0) return set_error("bad arguments"), FERRY_E_INVAL;
+  cudaError_t e = cudaHostAlloc(out, bytes, cudaHostAllocMapped | cudaHostAllocPortable);
+  if (e != cudaSuccess) {
+    *out = nullptr;
+    return cuda_status(e, "cudaHostAlloc");
+  }
+  return FERRY_OK;
+}
+
+int ferry_host_free(void* p) {
+  if (p) FERRY_TRY(cudaFreeHost(p));
+  return FERRY_OK;
+}
+
+int ferry_kv_register(ferry_ctx* c, void* host_pool, size_t bytes) {
+  if (!c || !host_pool || bytes < (size_t)kUnitBytes || ((uintptr_t)host_pool & 15))
+    return set_error("kv_register: need a 16-byte aligned pool of >= one page unit"), FERRY_E_INVAL;
+  DeviceGuard guard(c->device);
+  void* dev = nullptr;
+  cudaError_t e = cudaHostGetDevicePointer(&dev, host_pool, 0);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error("kv_register: pool is not pinned+mapped host memory (use ferry_host_alloc)"),
+           FERRY_E_INVAL;
+  }
+  const uint64_t units = bytes / kUnitBytes;
+  float* summ = nullptr;
+  int rc = dev_alloc(&summ, (size_t)units * kHeadDim, 0);
+  if (rc) return rc;
+  cudaFree(c->summ);
+  c->summ = summ;
+  c->pool_dev = (uint8_t*)dev;
+  c->pool_units = units;
+  return FERRY_OK;
+}
+
+int ferry_kv_generate(void* stream, uint64_t seed, uint64_t unit0, int64_t n_units, void* dst) {
+  return launch_kv_generate((cudaStream_t)stream, seed, unit0, n_units, dst);
+}
+
+int ferry_page_summary_update(ferry_ctx* c, void* stream, int64_t unit0, int64_t n_units) {
+  if (!c) return set_error("ctx is NULL"), FERRY_E_INVAL;
+  if (!c->pool_dev) return set_error("no host pool registered"), FERRY_E_STATE;
+  if (unit0 < 0 || n_units < 0 || (uint64_t)(unit0 + n_units) > c->pool_units)
+    return set_error("summary range outside the pool"), FERRY_E_INVAL;
+  DeviceGuard guard(c->device);
+  return launch_summary((cudaStream_t)stream, c->pool_dev, unit0, n_units, c->summ);
+}
+
+int ferry_requests_begin(ferry_ctx* c, void* stream, const int32_t* d_req_ids,
+                         const int32_t* d_n_pages, int n) {
+  if (!c || n < 0 || n > c->cfg.num_requests || (n && (!d_req_ids || !d_n_pages)))
+    return set_error("requests_begin: bad arguments"), FERRY_E_INVAL;
+  DeviceGuard guard(c->device);
+  return launch_lru_reset(&c->lru, (cudaStream_t)stream, d_req_ids, n, c->lanes_per_req, d_n_pages,
+                          c->ctx_pages);
+}
+
+static int check_batch(const ferry_ctx* c, const int32_t* req_ids, int n_req) {
+  if (!c) return set_error("ctx is NULL"), FERRY_E_INVAL;
+  if (n_req < 0 || n_req > c->cfg.num_requests || (n_req && !req_ids))
+    return set_error("batch of %d requests (max %d)", n_req, c->cfg.num_requests), FERRY_E_INVAL;
+  return FERRY_OK;
+}
+
+int ferry_select_topk(ferry_ctx* c, void* stream, const uint16_t* d_q, const int32_t* d_req_ids,
+                      int n_req, int32_t* d_sel, int32_t* d_n_sel) {
+  int rc = check_batch(c, d_req_ids, n_req);
+  if (rc) return rc;
+  if (!c->summ) return set_error("no host pool registered (summaries missing)"), FERRY_E_STATE;
+  if (n_req && (!d_q || !d_sel || !d_n_sel)) return set_error("select: NULL buffer"), FERRY_E_INVAL;
+  DeviceGuard guard(c->device);
+  return launch_select(c, (cudaStream_t)stream, d_q, d_req_ids, n_req, d_sel, d_n_sel);
+}
+
+int ferry_detect_misses(ferry_ctx* c, void* stream, const int32_t* d_req_ids, int n_req,
+                        const int32_t* d_sel, const int32_t* d_n_sel, int32_t* d_item_slot,
+                        int32_t* d_miss_page, int32_t* d_miss_slot, int32_t* d_n_miss,
+                        uint8_t* d_is_miss) {
+  int rc = check_batch(c, d_req_ids, n_req);
+  if (rc) return rc;
+  DeviceGuard guard(c->device);
+  return launch_lru(&c->lru, (cudaStream_t)stream, nullptr, d_req_ids, c->lanes_per_req, nullptr,
+                    n_req * c->lanes_per_req, d_sel, c->cfg.top_k, d_n_sel, 1, d_is_miss,
+                    d_item_slot, d_miss_page, d_miss_slot, d_n_miss);
+}
+
+int ferry_gather_misses(ferry_ctx* c, void* stream, const int32_t* d_req_ids, int n_req,
+                        const int32_t* d_miss_page, const int32_t* d_miss_slot,
+                        const int32_t* d_n_miss) {
+  int rc = check_batch(c, d_req_ids, n_req);
+  if (rc) return rc;
+  if (n_req && (!d_miss_page || !d_miss_slot || !d_n_miss))
+    return set_error("gather: NULL buffer"), FERRY_E_INVAL;
+  DeviceGuard guard(c->device);
+  return launch_gather(c, (cudaStream_t)stream, d_req_ids, n_req, d_miss_page, d_miss_slot,
+                       d_n_miss);
+}
+
+int ferry_sparse_decode(ferry_ctx* c, void* stream, const uint16_t* d_q, const int32_t* d_req_ids,
+                        int n_req, const int32_t* d_item_slot, const int32_t* d_n_sel,
+                        float* d_out) {
+  int rc = check_batch(c, d_req_ids, n_req);
+  if (rc) return rc;
+  if (n_req && (!d_q || !d_item_slot || !d_n_sel || !d_out))
+    return set_error("sparse_decode: NULL buffer"), FERRY_E_INVAL;
+  DeviceGuard guard(c->device);
+  return launch_attention(c, (cudaStream_t)stream, d_q, d_req_ids, n_req, d_item_slot, d_n_sel,
+                          d_out);
+}
+
+int ferry_decode_step(ferry_ctx* c, void* stream, const uint16_t* d_q, const int32_t* d_req_ids,
+                      int n_req, float* d_out) {
+  int rc = check_batch(c, d_req_ids, n_req);
+  if (rc) return rc;
+  if (!c->summ || !c->pool_dev) return set_error("no host pool registered"), FERRY_E_STATE;
+  if (n_req && (!d_q || !d_out)) return set_error("decode_step: NULL buffer"), FERRY_E_INVAL;
+  DeviceGuard guard(c->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  if ((rc = launch_select(c, st, d_q, d_req_ids, n_req, c->ws_sel, c->ws_nsel))) return rc;
+  if ((rc = launch_lru(&c->lru, st, nullptr, d_req_ids, c->lanes_per_req, nullptr,
+                       n_req * c->lanes_per_req, c->ws_sel, c->cfg.top_k, c->ws_nsel, 1, nullptr,
+                       c->ws_islot, c->ws_mpage, c->ws_mslot, c->ws_nmiss)))
+    return rc;
+  if ((rc = launch_gather(c, st, d_req_ids, n_req, c->ws_mpage, c->ws_mslot, c->ws_nmiss))) return rc;
+  return launch_attention(c, st, d_q, d_req_ids, n_req, c->ws_islot, c->ws_nsel, d_out);
+}
+
+int ferry_stats_read(ferry_ctx* c, uint64_t* stats, int reset) {
+  if (!c || !stats) return set_error("bad arguments"), FERRY_E_INVAL;
+  DeviceGuard guard(c->device);
+  FERRY_TRY(cudaDeviceSynchronize());
+  FERRY_TRY(cudaMemcpy(stats, c->stats, 16, cudaMemcpyDeviceToHost));
+  if (reset) FERRY_TRY(cudaMemset(c->stats, 0, 16));
+  return FERRY_OK;
+}
+
+int ferry_debug_read(ferry_ctx* c, int which, size_t offset, size_t bytes, void* host_dst) {
+  if (!c || !host_dst) return set_error("bad arguments"), FERRY_E_INVAL;
+  const uint8_t* base = nullptr;
+  size_t size = 0;
+  const size_t R = c->cfg.num_requests, LH = c->lanes_per_req, k = c->cfg.top_k;
+  switch (which) {
+    case 0: base = c->cache; size = (size_t)c->lanes * c->cfg.cache_pages * kUnitBytes; break;
+    case 1: base = (uint8_t*)c->lru.page_slot; size = (size_t)c->lanes * c->cfg.max_pages * 4; break;
+    case 2: base = (uint8_t*)c->lru.order; size = (size_t)c->lanes * c->cfg.cache_pages * 4; break;
+    case 3: base = (uint8_t*)c->lru.size; size = (size_t)c->lanes * 4; break;
+    case 4: base = (uint8_t*)c->summ; size = (size_t)c->pool_units * kHeadDim * 4; break;
+    case 5: base = (uint8_t*)c->ctx_pages; size = R * 4; break;
+    case 6: base = (uint8_t*)c->ws; size = R * LH * (4 * k + 2) * 4; break;
+    default: return set_error("debug_read: unknown buffer %d", which), FERRY_E_INVAL;
+  }
+  if (!base || offset > size || bytes > size - offset)
+    return set_error("debug_read: range outside buffer %d", which), FERRY_E_INVAL;
+  DeviceGuard guard(c->device);
+  FERRY_TRY(cudaDeviceSynchronize());
+  FERRY_TRY(cudaMemcpy(host_dst, base + offset, bytes, cudaMemcpyDeviceToHost));
+  return FERRY_OK;
+}
+
+int ferry_lru_create(int device, int lanes, int capacity, int ids, ferry_lru** out) {
+  if (!out || lanes < 1 || capacity < 1 || ids < 1) return set_error("bad arguments"), FERRY_E_INVAL;
+  *out = nullptr;
+  DeviceGuard guard(device);
+  if (!guard.ok) return FERRY_E_CUDA;
+  auto* L = new ferry_lru;
+  L->device = device;
+  uint32_t* err = nullptr;
+  int rc = dev_alloc(&err, 1, 0);
+  if (!rc) rc = alloc_lru_state(L, lanes, capacity, ids, err);
+  if (rc) {
+    free_lru_state(L);
+    cudaFree(err);
+    delete L;
+    return rc;
+  }
+  *out = L;
+  return FERRY_OK;
+}
+
+int ferry_lru_destroy(ferry_lru* L) {
+  if (!L) return FERRY_OK;
+  DeviceGuard guard(L->device);
+  cudaDeviceSynchronize();
+  free_lru_state(L);
+  cudaFree(L->err);
+  delete L;
+  return FERRY_OK;
+}
+
+int ferry_lru_touch(ferry_lru* L, void* stream, const int32_t* d_lane_ids, const uint8_t* d_reset,
+                    int n, const int32_t* d_sel, int k, const int32_t* d_n_sel, int flags,
+                    uint8_t* d_is_miss, int32_t* d_item_slot, int32_t* d_miss_page,
+                    int32_t* d_miss_slot, int32_t* d_n_miss) {
+  if (!L || n < 0 || (n && !d_lane_ids)) return set_error("bad arguments"), FERRY_E_INVAL;
+  DeviceGuard guard(L->device);
+  return launch_lru(L, (cudaStream_t)stream, d_lane_ids, nullptr, 1, d_reset, n, d_sel, k, d_n_sel,
+                    (flags & FERRY_LRU_DISTINCT) ? 1 : 0, d_is_miss, d_item_slot, d_miss_page,
+                    d_miss_slot, d_n_miss);
+}
+
+int ferry_lru_read(ferry_lru* L, int lane, int32_t* page_slot, int32_t* lru_slots, int32_t* size) {
+  if (!L || lane < 0 || lane >= L->lanes || !page_slot || !lru_slots || !size)
+    return set_error("bad arguments"), FERRY_E_INVAL;
+  DeviceGuard guard(L->device);
+  FERRY_TRY(cudaDeviceSynchronize());
+  uint32_t e = 0;
+  FERRY_TRY(cudaMemcpy(&e, L->err, 4, cudaMemcpyDeviceToHost));
+  FERRY_TRY(cudaMemcpy(page_slot, L->page_slot + (size_t)lane * L->ids, (size_t)L->ids * 4,
+                       cudaMemcpyDeviceToHost));
+  FERRY_TRY(cudaMemcpy(lru_slots, L->order + (size_t)lane * L->cap, (size_t)L->cap * 4,
+                       cudaMemcpyDeviceToHost));
+  FERRY_TRY(cudaMemcpy(size, L->size + lane, 4, cudaMemcpyDeviceToHost));
+  if (e) {
+    cudaMemset(L->err, 0, 4);
+    return set_error("a kernel saw an out-of-range index"), FERRY_E_RANGE;
+  }
+  return FERRY_OK;
+}
+
+}  // extern "C"

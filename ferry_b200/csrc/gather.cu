@@ -1,0 +1,74 @@
+// gather.cu -- miss gather: missed page units from the pinned host pool (or a
+// peer GPU's memory) into their HBM cache slots.
+//
+// The reference moves misses with host-driven cudaMemcpyAsync through a
+// pinned ring (HostStagedChannel::submit, src/comm/host_staged_channel.cpp:43-74)
+// after sorting and run-merging them on the CPU
+// (src/runtime/wla_multigpu.cuh:2544-2593). Here the GPU pulls the pages
+// itself: one warp per missed page unit, 16 outstanding 16-byte loads per lane
+// (the whole 8 KiB unit in flight per warp), then 16 coalesced stores. The
+// copy is index-driven straight from the miss list, so there is no host hop,
+// no run merging and no per-run launch.
+#include "common.cuh"
+
+namespace ferry {
+namespace {
+
+__global__ void __launch_bounds__(256) gather_kernel(
+    const uint8_t* __restrict__ pool, uint64_t pool_units, uint8_t* __restrict__ cache, int N,
+    int C, const int32_t* __restrict__ req_ids, int lanes_per_req, int64_t lanes_total,
+    int n_lanes, const int32_t* __restrict__ miss_page, const int32_t* __restrict__ miss_slot,
+    const int32_t* __restrict__ n_miss, int k, unsigned long long* stats, uint32_t* err) {
+  const int t = threadIdx.x & 31;
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t total = (int64_t)n_lanes * k;
+  uint32_t copied = 0;
+  for (int64_t f = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); f < total;
+       f += nw) {
+    const int a = (int)(f / k), i = (int)(f % k);
+    if (i >= n_miss[a]) continue;  // warp-uniform
+    const int page = miss_page[(size_t)a * k + i];
+    const int slot = miss_slot[(size_t)a * k + i];
+    const int64_t gl = (int64_t)req_ids[a / lanes_per_req] * lanes_per_req + a % lanes_per_req;
+    if (page < 0 || page >= N || slot < 0 || slot >= C || gl < 0 || gl >= lanes_total) {
+      if (t == 0) record_error(err, kErrRange);
+      continue;
+    }
+    const uint64_t unit = ((uint64_t)gl * (uint64_t)N + (uint64_t)page) % pool_units;
+    const uint8_t* src = pool + unit * kUnitBytes;
+    uint8_t* dst = cache + ((uint64_t)gl * C + slot) * kUnitBytes;
+    uint4 r[kUnitBytes / (32 * 16)];
+#pragma unroll
+    for (int j = 0; j < kUnitBytes / (32 * 16); ++j) r[j] = ld_nc_v4(src + (size_t)(t + 32 * j) * 16);
+#pragma unroll
+    for (int j = 0; j < kUnitBytes / (32 * 16); ++j) st_v4(dst + (size_t)(t + 32 * j) * 16, r[j]);
+    ++copied;
+  }
+  if (t == 0 && copied && stats) {
+    atomicAdd(&stats[0], (unsigned long long)copied);
+    atomicAdd(&stats[1], (unsigned long long)copied * kUnitBytes);
+  }
+}
+
+}  // namespace
+
+int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, int n_req,
+                  const int32_t* miss_page, const int32_t* miss_slot, const int32_t* n_miss) {
+  if (n_req <= 0) return FERRY_OK;
+  if (!c->pool_dev) {
+    set_error("gather: no host pool registered");
+    return FERRY_E_STATE;
+  }
+  const int n_lanes = n_req * c->lanes_per_req;
+  const int64_t items = (int64_t)n_lanes * c->cfg.top_k;
+  // enough warps to keep the host link saturated, capped at 16 CTAs per SM
+  const int64_t blocks = std::min<int64_t>((items + 7) / 8, (int64_t)c->num_sms * 16);
+  gather_kernel<<<(unsigned)blocks, 256, 0, st>>>(
+      c->pool_dev, c->pool_units, c->cache, c->cfg.max_pages, c->cfg.cache_pages, req_ids,
+      c->lanes_per_req, c->lanes, n_lanes, miss_page, miss_slot, n_miss, c->cfg.top_k, c->stats,
+      c->err);
+  FERRY_TRY(cudaGetLastError());
+  return FERRY_OK;
+}
+
+}  // namespace ferry

@@ -1,0 +1,105 @@
+// kvgen.cu -- procedural KV pool generator and page-summary kernel.
+#include "common.cuh"
+
+namespace ferry {
+namespace {
+
+// Element e of page unit u: Irwin-Hall sum of twelve 16-bit uniforms drawn
+// from three splitmix64 outputs, z = (sum - 6*65536) / 65536 (variance 1,
+// exact in fp32), rounded once to fp16.
+__device__ __forceinline__ uint16_t kv_elem(uint64_t seed, uint64_t unit, uint32_t e) {
+  const uint64_t base = mix64(seed ^ mix64(unit * 4096ull + e));
+  uint32_t acc = 0;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const uint64_t h = mix64(base + (uint64_t)j);
+    acc += (uint32_t)(h & 0xFFFF) + (uint32_t)((h >> 16) & 0xFFFF) +
+           (uint32_t)((h >> 32) & 0xFFFF) + (uint32_t)(h >> 48);
+  }
+  const float z = __fmul_rn((float)((int32_t)acc - 6 * 65536), 1.0f / 65536.0f);
+  return __half_as_ushort(__float2half_rn(z));
+}
+
+// One thread writes 8 consecutive elements (one 16-byte store) so that
+// destinations in mapped host memory see full-width PCIe writes.
+__global__ void __launch_bounds__(256) kv_generate_kernel(uint64_t seed, uint64_t unit0,
+                                                          int64_t n_vec, uint4* dst) {
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < n_vec;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t unit = unit0 + (uint64_t)(v / (kUnitElems / 8));
+    const uint32_t e0 = (uint32_t)(v % (kUnitElems / 8)) * 8;
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      w[j] = (uint32_t)kv_elem(seed, unit, e0 + 2 * j) |
+             ((uint32_t)kv_elem(seed, unit, e0 + 2 * j + 1) << 16);
+    dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// summary[d] = (k_0[d] + ... + k_15[d]) * (1/16), token order, fp32. One warp
+// per unit; lane l owns dims 4l..4l+3 (8-byte loads, 256 B per row).
+__global__ void __launch_bounds__(256) summary_kernel(const uint8_t* __restrict__ pool,
+                                                      int64_t unit0, int64_t n_units,
+                                                      float* __restrict__ summ) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t u = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < n_units;
+       u += warps) {
+    const uint8_t* K = pool + (size_t)(unit0 + u) * kUnitBytes;
+    uint2 raw[kPageTokens];
+#pragma unroll
+    for (int t = 0; t < kPageTokens; ++t)
+      raw[t] = *reinterpret_cast<const uint2*>(K + t * kHeadDim * 2 + lane * 8);
+    float acc[4];
+#pragma unroll
+    for (int t = 0; t < kPageTokens; ++t) {
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw[t].x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw[t].y));
+      if (t == 0) {
+        acc[0] = a.x; acc[1] = a.y; acc[2] = b.x; acc[3] = b.y;
+      } else {
+        acc[0] = __fadd_rn(acc[0], a.x);
+        acc[1] = __fadd_rn(acc[1], a.y);
+        acc[2] = __fadd_rn(acc[2], b.x);
+        acc[3] = __fadd_rn(acc[3], b.y);
+      }
+    }
+    float4 s = make_float4(__fmul_rn(acc[0], 0.0625f), __fmul_rn(acc[1], 0.0625f),
+                           __fmul_rn(acc[2], 0.0625f), __fmul_rn(acc[3], 0.0625f));
+    reinterpret_cast<float4*>(summ + (size_t)(unit0 + u) * kHeadDim)[lane] = s;
+  }
+}
+
+}  // namespace
+
+int launch_kv_generate(cudaStream_t st, uint64_t seed, uint64_t unit0, int64_t n_units,
+                       void* dst) {
+  if (n_units <= 0) return FERRY_OK;
+  if (!dst || ((uintptr_t)dst & 15)) {
+    set_error("ferry_kv_generate: dst must be non-null and 16-byte aligned");
+    return FERRY_E_INVAL;
+  }
+  // pinned host memory: write through its device-side alias
+  cudaPointerAttributes attr{};
+  if (cudaPointerGetAttributes(&attr, dst) == cudaSuccess && attr.type == cudaMemoryTypeHost &&
+      attr.devicePointer)
+    dst = attr.devicePointer;
+  cudaGetLastError();
+  const int64_t n_vec = n_units * (kUnitElems / 8);
+  const int64_t blocks = std::min<int64_t>((n_vec + 255) / 256, 148 * 16);
+  kv_generate_kernel<<<(unsigned)blocks, 256, 0, st>>>(seed, unit0, n_vec, (uint4*)dst);
+  FERRY_TRY(cudaGetLastError());
+  return FERRY_OK;
+}
+
+int launch_summary(cudaStream_t st, const uint8_t* pool, int64_t unit0, int64_t n_units,
+                   float* summ) {
+  if (n_units <= 0) return FERRY_OK;
+  const int64_t blocks = std::min<int64_t>((n_units + 7) / 8, 148 * 16);
+  summary_kernel<<<(unsigned)blocks, 256, 0, st>>>(pool, unit0, n_units, summ);
+  FERRY_TRY(cudaGetLastError());
+  return FERRY_OK;
+}
+
+}  // namespace ferry

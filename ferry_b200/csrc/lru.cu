@@ -1,0 +1,337 @@
+// lru.cu -- miss detection against the HBM page cache (exact LRU per lane).
+//
+// Semantics (same as the reference deque LRU, src/workloads/missstream.cuh:137-161,
+// processed in selection order): a hit moves the page to MRU; a miss evicts
+// the LRU front when the lane holds `cap` pages, then appends the page. Slot
+// rule: a miss takes slot `size` while the lane is not full, else the slot of
+// the page it evicts. Per-lane state in HBM: page_slot[ids] (page -> slot or
+// -1), slot_page[cap], order[cap] (slots, LRU front first), size.
+//
+// One warp per lane. The warp loads the lane's order and slot table plus the
+// selection's page-table entries into shared memory (coalesced / gathered),
+// lane 0 replays the selection sequentially on shared memory only -- O(1) per
+// item using two lazily-deleted queues: the old order (pointer p, an entry is
+// live while its slot has not been touched this step) and this step's touch
+// list (pointer q, an entry is live while it is its slot's latest touch) --
+// and the warp then writes back the compacted order, slot table, page-table
+// deltas (evictions first, then final residents), and the miss list.
+#include "common.cuh"
+
+namespace ferry {
+namespace {
+
+struct LruArgs {
+  int32_t* page_slot;
+  int32_t* slot_page;
+  int32_t* order;
+  int32_t* size;
+  int lanes, cap, ids;
+  const int32_t* lane_ids;  // nullable: derive from req_ids
+  const int32_t* req_ids;
+  int lanes_per_req;
+  const uint8_t* reset;  // nullable
+  int n;
+  const int32_t* sel;
+  int k;
+  const int32_t* n_sel;
+  int distinct;
+  uint8_t* is_miss;  // nullable
+  int32_t* item_slot;
+  int32_t* miss_page;
+  int32_t* miss_slot;
+  int32_t* n_miss;
+  uint32_t* err;
+  int warp_ints;  // shared-memory ints per warp
+};
+
+__global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
+  extern __shared__ int32_t smem_i[];
+  const int t = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int a = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (a >= A.n) return;
+  const int C = A.cap, k = A.k;
+  int32_t* old = smem_i + (size_t)warp * A.warp_ints;
+  int32_t* spg = old + C;
+  int32_t* seq = spg + C;
+  int32_t* sel_s = seq + C;
+  int32_t* islot = sel_s + k;
+  int32_t* prev = islot + k;
+  int32_t* newl = prev + k;
+  int32_t* evict = newl + k;
+  uint8_t* mflag = reinterpret_cast<uint8_t*>(evict + k);
+  const uint32_t lt = (1u << t) - 1u;
+
+  const int64_t lane = A.lane_ids ? (int64_t)A.lane_ids[a]
+                                  : (int64_t)A.req_ids[a / A.lanes_per_req] * A.lanes_per_req +
+                                        a % A.lanes_per_req;
+  int n = A.n_sel[a];
+  if (lane < 0 || lane >= A.lanes || n < 0 || n > k) {
+    if (t == 0) {
+      record_error(A.err, kErrRange);
+      A.n_miss[a] = 0;
+    }
+    for (int i = t; i < k; i += 32) {
+      A.item_slot[(size_t)a * k + i] = -1;
+      if (A.is_miss) A.is_miss[(size_t)a * k + i] = 0;
+    }
+    return;
+  }
+  int32_t* ps = A.page_slot + lane * A.ids;
+  int32_t* sp = A.slot_page + lane * C;
+  int32_t* od = A.order + lane * C;
+  int sz0 = A.size[lane];
+  if (sz0 < 0 || sz0 > C) {
+    if (t == 0) record_error(A.err, kErrRange);
+    sz0 = 0;
+  }
+  const bool rst = A.reset && A.reset[a];
+
+  bool corrupt = false;
+  for (int j = t; j < sz0; j += 32) {
+    int o = od[j];
+    if (o < 0 || o >= C) {
+      corrupt = true;
+      o = 0;
+    }
+    old[j] = o;
+  }
+  if (__any_sync(0xffffffffu, corrupt) && t == 0) record_error(A.err, kErrRange);
+  for (int s = t; s < C; s += 32) {
+    spg[s] = s < sz0 ? sp[s] : -1;
+    seq[s] = -1;
+  }
+  __syncwarp();
+  if (rst) {
+    for (int s = t; s < sz0; s += 32) {
+      const int pg = spg[s];
+      if (pg >= 0 && pg < A.ids) ps[pg] = -1;
+      spg[s] = -1;
+    }
+    sz0 = 0;
+  }
+  __syncwarp();
+  bool bad = false;
+  for (int i = t; i < n; i += 32) {
+    int x = A.sel[(size_t)a * k + i];
+    if (x < 0 || x >= A.ids) {
+      bad = true;
+      x = -1;
+    }
+    sel_s[i] = x;
+    islot[i] = (x >= 0 && !rst) ? ps[x] : -1;
+  }
+  if (__any_sync(0xffffffffu, bad) && t == 0) record_error(A.err, kErrRange);
+  __syncwarp();
+  if (!A.distinct) {
+    for (int i = t; i < n; i += 32) {
+      const int x = sel_s[i];
+      int pj = -1;
+      if (x >= 0)
+        for (int j = i - 1; j >= 0; --j)
+          if (sel_s[j] == x) {
+            pj = j;
+            break;
+          }
+      prev[i] = pj;
+    }
+    __syncwarp();
+  }
+
+  // ---- sequential replay on shared memory (lane 0)
+  int p = 0, qn = 0, nn = 0, sz = sz0, ne = 0;
+  if (t == 0) {
+    for (int i = 0; i < n; ++i) {
+      const int x = sel_s[i];
+      if (x < 0) {
+        islot[i] = -1;
+        mflag[i] = 0;
+        continue;
+      }
+      int s = (!A.distinct && prev[i] >= 0) ? islot[prev[i]] : islot[i];
+      const bool hit = s >= 0 && s < C && spg[s] == x;
+      if (hit) {
+        seq[s] = nn;
+        newl[nn++] = s;
+        islot[i] = s;
+        mflag[i] = 0;
+      } else {
+        if (sz >= C) {
+          while (p < sz0 && seq[old[p]] != -1) ++p;
+          if (p < sz0) {
+            s = old[p++];
+          } else {
+            while (qn < nn - 1 && seq[newl[qn]] != qn) ++qn;
+            s = newl[qn++];
+          }
+          evict[ne++] = spg[s];
+        } else {
+          s = sz++;
+        }
+        spg[s] = x;
+        seq[s] = nn;
+        newl[nn++] = s;
+        islot[i] = s;
+        mflag[i] = 1;
+      }
+    }
+  }
+  __syncwarp();
+  p = __shfl_sync(0xffffffffu, p, 0);
+  qn = __shfl_sync(0xffffffffu, qn, 0);
+  nn = __shfl_sync(0xffffffffu, nn, 0);
+  sz = __shfl_sync(0xffffffffu, sz, 0);
+  ne = __shfl_sync(0xffffffffu, ne, 0);
+
+  // ---- new LRU order: live old entries, then live touch-list entries
+  int outp = 0;
+  for (int j0 = p; j0 < sz0; j0 += 32) {
+    const int j = j0 + t;
+    const bool live = j < sz0 && seq[old[j]] == -1;
+    const uint32_t m = __ballot_sync(0xffffffffu, live);
+    if (live) od[outp + __popc(m & lt)] = old[j];
+    outp += __popc(m);
+  }
+  for (int j0 = qn; j0 < nn; j0 += 32) {
+    const int j = j0 + t;
+    const bool live = j < nn && seq[newl[j]] == j;
+    const uint32_t m = __ballot_sync(0xffffffffu, live);
+    if (live) od[outp + __popc(m & lt)] = newl[j];
+    outp += __popc(m);
+  }
+  if (t == 0) A.size[lane] = sz;
+  for (int i = t; i < n; i += 32)
+    if (mflag[i]) sp[islot[i]] = spg[islot[i]];
+  // page table: evictions first, then the final residents among the misses
+  for (int e = t; e < ne; e += 32) {
+    const int v = evict[e];
+    if (v >= 0 && v < A.ids) ps[v] = -1;
+  }
+  __syncwarp();
+  for (int i = t; i < n; i += 32)
+    if (mflag[i]) {
+      const int s = islot[i];
+      if (spg[s] == sel_s[i]) ps[sel_s[i]] = s;
+    }
+
+  // ---- outputs
+  int nm = 0;
+  for (int i0 = 0; i0 < n; i0 += 32) {
+    const int i = i0 + t;
+    const bool f = i < n && mflag[i];
+    const uint32_t m = __ballot_sync(0xffffffffu, f);
+    if (f) {
+      const int r = nm + __popc(m & lt);
+      A.miss_page[(size_t)a * k + r] = sel_s[i];
+      A.miss_slot[(size_t)a * k + r] = islot[i];
+    }
+    nm += __popc(m);
+  }
+  for (int i = t; i < k; i += 32) {
+    A.item_slot[(size_t)a * k + i] = i < n ? islot[i] : -1;
+    if (A.is_miss) A.is_miss[(size_t)a * k + i] = i < n ? mflag[i] : 0;
+  }
+  if (t == 0) A.n_miss[a] = nm;
+}
+
+// Empty every lane of the listed requests and record their context length.
+__global__ void __launch_bounds__(256) lru_reset_kernel(int32_t* page_slot, int32_t* slot_page,
+                                                        int32_t* size, int lanes, int cap, int ids,
+                                                        const int32_t* req_ids, int n,
+                                                        int lanes_per_req, const int32_t* n_pages,
+                                                        int32_t* ctx_pages, int max_pages,
+                                                        uint32_t* err) {
+  const int t = threadIdx.x & 31;
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (w >= n * lanes_per_req) return;
+  const int i = w / lanes_per_req;
+  const int64_t lane = (int64_t)req_ids[i] * lanes_per_req + w % lanes_per_req;
+  if (lane < 0 || lane >= lanes) {
+    if (t == 0) record_error(err, kErrRange);
+    return;
+  }
+  int sz = size[lane];
+  if (sz < 0 || sz > cap) sz = cap;
+  int32_t* ps = page_slot + lane * ids;
+  const int32_t* sp = slot_page + lane * cap;
+  for (int s = t; s < sz; s += 32) {
+    const int pg = sp[s];
+    if (pg >= 0 && pg < ids) ps[pg] = -1;
+  }
+  if (t == 0) {
+    size[lane] = 0;
+    if (w % lanes_per_req == 0 && ctx_pages) {
+      int np = n_pages[i];
+      if (np < 0 || np > max_pages) {
+        record_error(err, kErrRange);
+        np = np < 0 ? 0 : max_pages;
+      }
+      ctx_pages[req_ids[i]] = np;
+    }
+  }
+}
+
+}  // namespace
+
+int launch_lru(const ferry_lru* L, cudaStream_t st, const int32_t* lane_ids,
+               const int32_t* req_ids, int lanes_per_req, const uint8_t* reset, int n,
+               const int32_t* sel, int k, const int32_t* n_sel, int distinct, uint8_t* is_miss,
+               int32_t* item_slot, int32_t* miss_page, int32_t* miss_slot, int32_t* n_miss) {
+  if (n <= 0) return FERRY_OK;
+  if (k <= 0 || !sel || !n_sel || !item_slot || !miss_page || !miss_slot || !n_miss) {
+    set_error("lru: bad arguments");
+    return FERRY_E_INVAL;
+  }
+  LruArgs A{};
+  A.page_slot = L->page_slot;
+  A.slot_page = L->slot_page;
+  A.order = L->order;
+  A.size = L->size;
+  A.lanes = L->lanes;
+  A.cap = L->cap;
+  A.ids = L->ids;
+  A.lane_ids = lane_ids;
+  A.req_ids = req_ids;
+  A.lanes_per_req = lanes_per_req;
+  A.reset = reset;
+  A.n = n;
+  A.sel = sel;
+  A.k = k;
+  A.n_sel = n_sel;
+  A.distinct = distinct;
+  A.is_miss = is_miss;
+  A.item_slot = item_slot;
+  A.miss_page = miss_page;
+  A.miss_slot = miss_slot;
+  A.n_miss = n_miss;
+  A.err = L->err;
+  // old, spg, seq (cap each) + sel, islot, prev, newl, evict (k each) + k flag bytes
+  A.warp_ints = ((3 * L->cap + 5 * k) + (k + 3) / 4 + 3) & ~3;
+  const size_t per_warp = (size_t)A.warp_ints * 4;
+  int warps = (int)std::min<size_t>(8, std::max<size_t>(1, (96 * 1024) / per_warp));
+  const size_t smem = per_warp * warps;
+  if (smem > 227 * 1024) {
+    set_error("lru: capacity %d / k %d need %zu bytes of shared memory per lane", L->cap, k,
+              per_warp);
+    return FERRY_E_INVAL;
+  }
+  if (smem > 48 * 1024)
+    FERRY_TRY(cudaFuncSetAttribute(lru_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)smem));
+  const unsigned grid = (unsigned)((n + warps - 1) / warps);
+  lru_kernel<<<grid, warps * 32, smem, st>>>(A);
+  FERRY_TRY(cudaGetLastError());
+  return FERRY_OK;
+}
+
+int launch_lru_reset(const ferry_lru* L, cudaStream_t st, const int32_t* req_ids, int n,
+                     int lanes_per_req, const int32_t* n_pages, int32_t* ctx_pages) {
+  if (n <= 0) return FERRY_OK;
+  const int warps = n * lanes_per_req;
+  lru_reset_kernel<<<(warps + 7) / 8, 256, 0, st>>>(L->page_slot, L->slot_page, L->size, L->lanes,
+                                                    L->cap, L->ids, req_ids, n, lanes_per_req,
+                                                    n_pages, ctx_pages, L->ids, L->err);
+  FERRY_TRY(cudaGetLastError());
+  return FERRY_OK;
+}
+
+}  // namespace ferry

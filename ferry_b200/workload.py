@@ -1,0 +1,136 @@
+"""Synthetic, seeded workloads of the sparse KV-cache miss-stream decode path.
+
+No public dataset is involved. The KV pool is procedural (``ferry_kv_generate``:
+counter hash -> Irwin-Hall N(0,1) -> fp16). Queries follow a per-(request,
+layer, head) AR(1) process, q_s = rho * q_{s-1} + sqrt(1 - rho^2) * eps_s, with
+rho calibrated so that consecutive steps re-select about 66% of their pages --
+the reuse share of the reference's synthetic selector
+(src/workloads/missstream.cuh:127). Arrivals are Poisson at ``arrival_rate``
+requests/s mapped onto a logical decode tick of ``tick_ms`` (the reference's
+measured clean decode step is 19.6 ms, results/realtrace_20261021.md:26), so
+the batch composition of every step is deterministic.
+"""
+from __future__ import annotations
+
+import dataclasses
+import math
+
+import numpy as np
+
+
+@dataclasses.dataclass(frozen=True)
+class Workload:
+    name: str
+    num_requests: int
+    num_layers: int
+    q_heads: int
+    kv_heads: int
+    ctx_tokens: int
+    top_k: int
+    cache_frac: float
+    steps: int
+    arrival_rate: float
+    tick_ms: float = 20.0
+    q_rho: float = 0.78
+    seed: int = 42
+    head_dim: int = 128
+    page_tokens: int = 16
+
+    @property
+    def max_pages(self) -> int:
+        return self.ctx_tokens // self.page_tokens
+
+    @property
+    def cache_pages(self) -> int:
+        return max(self.top_k, int(round(self.cache_frac * self.max_pages)))
+
+    @property
+    def lanes_per_req(self) -> int:
+        return self.num_layers * self.kv_heads
+
+    @property
+    def group(self) -> int:
+        return self.q_heads // self.kv_heads
+
+    @property
+    def pool_units(self) -> int:
+        return self.num_requests * self.lanes_per_req * self.max_pages
+
+    def cfg_dict(self) -> dict:
+        return dict(num_requests=self.num_requests, num_layers=self.num_layers,
+                    q_heads=self.q_heads, kv_heads=self.kv_heads, head_dim=self.head_dim,
+                    page_tokens=self.page_tokens, max_pages=self.max_pages,
+                    cache_pages=self.cache_pages, top_k=self.top_k)
+
+    # ---- bytes per decoded token (algorithmic roofline numerators)
+    def attn_bytes_per_token(self) -> int:
+        """KV of the selected pages: L * Hkv * k * 16 * 128 * 2 (K,V) * 2 B."""
+        return self.num_layers * self.kv_heads * self.top_k * self.page_tokens * self.head_dim * 4
+
+    def select_bytes_per_token(self) -> int:
+        """fp32 page summaries read by selection: L * Hkv * N * 128 * 4 B."""
+        return self.num_layers * self.kv_heads * self.max_pages * self.head_dim * 4
+
+    def qo_bytes_per_token(self) -> int:
+        return self.num_layers * self.q_heads * self.head_dim * (2 + 4)
+
+
+# configs[0] of the benchmark: single-layer Llama-7B-shaped sparse decode.
+CFG1 = Workload(name="cfg1", num_requests=16, num_layers=1, q_heads=32, kv_heads=32,
+                ctx_tokens=4096, top_k=64, cache_frac=0.25, steps=200, arrival_rate=50.0)
+
+WORKLOADS = {"cfg1": CFG1}
+
+
+def small(name: str = "tiny", **kw) -> Workload:
+    """A small workload for parity tests (the oracle finishes it in seconds)."""
+    base = dict(name=name, num_requests=4, num_layers=2, q_heads=4, kv_heads=4,
+                ctx_tokens=1024, top_k=16, cache_frac=0.25, steps=6, arrival_rate=200.0)
+    base.update(kw)
+    return Workload(**base)
+
+
+def arrival_ticks(w: Workload) -> np.ndarray:
+    """Decode tick at which each request joins (Poisson arrivals, seeded)."""
+    rng = np.random.default_rng(w.seed)
+    gaps = rng.exponential(1000.0 / w.arrival_rate, size=w.num_requests)
+    t_ms = np.cumsum(gaps)
+    return np.ceil(t_ms / w.tick_ms).astype(np.int64)
+
+
+class Schedule:
+    """Which requests decode at each tick of a job, and at which step.
+
+    A job runs every request for ``w.steps`` decode steps from its join tick;
+    ticks before the first arrival are skipped. ``tick(i)`` cycles over jobs:
+    job j (ticks [j*T, (j+1)*T)) replays the same arrivals with fresh request
+    state, so any number of ticks can be timed.
+    """
+
+    def __init__(self, w: Workload):
+        self.w = w
+        join = arrival_ticks(w)
+        self.join = join - join.min()
+        self.length = int(self.join.max()) + w.steps
+        self.total_tokens = w.num_requests * w.steps
+
+    def tick(self, i: int):
+        t = i % self.length
+        step = t - self.join
+        active = np.nonzero((step >= 0) & (step < self.w.steps))[0].astype(np.int32)
+        return active, step[active].astype(np.int32), i // self.length
+
+
+def q_stream(w: Workload, req: int, steps: int | None = None, job: int = 0) -> np.ndarray:
+    """AR(1) queries of one request: [steps][num_layers][q_heads][128] float16."""
+    steps = w.steps if steps is None else steps
+    rng = np.random.default_rng([w.seed, 7919, job, req])
+    shape = (w.num_layers, w.q_heads, w.head_dim)
+    out = np.empty((steps,) + shape, np.float16)
+    q = rng.standard_normal(shape, dtype=np.float32)
+    c = math.sqrt(1.0 - w.q_rho ** 2)
+    for s in range(steps):
+        if s:
+            q = w.q_rho * q + c * rng.standard_normal(shape, dtype=np.float32)
+        out[s] = q
+    return out

@@ -1,0 +1,343 @@
+"""CUDA path vs the CPU oracle on the same seeded inputs (B200 only).
+
+Selections, miss lists, page tables, slot assignment and gathered bytes must be
+bit-exact; attention outputs within 2e-3 relative error, measured per output
+row (lane, q head) as max|gpu - ref| / max|ref|.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ATTN_RTOL = 2e-3
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch
+
+
+def _rel_err(gpu, ref):
+    g = gpu.reshape(-1, 128).astype(np.float64)
+    r = ref.reshape(-1, 128).astype(np.float64)
+    scale = np.maximum(np.abs(r).max(axis=1), 1e-30)
+    return float((np.abs(g - r).max(axis=1) / scale).max())
+
+
+class Harness:
+    """A Decoder plus the oracle state that mirrors it."""
+
+    def __init__(self, torch, w, n_pages=None):
+        import oracle
+        from ferry_b200.engine import Decoder
+
+        self.t, self.w, self.o = torch, w, oracle
+        self.dec = Decoder(w, 0)
+        self.pool = self.dec.register_pool()
+        U = w.pool_units
+        self.units = self.pool.numpy(np.uint16).reshape(U, 4096)
+        self.summ = oracle.page_summary(self.units)
+        self.N, self.LH = w.max_pages, w.lanes_per_req
+        self.lru = oracle.LruLanes(w.num_requests * self.LH, w.cache_pages, self.N)
+        self.n_pages = np.full(w.num_requests, self.N, np.int32) if n_pages is None else np.asarray(n_pages, np.int32)
+        self.dev = torch.device("cuda", 0)
+
+    def begin(self, reqs):
+        reqs = np.asarray(reqs, np.int32)
+        t = self.t
+        self.dec.begin(t.from_numpy(reqs).to(self.dev), t.from_numpy(self.n_pages[reqs]).to(self.dev))
+        # mirror: empty the lanes in the oracle
+        lanes = (reqs[:, None] * self.LH + np.arange(self.LH)[None]).ravel().astype(np.int32)
+        k = self.w.top_k
+        self.lru.step(lanes, np.zeros((len(lanes), k), np.int32), n_sel=np.zeros(len(lanes), np.int32),
+                      reset=np.ones(len(lanes), np.uint8))
+
+    def glanes(self, reqs):
+        reqs = np.asarray(reqs, np.int32)
+        return (reqs[:, None] * self.LH + np.arange(self.LH)[None]).ravel().astype(np.int32)
+
+    def oracle_select(self, q, reqs):
+        w = self.w
+        gl = self.glanes(reqs)
+        idx = (gl[:, None].astype(np.int64) * self.N + np.arange(self.N)[None]) % w.pool_units
+        summ = self.summ[idx]
+        npg = np.repeat(self.n_pages[np.asarray(reqs)], self.LH)
+        qq = q.reshape(len(gl), w.group, 128).view(np.uint16)
+        return self.o.select_topk(qq, summ, npg, w.top_k)
+
+    def run_step(self, q_np, reqs, fused=False):
+        t, w, dec = self.t, self.w, self.dec
+        ids = t.from_numpy(np.asarray(reqs, np.int32)).to(self.dev)
+        q = t.from_numpy(q_np).to(self.dev)
+        out = t.zeros((len(reqs), w.num_layers, w.q_heads, 128), dtype=t.float32, device=self.dev)
+        if fused:
+            dec.step(q, ids, out)
+        else:
+            dec.select(q, ids)
+            dec.detect(ids)
+            dec.gather(ids)
+            dec.attention(q, ids, out)
+        t.cuda.synchronize()
+        dec.check()
+        return out.cpu().numpy()
+
+    def check_step(self, q_np, reqs):
+        """Separate-call step, every intermediate compared with the oracle."""
+        w, dec = self.w, self.dec
+        out = self.run_step(q_np, reqs)
+        nl = len(reqs) * self.LH
+        sel_ref, ns_ref = self.oracle_select(q_np, reqs)
+        sel = dec.sel[:nl].cpu().numpy()
+        ns = dec.n_sel[:nl].cpu().numpy()
+        assert (ns == ns_ref).all()
+        assert (sel == sel_ref).all()
+        gl = self.glanes(reqs)
+        im, islot, mp, ms, nm = self.lru.step(gl, sel_ref, n_sel=ns_ref)
+        assert (dec.n_miss[:nl].cpu().numpy() == nm).all()
+        assert (dec.is_miss[:nl].cpu().numpy() == im).all()
+        assert (dec.item_slot[:nl].cpu().numpy() == islot).all()
+        gmp, gms = dec.miss_page[:nl].cpu().numpy(), dec.miss_slot[:nl].cpu().numpy()
+        for a in range(nl):
+            assert (gmp[a, : nm[a]] == mp[a, : nm[a]]).all()
+            assert (gms[a, : nm[a]] == ms[a, : nm[a]]).all()
+        # gathered bytes: every selected page's slot holds that page's pool unit
+        C_ = w.cache_pages
+        pages = np.zeros((nl, w.top_k, 4096), np.uint16)
+        for a in range(nl):
+            for j in range(ns_ref[a]):
+                unit = (int(gl[a]) * self.N + int(sel_ref[a, j])) % w.pool_units
+                cached = dec.debug_read(0, np.uint16, 4096, offset_elems=(int(gl[a]) * C_ + int(islot[a, j])) * 4096)
+                assert (cached == self.units[unit]).all()
+                pages[a, j] = self.units[unit]
+        ref = self.o.sparse_decode(q_np.reshape(nl, w.group, 128).view(np.uint16), pages, ns_ref, 128 ** -0.5)
+        assert _rel_err(out.reshape(nl, w.group, 128), ref) <= ATTN_RTOL
+        return out, int(nm.sum())
+
+    def close(self):
+        self.dec.close()
+
+
+def _q(w, reqs, step, job=0):
+    from ferry_b200.workload import q_stream
+
+    return np.stack([q_stream(w, int(r), steps=step + 1, job=job)[step] for r in reqs])
+
+
+def test_kvgen_and_summaries_bit_exact(torch_cuda):
+    from ferry_b200.workload import small
+
+    import oracle
+
+    w = small(num_requests=2)
+    h = Harness(torch_cuda, w)
+    try:
+        U = w.pool_units
+        for u in [0, 1, 17, U // 2, U - 1]:
+            assert (h.units[u] == oracle.kv_gen(w.seed, u, 1)[0]).all()
+        gpu_summ = h.dec.debug_read(4, np.float32, U * 128).reshape(U, 128)
+        assert (gpu_summ.view(np.uint32) == h.summ.view(np.uint32)).all()
+    finally:
+        h.close()
+
+
+@pytest.mark.parametrize("shape", [
+    dict(),                                            # G=1, C=k
+    dict(q_heads=8, kv_heads=2, cache_frac=0.5),       # GQA group 4, C=2k
+    dict(q_heads=8, kv_heads=1, ctx_tokens=2048, top_k=32, cache_frac=0.25),  # group 8
+])
+def test_decode_steps_match_oracle(torch_cuda, shape):
+    from ferry_b200.workload import small
+
+    w = small(**shape)
+    reqs = list(range(w.num_requests))
+    n_pages = [w.max_pages, w.max_pages - 5, w.top_k // 2, w.top_k][: w.num_requests]
+    h = Harness(torch_cuda, w, n_pages=n_pages)
+    try:
+        h.begin(reqs)
+        misses = []
+        for s in range(4):
+            _, nm = h.check_step(_q(w, reqs, s), reqs)
+            misses.append(nm)
+        assert misses[0] > 0 and misses[1] < misses[0]    # warm cache after the first step
+        # restart two requests mid-run: their lanes come back cold
+        h.begin([1, 3])
+        h.check_step(_q(w, reqs, 4, job=1), reqs)
+        # a partial batch in a different order
+        h.check_step(_q(w, [2, 0], 5), [2, 0])
+    finally:
+        h.close()
+
+
+def test_fused_step_equals_separate_calls(torch_cuda):
+    from ferry_b200.workload import small
+
+    w = small()
+    reqs = [0, 1, 2, 3]
+    a, b = Harness(torch_cuda, w), Harness(torch_cuda, w)
+    try:
+        a.begin(reqs)
+        b.begin(reqs)
+        for s in range(3):
+            q = _q(w, reqs, s)
+            oa = a.run_step(q, reqs)
+            ob = b.run_step(q, reqs, fused=True)
+            assert (oa.view(np.uint32) == ob.view(np.uint32)).all()
+        la = a.dec.debug_read(1, np.int32, w.num_requests * w.lanes_per_req * w.max_pages)
+        lb = b.dec.debug_read(1, np.int32, w.num_requests * w.lanes_per_req * w.max_pages)
+        assert (la == lb).all()
+        ua, _ = a.dec.stats()
+        ub, nb = b.dec.stats()
+        assert ua == ub and nb == ub * 8192
+    finally:
+        a.close()
+        b.close()
+
+
+def _lru_touch(torch, L, lanes, sel, n_sel=None, reset=None, distinct=False):
+    from ferry_b200 import _abi
+
+    dev = torch.device("cuda", 0)
+    n, k = sel.shape
+    d = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+    lanes_d, sel_d = d(lanes.astype(np.int32)), d(sel.astype(np.int32))
+    ns_d = d(np.full(n, k, np.int32) if n_sel is None else n_sel.astype(np.int32))
+    rs_d = None if reset is None else d(reset.astype(np.uint8))
+    im = torch.zeros((n, k), dtype=torch.uint8, device=dev)
+    isl, mp, ms = (torch.full((n, k), -1, dtype=torch.int32, device=dev) for _ in range(3))
+    nm = torch.zeros(n, dtype=torch.int32, device=dev)
+    p = lambda t: None if t is None else C.c_void_p(t.data_ptr())
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    _abi.call("ferry_lru_touch", L, st, p(lanes_d), p(rs_d), n, p(sel_d), k, p(ns_d),
+              _abi.LRU_DISTINCT if distinct else 0, p(im), p(isl), p(mp), p(ms), p(nm))
+    torch.cuda.synchronize()
+    return im.cpu().numpy(), isl.cpu().numpy(), mp.cpu().numpy(), ms.cpu().numpy(), nm.cpu().numpy()
+
+
+def _lru_state(L, lane, ids, cap):
+    from ferry_b200 import _abi
+
+    ps = np.zeros(ids, np.int32)
+    order = np.zeros(cap, np.int32)
+    size = np.zeros(1, np.int32)
+    _abi.call("ferry_lru_read", L, lane, ps.ctypes.data_as(C.c_void_p), order.ctypes.data_as(C.c_void_p),
+              size.ctypes.data_as(C.c_void_p))
+    return ps, order[: size[0]], int(size[0])
+
+
+@pytest.mark.parametrize("which", ["fixture", "default"])
+def test_lru_kernel_on_reference_block_stream(torch_cuda, which):
+    """The device LRU replays the reference's own per-(request, layer) block
+    stream (duplicates included) with the reference's exact hit/miss flags."""
+    import oracle
+    from ferry_b200 import _abi
+
+    if which == "fixture":
+        z = np.load(os.path.join(GOLDEN, "refstream_small.npz"))
+        R, L_, S, G, hot = [int(x) for x in z["spec"][:5]]
+        blocks, miss = z["blocks"], z["is_miss"]
+    else:
+        R, L_, S, G, hot = 48, 12, 16, 64, 128
+        blocks, miss, tot = oracle.replay_miss_stream(oracle.miss_spec())
+        assert int(tot[1]) == 79550
+    ids = 64 + 8 * S
+    B = blocks.reshape(R, S, L_, G).astype(np.int32)
+    M = miss.reshape(R, S, L_, G)
+    h = C.c_void_p()
+    _abi.call("ferry_lru_create", 0, R * L_, hot, ids, C.byref(h))
+    mirror = oracle.LruLanes(R * L_, hot, ids)
+    try:
+        lanes = np.arange(R * L_, dtype=np.int32)
+        total_miss = 0
+        for s in range(S):
+            sel = B[:, s].reshape(R * L_, G)
+            im, isl, mp, ms, nm = _lru_touch(torch_cuda, h, lanes, sel)
+            assert (im == M[:, s].reshape(R * L_, G)).all()
+            rim, risl, rmp, rms, rnm = mirror.step(lanes, sel)
+            assert (isl == risl).all() and (nm == rnm).all()
+            for a in range(0, R * L_, 7):
+                assert (mp[a, : nm[a]] == rmp[a, : nm[a]]).all() and (ms[a, : nm[a]] == rms[a, : nm[a]]).all()
+            total_miss += int(nm.sum())
+        assert total_miss == int(M.sum())
+        for lane in [0, 1, R * L_ // 2, R * L_ - 1]:
+            g = _lru_state(h, lane, ids, hot)
+            r = mirror.state(lane)
+            assert (g[0] == r[0]).all() and (g[1] == r[1]).all() and g[2] == r[2]
+    finally:
+        _abi.call("ferry_lru_destroy", h)
+
+
+def test_lru_kernel_over_capacity_and_resets(torch_cuda):
+    """k > capacity (intra-step self eviction), resets and partial n_sel."""
+    import oracle
+    from ferry_b200 import _abi
+
+    rng = np.random.default_rng(9)
+    lanes_n, cap, ids, k = 16, 6, 40, 10
+    h = C.c_void_p()
+    _abi.call("ferry_lru_create", 0, lanes_n, cap, ids, C.byref(h))
+    mirror = oracle.LruLanes(lanes_n, cap, ids)
+    try:
+        for s in range(12):
+            lanes = rng.permutation(lanes_n)[:11].astype(np.int32)
+            sel = rng.integers(0, ids, size=(11, k)).astype(np.int32)
+            n_sel = rng.integers(0, k + 1, size=11).astype(np.int32)
+            reset = (rng.random(11) < 0.2).astype(np.uint8)
+            im, isl, mp, ms, nm = _lru_touch(torch_cuda, h, lanes, sel, n_sel, reset)
+            rim, risl, rmp, rms, rnm = mirror.step(lanes, sel, n_sel=n_sel, reset=reset)
+            for a in range(11):
+                n = n_sel[a]
+                assert (im[a, :n] == rim[a, :n]).all() and nm[a] == rnm[a]
+                assert (mp[a, : nm[a]] == rmp[a, : nm[a]]).all()
+        for lane in range(lanes_n):
+            g, r = _lru_state(h, lane, ids, cap), mirror.state(lane)
+            assert (g[0] == r[0]).all() and (g[1] == r[1]).all() and g[2] == r[2]
+    finally:
+        _abi.call("ferry_lru_destroy", h)
+
+
+def test_out_of_range_ids_are_reported_not_faulted(torch_cuda):
+    from ferry_b200 import _abi
+
+    h = C.c_void_p()
+    _abi.call("ferry_lru_create", 0, 2, 4, 8, C.byref(h))
+    try:
+        sel = np.array([[1, 99, 2, -3]], np.int32)
+        im, isl, mp, ms, nm = _lru_touch(torch_cuda, h, np.array([1], np.int32), sel)
+        assert nm.tolist() == [2] and im.tolist() == [[1, 0, 1, 0]]
+        ps = np.zeros(8, np.int32)
+        order = np.zeros(4, np.int32)
+        size = np.zeros(1, np.int32)
+        rc = _abi.lib().ferry_lru_read(h, 1, ps.ctypes.data_as(C.c_void_p), order.ctypes.data_as(C.c_void_p),
+                                       size.ctypes.data_as(C.c_void_p))
+        assert rc == _abi.E_RANGE
+        assert size[0] == 2 and ps[1] == 0 and ps[2] == 1
+    finally:
+        _abi.call("ferry_lru_destroy", h)
+
+
+def test_empty_batch_and_bad_batch(torch_cuda):
+    from ferry_b200 import FerryError
+    from ferry_b200.workload import small
+
+    w = small(num_requests=2)
+    h = Harness(torch_cuda, w)
+    try:
+        t = torch_cuda
+        ids = t.zeros(0, dtype=t.int32, device="cuda")
+        q = t.zeros((0, w.num_layers, w.q_heads, 128), dtype=t.float16, device="cuda")
+        out = t.zeros((0, w.num_layers, w.q_heads, 128), dtype=t.float32, device="cuda")
+        h.dec.step(q, ids, out)
+        with pytest.raises(FerryError):
+            big = t.zeros(3, dtype=t.int32, device="cuda")
+            h.dec.step(q, big, out)
+        h.dec.check()
+    finally:
+        h.close()

@@ -91,7 +91,7 @@ class Clocks:
         sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i]})
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
         return {"sm_mhz": float(np.median(sm)) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
                 "samples": len(rows)}

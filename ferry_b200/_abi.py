@@ -23,7 +23,7 @@ EXPORTS = [
     "ferry_ctx_check", "ferry_host_alloc", "ferry_host_free", "ferry_kv_register",
     "ferry_kv_generate", "ferry_page_summary_update", "ferry_requests_begin",
     "ferry_select_topk", "ferry_detect_misses", "ferry_gather_misses", "ferry_sparse_decode",
-    "ferry_decode_step", "ferry_stats_read", "ferry_debug_read", "ferry_lru_create",
+    "ferry_sparse_decode_noalloc", "ferry_decode_step", "ferry_stats_read", "ferry_debug_read", "ferry_lru_create",
     "ferry_lru_destroy", "ferry_lru_touch", "ferry_lru_read",
 ]
 
@@ -61,6 +61,7 @@ _SIGS = {
     "ferry_detect_misses": (I, [V, V, V, I, V, V, V, V, V, V, V]),
     "ferry_gather_misses": (I, [V, V, V, I, V, V, V]),
     "ferry_sparse_decode": (I, [V, V, V, V, I, V, V, V]),
+    "ferry_sparse_decode_noalloc": (I, [V, V, I, I, I, I, I, V, V, I, V, V, V]),
     "ferry_decode_step": (I, [V, V, V, V, I, V]),
     "ferry_stats_read": (I, [V, V, I]),
     "ferry_debug_read": (I, [V, I, C.c_size_t, C.c_size_t, V]),

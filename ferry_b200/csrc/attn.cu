@@ -15,6 +15,8 @@
 // Each chunk writes a partial (o[128], m, l) to scratch; the warp that
 // finishes a lane's last chunk (atomic count) combines the partials and
 // writes out[lane][g][128] in fp32.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace ferry {
@@ -298,3 +300,144 @@ int launch_attention(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,
 }
 
 }  // namespace ferry
+
+// ---------------------------------------------------------------------------
+// Allocation-free attention entry point.
+//
+// Some callers cannot call cudaMalloc: a serving engine that hands all of HBM
+// to its own KV arena or caching allocator at start-up (an extra cudaMalloc
+// fails or fragments that pool), and a decode loop on the latency-critical
+// path, where cudaMalloc's implicit device synchronisation would stall every
+// stream. ferry_sparse_decode_noalloc serves them: it runs the same attention
+// kernel, but its split-K partials and per-lane counters live in the
+// fixed-size array below instead of a ctx allocation, and the call allocates
+// nothing. The array is a file-scope __device__ object, so every GPU that
+// loads this library holds its 4 MiB until the process exits.
+//
+// Host code never passes g_noalloc_scratch itself to a kernel -- in host code
+// that name is only a host-side stand-in for the symbol. The device address is
+// looked up with cudaGetSymbolAddress the first time the entry point runs on
+// a device (with that device current) and cached per device; do that first
+// call before any stream capture. All calls share the array and it keeps the
+// last call's contents: each call clears the counters it needs before its
+// kernel, and calls that overlap on the GPU (different streams, or different
+// host threads on one device) race on it.
+// ---------------------------------------------------------------------------
+namespace ferry {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 4u << 20;
+constexpr size_t kNoAllocCounterBytes = 64u << 10;  // up to 16384 lanes of counters
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+int noalloc_scratch(int dev, void** out) {
+  if (dev < 0 || dev >= kMaxDevices) {
+    set_error("sparse_decode_noalloc: device %d out of range", dev);
+    return FERRY_E_INVAL;
+  }
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return FERRY_OK;
+}
+
+}  // namespace
+}  // namespace ferry
+
+extern "C" int ferry_sparse_decode_noalloc(void* stream, const void* d_cache, int cache_pages,
+                                           int num_requests, int lanes_per_req, int group,
+                                           int top_k, const uint16_t* d_q,
+                                           const int32_t* d_req_ids, int n_req,
+                                           const int32_t* d_item_slot, const int32_t* d_n_sel,
+                                           float* d_out) {
+  using namespace ferry;
+  if (cache_pages < 1 || num_requests < 1 || lanes_per_req < 1 || top_k < 1 ||
+      top_k > cache_pages || (group != 1 && group != 2 && group != 4 && group != 8) ||
+      n_req < 0 || n_req > num_requests) {
+    set_error("sparse_decode_noalloc: bad geometry");
+    return FERRY_E_INVAL;
+  }
+  if (n_req == 0) return FERRY_OK;
+  if (!d_cache || !d_q || !d_req_ids || !d_item_slot || !d_n_sel || !d_out) {
+    set_error("sparse_decode_noalloc: NULL buffer");
+    return FERRY_E_INVAL;
+  }
+  const int64_t n_lanes = (int64_t)n_req * lanes_per_req;
+  if (n_lanes * 4 > (int64_t)kNoAllocCounterBytes) {
+    set_error("sparse_decode_noalloc: %lld lanes exceed the %zu-lane maximum", (long long)n_lanes,
+              kNoAllocCounterBytes / 4);
+    return FERRY_E_INVAL;
+  }
+  int dev = 0, sms = 148;
+  FERRY_TRY(cudaGetDevice(&dev));
+  FERRY_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  // chunking as in the ctx path, coarsened until the partials fit the array
+  const size_t part_cap = kNoAllocScratchBytes - kNoAllocCounterBytes;
+  const int64_t warps = (int64_t)sms * 2 * 4;
+  int pc = 16;
+  while (pc > 2 && n_lanes * ((top_k + pc - 1) / pc) < 4 * warps) pc >>= 1;
+  auto need = [&](int p) {
+    return (size_t)n_lanes * ((top_k + p - 1) / p) * group * kPartStride * sizeof(float);
+  };
+  while (need(pc) > part_cap && pc < top_k) pc *= 2;
+  if (need(pc) > part_cap) {
+    set_error("sparse_decode_noalloc: batch needs %zu bytes of partials; the fixed scratch "
+              "holds %zu",
+              need(pc), part_cap);
+    return FERRY_E_INVAL;
+  }
+  void* base = nullptr;
+  int rc = noalloc_scratch(dev, &base);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  uint32_t* lane_done = reinterpret_cast<uint32_t*>(base);
+  float* part = reinterpret_cast<float*>(static_cast<unsigned char*>(base) + kNoAllocCounterBytes);
+  FERRY_TRY(cudaMemsetAsync(lane_done, 0, (size_t)n_lanes * 4, st));
+
+  AttnArgs A{};
+  A.q = d_q;
+  A.req_ids = d_req_ids;
+  A.lanes_per_req = lanes_per_req;
+  A.n_lanes = (int)n_lanes;
+  A.lanes_total = (int64_t)num_requests * lanes_per_req;
+  A.cache = static_cast<const uint8_t*>(d_cache);
+  A.C = cache_pages;
+  A.item_slot = d_item_slot;
+  A.n_sel = d_n_sel;
+  A.k = top_k;
+  A.chunk_pages = pc;
+  A.cpl = (top_k + pc - 1) / pc;
+  A.total = (int)(n_lanes * A.cpl);
+  A.part = part;
+  A.lane_done = lane_done;
+  A.out = d_out;
+  A.err = nullptr;  // no error word here: out-of-range ids are skipped, not reported
+  A.qscale = 1.4426950408889634f / sqrtf((float)kHeadDim);
+  const size_t smem = (size_t)kAttnWarps * kStages * (kUnitBytes + 8);
+  const int blocks = std::max(1, std::min(sms * 2, (A.total + kAttnWarps - 1) / kAttnWarps));
+  switch (group) {
+#define FERRY_NOALLOC_CASE(GG)                                                                \
+  case GG:                                                                                    \
+    FERRY_TRY(cudaFuncSetAttribute(attn_kernel<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                   (int)smem));                                               \
+    attn_kernel<GG><<<blocks, kAttnWarps * 32, smem, st>>>(A);                                \
+    break;
+    FERRY_NOALLOC_CASE(1)
+    FERRY_NOALLOC_CASE(2)
+    FERRY_NOALLOC_CASE(4)
+    FERRY_NOALLOC_CASE(8)
+#undef FERRY_NOALLOC_CASE
+  }
+  FERRY_TRY(cudaGetLastError());
+  return FERRY_OK;
+}

@@ -154,6 +154,27 @@ int ferry_sparse_decode(ferry_ctx* ctx, void* stream, const uint16_t* d_q,
                         const int32_t* d_req_ids, int n_req, const int32_t* d_item_slot,
                         const int32_t* d_n_sel, float* d_out);
 
+/* Allocation-free variant of ferry_sparse_decode. No counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc -- a serving
+ * engine that gives all of HBM to its own KV arena or caching allocator at
+ * start-up, or a decode loop on the latency-critical path where cudaMalloc's
+ * implicit device synchronisation would stall every stream. It needs no ctx:
+ * the caller passes the page cache (d_cache, num_requests * lanes_per_req *
+ * cache_pages page units, lane-major) and its geometry (group = q heads per kv
+ * head) plus the same q / req_ids / item_slot / n_sel / out as
+ * ferry_sparse_decode, on the current device. Scratch is a fixed 4 MiB
+ * __device__ array inside the library (held by every GPU that loads it until
+ * exit): at most 16384 lanes per call, and batches whose split-K partials do
+ * not fit are rejected with FERRY_E_INVAL. The first call on a device looks up
+ * the array's address (call it once before any stream capture). Calls share
+ * the array, so calls that overlap on the GPU race; out-of-range ids are
+ * skipped, not reported. */
+int ferry_sparse_decode_noalloc(void* stream, const void* d_cache, int cache_pages,
+                                int num_requests, int lanes_per_req, int group, int top_k,
+                                const uint16_t* d_q, const int32_t* d_req_ids, int n_req,
+                                const int32_t* d_item_slot, const int32_t* d_n_sel,
+                                float* d_out);
+
 /* One decode step = select -> detect -> gather -> attention on ctx-owned
  * workspace. Replaces exec_step mode C (src/runtime/wla_multigpu.cuh:2527-2604)
  * and run_miss_workload mode C (src/workloads/kv_exec.cuh:187-292). */

@@ -1,20 +1,31 @@
 // attn.cu -- paged sparse decode attention over the selected pages.
 //
-// Work is split into chunks of `chunk_pages` selected pages of one lane
-// (request, layer, kv_head); each warp walks a static stride of chunks and
-// streams their pages through a 3-stage shared-memory ring, each stage filled
-// by one 8 KiB cp.async.bulk (TMA engine) copy completing on an mbarrier. The
-// load cursor runs up to 3 pages ahead across chunk boundaries, so a warp's
-// copies never drain between chunks.
+// Work split. The batch's selected pages are laid out flat, index
+// x = lane * k + j (j < k; indices j >= n_sel[lane] are skipped). Warp w of nw
+// owns the contiguous range [w*T/nw, (w+1)*T/nw), T = n_lanes * k, so every
+// warp streams the same number of page slots (+-1) and no SM idles in a tail.
+// A warp's range covers a few lane segments; each segment leaves one partial
+// (o[128], m, l) in scratch slot lane + w (unique: ranges are ordered), and
+// the warp that completes a lane's last segment (atomic count) combines its
+// <= 32 partials -- one per warp lane -- into out.
 //
-// Per page and q head (lane l owns dims 4l..4l+3):
-//   logits  16 partial dots, then a transpose-reduce across the warp (8+4+2+1
-//           shuffles + 1) leaves token t>>1 in lane t,
-//   softmax online, base-2 (q pre-scaled by log2(e)/sqrt(128)),
-//   PV      p of token tt broadcast from lane 2tt, fp32 FMA into 4 dims.
-// Each chunk writes a partial (o[128], m, l) to scratch; the warp that
-// finishes a lane's last chunk (atomic count) combines the partials and
-// writes out[lane][g][128] in fp32.
+// Streaming. Each warp owns a 2-stage shared-memory ring; a stage is one 8 KiB
+// page unit filled by a single cp.async.bulk (TMA engine) completing on an
+// mbarrier (bounded waits). The load cursor walks the same flat range one page
+// ahead of compute, across lane boundaries. 2 stages keep the CTA at 64 KiB,
+// 3 CTAs (12 warps) per SM.
+//
+// Math per page and q head (fp32 accumulation). Half-warp h = t>>4 handles the
+// tokens of parity h; lane t owns dims 8*(t&15)..+8 (16-byte shared loads).
+//   QK: 8 partial dots per lane; lane t loads token 2*(i ^ m)+h at step i,
+//       m = (t&15)>>1, so the transpose-reduce over the half-warp (xor 8,4,2
+//       keep the low half, then xor 1 sums) needs no selects: 4+2+1+1
+//       shuffles leave token 2*m+h in lanes t and t^1.
+//   softmax: online, base 2 (q pre-scaled by log2(e)/sqrt(128)), max over the
+//       16 tokens by xor 2,4,8,16.
+//   PV: p written to a 16-float shared slot per warp, read back as 2 float4,
+//       8 tokens x 8 dims of FMA per lane; the two half-warps' o are summed
+//       once per segment.
 #include <mutex>
 
 #include "common.cuh"
@@ -23,8 +34,9 @@ namespace ferry {
 namespace {
 
 constexpr int kAttnWarps = 4;
-constexpr int kStages = 3;
+constexpr int kStages = 2;
 constexpr uint32_t kFull = 0xffffffffu;
+constexpr size_t kAttnSmem = (size_t)kAttnWarps * (kStages * kUnitBytes + kStages * 8 + 64);
 
 struct AttnArgs {
   const uint16_t* q;
@@ -37,9 +49,8 @@ struct AttnArgs {
   const int32_t* item_slot;
   const int32_t* n_sel;
   int k;
-  int chunk_pages;
-  int cpl;
-  int total;
+  int64_t T;  // n_lanes * k
+  int nw;     // warps sharing the flat range
   float* part;
   uint32_t* lane_done;
   float* out;
@@ -47,59 +58,84 @@ struct AttnArgs {
   float qscale;
 };
 
-__device__ __forceinline__ float2 h2f2(uint32_t w) {
-  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+__device__ __forceinline__ void h8_to_f(const uint4& r, float* f) {
+  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    f[2 * i] = v.x;
+    f[2 * i + 1] = v.y;
+  }
+}
+
+// end (exclusive, lane-relative) of the pages a warp processes in the lane
+// starting at flat index base: its range end, the lane end, and n_sel
+__device__ __forceinline__ int seg_end(int64_t x_hi, int64_t base, int k, int n) {
+  int64_t e = x_hi - base;
+  if (e > k) e = k;
+  if (e > n) e = n;
+  return (int)e;
+}
+
+// warp whose range holds flat index x
+__device__ __forceinline__ int warp_of(int64_t x, int nw, int64_t T) {
+  return (int)(((x + 1) * nw - 1) / T);
 }
 
 template <int G>
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnArgs A) {
+__global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_kernel(AttnArgs A) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, t = threadIdx.x & 31;
+  const int w = blockIdx.x * kAttnWarps + warp;
+  if (w >= A.nw) return;
   uint8_t* ring = smem + (size_t)warp * kStages * kUnitBytes;
-  uint64_t* bars =
-      reinterpret_cast<uint64_t*>(smem + (size_t)kAttnWarps * kStages * kUnitBytes) + warp * kStages;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kAttnWarps * kStages * kUnitBytes) +
+                   warp * kStages;
+  float* psm = reinterpret_cast<float*>(smem + (size_t)kAttnWarps * (kStages * kUnitBytes + kStages * 8)) +
+               warp * 16;
+  const int64_t x_lo = (int64_t)w * A.T / A.nw, x_hi = (int64_t)(w + 1) * A.T / A.nw;
+  if (x_lo >= x_hi) return;
   if (t == 0) {
 #pragma unroll
     for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
   }
   __syncwarp();
+  const int k = A.k;
+  const int h = t >> 4, d0 = 8 * (t & 15), m4 = (t & 15) >> 1;
 
-  const int gw = blockIdx.x * kAttnWarps + warp;
-  const int nw = gridDim.x * kAttnWarps;
-  const int PC = A.chunk_pages;
-
-  // ---- load cursor (runs ahead of compute, across chunks)
-  int lc = gw, lp = 0, l_np = 0, l_base = 0;
-  int64_t l_unit0 = 0;
-  // pages of chunk c (0 when the lane's request id or n_sel is out of range)
-  auto chunk_pages = [&](int c, int64_t* unit0) -> int {
-    const int a = c / A.cpl, j = c % A.cpl;
+  // valid pages of lane a (0 when its request id or n_sel is out of range)
+  auto lane_pages = [&](int a, int64_t* unit0) -> int {
     const int64_t gl =
         (int64_t)A.req_ids[a / A.lanes_per_req] * A.lanes_per_req + a % A.lanes_per_req;
     const int n = A.n_sel[a];
-    if (gl < 0 || gl >= A.lanes_total || n < 0 || n > A.k) {
-      if (t == 0 && j == 0) record_error(A.err, kErrRange);
+    if (gl < 0 || gl >= A.lanes_total || n < 0 || n > k) {
+      if (t == 0) record_error(A.err, kErrRange);
       return 0;
     }
     *unit0 = gl * A.C;
-    return max(0, min(PC, n - j * PC));
+    return n;
   };
-  auto load_chunk = [&](int c) {
-    l_np = chunk_pages(c, &l_unit0);
-    l_base = (c / A.cpl) * A.k + (c % A.cpl) * PC;
+
+  // ---- load cursor
+  int la = (int)(x_lo / k), lj = 0, lend = 0;
+  int64_t lunit0 = 0;
+  auto lane_begin = [&]() {
+    const int n = lane_pages(la, &lunit0);
+    const int64_t base = (int64_t)la * k;
+    lj = (int)(max(x_lo, base) - base);
+    lend = seg_end(x_hi, base, k, n);
   };
-  if (lc < A.total) load_chunk(lc);
+  lane_begin();
   uint32_t it_load = 0, it_use = 0;
   auto issue = [&]() {
-    while (lc < A.total && lp >= l_np) {
-      lc += nw;
-      lp = 0;
-      if (lc < A.total) load_chunk(lc);
+    while ((int64_t)la * k < x_hi && lj >= lend) {
+      ++la;
+      if ((int64_t)la * k < x_hi) lane_begin();
     }
-    if (lc >= A.total) return;
+    if ((int64_t)la * k >= x_hi) return;
     if (t == 0) {
-      int slot = A.item_slot[l_base + lp];
+      int slot = A.item_slot[(size_t)la * k + lj];
       if (slot < 0 || slot >= A.C) {
         record_error(A.err, kErrRange);
         slot = 0;
@@ -107,104 +143,111 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnArgs A) {
       const uint32_t s = it_load % kStages;
       fence_proxy_async_smem();
       mbar_arrive_expect_tx(&bars[s], kUnitBytes);
-      bulk_load(ring + (size_t)s * kUnitBytes, A.cache + (size_t)(l_unit0 + slot) * kUnitBytes,
+      bulk_load(ring + (size_t)s * kUnitBytes, A.cache + (size_t)(lunit0 + slot) * kUnitBytes,
                 kUnitBytes, &bars[s]);
     }
-    ++lp;
+    ++lj;
     ++it_load;
   };
 #pragma unroll
   for (int s = 0; s < kStages; ++s) issue();
 
   bool ok = true;
-  for (int c = gw; c < A.total && ok; c += nw) {
-    const int a = c / A.cpl;
-    int64_t unit0_unused = 0;
-    const int np = chunk_pages(c, &unit0_unused);
-    float qv[G][4], m[G], l[G], o[G][4];
+  for (int a = (int)(x_lo / k); (int64_t)a * k < x_hi && ok; ++a) {
+    int64_t unit0 = 0;
+    const int n = lane_pages(a, &unit0);
+    const int64_t base = (int64_t)a * k;
+    const int jlo = (int)(max(x_lo, base) - base);
+    const int jhi = seg_end(x_hi, base, k, n);
+    float qv[G][8], mx[G], ls[G], o[G][8];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      const uint2 raw = *reinterpret_cast<const uint2*>(A.q + ((size_t)a * G + g) * kHeadDim + t * 4);
-      const float2 x = h2f2(raw.x), y = h2f2(raw.y);
-      qv[g][0] = x.x * A.qscale; qv[g][1] = x.y * A.qscale;
-      qv[g][2] = y.x * A.qscale; qv[g][3] = y.y * A.qscale;
-      m[g] = -INFINITY; l[g] = 0.f;
-      o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+      const uint4 raw = *reinterpret_cast<const uint4*>(A.q + ((size_t)a * G + g) * kHeadDim + d0);
+      h8_to_f(raw, qv[g]);
+#pragma unroll
+      for (int d = 0; d < 8; ++d) {
+        qv[g][d] *= A.qscale;
+        o[g][d] = 0.f;
+      }
+      mx[g] = -INFINITY;
+      ls[g] = 0.f;
     }
-    for (int pp = 0; pp < np; ++pp) {
+    for (int j = jlo; j < jhi; ++j) {
       const uint32_t s = it_use % kStages, par = (it_use / kStages) & 1u;
       if (!mbar_wait(&bars[s], par, A.err)) {
         ok = false;
         break;
       }
       const uint8_t* pg = ring + (size_t)s * kUnitBytes;
-      const uint2* Kr = reinterpret_cast<const uint2*>(pg) + t;
-      const uint2* Vr = reinterpret_cast<const uint2*>(pg + kUnitBytes / 2) + t;
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        float v[16];
+        float v[8];
 #pragma unroll
-        for (int tt = 0; tt < 16; ++tt) {
-          const uint2 kk = Kr[tt * 32];
-          const float2 k01 = h2f2(kk.x), k23 = h2f2(kk.y);
-          float acc = qv[g][0] * k01.x;
-          acc = fmaf(qv[g][1], k01.y, acc);
-          acc = fmaf(qv[g][2], k23.x, acc);
-          v[tt] = fmaf(qv[g][3], k23.y, acc);
+        for (int i = 0; i < 8; ++i) {
+          const int tok = 2 * (i ^ m4) + h;
+          float kf[8];
+          h8_to_f(*reinterpret_cast<const uint4*>(pg + tok * 256 + d0 * 2), kf);
+          float acc = qv[g][0] * kf[0];
+#pragma unroll
+          for (int d = 1; d < 8; ++d) acc = fmaf(qv[g][d], kf[d], acc);
+          v[i] = acc;
         }
-        // transpose-reduce: token (t >> 1) ends in lanes t and t^1
-        float w8[8], w4[4], w2[2];
-        const bool b4 = t & 16, b3 = t & 8, b2 = t & 4, b1 = t & 2;
+        float w4[4], w2[2];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          w8[i] = (b4 ? v[8 + i] : v[i]) + __shfl_xor_sync(kFull, b4 ? v[i] : v[8 + i], 16);
+        for (int i = 0; i < 4; ++i) w4[i] = v[i] + __shfl_xor_sync(kFull, v[4 + i], 8);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          w4[i] = (b3 ? w8[4 + i] : w8[i]) + __shfl_xor_sync(kFull, b3 ? w8[i] : w8[4 + i], 8);
-#pragma unroll
-        for (int i = 0; i < 2; ++i)
-          w2[i] = (b2 ? w4[2 + i] : w4[i]) + __shfl_xor_sync(kFull, b2 ? w4[i] : w4[2 + i], 4);
-        float sc = (b1 ? w2[1] : w2[0]) + __shfl_xor_sync(kFull, b1 ? w2[0] : w2[1], 2);
-        sc += __shfl_xor_sync(kFull, sc, 1);
+        for (int i = 0; i < 2; ++i) w2[i] = w4[i] + __shfl_xor_sync(kFull, w4[2 + i], 4);
+        float sc = w2[0] + __shfl_xor_sync(kFull, w2[1], 2);
+        sc += __shfl_xor_sync(kFull, sc, 1);  // token 2*m4 + h
         float pm = sc;
         pm = fmaxf(pm, __shfl_xor_sync(kFull, pm, 2));
         pm = fmaxf(pm, __shfl_xor_sync(kFull, pm, 4));
         pm = fmaxf(pm, __shfl_xor_sync(kFull, pm, 8));
         pm = fmaxf(pm, __shfl_xor_sync(kFull, pm, 16));
-        const float mn = fmaxf(m[g], pm);
-        const float alpha = exp2f(m[g] - mn);  // 0 on the first page (m = -inf)
+        const float mn = fmaxf(mx[g], pm);
+        const float alpha = exp2f(mx[g] - mn);  // 0 on a segment's first page
         const float p = exp2f(sc - mn);
-        l[g] = l[g] * alpha + ((t & 1) ? 0.f : p);
+        ls[g] = ls[g] * alpha + ((t & 1) ? 0.f : p);
+        mx[g] = mn;
+        if (!(t & 1)) psm[h * 8 + m4] = p;  // slot of token 2*m4 + h
+        __syncwarp();
+        const float4 pa = *reinterpret_cast<const float4*>(psm + h * 8);
+        const float4 pb = *reinterpret_cast<const float4*>(psm + h * 8 + 4);
+        const float pt[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
 #pragma unroll
-        for (int d = 0; d < 4; ++d) o[g][d] *= alpha;
-        m[g] = mn;
+        for (int d = 0; d < 8; ++d) o[g][d] *= alpha;
 #pragma unroll
-        for (int tt = 0; tt < 16; ++tt) {
-          const float pt = __shfl_sync(kFull, p, 2 * tt);
-          const uint2 vv = Vr[tt * 32];
-          const float2 v01 = h2f2(vv.x), v23 = h2f2(vv.y);
-          o[g][0] = fmaf(pt, v01.x, o[g][0]);
-          o[g][1] = fmaf(pt, v01.y, o[g][1]);
-          o[g][2] = fmaf(pt, v23.x, o[g][2]);
-          o[g][3] = fmaf(pt, v23.y, o[g][3]);
+        for (int i = 0; i < 8; ++i) {
+          float vf[8];
+          h8_to_f(*reinterpret_cast<const uint4*>(pg + kUnitBytes / 2 + (2 * i + h) * 256 + d0 * 2), vf);
+#pragma unroll
+          for (int d = 0; d < 8; ++d) o[g][d] = fmaf(pt[i], vf[d], o[g][d]);
         }
+        __syncwarp();  // psm reused by the next head / page
       }
-      __syncwarp();
       ++it_use;
       issue();
     }
     if (!ok) break;
-    // ---- partial of this chunk
-    float* pc = A.part + (size_t)c * G * kPartStride;
+    // ---- partial of this lane segment: slot a + w
+    const int wf = warp_of(base, A.nw, A.T);
+    const int parts = warp_of(base + k - 1, A.nw, A.T) - wf + 1;
+    float* pc = A.part + ((size_t)a + w) * G * kPartStride;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      float ls = l[g];
+      float lsum = ls[g];
 #pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) ls += __shfl_xor_sync(kFull, ls, off);
-      reinterpret_cast<float4*>(pc + g * kPartStride)[t] = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
+      for (int off = 16; off >= 1; off >>= 1) lsum += __shfl_xor_sync(kFull, lsum, off);
+#pragma unroll
+      for (int d = 0; d < 8; ++d) o[g][d] += __shfl_xor_sync(kFull, o[g][d], 16);
+      if (t < 16) {
+        float4* dst = reinterpret_cast<float4*>(pc + g * kPartStride + d0);
+        dst[0] = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
+        dst[1] = make_float4(o[g][4], o[g][5], o[g][6], o[g][7]);
+      }
       if (t == 0) {
-        pc[g * kPartStride + 128] = m[g];
-        pc[g * kPartStride + 129] = ls;
+        pc[g * kPartStride + 128] = mx[g];
+        pc[g * kPartStride + 129] = lsum;
       }
     }
     __threadfence();
@@ -212,26 +255,31 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnArgs A) {
     uint32_t done = 0;
     if (t == 0) done = atomicAdd(&A.lane_done[a], 1u);
     done = __shfl_sync(kFull, done, 0);
-    if (done == (uint32_t)A.cpl - 1) {
+    if (done == (uint32_t)parts - 1) {
+      // combine: lane j holds partial j's (m, l); the o loads are independent
       __threadfence();
-      const float* pl = A.part + (size_t)a * A.cpl * G * kPartStride;
+      const float* pl = A.part + ((size_t)a + wf) * G * kPartStride;
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        float M = -INFINITY;
-        for (int jj = 0; jj < A.cpl; ++jj) M = fmaxf(M, __ldcg(pl + ((size_t)jj * G + g) * kPartStride + 128));
-        float L = 0.f;
+        const float* pj = pl + ((size_t)t * G + g) * kPartStride;
+        const bool have = t < parts;
+        const float mj = have ? __ldcg(pj + 128) : -INFINITY;
+        const float lj2 = have ? __ldcg(pj + 129) : 0.f;
+        float M = mj;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) M = fmaxf(M, __shfl_xor_sync(kFull, M, off));
+        const float wj = (M == -INFINITY || mj == -INFINITY) ? 0.f : exp2f(mj - M);
+        float L = lj2 * wj;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) L += __shfl_xor_sync(kFull, L, off);
         float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (M != -INFINITY) {
-          for (int jj = 0; jj < A.cpl; ++jj) {
-            const float* pj = pl + ((size_t)jj * G + g) * kPartStride;
-            const float mj = __ldcg(pj + 128);
-            if (mj == -INFINITY) continue;
-            const float w = exp2f(mj - M);
-            L = fmaf(__ldcg(pj + 129), w, L);
-            const float4 oj = __ldcg(reinterpret_cast<const float4*>(pj) + t);
-            O.x = fmaf(oj.x, w, O.x); O.y = fmaf(oj.y, w, O.y);
-            O.z = fmaf(oj.z, w, O.z); O.w = fmaf(oj.w, w, O.w);
-          }
+#pragma unroll 8
+        for (int jj = 0; jj < parts; ++jj) {
+          const float wt = __shfl_sync(kFull, wj, jj);
+          const float4 oj =
+              __ldcg(reinterpret_cast<const float4*>(pl + ((size_t)jj * G + g) * kPartStride) + t);
+          O.x = fmaf(oj.x, wt, O.x); O.y = fmaf(oj.y, wt, O.y);
+          O.z = fmaf(oj.z, wt, O.z); O.w = fmaf(oj.w, wt, O.w);
         }
         const float inv = L > 0.f ? 1.f / L : 0.f;
         reinterpret_cast<float4*>(A.out + ((size_t)a * G + g) * kHeadDim)[t] =
@@ -250,7 +298,42 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnArgs A) {
   }
 }
 
+// Warps that share the flat range: as many as fit resident, at least ~4 page
+// slots each, and at most 31 per lane so a lane has <= 32 partials.
+int attn_warps(int64_t T, int64_t n_lanes, int resident) {
+  int64_t nw = std::min<int64_t>(resident, std::max<int64_t>(1, T / 4));
+  nw = std::min<int64_t>(nw, std::max<int64_t>(1, 31 * n_lanes));
+  if (nw >= kAttnWarps) nw = nw / kAttnWarps * kAttnWarps;
+  return (int)nw;
+}
+
+template <int G>
+int launch_g(const AttnArgs& A, cudaStream_t st) {
+  FERRY_TRY(cudaFuncSetAttribute(attn_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kAttnSmem));
+  const int blocks = (A.nw + kAttnWarps - 1) / kAttnWarps;
+  attn_kernel<G><<<blocks, kAttnWarps * 32, kAttnSmem, st>>>(A);
+  FERRY_TRY(cudaGetLastError());
+  return FERRY_OK;
+}
+
+int launch_attn(const AttnArgs& A, int group, cudaStream_t st) {
+  switch (group) {
+    case 1: return launch_g<1>(A, st);
+    case 2: return launch_g<2>(A, st);
+    case 4: return launch_g<4>(A, st);
+    case 8: return launch_g<8>(A, st);
+    default:
+      set_error("attention: unsupported GQA group %d", group);
+      return FERRY_E_INVAL;
+  }
+}
+
+int resident_warps(int sms) { return sms * 3 * kAttnWarps; }
+
 }  // namespace
+
+size_t attention_partial_slots(int64_t lanes, int sms) { return (size_t)lanes + resident_warps(sms); }
 
 int launch_attention(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,
                      const int32_t* req_ids, int n_req, const int32_t* item_slot,
@@ -267,36 +350,14 @@ int launch_attention(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,
   A.item_slot = item_slot;
   A.n_sel = n_sel;
   A.k = c->cfg.top_k;
-  A.chunk_pages = c->chunk_pages;
-  A.cpl = c->chunks_per_lane;
-  A.total = A.n_lanes * A.cpl;
+  A.T = (int64_t)A.n_lanes * A.k;
+  A.nw = attn_warps(A.T, A.n_lanes, resident_warps(c->num_sms));
   A.part = c->part;
   A.lane_done = c->lane_done;
   A.out = out;
   A.err = c->err;
   A.qscale = 1.4426950408889634f / sqrtf((float)kHeadDim);
-  const size_t smem = (size_t)kAttnWarps * kStages * (kUnitBytes + 8);
-  const int max_blocks = c->num_sms * 2;
-  const int blocks = std::max(1, std::min(max_blocks, (A.total + kAttnWarps - 1) / kAttnWarps));
-#define FERRY_ATTN_CASE(GG)                                                                   \
-  case GG: {                                                                                  \
-    FERRY_TRY(cudaFuncSetAttribute(attn_kernel<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                   (int)smem));                                               \
-    attn_kernel<GG><<<blocks, kAttnWarps * 32, smem, st>>>(A);                                \
-    break;                                                                                    \
-  }
-  switch (c->group) {
-    FERRY_ATTN_CASE(1)
-    FERRY_ATTN_CASE(2)
-    FERRY_ATTN_CASE(4)
-    FERRY_ATTN_CASE(8)
-    default:
-      set_error("attention: unsupported GQA group %d", c->group);
-      return FERRY_E_INVAL;
-  }
-#undef FERRY_ATTN_CASE
-  FERRY_TRY(cudaGetLastError());
-  return FERRY_OK;
+  return launch_attn(A, c->group, st);
 }
 
 }  // namespace ferry
@@ -381,21 +442,19 @@ extern "C" int ferry_sparse_decode_noalloc(void* stream, const void* d_cache, in
   int dev = 0, sms = 148;
   FERRY_TRY(cudaGetDevice(&dev));
   FERRY_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  // chunking as in the ctx path, coarsened until the partials fit the array
+  // partial slots = lanes + warps; use fewer warps when the array is the limit
   const size_t part_cap = kNoAllocScratchBytes - kNoAllocCounterBytes;
-  const int64_t warps = (int64_t)sms * 2 * 4;
-  int pc = 16;
-  while (pc > 2 && n_lanes * ((top_k + pc - 1) / pc) < 4 * warps) pc >>= 1;
-  auto need = [&](int p) {
-    return (size_t)n_lanes * ((top_k + p - 1) / p) * group * kPartStride * sizeof(float);
-  };
-  while (need(pc) > part_cap && pc < top_k) pc *= 2;
-  if (need(pc) > part_cap) {
+  const size_t slot_bytes = (size_t)group * kPartStride * sizeof(float);
+  const int64_t T = n_lanes * top_k;
+  int nw = attn_warps(T, n_lanes, resident_warps(sms));
+  const int64_t fit = (int64_t)(part_cap / slot_bytes) - n_lanes;
+  if (fit < 1) {
     set_error("sparse_decode_noalloc: batch needs %zu bytes of partials; the fixed scratch "
               "holds %zu",
-              need(pc), part_cap);
+              (size_t)(n_lanes + 1) * slot_bytes, part_cap);
     return FERRY_E_INVAL;
   }
+  if (nw > fit) nw = fit >= kAttnWarps ? (int)(fit / kAttnWarps * kAttnWarps) : (int)fit;
   void* base = nullptr;
   int rc = noalloc_scratch(dev, &base);
   if (rc) return rc;
@@ -415,29 +474,12 @@ extern "C" int ferry_sparse_decode_noalloc(void* stream, const void* d_cache, in
   A.item_slot = d_item_slot;
   A.n_sel = d_n_sel;
   A.k = top_k;
-  A.chunk_pages = pc;
-  A.cpl = (top_k + pc - 1) / pc;
-  A.total = (int)(n_lanes * A.cpl);
+  A.T = T;
+  A.nw = nw;
   A.part = part;
   A.lane_done = lane_done;
   A.out = d_out;
   A.err = nullptr;  // no error word here: out-of-range ids are skipped, not reported
   A.qscale = 1.4426950408889634f / sqrtf((float)kHeadDim);
-  const size_t smem = (size_t)kAttnWarps * kStages * (kUnitBytes + 8);
-  const int blocks = std::max(1, std::min(sms * 2, (A.total + kAttnWarps - 1) / kAttnWarps));
-  switch (group) {
-#define FERRY_NOALLOC_CASE(GG)                                                                \
-  case GG:                                                                                    \
-    FERRY_TRY(cudaFuncSetAttribute(attn_kernel<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                   (int)smem));                                               \
-    attn_kernel<GG><<<blocks, kAttnWarps * 32, smem, st>>>(A);                                \
-    break;
-    FERRY_NOALLOC_CASE(1)
-    FERRY_NOALLOC_CASE(2)
-    FERRY_NOALLOC_CASE(4)
-    FERRY_NOALLOC_CASE(8)
-#undef FERRY_NOALLOC_CASE
-  }
-  FERRY_TRY(cudaGetLastError());
-  return FERRY_OK;
+  return launch_attn(A, group, st);
 }

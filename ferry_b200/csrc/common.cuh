@@ -149,8 +149,6 @@ struct ferry_ctx {
   int group = 1;          // q heads per kv head
   int lanes_per_req = 0;  // L * Hkv
   int64_t lanes = 0;      // R * L * Hkv
-  int chunk_pages = 8;    // attention split size (pages per work chunk)
-  int chunks_per_lane = 0;
 
   uint8_t* cache = nullptr;  // lanes * C units
   ferry_lru lru;             // page tables + LRU order, lanes x (C, N)
@@ -167,7 +165,7 @@ struct ferry_ctx {
           *ws_mslot = nullptr, *ws_nmiss = nullptr;
 
   // attention scratch
-  float* part = nullptr;          // lanes * chunks_per_lane * group * kPartStride
+  float* part = nullptr;          // attention_partial_slots * group * kPartStride
   uint32_t* lane_done = nullptr;  // lanes
   uint32_t* grid_done = nullptr;  // 1
 
@@ -193,6 +191,8 @@ int launch_lru_reset(const ferry_lru* L, cudaStream_t st, const int32_t* req_ids
                      int lanes_per_req, const int32_t* n_pages, int32_t* ctx_pages);
 int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, int n_req,
                   const int32_t* miss_page, const int32_t* miss_slot, const int32_t* n_miss);
+// partial slots the attention kernel needs for `lanes` lanes on `sms` SMs
+size_t attention_partial_slots(int64_t lanes, int sms);
 int launch_attention(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,
                      const int32_t* req_ids, int n_req, const int32_t* item_slot,
                      const int32_t* n_sel, float* out);

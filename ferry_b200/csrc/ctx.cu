@@ -134,13 +134,6 @@ int ferry_ctx_create(int device, const ferry_cfg* cfg, ferry_ctx** out) {
   c->lanes_per_req = cfg->num_layers * cfg->kv_heads;
   c->lanes = (int64_t)cfg->num_requests * c->lanes_per_req;
   cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
-  // attention chunking: smallest power-of-two chunk (>= 2 pages) that still
-  // gives every warp of the persistent grid ~4 chunks at a full batch
-  const int64_t warps = (int64_t)c->num_sms * 2 * 4;
-  int pc = 16;
-  while (pc > 2 && c->lanes * ((cfg->top_k + pc - 1) / pc) < 4 * warps) pc >>= 1;
-  c->chunk_pages = pc;
-  c->chunks_per_lane = (cfg->top_k + pc - 1) / pc;
 
   const size_t R = cfg->num_requests, k = cfg->top_k;
   const size_t LH = c->lanes_per_req;
@@ -163,7 +156,7 @@ int ferry_ctx_create(int device, const ferry_cfg* cfg, ferry_ctx** out) {
   c->ws_mslot = c->ws_mpage + R * LH * k;
   c->ws_nsel = c->ws_mslot + R * LH * k;
   c->ws_nmiss = c->ws_nsel + R * LH;
-  FERRY_CK(dev_alloc(&c->part, (size_t)c->lanes * c->chunks_per_lane * c->group * kPartStride, 0));
+  FERRY_CK(dev_alloc(&c->part, attention_partial_slots(c->lanes, c->num_sms) * c->group * kPartStride, 0));
   FERRY_CK(dev_alloc(&c->lane_done, (size_t)c->lanes, 0));
 #undef FERRY_CK
   FERRY_TRY(cudaDeviceSynchronize());

@@ -326,10 +326,10 @@ def run_ferry(args, w):
     e2e_value = e2e_tokens / (e2e_ms / 1e3)
 
     # ---------------------------------------------------------------- link peak (H2D from pinned)
-    src = torch.empty(512 << 20, dtype=torch.uint8).pin_memory()
-    dst = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    src = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
     best = 0.0
-    for _ in range(4):
+    for _ in range(5):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(st)
         dst.copy_(src, non_blocking=True)
@@ -373,7 +373,10 @@ def run_ferry(args, w):
             "roofline": {"bound": "hbm", "kernel": "attn_kernel", "achieved": achieved,
                          "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                          "peak_kind": peak_kind,
-                         "traffic": (traffic or {}).get("attn_bytes_per_launch"),
+                         # ncu DRAM bytes of a full-batch launch, scaled by this
+                         # run's algorithmic bytes per launch (profiles/ncu_traffic.json)
+                         "traffic": (traffic["traffic_over_algorithmic"] * attn_bytes / max(1, n_launch)
+                                     if traffic else None),
                          "bytes_per_launch": attn_bytes / max(1, n_launch)},
             "roofline_select": {"bound": "hbm", "achieved": sel_ach, "peak": hbm_peak,
                                 "unit": "GB/s", "frac": sel_ach / hbm_peak},

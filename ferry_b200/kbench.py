@@ -1,0 +1,83 @@
+"""Per-kernel timing of the decode path at a workload's full batch.
+
+    python -m ferry_b200.kbench [--workload cfg1] [--iters 50]
+
+Fills the cache with a few decode steps, then times each kernel alone with
+CUDA events over back-to-back launches on the same inputs (selected KV larger
+than L2, so each attention launch streams from HBM). Prints one JSON line:
+microseconds, algorithmic bytes and GB/s per kernel. ``-k regex:<kernel>``
+under ncu captures the same launches.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import numpy as np
+import torch
+
+from .engine import Decoder
+from .workload import WORKLOADS, q_stream
+
+
+def _time(fn, iters: int, warm: int = 3) -> float:
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) * 1e3 / iters  # us
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--workload", default="cfg1")
+    ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--device", type=int, default=0)
+    args = ap.parse_args()
+    w = WORKLOADS[args.workload]
+    torch.cuda.set_device(args.device)
+    dev = torch.device("cuda", args.device)
+    dec = Decoder(w, args.device)
+    dec.register_pool()
+    R = w.num_requests
+    ids = torch.arange(R, dtype=torch.int32, device=dev)
+    dec.begin(ids, torch.full((R,), w.max_pages, dtype=torch.int32, device=dev))
+    qs = [torch.from_numpy(np.stack([q_stream(w, r, steps=s + 1)[s] for r in range(R)])).to(dev)
+          for s in range(4)]
+    out = torch.empty((R, w.num_layers, w.q_heads, 128), dtype=torch.float32, device=dev)
+    for s in range(3):
+        dec.select(qs[s], ids)
+        dec.detect(ids)
+        dec.gather(ids)
+        dec.attention(qs[s], ids, out)
+    q = qs[3]
+    dec.select(q, ids)
+    dec.detect(ids)  # leaves this step's misses in the miss list
+    torch.cuda.synchronize()
+    dec.check()
+    units = int(dec.n_miss.sum().item())
+    res = {"workload": w.name, "batch_requests": R}
+    # gather re-copies the same miss list each launch (idempotent)
+    t = _time(lambda: dec.gather(ids), max(3, args.iters // 5))
+    res["gather"] = {"us": t, "bytes": units * 8192, "GB_s": units * 8192 / t / 1e3}
+    dec.gather(ids)
+    t = _time(lambda: dec.attention(q, ids, out), args.iters)
+    b = R * w.attn_bytes_per_token() + R * w.qo_bytes_per_token()
+    res["attention"] = {"us": t, "bytes": b, "GB_s": b / t / 1e3}
+    t = _time(lambda: dec.select(q, ids), args.iters)
+    b = R * w.select_bytes_per_token()
+    res["select"] = {"us": t, "bytes": b, "GB_s": b / t / 1e3}
+    t = _time(lambda: dec.detect(ids), args.iters)  # all hits after the first launch
+    res["detect"] = {"us": t}
+    dec.check()
+    dec.close()
+    print(json.dumps(res))
+
+
+if __name__ == "__main__":
+    main()

@@ -23,9 +23,16 @@ EXPORTS = [
     "ferry_ctx_check", "ferry_host_alloc", "ferry_host_free", "ferry_kv_register",
     "ferry_kv_generate", "ferry_page_summary_update", "ferry_requests_begin",
     "ferry_select_topk", "ferry_detect_misses", "ferry_gather_misses", "ferry_sparse_decode",
-    "ferry_sparse_decode_noalloc", "ferry_decode_step", "ferry_stats_read", "ferry_debug_read", "ferry_lru_create",
-    "ferry_lru_destroy", "ferry_lru_touch", "ferry_lru_read",
+    "ferry_sparse_decode_noalloc", "ferry_decode_step", "ferry_stats_read", "ferry_debug_read",
+    "ferry_ctx_export", "ferry_ctx_import", "ferry_ctx_link", "ferry_migrate_requests",
+    "ferry_slot_states", "ferry_deque_create", "ferry_deque_destroy", "ferry_deque_push",
+    "ferry_deque_pop", "ferry_deque_steal", "ferry_deque_size", "ferry_deque_export",
+    "ferry_deque_import", "ferry_deque_peer_view", "ferry_deque_stress",
+    "ferry_lru_create", "ferry_lru_destroy", "ferry_lru_touch", "ferry_lru_read",
 ]
+MAX_PEERS = 8
+CTX_HANDLE_BYTES = 1024
+MIGRATE_FULL, MIGRATE_DELTA = 0, 1
 
 
 class FerryError(RuntimeError):
@@ -56,7 +63,7 @@ _SIGS = {
     "ferry_kv_register": (I, [V, V, C.c_size_t]),
     "ferry_kv_generate": (I, [V, C.c_uint64, C.c_uint64, C.c_int64, V]),
     "ferry_page_summary_update": (I, [V, V, C.c_int64, C.c_int64]),
-    "ferry_requests_begin": (I, [V, V, V, V, I]),
+    "ferry_requests_begin": (I, [V, V, V, V, V, I]),
     "ferry_select_topk": (I, [V, V, V, V, I, V, V]),
     "ferry_detect_misses": (I, [V, V, V, I, V, V, V, V, V, V, V]),
     "ferry_gather_misses": (I, [V, V, V, I, V, V, V]),
@@ -65,6 +72,21 @@ _SIGS = {
     "ferry_decode_step": (I, [V, V, V, V, I, V]),
     "ferry_stats_read": (I, [V, V, I]),
     "ferry_debug_read": (I, [V, I, C.c_size_t, C.c_size_t, V]),
+    "ferry_ctx_export": (I, [V, V]),
+    "ferry_ctx_import": (I, [V, I, V]),
+    "ferry_ctx_link": (I, [V, I, V]),
+    "ferry_migrate_requests": (I, [V, V, I, V, V, I, I]),
+    "ferry_slot_states": (I, [V, V, I]),
+    "ferry_deque_create": (I, [I, C.c_uint64, C.POINTER(V)]),
+    "ferry_deque_destroy": (I, [V]),
+    "ferry_deque_push": (I, [V, V, V, I, V]),
+    "ferry_deque_pop": (I, [V, V, V, I, V]),
+    "ferry_deque_steal": (I, [V, V, V, I, V]),
+    "ferry_deque_size": (I, [V, V, V]),
+    "ferry_deque_export": (I, [V, V]),
+    "ferry_deque_import": (I, [I, V, C.c_uint64, C.POINTER(V)]),
+    "ferry_deque_peer_view": (I, [I, V, C.POINTER(V)]),
+    "ferry_deque_stress": (I, [I, C.c_uint64, I, I, I, V, V]),
     "ferry_lru_create": (I, [I, I, I, I, C.POINTER(V)]),
     "ferry_lru_destroy": (I, [V]),
     "ferry_lru_touch": (I, [V, V, V, V, I, V, I, V, I, V, V, V, V, V]),

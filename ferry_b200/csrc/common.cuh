@@ -4,8 +4,10 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstdio>
+#include <cstring>
 #include <string>
 
 #include "ferry_cuda.h"
@@ -143,6 +145,21 @@ struct ferry_lru {
   uint32_t* err = nullptr;       // device error record
 };
 
+// Another GPU's ctx buffers as this ctx's device sees them (peer mapping or
+// CUDA IPC mapping); see peer.cu.
+struct ferry_peer {
+  bool ipc = false;
+  int device = -1;
+  uint8_t* cache = nullptr;
+  int32_t* page_slot = nullptr;
+  int32_t* slot_page = nullptr;
+  int32_t* order = nullptr;
+  int32_t* size = nullptr;
+  int32_t* ctx_pages = nullptr;
+  int32_t* slot_state = nullptr;
+  int64_t* req_base = nullptr;
+};
+
 struct ferry_ctx {
   int device = -1;
   ferry_cfg cfg{};
@@ -153,6 +170,7 @@ struct ferry_ctx {
   uint8_t* cache = nullptr;  // lanes * C units
   ferry_lru lru;             // page tables + LRU order, lanes x (C, N)
   int32_t* ctx_pages = nullptr;  // R
+  int64_t* req_base = nullptr;   // R: pool unit of the request's (lane 0, page 0)
 
   // host pool
   uint8_t* pool_dev = nullptr;  // device-visible address of the pinned pool
@@ -170,7 +188,9 @@ struct ferry_ctx {
   uint32_t* grid_done = nullptr;  // 1
 
   uint32_t* err = nullptr;                // device error record
-  unsigned long long* stats = nullptr;    // [0] units gathered, [1] bytes
+  unsigned long long* stats = nullptr;    // [0,1] units/bytes gathered, [2,3] units/bytes migrated in
+  int32_t* slot_state = nullptr;          // R: 2 = request migrated away by a peer
+  ferry_peer peers[FERRY_MAX_PEERS];
   int num_sms = 148;
 };
 
@@ -188,9 +208,11 @@ int launch_lru(const ferry_lru* L, cudaStream_t st, const int32_t* lane_ids, con
                const int32_t* n_sel, int distinct, uint8_t* is_miss, int32_t* item_slot,
                int32_t* miss_page, int32_t* miss_slot, int32_t* n_miss);
 int launch_lru_reset(const ferry_lru* L, cudaStream_t st, const int32_t* req_ids, int n,
-                     int lanes_per_req, const int32_t* n_pages, int32_t* ctx_pages);
+                     int lanes_per_req, const int32_t* n_pages, int32_t* ctx_pages,
+                     const int64_t* pool_base, int64_t* req_base);
 int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, int n_req,
                   const int32_t* miss_page, const int32_t* miss_slot, const int32_t* n_miss);
+void close_all_peers(ferry_ctx* c);
 // partial slots the attention kernel needs for `lanes` lanes on `sms` SMs
 size_t attention_partial_slots(int64_t lanes, int sms);
 int launch_attention(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,

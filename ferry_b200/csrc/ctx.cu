@@ -3,6 +3,7 @@
 #include <cstdarg>
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "common.cuh"
 
@@ -76,9 +77,12 @@ int alloc_lru_state(ferry_lru* L, int64_t lanes, int cap, int ids, uint32_t* err
 
 void destroy_ctx(ferry_ctx* c) {
   if (!c) return;
+  close_all_peers(c);
+  cudaFree(c->slot_state);
   free_lru_state(&c->lru);
   cudaFree(c->cache);
   cudaFree(c->ctx_pages);
+  cudaFree(c->req_base);
   cudaFree(c->summ);
   cudaFree(c->ws);
   cudaFree(c->part);
@@ -143,11 +147,19 @@ int ferry_ctx_create(int device, const ferry_cfg* cfg, ferry_ctx** out) {
     return rc;             \
   }
   FERRY_CK(dev_alloc(&c->err, 1, 0));
-  FERRY_CK(dev_alloc(&c->stats, 2, 0));
+  FERRY_CK(dev_alloc(&c->stats, 4, 0));
+  FERRY_CK(dev_alloc(&c->slot_state, (size_t)cfg->num_requests, 0));
   FERRY_CK(dev_alloc(&c->cache, (size_t)c->lanes * cfg->cache_pages * kUnitBytes, 0));
   FERRY_CK(alloc_lru_state(&c->lru, c->lanes, cfg->cache_pages, cfg->max_pages, c->err));
   c->lru.device = device;
   FERRY_CK(dev_alloc(&c->ctx_pages, R, 0));
+  FERRY_CK(dev_alloc(&c->req_base, R, 0));
+  {
+    // default home of request slot r in the host pool: units r*L*Hkv*N onwards
+    std::vector<int64_t> base(R);
+    for (size_t r = 0; r < R; ++r) base[r] = (int64_t)r * (int64_t)LH * cfg->max_pages;
+    FERRY_TRY(cudaMemcpy(c->req_base, base.data(), R * 8, cudaMemcpyHostToDevice));
+  }
   const size_t ws_ints = R * LH * (4 * k + 2);
   FERRY_CK(dev_alloc(&c->ws, ws_ints, 0));
   c->ws_sel = c->ws;
@@ -236,12 +248,12 @@ int ferry_page_summary_update(ferry_ctx* c, void* stream, int64_t unit0, int64_t
 }
 
 int ferry_requests_begin(ferry_ctx* c, void* stream, const int32_t* d_req_ids,
-                         const int32_t* d_n_pages, int n) {
+                         const int32_t* d_n_pages, const int64_t* d_pool_base, int n) {
   if (!c || n < 0 || n > c->cfg.num_requests || (n && (!d_req_ids || !d_n_pages)))
     return set_error("requests_begin: bad arguments"), FERRY_E_INVAL;
   DeviceGuard guard(c->device);
   return launch_lru_reset(&c->lru, (cudaStream_t)stream, d_req_ids, n, c->lanes_per_req, d_n_pages,
-                          c->ctx_pages);
+                          c->ctx_pages, d_pool_base, c->req_base);
 }
 
 static int check_batch(const ferry_ctx* c, const int32_t* req_ids, int n_req) {
@@ -318,8 +330,8 @@ int ferry_stats_read(ferry_ctx* c, uint64_t* stats, int reset) {
   if (!c || !stats) return set_error("bad arguments"), FERRY_E_INVAL;
   DeviceGuard guard(c->device);
   FERRY_TRY(cudaDeviceSynchronize());
-  FERRY_TRY(cudaMemcpy(stats, c->stats, 16, cudaMemcpyDeviceToHost));
-  if (reset) FERRY_TRY(cudaMemset(c->stats, 0, 16));
+  FERRY_TRY(cudaMemcpy(stats, c->stats, 32, cudaMemcpyDeviceToHost));
+  if (reset) FERRY_TRY(cudaMemset(c->stats, 0, 32));
   return FERRY_OK;
 }
 
@@ -336,6 +348,7 @@ int ferry_debug_read(ferry_ctx* c, int which, size_t offset, size_t bytes, void*
     case 4: base = (uint8_t*)c->summ; size = (size_t)c->pool_units * kHeadDim * 4; break;
     case 5: base = (uint8_t*)c->ctx_pages; size = R * 4; break;
     case 6: base = (uint8_t*)c->ws; size = R * LH * (4 * k + 2) * 4; break;
+    case 7: base = (uint8_t*)c->req_base; size = R * 8; break;
     default: return set_error("debug_read: unknown buffer %d", which), FERRY_E_INVAL;
   }
   if (!base || offset > size || bytes > size - offset)

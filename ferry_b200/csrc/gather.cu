@@ -18,7 +18,8 @@ __global__ void __launch_bounds__(256) gather_kernel(
     const uint8_t* __restrict__ pool, uint64_t pool_units, uint8_t* __restrict__ cache, int N,
     int C, const int32_t* __restrict__ req_ids, int lanes_per_req, int64_t lanes_total,
     int n_lanes, const int32_t* __restrict__ miss_page, const int32_t* __restrict__ miss_slot,
-    const int32_t* __restrict__ n_miss, int k, unsigned long long* stats, uint32_t* err) {
+    const int32_t* __restrict__ n_miss, int k, const int64_t* __restrict__ req_base,
+    unsigned long long* stats, uint32_t* err) {
   const int t = threadIdx.x & 31;
   const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int64_t total = (int64_t)n_lanes * k;
@@ -29,12 +30,14 @@ __global__ void __launch_bounds__(256) gather_kernel(
     if (i >= n_miss[a]) continue;  // warp-uniform
     const int page = miss_page[(size_t)a * k + i];
     const int slot = miss_slot[(size_t)a * k + i];
-    const int64_t gl = (int64_t)req_ids[a / lanes_per_req] * lanes_per_req + a % lanes_per_req;
+    const int req = req_ids[a / lanes_per_req];
+    const int64_t gl = (int64_t)req * lanes_per_req + a % lanes_per_req;
     if (page < 0 || page >= N || slot < 0 || slot >= C || gl < 0 || gl >= lanes_total) {
       if (t == 0) record_error(err, kErrRange);
       continue;
     }
-    const uint64_t unit = ((uint64_t)gl * (uint64_t)N + (uint64_t)page) % pool_units;
+    const uint64_t unit =
+        (uint64_t)(req_base[req] + (int64_t)(a % lanes_per_req) * N + page) % pool_units;
     const uint8_t* src = pool + unit * kUnitBytes;
     uint8_t* dst = cache + ((uint64_t)gl * C + slot) * kUnitBytes;
     uint4 r[kUnitBytes / (32 * 16)];
@@ -65,8 +68,8 @@ int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, i
   const int64_t blocks = std::min<int64_t>((items + 7) / 8, (int64_t)c->num_sms * 16);
   gather_kernel<<<(unsigned)blocks, 256, 0, st>>>(
       c->pool_dev, c->pool_units, c->cache, c->cfg.max_pages, c->cfg.cache_pages, req_ids,
-      c->lanes_per_req, c->lanes, n_lanes, miss_page, miss_slot, n_miss, c->cfg.top_k, c->stats,
-      c->err);
+      c->lanes_per_req, c->lanes, n_lanes, miss_page, miss_slot, n_miss, c->cfg.top_k, c->req_base,
+      c->stats, c->err);
   FERRY_TRY(cudaGetLastError());
   return FERRY_OK;
 }

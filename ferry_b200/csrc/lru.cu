@@ -239,6 +239,7 @@ __global__ void __launch_bounds__(256) lru_reset_kernel(int32_t* page_slot, int3
                                                         const int32_t* req_ids, int n,
                                                         int lanes_per_req, const int32_t* n_pages,
                                                         int32_t* ctx_pages, int max_pages,
+                                                        const int64_t* pool_base, int64_t* req_base,
                                                         uint32_t* err) {
   const int t = threadIdx.x & 31;
   const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -266,6 +267,9 @@ __global__ void __launch_bounds__(256) lru_reset_kernel(int32_t* page_slot, int3
         np = np < 0 ? 0 : max_pages;
       }
       ctx_pages[req_ids[i]] = np;
+      if (req_base)
+        req_base[req_ids[i]] = pool_base ? pool_base[i]
+                                         : (int64_t)req_ids[i] * lanes_per_req * (int64_t)max_pages;
     }
   }
 }
@@ -324,12 +328,14 @@ int launch_lru(const ferry_lru* L, cudaStream_t st, const int32_t* lane_ids,
 }
 
 int launch_lru_reset(const ferry_lru* L, cudaStream_t st, const int32_t* req_ids, int n,
-                     int lanes_per_req, const int32_t* n_pages, int32_t* ctx_pages) {
+                     int lanes_per_req, const int32_t* n_pages, int32_t* ctx_pages,
+                     const int64_t* pool_base, int64_t* req_base) {
   if (n <= 0) return FERRY_OK;
   const int warps = n * lanes_per_req;
   lru_reset_kernel<<<(warps + 7) / 8, 256, 0, st>>>(L->page_slot, L->slot_page, L->size, L->lanes,
                                                     L->cap, L->ids, req_ids, n, lanes_per_req,
-                                                    n_pages, ctx_pages, L->ids, L->err);
+                                                    n_pages, ctx_pages, L->ids, pool_base, req_base,
+                                                    L->err);
   FERRY_TRY(cudaGetLastError());
   return FERRY_OK;
 }

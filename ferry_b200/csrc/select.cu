@@ -40,7 +40,8 @@ __device__ __forceinline__ uint32_t block_excl_scan(bool flag, uint32_t* warp_to
 template <int G>
 __global__ void __launch_bounds__(kSelThreads) select_kernel(
     const uint16_t* __restrict__ q, const int32_t* __restrict__ req_ids, int lanes_per_req,
-    const int32_t* __restrict__ ctx_pages, const float* __restrict__ summ, uint64_t pool_units,
+    const int32_t* __restrict__ ctx_pages, const int64_t* __restrict__ req_base,
+    const float* __restrict__ summ, uint64_t pool_units,
     int N, int k, int num_requests, int32_t* __restrict__ sel_out,
     int32_t* __restrict__ n_sel_out, uint32_t* err) {
   extern __shared__ uint32_t keys[];  // N entries
@@ -77,7 +78,8 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
     const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
     qv[g][0] = x.x; qv[g][1] = x.y; qv[g][2] = y.x; qv[g][3] = y.y;
   }
-  const uint64_t ubase = (uint64_t)gl * (uint64_t)N;
+  // pool units of this lane: request home + lane-in-request * N (+ page)
+  const uint64_t ubase = (uint64_t)(req_base[req] + (int64_t)(a % lanes_per_req) * N);
   constexpr int U = 4;
   for (int p0 = warp * U; p0 < np; p0 += kSelWarps * U) {
     float4 s[U];
@@ -192,7 +194,7 @@ int launch_select(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,
     if (smem > 48 * 1024)                                                                     \
       FERRY_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,       \
                                      (int)smem));                                             \
-    kern<<<grid, kSelThreads, smem, st>>>(q, req_ids, c->lanes_per_req, c->ctx_pages, c->summ, \
+    kern<<<grid, kSelThreads, smem, st>>>(q, req_ids, c->lanes_per_req, c->ctx_pages, c->req_base, c->summ, \
                                           c->pool_units, N, k, c->cfg.num_requests, sel,      \
                                           n_sel, c->err);                                     \
     break;                                                                                    \

@@ -95,9 +95,12 @@ class Decoder:
         self.pool = pool
         return pool
 
-    def begin(self, req_ids: torch.Tensor, n_pages: torch.Tensor, stream=None):
+    def begin(self, req_ids: torch.Tensor, n_pages: torch.Tensor, stream=None,
+              pool_base: torch.Tensor | None = None):
+        """Start requests (cold lanes). pool_base (int64, optional): each
+        request's first unit in the host pool; default slot * L * Hkv * N."""
         call("ferry_requests_begin", self.ctx, _stream(stream), _ptr(req_ids), _ptr(n_pages),
-             int(req_ids.numel()))
+             _ptr(pool_base), int(req_ids.numel()))
 
     # ------------------------------------------------------------------ steps
     def select(self, q: torch.Tensor, req_ids: torch.Tensor, stream=None):
@@ -127,9 +130,14 @@ class Decoder:
         call("ferry_ctx_check", self.ctx)
 
     def stats(self, reset: bool = False) -> tuple[int, int]:
-        s = (C.c_uint64 * 2)()
+        """(page units gathered, gather bytes) since the last reset."""
+        return self.all_stats(reset)[:2]
+
+    def all_stats(self, reset: bool = False) -> tuple[int, int, int, int]:
+        """(units gathered, gather bytes, units migrated in, migration bytes)."""
+        s = (C.c_uint64 * 4)()
         call("ferry_stats_read", self.ctx, s, int(reset))
-        return int(s[0]), int(s[1])
+        return int(s[0]), int(s[1]), int(s[2]), int(s[3])
 
     def debug_read(self, which: int, dtype, count: int, offset_elems: int = 0) -> np.ndarray:
         out = np.empty(count, dtype)

@@ -108,13 +108,17 @@ int ferry_kv_generate(void* stream, uint64_t seed, uint64_t unit0, int64_t n_uni
  * (tools/capture_miss_trace.py:139-147). */
 int ferry_page_summary_update(ferry_ctx* ctx, void* stream, int64_t unit0, int64_t n_units);
 
-/* Start (or restart) requests: set their context length in pages and empty
- * their lanes' cache state. d_req_ids / d_n_pages: n device ints. Replaces the
- * per-request LRU state creation of replay_miss_stream
- * (src/workloads/missstream.cuh:107-114) and kv_handoff(carry=false)
+/* Start (or restart) requests: set their context length in pages, their home
+ * in the host pool, and empty their lanes' cache state. d_req_ids / d_n_pages:
+ * n device ints; d_pool_base: n device int64 (nullable) -- the pool unit of
+ * the request's (lane 0, page 0); lane l of the request, page p is unit
+ * (base + l * max_pages + p) % pool_units. NULL uses req * L * Hkv * max_pages.
+ * Replaces the per-request LRU state creation of replay_miss_stream
+ * (src/workloads/missstream.cuh:107-114), the slab offsets wla_slab_off
+ * (src/runtime/wla_multigpu.cuh:323-332) and kv_handoff(carry=false)
  * (src/runtime/wla_multigpu.cuh:1970-1987). */
 int ferry_requests_begin(ferry_ctx* ctx, void* stream, const int32_t* d_req_ids,
-                         const int32_t* d_n_pages, int n);
+                         const int32_t* d_n_pages, const int64_t* d_pool_base, int n);
 
 /* ---- the four hot-path steps --------------------------------------------- */
 
@@ -181,15 +185,70 @@ int ferry_sparse_decode_noalloc(void* stream, const void* d_cache, int cache_pag
 int ferry_decode_step(ferry_ctx* ctx, void* stream, const uint16_t* d_q,
                       const int32_t* d_req_ids, int n_req, float* d_out);
 
-/* Read (and optionally zero) the ctx counters: stats[0] = page units gathered,
- * stats[1] = gather bytes. Synchronous. */
+/* Read (and optionally zero) the ctx counters into stats[4]: [0] page units
+ * gathered, [1] gather bytes, [2] page units migrated in, [3] migration bytes.
+ * Synchronous. */
 int ferry_stats_read(ferry_ctx* ctx, uint64_t* stats, int reset);
 
 /* Copy ctx device state to host for checking (synchronous).
  * which: 0 cache bytes, 1 page_slot, 2 lru order, 3 lru size, 4 summaries,
- * 5 ctx pages, 6 decode-step workspace (sel | n_sel | item_slot | miss_page |
- * miss_slot | n_miss, each sized for num_requests). */
+ * 5 ctx pages, 6 decode-step workspace (sel | item_slot | miss_page |
+ * miss_slot | n_sel | n_miss, each sized for num_requests), 7 request pool
+ * bases (int64). */
 int ferry_debug_read(ferry_ctx* ctx, int which, size_t offset, size_t bytes, void* host_dst);
+
+/* ---- multi-GPU: request migration over NVLink ------------------------------
+ * Replaces steal_from's transfer (src/runtime/wla_multigpu.cuh:1353-1468:
+ * gather kernel -> D2H -> H2D through the host ring -> scatter kernel) and
+ * kv_handoff (:1970-1987). A peer is another GPU's ctx of the same geometry,
+ * mapped into this ctx's device: ferry_ctx_link for a ctx in this process
+ * (enables peer access), or ferry_ctx_export (owner) + ferry_ctx_import
+ * (thief) through CUDA IPC for one process per GPU. Migration runs on the
+ * thief: it pulls each request's lane state (LRU order, slot table, page
+ * table, context length) and its cache pages with 128-bit peer loads --
+ * FERRY_MIGRATE_DELTA copies only resident slots (the reference's kv-mode
+ * delta), FERRY_MIGRATE_FULL every slot -- then marks the victim's request
+ * slot as migrated (ferry_slot_states reads those marks). */
+#define FERRY_MAX_PEERS 8
+#define FERRY_CTX_HANDLE_BYTES 1024
+#define FERRY_MIGRATE_FULL 0
+#define FERRY_MIGRATE_DELTA 1
+int ferry_ctx_export(ferry_ctx* ctx, void* handle /* FERRY_CTX_HANDLE_BYTES */);
+int ferry_ctx_import(ferry_ctx* ctx, int peer_slot, const void* handle);
+int ferry_ctx_link(ferry_ctx* ctx, int peer_slot, ferry_ctx* peer);
+int ferry_migrate_requests(ferry_ctx* ctx, void* stream, int peer_slot, const int32_t* d_src_req,
+                           const int32_t* d_dst_req, int n, int mode);
+/* Synchronous copy of the R request-slot states (2 = migrated away by a peer);
+ * clear_migrated resets those marks to 0 after reading. */
+int ferry_slot_states(ferry_ctx* ctx, int32_t* host_out, int clear_migrated);
+
+/* ---- multi-GPU: device-visible work-stealing deque --------------------------
+ * Replaces the reference's host std::deque + mutex steal path
+ * (src/runtime/wla_multigpu.cuh:1063-1506) and its device ring with unbounded
+ * spins (src/queue/gpu_bounded_queue.cuh:70-198). Chase-Lev deque of 64-bit
+ * tasks in the owner GPU's memory: the owner pushes and pops at the bottom,
+ * any GPU that maps it steals from the top with a system-scope CAS. No call
+ * waits on another party: a steal gives up after a bounded number of lost
+ * races and reports the tasks it got. Results land in device memory on the
+ * caller's stream (d_pushed / d_count / d_size). */
+typedef struct ferry_deque ferry_deque;
+int ferry_deque_create(int device, uint64_t capacity, ferry_deque** out);
+int ferry_deque_destroy(ferry_deque* q);
+int ferry_deque_push(ferry_deque* q, void* stream, const uint64_t* d_tasks, int n, int32_t* d_pushed);
+int ferry_deque_pop(ferry_deque* q, void* stream, uint64_t* d_out, int max_n, int32_t* d_count);
+int ferry_deque_steal(ferry_deque* q, void* stream, uint64_t* d_out, int max_n, int32_t* d_count);
+int ferry_deque_size(ferry_deque* q, void* stream, int64_t* d_size);
+/* IPC export (64-byte handle) / import of an owner's deque, and a
+ * same-process view from another device (enables peer access). */
+int ferry_deque_export(ferry_deque* q, void* handle64);
+int ferry_deque_import(int device, const void* handle64, uint64_t capacity, ferry_deque** out);
+int ferry_deque_peer_view(int device, ferry_deque* owner, ferry_deque** out);
+/* Exactly-once check under contention (the twin of the reference's
+ * bench_queue, src/benches/bench_queue.cu:26-123): one owner block pushes and
+ * pops n_tasks while `thieves` blocks steal concurrently (cooperative launch);
+ * reports tasks taken and how many task ids were not taken exactly once. */
+int ferry_deque_stress(int device, uint64_t capacity, int n_tasks, int thieves, int batch,
+                       uint64_t* taken, int32_t* dup_or_missing);
 
 /* ---- standalone LRU lanes (generic miss detector) -------------------------
  * The same device kernel as ferry_detect_misses on its own state, for any lane

@@ -1,0 +1,258 @@
+"""Multi-GPU building blocks on the device: the work-stealing deque and request
+migration (bit-exact state + cache transfer, then identical decoding on the
+thief). Same-device variants run on one GPU; cross-device variants need two."""
+import ctypes as C
+import multiprocessing as mp
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch
+
+
+def _p(t):
+    return C.c_void_p(t.data_ptr())
+
+
+# --------------------------------------------------------------------------- deque
+
+
+@pytest.mark.parametrize("cap,n,thieves,batch", [(1024, 1 << 16, 64, 16), (8, 20000, 31, 3),
+                                                 (1 << 16, 1 << 17, 128, 32)])
+def test_deque_exactly_once_under_contention(torch_cuda, cap, n, thieves, batch):
+    from ferry_b200 import _abi
+
+    taken = C.c_uint64()
+    bad = C.c_int32()
+    _abi.call("ferry_deque_stress", 0, cap, n, thieves, batch, C.byref(taken), C.byref(bad))
+    assert taken.value == n and bad.value == 0
+
+
+def test_deque_owner_and_thief_ends(torch_cuda):
+    from ferry_b200 import _abi
+
+    t = torch_cuda
+    q = C.c_void_p()
+    _abi.call("ferry_deque_create", 0, 16, C.byref(q))
+    try:
+        st = C.c_void_p(t.cuda.current_stream().cuda_stream)
+        tasks = t.arange(10, dtype=t.int64, device="cuda")
+        cnt = t.zeros(1, dtype=t.int32, device="cuda")
+        out = t.full((16,), -1, dtype=t.int64, device="cuda")
+        size = t.zeros(1, dtype=t.int64, device="cuda")
+        _abi.call("ferry_deque_push", q, st, _p(tasks), 10, _p(cnt))
+        assert cnt.item() == 10
+        _abi.call("ferry_deque_steal", q, st, _p(out), 3, _p(cnt))
+        assert cnt.item() == 3 and out[:3].tolist() == [0, 1, 2]
+        _abi.call("ferry_deque_pop", q, st, _p(out), 2, _p(cnt))
+        assert cnt.item() == 2 and out[:2].tolist() == [9, 8]
+        _abi.call("ferry_deque_size", q, st, _p(size))
+        assert size.item() == 5
+        # overflow: capacity 16 holds 11 more at most
+        more = t.arange(100, 120, dtype=t.int64, device="cuda")
+        _abi.call("ferry_deque_push", q, st, _p(more), 20, _p(cnt))
+        assert cnt.item() == 11
+        _abi.call("ferry_deque_pop", q, st, _p(out), 16, _p(cnt))
+        assert cnt.item() == 16 and out[:16].tolist() == list(range(110, 99, -1)) + [7, 6, 5, 4, 3]
+        _abi.call("ferry_deque_steal", q, st, _p(out), 4, _p(cnt))
+        assert cnt.item() == 0
+    finally:
+        _abi.call("ferry_deque_destroy", q)
+
+
+def test_deque_steal_from_peer_device(torch_cuda):
+    from ferry_b200 import _abi
+
+    t = torch_cuda
+    if t.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    q = C.c_void_p()
+    v = C.c_void_p()
+    _abi.call("ferry_deque_create", 0, 64, C.byref(q))
+    _abi.call("ferry_deque_peer_view", 1, q, C.byref(v))
+    try:
+        with t.cuda.device(0):
+            tasks = t.arange(40, dtype=t.int64, device="cuda:0")
+            cnt0 = t.zeros(1, dtype=t.int32, device="cuda:0")
+            _abi.call("ferry_deque_push", q, C.c_void_p(t.cuda.current_stream(0).cuda_stream), _p(tasks), 40, _p(cnt0))
+            t.cuda.synchronize(0)
+        with t.cuda.device(1):
+            out = t.full((32,), -1, dtype=t.int64, device="cuda:1")
+            cnt1 = t.zeros(1, dtype=t.int32, device="cuda:1")
+            _abi.call("ferry_deque_steal", v, C.c_void_p(t.cuda.current_stream(1).cuda_stream), _p(out), 25, _p(cnt1))
+            t.cuda.synchronize(1)
+            assert cnt1.item() == 25 and out[:25].tolist() == list(range(25))
+        with t.cuda.device(0):
+            out0 = t.full((32,), -1, dtype=t.int64, device="cuda:0")
+            _abi.call("ferry_deque_pop", q, C.c_void_p(t.cuda.current_stream(0).cuda_stream), _p(out0), 32, _p(cnt0))
+            t.cuda.synchronize(0)
+            assert cnt0.item() == 15 and sorted(out0[:15].tolist()) == list(range(25, 40))
+    finally:
+        _abi.call("ferry_deque_destroy", v)
+        _abi.call("ferry_deque_destroy", q)
+
+
+# --------------------------------------------------------------------------- migration
+
+
+def _workload():
+    from ferry_b200.workload import small
+
+    return small(num_requests=4, num_layers=2, q_heads=8, kv_heads=4, ctx_tokens=1024, top_k=16,
+                 cache_frac=0.5)
+
+
+def _q(w, reqs, step):
+    from ferry_b200.workload import q_stream
+
+    return np.stack([q_stream(w, int(r), steps=step + 1)[step] for r in reqs])
+
+
+def _lane_state(dec, w, req):
+    LH, N, C_ = w.lanes_per_req, w.max_pages, w.cache_pages
+    lanes = range(req * LH, (req + 1) * LH)
+    out = []
+    for l in lanes:
+        size = int(dec.debug_read(3, np.int32, 1, offset_elems=l)[0])
+        order = dec.debug_read(2, np.int32, C_, offset_elems=l * C_)[:size]
+        ps = dec.debug_read(1, np.int32, N, offset_elems=l * N)
+        cache = dec.debug_read(0, np.uint16, size * 4096, offset_elems=l * C_ * 4096) if size else np.zeros(0, np.uint16)
+        out.append((size, order.copy(), ps.copy(), cache.copy()))
+    return out
+
+
+def _run_steps(t, dec, w, reqs, steps, dev):
+    ids = t.from_numpy(np.asarray(reqs, np.int32)).to(dev)
+    out = t.zeros((len(reqs), w.num_layers, w.q_heads, 128), dtype=t.float32, device=dev)
+    for s in steps:
+        q = t.from_numpy(_q(w, reqs, s)).to(dev)
+        dec.step(q, ids, out)
+    t.cuda.synchronize(dev)
+    dec.check()
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("devices,mode", [((0, 0), 1), ((0, 0), 0), ((0, 1), 1)])
+def test_migrate_requests_bit_exact_then_same_decode(torch_cuda, devices, mode):
+    from ferry_b200 import _abi
+    from ferry_b200.engine import Decoder
+
+    t = torch_cuda
+    if max(devices) >= t.cuda.device_count():
+        pytest.skip("needs two GPUs")
+    w = _workload()
+    src, dst = Decoder(w, devices[0]), Decoder(w, devices[1])
+    try:
+        d0, d1 = t.device("cuda", devices[0]), t.device("cuda", devices[1])
+        for dec, d in ((src, d0), (dst, d1)):
+            dec.register_pool()
+            ids = t.arange(4, dtype=t.int32, device=d)
+            dec.begin(ids, t.full((4,), w.max_pages, dtype=t.int32, device=d))
+        _run_steps(t, src, w, [0, 1, 2, 3], range(3), d0)
+        _run_steps(t, dst, w, [0, 1, 2, 3], [7], d1)  # the thief's slots hold other state
+        before = {r: _lane_state(src, w, r) for r in (1, 3)}
+        _abi.call("ferry_ctx_link", dst.ctx, 0, src.ctx)
+        with t.cuda.device(d1):
+            s_ids = t.tensor([1, 3], dtype=t.int32, device=d1)
+            d_ids = t.tensor([0, 2], dtype=t.int32, device=d1)
+            _abi.call("ferry_migrate_requests", dst.ctx, C.c_void_p(t.cuda.current_stream(d1).cuda_stream),
+                      0, _p(s_ids), _p(d_ids), 2, mode)
+            t.cuda.synchronize(d1)
+        dst.check()
+        for sr, dr in ((1, 0), (3, 2)):
+            got = _lane_state(dst, w, dr)
+            for (sz, order, ps, cache), (sz2, order2, ps2, cache2) in zip(before[sr], got):
+                assert sz == sz2 and (order == order2).all() and (ps == ps2).all() and (cache == cache2).all()
+        states = np.zeros(w.num_requests, np.int32)
+        _abi.call("ferry_slot_states", src.ctx, states.ctypes.data_as(C.c_void_p), 1)
+        assert states.tolist() == [0, 2, 0, 2]
+        units, nbytes, mu, mb = dst.all_stats()
+        resident = sum(s[0] for r in (1, 3) for s in before[r])
+        assert mu == (resident if mode == 1 else 2 * w.lanes_per_req * w.cache_pages) and mb == mu * 8192
+        # the thief decodes the migrated requests exactly as the victim would
+        out_v = _run_steps(t, src, w, [1, 3], [3, 4], d0)
+        out_t = _run_steps(t, dst, w, [0, 2], [], d1)  # no-op (keeps state)
+        ids_t = t.tensor([0, 2], dtype=t.int32, device=d1)
+        o = t.zeros((2, w.num_layers, w.q_heads, 128), dtype=t.float32, device=d1)
+        for s in (3, 4):
+            # queries of the original request ids
+            q = t.from_numpy(_q(w, [1, 3], s)).to(d1)
+            dst.step(q, ids_t, o)
+        t.cuda.synchronize(d1)
+        dst.check()
+        assert (o.cpu().numpy().view(np.uint32) == out_v.view(np.uint32)).all()
+        del out_t
+    finally:
+        dst.close()
+        src.close()
+
+
+def _ipc_owner(conn, device):
+    import torch
+
+    from ferry_b200 import _abi
+    from ferry_b200.engine import Decoder
+
+    w = _workload()
+    dec = Decoder(w, device)
+    dec.register_pool()
+    d = torch.device("cuda", device)
+    ids = torch.arange(4, dtype=torch.int32, device=d)
+    dec.begin(ids, torch.full((4,), w.max_pages, dtype=torch.int32, device=d))
+    _run_steps(torch, dec, w, [0, 1, 2, 3], range(3), d)
+    handle = (C.c_uint8 * _abi.CTX_HANDLE_BYTES)()
+    _abi.call("ferry_ctx_export", dec.ctx, handle)
+    conn.send((bytes(handle), _lane_state(dec, w, 2)))
+    conn.recv()  # wait until the importer is done
+    states = np.zeros(4, np.int32)
+    _abi.call("ferry_slot_states", dec.ctx, states.ctypes.data_as(C.c_void_p), 0)
+    conn.send(states.tolist())
+    dec.close()
+
+
+def test_migrate_over_cuda_ipc(torch_cuda):
+    """One process per GPU: the owner exports its ctx, a second process imports
+    it and pulls a request (same device when only one GPU is present)."""
+    from ferry_b200 import _abi
+    from ferry_b200.engine import Decoder
+
+    t = torch_cuda
+    dev_owner = 1 if t.cuda.device_count() > 1 else 0
+    ctx = mp.get_context("spawn")
+    parent, child = ctx.Pipe()
+    p = ctx.Process(target=_ipc_owner, args=(child, dev_owner))
+    p.start()
+    try:
+        handle, expected = parent.recv()
+        w = _workload()
+        dec = Decoder(w, 0)
+        try:
+            dec.register_pool()
+            buf = (C.c_uint8 * _abi.CTX_HANDLE_BYTES).from_buffer_copy(handle)
+            _abi.call("ferry_ctx_import", dec.ctx, 3, buf)
+            s_ids = t.tensor([2], dtype=t.int32, device="cuda:0")
+            d_ids = t.tensor([1], dtype=t.int32, device="cuda:0")
+            _abi.call("ferry_migrate_requests", dec.ctx, C.c_void_p(t.cuda.current_stream(0).cuda_stream), 3,
+                      _p(s_ids), _p(d_ids), 1, 1)
+            t.cuda.synchronize(0)
+            dec.check()
+            got = _lane_state(dec, w, 1)
+            for (sz, order, ps, cache), (sz2, order2, ps2, cache2) in zip(expected, got):
+                assert sz == sz2 and (order == order2).all() and (ps == ps2).all() and (cache == cache2).all()
+        finally:
+            dec.close()
+        parent.send("done")
+        assert parent.recv() == [0, 0, 2, 0]
+    finally:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()

@@ -28,6 +28,8 @@ EXPORTS = [
     "ferry_slot_states", "ferry_deque_create", "ferry_deque_destroy", "ferry_deque_push",
     "ferry_deque_pop", "ferry_deque_steal", "ferry_deque_size", "ferry_deque_export",
     "ferry_deque_import", "ferry_deque_peer_view", "ferry_deque_stress",
+    "ferry_exec_create", "ferry_exec_destroy", "ferry_exec_link_peer", "ferry_exec_admit",
+    "ferry_exec_set_global", "ferry_exec_owned", "ferry_exec_tick",
     "ferry_lru_create", "ferry_lru_destroy", "ferry_lru_touch", "ferry_lru_read",
 ]
 MAX_PEERS = 8
@@ -46,6 +48,17 @@ class Cfg(C.Structure):
                 ("kv_heads", C.c_int), ("head_dim", C.c_int), ("page_tokens", C.c_int),
                 ("max_pages", C.c_int), ("cache_pages", C.c_int), ("top_k", C.c_int),
                 ("kv_dtype", C.c_int)]
+
+
+class ExecCfg(C.Structure):
+    _fields_ = [("rank", C.c_int), ("world", C.c_int), ("max_batch", C.c_int),
+                ("steal_batch", C.c_int), ("migrate_mode", C.c_int), ("steps_per_req", C.c_int),
+                ("total_requests", C.c_int)]
+
+
+class TickStats(C.Structure):
+    _fields_ = [("decoded", C.c_int), ("finished", C.c_int), ("stolen", C.c_int),
+                ("stolen_from", C.c_int), ("queued", C.c_int), ("tick_ms", C.c_float)]
 
 
 _lib = None
@@ -87,6 +100,13 @@ _SIGS = {
     "ferry_deque_import": (I, [I, V, C.c_uint64, C.POINTER(V)]),
     "ferry_deque_peer_view": (I, [I, V, C.POINTER(V)]),
     "ferry_deque_stress": (I, [I, C.c_uint64, I, I, I, V, V]),
+    "ferry_exec_create": (I, [V, V, C.POINTER(ExecCfg), V, C.POINTER(V)]),
+    "ferry_exec_destroy": (I, [V]),
+    "ferry_exec_link_peer": (I, [V, I, I, V]),
+    "ferry_exec_admit": (I, [V, V, V, I]),
+    "ferry_exec_set_global": (I, [V, C.c_int64]),
+    "ferry_exec_owned": (I, [V, V, I, C.POINTER(I)]),
+    "ferry_exec_tick": (I, [V, V, C.POINTER(TickStats)]),
     "ferry_lru_create": (I, [I, I, I, I, C.POINTER(V)]),
     "ferry_lru_destroy": (I, [V]),
     "ferry_lru_touch": (I, [V, V, V, V, I, V, I, V, I, V, V, V, V, V]),

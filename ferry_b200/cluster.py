@@ -1,0 +1,228 @@
+"""Multi-GPU miss-stream decode: one process per GPU, work stealing, NVLink
+migration, and the page-ownership exchange over NCCL.
+
+Each rank owns a ``ferry_ctx`` (its HBM page cache and page tables), a device
+work-stealing deque of decode tasks and a ``ferry_exec`` (the C++ tick loop,
+``include/ferry_cuda.h``). At start-up the ranks swap CUDA IPC handles of
+their ctx and deque (``all_gather_object``), so every executor can steal from
+any peer's deque and pull a stolen request's state straight out of the peer's
+HBM. Every ``epoch`` ticks the ranks exchange their ownership rows -- which
+requests each GPU holds, how many it admitted and finished -- with one
+``all_gather`` (NCCL on GPU tensors; gloo on CPU). That table gives every rank
+the global pending count behind the fair-share steal threshold and the
+termination test; the data path itself never goes through a collective.
+
+The reference runs the same protocol with host threads, a mutex-guarded
+std::deque per GPU and host-staged copies (src/runtime/wla_multigpu.cuh:
+793-806 dispatch, :1063-1506 steal_from, :2291-2775 run_wla_multigpu).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import dataclasses
+import math
+
+import numpy as np
+
+from . import _abi
+from ._abi import call
+from .workload import Workload, arrival_ticks, q_stream
+
+# ---------------------------------------------------------------- host logic (CPU-testable)
+
+
+def assign_ranks(n_req: int, world: int, policy: str = "rr", seed: int = 42,
+                 zipf_a: float = 1.5) -> np.ndarray:
+    """Home GPU of every request. 'rr': round-robin (the reference's RR
+    dispatch); 'zipf': P(rank i) proportional to 1/(i+1)^a, which with a = 1.5
+    puts ~80% of requests on two of eight GPUs (the benchmark's skewed config;
+    the reference's own skew is 80% on half the GPUs,
+    src/runtime/wla_multigpu.cuh:483-492)."""
+    if policy == "rr":
+        return (np.arange(n_req) % world).astype(np.int32)
+    if policy == "zipf":
+        p = 1.0 / np.arange(1, world + 1) ** zipf_a
+        p /= p.sum()
+        rng = np.random.default_rng([seed, 1501])
+        return rng.choice(world, size=n_req, p=p).astype(np.int32)
+    raise ValueError(f"unknown policy {policy!r}")
+
+
+def ownership_row(finished: int, admitted: int, owned: np.ndarray, cap: int) -> np.ndarray:
+    row = np.full(cap + 3, -1, np.int64)
+    row[0], row[1], row[2] = finished, admitted, len(owned)
+    row[3:3 + len(owned)] = owned[:cap]
+    return row
+
+
+def merge_ownership(rows: np.ndarray, total_requests: int):
+    """rows: [world][cap + 3] gathered ownership rows -> (owner_of[total],
+    finished_total, admitted_total). A request absent from every row is -1."""
+    owner = np.full(total_requests, -1, np.int32)
+    for rank, row in enumerate(rows):
+        n = int(row[2])
+        ids = row[3:3 + n]
+        ids = ids[(ids >= 0) & (ids < total_requests)]
+        owner[ids] = rank
+    return owner, int(rows[:, 0].sum()), int(rows[:, 1].sum())
+
+
+def exchange_ownership(finished: int, admitted: int, owned: np.ndarray, cap: int, total_requests: int,
+                       device=None):
+    """The page-ownership exchange: one all_gather of fixed-size rows (NCCL
+    when ``device`` is a CUDA device, else the default group's backend)."""
+    import torch
+    import torch.distributed as dist
+
+    row = torch.from_numpy(ownership_row(finished, admitted, owned, cap))
+    if device is not None:
+        row = row.to(device)
+    out = [torch.empty_like(row) for _ in range(dist.get_world_size())]
+    dist.all_gather(out, row)
+    rows = torch.stack(out).cpu().numpy()
+    return merge_ownership(rows, total_requests)
+
+
+@dataclasses.dataclass
+class ClusterStats:
+    rank: int
+    tokens: int
+    ticks: int
+    device_ms: float
+    steals: int
+    stolen_tasks: int
+    migrated_units: int
+    migrated_bytes: int
+    gathered_bytes: int
+    tick_ms: list
+
+
+# ---------------------------------------------------------------- per-rank runner (GPU)
+
+
+class RankRunner:
+    """One GPU's share of a multi-GPU job."""
+
+    def __init__(self, w: Workload, total_requests: int, world: int, rank: int, device: int,
+                 slots: int, max_batch: int, steal_batch: int = 4,
+                 migrate_mode: int = _abi.MIGRATE_DELTA, pool_units: int | None = None):
+        import torch
+        import torch.distributed as dist
+
+        from .engine import Decoder
+
+        self.w, self.world, self.rank, self.total = w, world, rank, total_requests
+        self.dev = torch.device("cuda", device)
+        torch.cuda.set_device(self.dev)
+        wl = dataclasses.replace(w, num_requests=slots)
+        self.dec = Decoder(wl, device)
+        self.dec.register_pool(units=pool_units or min(total_requests * w.lanes_per_req * w.max_pages, 1 << 17))
+        # resident query table [total][steps][L][Hq][128]
+        q = np.stack([q_stream(w, r) for r in range(total_requests)])
+        self.q_table = torch.from_numpy(q).to(self.dev)
+        self.deque = C.c_void_p()
+        call("ferry_deque_create", device, max(slots, 1), C.byref(self.deque))
+        cfg = _abi.ExecCfg(rank=rank, world=world, max_batch=max_batch, steal_batch=steal_batch,
+                           migrate_mode=migrate_mode, steps_per_req=w.steps, total_requests=total_requests)
+        self.exec = C.c_void_p()
+        call("ferry_exec_create", self.dec.ctx, self.deque, C.byref(cfg),
+             C.c_void_p(self.q_table.data_ptr()), C.byref(self.exec))
+        self.slots = slots
+        self.peer_deques = []
+        if world > 1:
+            h = (C.c_uint8 * _abi.CTX_HANDLE_BYTES)()
+            call("ferry_ctx_export", self.dec.ctx, h)
+            dh = (C.c_uint8 * 64)()
+            call("ferry_deque_export", self.deque, dh)
+            mine = (bytes(h), bytes(dh), slots)
+            allh = [None] * world
+            dist.all_gather_object(allh, mine)
+            slot = 0
+            for p in range(world):
+                if p == rank:
+                    continue
+                ch, qh, pslots = allh[p]
+                call("ferry_ctx_import", self.dec.ctx, slot, (C.c_uint8 * _abi.CTX_HANDLE_BYTES).from_buffer_copy(ch))
+                pq = C.c_void_p()
+                call("ferry_deque_import", device, (C.c_uint8 * 64).from_buffer_copy(qh), pslots, C.byref(pq))
+                self.peer_deques.append(pq)
+                call("ferry_exec_link_peer", self.exec, p, slot, pq)
+                slot += 1
+
+    def run(self, home: np.ndarray, join: np.ndarray, epoch: int = 4, max_ticks: int = 100000,
+            exchange_device=None) -> ClusterStats:
+        """Tick until every request of the job finished on some GPU. home/join:
+        each request's home rank and arrival tick."""
+        import torch
+
+        st = torch.cuda.current_stream(self.dev)
+        mine = np.nonzero(home == self.rank)[0]
+        admitted = finished = tokens = ticks = steals = stolen = 0
+        tick_ms = []
+        self.dec.all_stats(reset=True)
+        s = _abi.TickStats()
+        owned = np.zeros(self.slots, np.int32)
+        n_owned = C.c_int()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        t = 0
+        while t < max_ticks:
+            arr = mine[join[mine] == t].astype(np.int32)
+            if len(arr):
+                pages = np.full(len(arr), self.w.max_pages, np.int32)
+                call("ferry_exec_admit", self.exec, arr.ctypes.data_as(C.c_void_p),
+                     pages.ctypes.data_as(C.c_void_p), len(arr))
+                admitted += len(arr)
+            call("ferry_exec_tick", self.exec, C.c_void_p(st.cuda_stream), C.byref(s))
+            tokens += s.decoded
+            finished += s.finished
+            if s.stolen:
+                steals += 1
+                stolen += s.stolen
+            tick_ms.append(s.tick_ms)
+            t += 1
+            if t % epoch == 0:
+                call("ferry_exec_owned", self.exec, owned.ctypes.data_as(C.c_void_p), self.slots,
+                     C.byref(n_owned))
+                _, fin_all, adm_all = exchange_ownership(finished, admitted, owned[:n_owned.value],
+                                                         self.slots, self.total, exchange_device)
+                call("ferry_exec_set_global", self.exec, adm_all - fin_all)
+                if fin_all >= self.total:
+                    break
+        e1.record(st)
+        torch.cuda.synchronize(self.dev)
+        self.dec.check()
+        g_units, g_bytes, m_units, m_bytes = self.dec.all_stats()
+        return ClusterStats(rank=self.rank, tokens=tokens, ticks=t, device_ms=e0.elapsed_time(e1),
+                            steals=steals, stolen_tasks=stolen, migrated_units=m_units,
+                            migrated_bytes=m_bytes, gathered_bytes=g_bytes, tick_ms=tick_ms)
+
+    def close(self):
+        for pq in self.peer_deques:
+            call("ferry_deque_destroy", pq)
+        self.peer_deques = []
+        if self.exec:
+            call("ferry_exec_destroy", self.exec)
+            self.exec = None
+        if self.deque:
+            call("ferry_deque_destroy", self.deque)
+            self.deque = None
+        self.dec.close()
+
+
+def job_schedule(w: Workload, total_requests: int, world: int, policy: str):
+    """Arrival tick and home rank of each request of a multi-GPU job."""
+    wj = dataclasses.replace(w, num_requests=total_requests)
+    join = arrival_ticks(wj)
+    join = join - join.min()
+    home = assign_ranks(total_requests, world, policy, w.seed)
+    return home, join
+
+
+def slots_needed(home: np.ndarray, world: int, max_batch: int) -> int:
+    """Request slots per GPU: enough for the busiest home plus stolen work."""
+    return int(max(np.bincount(home, minlength=world).max(), max_batch) + max_batch)
+
+
+def ceil_div(a: int, b: int) -> int:
+    return int(math.ceil(a / b))

@@ -250,6 +250,53 @@ int ferry_deque_peer_view(int device, ferry_deque* owner, ferry_deque** out);
 int ferry_deque_stress(int device, uint64_t capacity, int n_tasks, int thieves, int batch,
                        uint64_t* taken, int32_t* dup_or_missing);
 
+/* ---- per-GPU executor with work stealing ----------------------------------
+ * The host runtime of one GPU: the counterpart of the reference's exec thread
+ * and WlaMultiGpuCtx tick/steal protocol (src/runtime/wla_multigpu.cuh:829-864
+ * tick_begin/tick_end, :1063-1506 steal_from, :1518-1526 fair_share,
+ * :2446-2704 exec loop). Work unit: a decode task (global request, local
+ * slot, step) in the GPU's own deque (capacity >= ctx num_requests). A tick
+ * reclaims slots of requests peers migrated away, admits pending arrivals,
+ * pops up to max_batch tasks, and -- when this GPU holds fewer than its fair
+ * share ceil(pending / world) -- steals min(steal_batch, size - fair,
+ * size / 2 + 1) tasks from the peer deque with the largest excess and
+ * migrates those requests over NVLink; then it runs ferry_decode_step on the
+ * batch (queries gathered from d_q_table, [total_requests][steps][L][Hq][128]
+ * fp16 on the ctx device) and pushes the next steps back. Request r's home in
+ * the host pool is r * L * Hkv * max_pages (every GPU registers a pool with
+ * the same content). */
+typedef struct ferry_exec ferry_exec;
+typedef struct ferry_exec_cfg {
+  int rank;           /* this GPU's rank */
+  int world;          /* number of ranks */
+  int max_batch;      /* tasks decoded per tick (<= ctx num_requests) */
+  int steal_batch;    /* most tasks one steal takes (the reference's steal_batch, default 4) */
+  int migrate_mode;   /* FERRY_MIGRATE_DELTA or FERRY_MIGRATE_FULL */
+  int steps_per_req;  /* decode steps of every request */
+  int total_requests; /* global request ids are [0, total_requests) */
+} ferry_exec_cfg;
+typedef struct ferry_tick_stats {
+  int decoded;      /* tasks decoded this tick */
+  int finished;     /* requests that finished */
+  int stolen;       /* tasks stolen this tick */
+  int stolen_from;  /* victim rank of that steal */
+  int queued;       /* tasks pushed back */
+  float tick_ms;    /* device time of the tick (CUDA events) */
+} ferry_tick_stats;
+int ferry_exec_create(ferry_ctx* ctx, ferry_deque* own, const ferry_exec_cfg* cfg,
+                      const uint16_t* d_q_table, ferry_exec** out);
+int ferry_exec_destroy(ferry_exec* x);
+/* Peer rank's deque (an IPC import or a peer view) and its ctx peer slot
+ * (already linked or imported into this executor's ctx). */
+int ferry_exec_link_peer(ferry_exec* x, int peer_rank, int ctx_peer_slot, ferry_deque* peer_deque);
+/* Queue arrivals for this GPU (host arrays); admitted when slots are free. */
+int ferry_exec_admit(ferry_exec* x, const int32_t* h_global_req, const int32_t* h_n_pages, int n);
+/* Unfinished requests across all GPUs, from the ownership exchange. */
+int ferry_exec_set_global(ferry_exec* x, int64_t global_pending);
+/* Global ids of the requests this GPU holds (the ownership table row). */
+int ferry_exec_owned(ferry_exec* x, int32_t* h_out, int cap, int* n);
+int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out);
+
 /* ---- standalone LRU lanes (generic miss detector) -------------------------
  * The same device kernel as ferry_detect_misses on its own state, for any lane
  * count / capacity / id domain -- e.g. the reference's per-(request, layer)

@@ -256,3 +256,62 @@ def test_migrate_over_cuda_ipc(torch_cuda):
         p.join(timeout=120)
         if p.is_alive():
             p.kill()
+
+
+# --------------------------------------------------------------------------- executor
+
+
+def _cluster_worker(rank, world, port, devices, out):
+    import os
+
+    import torch
+    import torch.distributed as dist
+
+    from ferry_b200.cluster import RankRunner
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    w = _workload()
+    w = type(w)(**{**w.__dict__, "steps": 6})
+    total = 12
+    home = np.zeros(total, np.int32)          # every request starts on rank 0
+    join = np.zeros(total, np.int64)
+    runner = RankRunner(w, total, world, rank, devices[rank], slots=total + 4, max_batch=4,
+                        steal_batch=4)
+    try:
+        stats = runner.run(home, join, epoch=2, max_ticks=400)
+    finally:
+        runner.close()
+    out.put((rank, stats.tokens, stats.stolen_tasks, stats.migrated_units, stats.ticks))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_executor_two_ranks_steal_and_migrate(torch_cuda):
+    """Rank 1 starts idle, steals from rank 0's deque and migrates the stolen
+    requests over NVLink / IPC; every (request, step) decodes exactly once."""
+    import socket
+
+    t = torch_cuda
+    devices = [0, 1] if t.cuda.device_count() > 1 else [0, 0]
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_cluster_worker, args=(r, 2, port, devices, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    try:
+        res = sorted(q.get(timeout=300) for _ in ps)
+    finally:
+        for p in ps:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    (r0, tok0, st0, mig0, ticks0), (r1, tok1, st1, mig1, ticks1) = res
+    assert tok0 + tok1 == 12 * 6
+    assert st1 > 0 and mig1 > 0 and tok1 > 0
+    assert ticks0 == ticks1

@@ -407,16 +407,95 @@ def main():
     ap.add_argument("--workload", default="cfg1")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--per-gpu", type=int, default=16, help="skew: requests per GPU on average")
+    ap.add_argument("--policy", default="zipf", help="skew: rr | zipf home assignment")
+    ap.add_argument("--no-steal", action="store_true", help="skew: disable work stealing")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     from ferry_b200.workload import WORKLOADS
 
+    if args.workload == "skew":
+        run_cluster(args)
+        return
     w = WORKLOADS[args.workload]
     if args.impl == "reference":
         run_reference(args, w)
     else:
         run_ferry(args, w)
+
+
+def run_cluster(args):
+    """--workload skew: the multi-GPU job with work stealing and NVLink
+    migration. cfg1-shaped requests (32/32 heads, 4096 tokens, top-64, 25%
+    cache), --per-gpu x N of them, homes drawn from Zipf(1.5) over the GPUs
+    (the skewed config's assignment), all arriving in the first ON burst;
+    every GPU decodes at most 16 requests per tick. Each request runs --steps
+    decode steps; a --warmup-step job runs first, untimed. value = all
+    tokens / max over ranks of the device time of the job."""
+    import dataclasses
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from ferry_b200 import _abi
+    from ferry_b200.cluster import RankRunner, job_schedule, slots_needed
+    from ferry_b200.workload import CFG1
+
+    ws, rank, local = _dist()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    else:
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29517", rank=0, world_size=1)
+    total = args.per_gpu * ws
+    max_batch = 16
+    steal = 0 if args.no_steal else 4
+
+    def job(steps):
+        w = dataclasses.replace(CFG1, steps=steps)
+        home, join = job_schedule(w, total, ws, args.policy)
+        join[:] = 0  # one ON burst: every request is there at tick 0
+        r = RankRunner(w, total, ws, rank, local, slots=slots_needed(home, ws, max_batch),
+                       max_batch=max_batch, steal_batch=steal)
+        try:
+            dist.barrier()
+            torch.cuda.synchronize(dev)
+            st = r.run(home, join, epoch=4, max_ticks=100000, exchange_device=dev if ws > 1 else None)
+        finally:
+            r.close()
+        return st, home
+
+    job(args.warmup)
+    st, home = job(args.steps)
+    t = torch.tensor([st.device_ms, st.tokens, st.migrated_bytes, st.mig_ms, st.mig_event_bytes,
+                      st.stolen_tasks, st.gathered_bytes], dtype=torch.float64, device=dev)
+    mx, sm = t.clone(), t.clone()
+    if ws > 1:
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+    if rank == 0:
+        ms = float(mx[0])
+        tokens = float(sm[1])
+        share = (np.bincount(home, minlength=ws) / len(home)).round(3).tolist()
+        mig_gbs = float(sm[4]) / (float(sm[3]) / 1e3) / 1e9 if float(sm[3]) > 0 else None
+        line = {"metric": METRIC, "value": tokens / (ms / 1e3), "unit": UNIT, "n_gpus": ws,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / max(1, st.ticks),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "fp16-kv/fp32-acc", "data": "synthetic (procedural KV, AR(1) queries, seeded)",
+                "config": {"workload": "skew: cfg1-shaped requests, Zipf(1.5) homes, one ON burst",
+                           "requests": total, "max_batch_per_gpu": max_batch,
+                           "steal_batch": steal, "home_share": share, "policy": args.policy,
+                           "parallelism": f"{ws} ranks, work stealing + NVLink migration"},
+                "steal": {"stolen_tasks": int(sm[5]), "migrated_bytes": float(sm[2]),
+                          "migration_GB_s": mig_gbs, "nvlink_peak_GB_s": 770.0,
+                          "migration_frac": mig_gbs / 770.0 if mig_gbs else None},
+                "gathered_bytes": float(sm[6]), "ticks": st.ticks}
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 if __name__ == "__main__":

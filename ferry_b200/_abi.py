@@ -58,7 +58,8 @@ class ExecCfg(C.Structure):
 
 class TickStats(C.Structure):
     _fields_ = [("decoded", C.c_int), ("finished", C.c_int), ("stolen", C.c_int),
-                ("stolen_from", C.c_int), ("queued", C.c_int), ("tick_ms", C.c_float)]
+                ("stolen_from", C.c_int), ("queued", C.c_int), ("tick_ms", C.c_float),
+                ("mig_ms", C.c_float), ("mig_bytes", C.c_int64)]
 
 
 _lib = None

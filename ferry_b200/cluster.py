@@ -95,6 +95,8 @@ class ClusterStats:
     migrated_bytes: int
     gathered_bytes: int
     tick_ms: list
+    mig_ms: float = 0.0          # device time of the migration kernels
+    mig_event_bytes: int = 0     # bytes those kernels moved
 
 
 # ---------------------------------------------------------------- per-rank runner (GPU)
@@ -158,6 +160,7 @@ class RankRunner:
         st = torch.cuda.current_stream(self.dev)
         mine = np.nonzero(home == self.rank)[0]
         admitted = finished = tokens = ticks = steals = stolen = 0
+        mig_ms, mig_b = 0.0, 0
         tick_ms = []
         self.dec.all_stats(reset=True)
         s = _abi.TickStats()
@@ -179,6 +182,8 @@ class RankRunner:
             if s.stolen:
                 steals += 1
                 stolen += s.stolen
+                mig_ms += s.mig_ms
+                mig_b += s.mig_bytes
             tick_ms.append(s.tick_ms)
             t += 1
             if t % epoch == 0:
@@ -195,7 +200,8 @@ class RankRunner:
         g_units, g_bytes, m_units, m_bytes = self.dec.all_stats()
         return ClusterStats(rank=self.rank, tokens=tokens, ticks=t, device_ms=e0.elapsed_time(e1),
                             steals=steals, stolen_tasks=stolen, migrated_units=m_units,
-                            migrated_bytes=m_bytes, gathered_bytes=g_bytes, tick_ms=tick_ms)
+                            migrated_bytes=m_bytes, gathered_bytes=g_bytes, tick_ms=tick_ms,
+                            mig_ms=mig_ms, mig_event_bytes=mig_b)
 
     def close(self):
         for pq in self.peer_deques:

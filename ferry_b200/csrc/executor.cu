@@ -94,7 +94,8 @@ struct ferry_exec {
   int32_t* h_begin = nullptr;
   int64_t* h_base = nullptr;
   std::vector<int32_t> slot_state;
-  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr, ev3 = nullptr;
+  uint64_t mig_bytes_seen = 0;
 };
 
 using namespace ferry;
@@ -119,8 +120,8 @@ void free_exec(ferry_exec* x) {
   cudaFreeHost(x->h_tasks); cudaFreeHost(x->h_push); cudaFreeHost(x->h_admit);
   cudaFreeHost(x->h_cnt); cudaFreeHost(x->h_sizes); cudaFreeHost(x->h_ids); cudaFreeHost(x->h_mig);
   cudaFreeHost(x->h_begin); cudaFreeHost(x->h_base);
-  if (x->ev0) cudaEventDestroy(x->ev0);
-  if (x->ev1) cudaEventDestroy(x->ev1);
+  for (cudaEvent_t e : {x->ev0, x->ev1, x->ev2, x->ev3})
+    if (e) cudaEventDestroy(e);
   delete x;
 }
 
@@ -220,6 +221,8 @@ int ferry_exec_create(ferry_ctx* ctx, ferry_deque* own, const ferry_exec_cfg* cf
   FX(cudaMallocHost(&x->h_base, (size_t)R * 8));
   FX(cudaEventCreate(&x->ev0));
   FX(cudaEventCreate(&x->ev1));
+  FX(cudaEventCreate(&x->ev2));
+  FX(cudaEventCreate(&x->ev3));
 #undef FX
   *out = x;
   return FERRY_OK;
@@ -336,9 +339,12 @@ int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out) {
           }
           if (got) {
             FERRY_TRY(cudaMemcpyAsync(x->d_mig, x->h_mig, (size_t)2 * S * 4, cudaMemcpyHostToDevice, st));
+            FERRY_TRY(cudaEventRecord(x->ev2, st));
             if ((rc = ferry_migrate_requests(x->ctx, st, x->peer_slot[victim], x->d_mig, x->d_mig + S, got,
                                              x->cfg.migrate_mode)))
               return rc;
+            FERRY_TRY(cudaEventRecord(x->ev3, st));
+            ts.mig_ms = -1.f;  // filled in after the tick's sync
             FERRY_TRY(cudaMemcpyAsync(x->d_tasks + n, x->h_tasks + n, (size_t)got * 8, cudaMemcpyHostToDevice, st));
             ts.stolen = got;
             ts.stolen_from = victim;
@@ -377,6 +383,14 @@ int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out) {
   FERRY_TRY(cudaStreamSynchronize(st));
   float ms = 0.f;
   FERRY_TRY(cudaEventElapsedTime(&ms, x->ev0, x->ev1));
+  if (ts.mig_ms < 0.f) {
+    FERRY_TRY(cudaEventElapsedTime(&ts.mig_ms, x->ev2, x->ev3));
+    uint64_t st4[4];
+    if ((rc = ferry_stats_read(x->ctx, st4, 0))) return rc;
+    // the counter may have been zeroed by ferry_stats_read(reset) since the last steal
+    ts.mig_bytes = (int64_t)(st4[3] >= x->mig_bytes_seen ? st4[3] - x->mig_bytes_seen : st4[3]);
+    x->mig_bytes_seen = st4[3];
+  }
   x->finished += ts.finished;
   ts.decoded = n;
   ts.tick_ms = ms;

@@ -33,12 +33,61 @@ def _time(fn, iters: int, warm: int = 3) -> float:
     return a.elapsed_time(b) * 1e3 / iters  # us
 
 
+def migrate_bench(w, iters: int) -> dict:
+    """Request migration over NVLink (the reference's run_mig_path axis,
+    src/benches/run_mig_path.cu:176-320): warm every request on GPU 1 (GPU 0
+    when only one exists), then time ferry_migrate_requests pulling all of
+    them into GPU 0 (delta: resident slots only)."""
+    import ctypes as C
+
+    from . import _abi
+
+    src_dev = 1 if torch.cuda.device_count() > 1 else 0
+    R = w.num_requests
+    src, dst = Decoder(w, src_dev), Decoder(w, 0)
+    try:
+        for dec, d in ((src, src_dev), (dst, 0)):
+            dec.register_pool()
+            dd = torch.device("cuda", d)
+            ids = torch.arange(R, dtype=torch.int32, device=dd)
+            dec.begin(ids, torch.full((R,), w.max_pages, dtype=torch.int32, device=dd))
+        sd = torch.device("cuda", src_dev)
+        ids = torch.arange(R, dtype=torch.int32, device=sd)
+        out = torch.empty((R, w.num_layers, w.q_heads, 128), dtype=torch.float32, device=sd)
+        for s in range(2):
+            q = torch.from_numpy(np.stack([q_stream(w, r, steps=s + 1)[s] for r in range(R)])).to(sd)
+            src.step(q, ids, out)
+        torch.cuda.synchronize(sd)
+        src.check()
+        _abi.call("ferry_ctx_link", dst.ctx, 0, src.ctx)
+        d0 = torch.device("cuda", 0)
+        s_ids = torch.arange(R, dtype=torch.int32, device=d0)
+        st = C.c_void_p(torch.cuda.current_stream(d0).cuda_stream)
+        fn = lambda: _abi.call("ferry_migrate_requests", dst.ctx, st, 0, C.c_void_p(s_ids.data_ptr()),
+                               C.c_void_p(s_ids.data_ptr()), R, _abi.MIGRATE_DELTA)
+        dst.all_stats(reset=True)
+        with torch.cuda.device(d0):
+            t = _time(fn, iters)
+        units, _, mu, mb = dst.all_stats()
+        dst.check()
+        per = mb / (iters + 3)
+        return {"src_device": src_dev, "requests": R, "bytes_per_call": per, "us": t,
+                "GB_s": per / t / 1e3, "nvlink_peak_GB_s": 770.0, "frac": per / t / 1e3 / 770.0}
+    finally:
+        dst.close()
+        src.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--workload", default="cfg1")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--device", type=int, default=0)
+    ap.add_argument("--migrate", action="store_true", help="time request migration over NVLink")
     args = ap.parse_args()
+    if args.migrate:
+        print(json.dumps({"migrate": migrate_bench(WORKLOADS[args.workload], args.iters)}))
+        return
     w = WORKLOADS[args.workload]
     torch.cuda.set_device(args.device)
     dev = torch.device("cuda", args.device)

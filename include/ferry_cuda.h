@@ -282,6 +282,8 @@ typedef struct ferry_tick_stats {
   int stolen_from;  /* victim rank of that steal */
   int queued;       /* tasks pushed back */
   float tick_ms;    /* device time of the tick (CUDA events) */
+  float mig_ms;     /* device time of this tick's migration kernels (0 without a steal) */
+  int64_t mig_bytes; /* page bytes migrated in this tick */
 } ferry_tick_stats;
 int ferry_exec_create(ferry_ctx* ctx, ferry_deque* own, const ferry_exec_cfg* cfg,
                       const uint16_t* d_q_table, ferry_exec** out);

@@ -30,6 +30,7 @@ EXPORTS = [
     "ferry_deque_import", "ferry_deque_peer_view", "ferry_deque_stress",
     "ferry_exec_create", "ferry_exec_destroy", "ferry_exec_link_peer", "ferry_exec_admit",
     "ferry_exec_set_global", "ferry_exec_owned", "ferry_exec_tick",
+    "ferry_trace_load", "ferry_probe_topology", "ferry_probe_link",
     "ferry_lru_create", "ferry_lru_destroy", "ferry_lru_touch", "ferry_lru_read",
 ]
 MAX_PEERS = 8
@@ -108,6 +109,9 @@ _SIGS = {
     "ferry_exec_set_global": (I, [V, C.c_int64]),
     "ferry_exec_owned": (I, [V, V, I, C.POINTER(I)]),
     "ferry_exec_tick": (I, [V, V, C.POINTER(TickStats)]),
+    "ferry_trace_load": (I, [C.c_char_p, I, I, I, I, I, I, V, C.c_int64, V, V]),
+    "ferry_probe_topology": (I, [C.POINTER(I), V, V, I]),
+    "ferry_probe_link": (I, [I, I, C.c_size_t, I, C.POINTER(C.c_double)]),
     "ferry_lru_create": (I, [I, I, I, I, C.POINTER(V)]),
     "ferry_lru_destroy": (I, [V]),
     "ferry_lru_touch": (I, [V, V, V, V, I, V, I, V, I, V, V, V, V, V]),

@@ -78,13 +78,42 @@ def migrate_bench(w, iters: int) -> dict:
         src.close()
 
 
+def probe() -> dict:
+    """Devices, P2P access / native peer atomics, and the two link peaks the
+    decode path uses (host -> device 0, and every peer -> device 0)."""
+    import ctypes as C
+
+    from . import _abi
+
+    n = C.c_int()
+    _abi.call("ferry_probe_topology", C.byref(n), None, None, 0)
+    cap = max(1, n.value)
+    p2p = (C.c_int32 * (cap * cap))()
+    at = (C.c_int32 * (cap * cap))()
+    _abi.call("ferry_probe_topology", C.byref(n), p2p, at, cap)
+    g = C.c_double()
+    _abi.call("ferry_probe_link", -1, 0, C.c_size_t(1 << 30), 5, C.byref(g))
+    res = {"devices": n.value, "p2p": [[p2p[i * cap + j] for j in range(n.value)] for i in range(n.value)],
+           "peer_atomics": [[at[i * cap + j] for j in range(n.value)] for i in range(n.value)],
+           "host_to_dev0_GB_s": g.value, "peer_to_dev0_GB_s": {}}
+    for s in range(1, n.value):
+        if p2p[0 * cap + s]:
+            _abi.call("ferry_probe_link", s, 0, C.c_size_t(1 << 30), 5, C.byref(g))
+            res["peer_to_dev0_GB_s"][s] = g.value
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--workload", default="cfg1")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--device", type=int, default=0)
     ap.add_argument("--migrate", action="store_true", help="time request migration over NVLink")
+    ap.add_argument("--probe", action="store_true", help="topology and link peaks")
     args = ap.parse_args()
+    if args.probe:
+        print(json.dumps({"probe": probe()}))
+        return
     if args.migrate:
         print(json.dumps({"migrate": migrate_bench(WORKLOADS[args.workload], args.iters)}))
         return

@@ -299,6 +299,29 @@ int ferry_exec_set_global(ferry_exec* x, int64_t global_pending);
 int ferry_exec_owned(ferry_exec* x, int32_t* h_out, int cap, int* n);
 int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out);
 
+/* ---- real selection traces (FMT1) ----------------------------------------
+ * Replaces load_miss_trace (src/workloads/miss_trace.cuh:75-185): reads the
+ * FMT1 trace of the reference's capture tool (tools/capture_miss_trace.py:
+ * 316-317, 368-370), checks every header field against the run, remaps raw
+ * block ids to dense ids in first-seen order and writes them in event order
+ * (request, step, layer, k) to blocks_out (capacity entries; NULL = count
+ * only). Returns the number of distinct ids and the largest per-request
+ * distinct count (the slab capacity). A mismatch or truncation returns
+ * FERRY_E_INVAL with the reason -- the reference exits the process instead. */
+int ferry_trace_load(const char* path, int requests, int steps, int layers, int sel_blocks,
+                     int kv_heads, int head_dim, int64_t* blocks_out, int64_t capacity,
+                     int64_t* unique_out, int32_t* slab_blocks_out);
+
+/* ---- topology and link probes ----------------------------------------------
+ * Replaces probe_topology / probe_host_staged_bandwidth
+ * (src/topo/topo.cpp:68-215). ferry_probe_topology: device count and, for
+ * cap >= n, n x n matrices (row stride cap) of P2P access and native peer
+ * atomics. ferry_probe_link: GB/s of a copy kernel on dst_dev reading `bytes`
+ * from pinned host memory (src_dev = -1) or from peer device src_dev over
+ * NVLink -- the access patterns of the miss gather and of migration. */
+int ferry_probe_topology(int* n_dev, int32_t* p2p, int32_t* atomics, int cap);
+int ferry_probe_link(int src_dev, int dst_dev, size_t bytes, int iters, double* gbs);
+
 /* ---- standalone LRU lanes (generic miss detector) -------------------------
  * The same device kernel as ferry_detect_misses on its own state, for any lane
  * count / capacity / id domain -- e.g. the reference's per-(request, layer)

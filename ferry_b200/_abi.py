@@ -15,6 +15,8 @@ OK, E_INVAL, E_OOM, E_TIMEOUT, E_CUDA, E_STATE, E_RANGE = range(7)
 _NAMES = {E_INVAL: "FERRY_E_INVAL", E_OOM: "FERRY_E_OOM", E_TIMEOUT: "FERRY_E_TIMEOUT",
           E_CUDA: "FERRY_E_CUDA", E_STATE: "FERRY_E_STATE", E_RANGE: "FERRY_E_RANGE"}
 KV_F16 = 0
+KV_E4M3 = 1
+UNIT_BYTES = {KV_F16: 8192, KV_E4M3: 4112}
 LRU_DISTINCT = 1
 
 # every symbol include/ferry_cuda.h declares
@@ -76,7 +78,7 @@ _SIGS = {
     "ferry_host_alloc": (I, [C.c_size_t, C.POINTER(V)]),
     "ferry_host_free": (I, [V]),
     "ferry_kv_register": (I, [V, V, C.c_size_t]),
-    "ferry_kv_generate": (I, [V, C.c_uint64, C.c_uint64, C.c_int64, V]),
+    "ferry_kv_generate": (I, [V, C.c_uint64, C.c_uint64, C.c_int64, V, I]),
     "ferry_page_summary_update": (I, [V, V, C.c_int64, C.c_int64]),
     "ferry_requests_begin": (I, [V, V, V, V, V, I]),
     "ferry_select_topk": (I, [V, V, V, V, I, V, V]),

@@ -22,6 +22,8 @@ constexpr int kHeadDim = 128;
 constexpr int kPageTokens = 16;
 constexpr int kUnitElems = 2 * kPageTokens * kHeadDim;  // K[16][128] then V[16][128]
 constexpr int kUnitBytes = kUnitElems * 2;              // fp16: 8192 bytes
+// e4m3 unit: K[16][128] | V[16][128] (1 byte each) | k_scale f32 | v_scale f32 | 8 pad
+constexpr int kUnitBytesF8 = kUnitElems + 16;           // 4112 bytes
 constexpr int kMaxGroup = 8;
 constexpr int kMaxPages = 16384;
 
@@ -164,6 +166,7 @@ struct ferry_ctx {
   int device = -1;
   ferry_cfg cfg{};
   int group = 1;          // q heads per kv head
+  int unit_bytes = ferry::kUnitBytes;  // 8192 (fp16) or 4112 (e4m3 + scales)
   int lanes_per_req = 0;  // L * Hkv
   int64_t lanes = 0;      // R * L * Hkv
 
@@ -198,9 +201,10 @@ namespace ferry {
 constexpr int kPartStride = 132;  // o[128], m, l, pad -> 16-byte rows
 
 // kernels' launchers (one per .cu)
-int launch_kv_generate(cudaStream_t st, uint64_t seed, uint64_t unit0, int64_t n_units, void* dst);
+int launch_kv_generate(cudaStream_t st, uint64_t seed, uint64_t unit0, int64_t n_units, void* dst,
+                       int kv_dtype);
 int launch_summary(cudaStream_t st, const uint8_t* pool, int64_t unit0, int64_t n_units,
-                   float* summ);
+                   float* summ, int kv_dtype);
 int launch_select(const ferry_ctx* c, cudaStream_t st, const uint16_t* q, const int32_t* req_ids,
                   int n_req, int32_t* sel, int32_t* n_sel);
 int launch_lru(const ferry_lru* L, cudaStream_t st, const int32_t* lane_ids, const int32_t* req_ids,
@@ -218,4 +222,26 @@ size_t attention_partial_slots(int64_t lanes, int sms);
 int launch_attention(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,
                      const int32_t* req_ids, int n_req, const int32_t* item_slot,
                      const int32_t* n_sel, float* out);
+// e4m3 KV path on tcgen05 tensor cores (attn_tc.cu)
+int launch_attention_tc(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,
+                        const int32_t* req_ids, int n_req, const int32_t* item_slot,
+                        const int32_t* n_sel, float* out);
+
+// 16-byte-vector copy of one page unit by one warp (unit_bytes % 16 == 0,
+// <= 8192): all of a lane's loads are issued before its stores.
+__device__ __forceinline__ void warp_copy_unit(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                               int unit_bytes, int t) {
+  const int n16 = unit_bytes >> 4;
+  uint4 r[kUnitBytes / (32 * 16)];
+#pragma unroll
+  for (int j = 0; j < kUnitBytes / (32 * 16); ++j) {
+    const int v = t + 32 * j;
+    if (v < n16) r[j] = ld_nc_v4(src + (size_t)v * 16);
+  }
+#pragma unroll
+  for (int j = 0; j < kUnitBytes / (32 * 16); ++j) {
+    const int v = t + 32 * j;
+    if (v < n16) st_v4(dst + (size_t)v * 16, r[j]);
+  }
+}
 }  // namespace ferry

@@ -96,7 +96,8 @@ int validate_cfg(const ferry_cfg* cfg) {
   if (!cfg) return set_error("cfg is NULL"), FERRY_E_INVAL;
   if (cfg->head_dim != kHeadDim) return set_error("head_dim must be 128"), FERRY_E_INVAL;
   if (cfg->page_tokens != kPageTokens) return set_error("page_tokens must be 16"), FERRY_E_INVAL;
-  if (cfg->kv_dtype != FERRY_KV_F16) return set_error("kv_dtype must be FERRY_KV_F16"), FERRY_E_INVAL;
+  if (cfg->kv_dtype != FERRY_KV_F16 && cfg->kv_dtype != FERRY_KV_E4M3)
+    return set_error("kv_dtype must be FERRY_KV_F16 or FERRY_KV_E4M3"), FERRY_E_INVAL;
   if (cfg->num_requests < 1 || cfg->num_layers < 1 || cfg->kv_heads < 1 || cfg->q_heads < 1)
     return set_error("num_requests, num_layers, q_heads, kv_heads must be >= 1"), FERRY_E_INVAL;
   if (cfg->q_heads % cfg->kv_heads)
@@ -149,7 +150,8 @@ int ferry_ctx_create(int device, const ferry_cfg* cfg, ferry_ctx** out) {
   FERRY_CK(dev_alloc(&c->err, 1, 0));
   FERRY_CK(dev_alloc(&c->stats, 4, 0));
   FERRY_CK(dev_alloc(&c->slot_state, (size_t)cfg->num_requests, 0));
-  FERRY_CK(dev_alloc(&c->cache, (size_t)c->lanes * cfg->cache_pages * kUnitBytes, 0));
+  c->unit_bytes = cfg->kv_dtype == FERRY_KV_E4M3 ? kUnitBytesF8 : kUnitBytes;
+  FERRY_CK(dev_alloc(&c->cache, (size_t)c->lanes * cfg->cache_pages * c->unit_bytes, 0));
   FERRY_CK(alloc_lru_state(&c->lru, c->lanes, cfg->cache_pages, cfg->max_pages, c->err));
   c->lru.device = device;
   FERRY_CK(dev_alloc(&c->ctx_pages, R, 0));
@@ -213,7 +215,7 @@ int ferry_host_free(void* p) {
 }
 
 int ferry_kv_register(ferry_ctx* c, void* host_pool, size_t bytes) {
-  if (!c || !host_pool || bytes < (size_t)kUnitBytes || ((uintptr_t)host_pool & 15))
+  if (!c || !host_pool || bytes < (size_t)c->unit_bytes || ((uintptr_t)host_pool & 15))
     return set_error("kv_register: need a 16-byte aligned pool of >= one page unit"), FERRY_E_INVAL;
   DeviceGuard guard(c->device);
   void* dev = nullptr;
@@ -223,7 +225,7 @@ int ferry_kv_register(ferry_ctx* c, void* host_pool, size_t bytes) {
     return set_error("kv_register: pool is not pinned+mapped host memory (use ferry_host_alloc)"),
            FERRY_E_INVAL;
   }
-  const uint64_t units = bytes / kUnitBytes;
+  const uint64_t units = bytes / c->unit_bytes;
   float* summ = nullptr;
   int rc = dev_alloc(&summ, (size_t)units * kHeadDim, 0);
   if (rc) return rc;
@@ -234,8 +236,9 @@ int ferry_kv_register(ferry_ctx* c, void* host_pool, size_t bytes) {
   return FERRY_OK;
 }
 
-int ferry_kv_generate(void* stream, uint64_t seed, uint64_t unit0, int64_t n_units, void* dst) {
-  return launch_kv_generate((cudaStream_t)stream, seed, unit0, n_units, dst);
+int ferry_kv_generate(void* stream, uint64_t seed, uint64_t unit0, int64_t n_units, void* dst,
+                      int kv_dtype) {
+  return launch_kv_generate((cudaStream_t)stream, seed, unit0, n_units, dst, kv_dtype);
 }
 
 int ferry_page_summary_update(ferry_ctx* c, void* stream, int64_t unit0, int64_t n_units) {
@@ -244,7 +247,7 @@ int ferry_page_summary_update(ferry_ctx* c, void* stream, int64_t unit0, int64_t
   if (unit0 < 0 || n_units < 0 || (uint64_t)(unit0 + n_units) > c->pool_units)
     return set_error("summary range outside the pool"), FERRY_E_INVAL;
   DeviceGuard guard(c->device);
-  return launch_summary((cudaStream_t)stream, c->pool_dev, unit0, n_units, c->summ);
+  return launch_summary((cudaStream_t)stream, c->pool_dev, unit0, n_units, c->summ, c->cfg.kv_dtype);
 }
 
 int ferry_requests_begin(ferry_ctx* c, void* stream, const int32_t* d_req_ids,
@@ -305,6 +308,8 @@ int ferry_sparse_decode(ferry_ctx* c, void* stream, const uint16_t* d_q, const i
   if (n_req && (!d_q || !d_item_slot || !d_n_sel || !d_out))
     return set_error("sparse_decode: NULL buffer"), FERRY_E_INVAL;
   DeviceGuard guard(c->device);
+  if (c->cfg.kv_dtype == FERRY_KV_E4M3)
+    return launch_attention_tc(c, (cudaStream_t)stream, d_q, d_req_ids, n_req, d_item_slot, d_n_sel, d_out);
   return launch_attention(c, (cudaStream_t)stream, d_q, d_req_ids, n_req, d_item_slot, d_n_sel,
                           d_out);
 }
@@ -323,6 +328,8 @@ int ferry_decode_step(ferry_ctx* c, void* stream, const uint16_t* d_q, const int
                        c->ws_islot, c->ws_mpage, c->ws_mslot, c->ws_nmiss)))
     return rc;
   if ((rc = launch_gather(c, st, d_req_ids, n_req, c->ws_mpage, c->ws_mslot, c->ws_nmiss))) return rc;
+  if (c->cfg.kv_dtype == FERRY_KV_E4M3)
+    return launch_attention_tc(c, st, d_q, d_req_ids, n_req, c->ws_islot, c->ws_nsel, d_out);
   return launch_attention(c, st, d_q, d_req_ids, n_req, c->ws_islot, c->ws_nsel, d_out);
 }
 
@@ -341,7 +348,7 @@ int ferry_debug_read(ferry_ctx* c, int which, size_t offset, size_t bytes, void*
   size_t size = 0;
   const size_t R = c->cfg.num_requests, LH = c->lanes_per_req, k = c->cfg.top_k;
   switch (which) {
-    case 0: base = c->cache; size = (size_t)c->lanes * c->cfg.cache_pages * kUnitBytes; break;
+    case 0: base = c->cache; size = (size_t)c->lanes * c->cfg.cache_pages * c->unit_bytes; break;
     case 1: base = (uint8_t*)c->lru.page_slot; size = (size_t)c->lanes * c->cfg.max_pages * 4; break;
     case 2: base = (uint8_t*)c->lru.order; size = (size_t)c->lanes * c->cfg.cache_pages * 4; break;
     case 3: base = (uint8_t*)c->lru.size; size = (size_t)c->lanes * 4; break;

@@ -18,7 +18,7 @@ __global__ void __launch_bounds__(256) gather_kernel(
     const uint8_t* __restrict__ pool, uint64_t pool_units, uint8_t* __restrict__ cache, int N,
     int C, const int32_t* __restrict__ req_ids, int lanes_per_req, int64_t lanes_total,
     int n_lanes, const int32_t* __restrict__ miss_page, const int32_t* __restrict__ miss_slot,
-    const int32_t* __restrict__ n_miss, int k, const int64_t* __restrict__ req_base,
+    const int32_t* __restrict__ n_miss, int k, const int64_t* __restrict__ req_base, int unit_bytes,
     unsigned long long* stats, uint32_t* err) {
   const int t = threadIdx.x & 31;
   const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -38,18 +38,14 @@ __global__ void __launch_bounds__(256) gather_kernel(
     }
     const uint64_t unit =
         (uint64_t)(req_base[req] + (int64_t)(a % lanes_per_req) * N + page) % pool_units;
-    const uint8_t* src = pool + unit * kUnitBytes;
-    uint8_t* dst = cache + ((uint64_t)gl * C + slot) * kUnitBytes;
-    uint4 r[kUnitBytes / (32 * 16)];
-#pragma unroll
-    for (int j = 0; j < kUnitBytes / (32 * 16); ++j) r[j] = ld_nc_v4(src + (size_t)(t + 32 * j) * 16);
-#pragma unroll
-    for (int j = 0; j < kUnitBytes / (32 * 16); ++j) st_v4(dst + (size_t)(t + 32 * j) * 16, r[j]);
+    const uint8_t* src = pool + unit * unit_bytes;
+    uint8_t* dst = cache + ((uint64_t)gl * C + slot) * unit_bytes;
+    warp_copy_unit(src, dst, unit_bytes, t);
     ++copied;
   }
   if (t == 0 && copied && stats) {
     atomicAdd(&stats[0], (unsigned long long)copied);
-    atomicAdd(&stats[1], (unsigned long long)copied * kUnitBytes);
+    atomicAdd(&stats[1], (unsigned long long)copied * unit_bytes);
   }
 }
 
@@ -69,7 +65,7 @@ int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, i
   gather_kernel<<<(unsigned)blocks, 256, 0, st>>>(
       c->pool_dev, c->pool_units, c->cache, c->cfg.max_pages, c->cfg.cache_pages, req_ids,
       c->lanes_per_req, c->lanes, n_lanes, miss_page, miss_slot, n_miss, c->cfg.top_k, c->req_base,
-      c->stats, c->err);
+      c->unit_bytes, c->stats, c->err);
   FERRY_TRY(cudaGetLastError());
   return FERRY_OK;
 }

@@ -1,4 +1,6 @@
-// kvgen.cu -- procedural KV pool generator and page-summary kernel.
+// kvgen.cu -- procedural KV pool generator and page-summary kernels.
+#include <cuda_fp8.h>
+
 #include "common.cuh"
 
 namespace ferry {
@@ -6,8 +8,8 @@ namespace {
 
 // Element e of page unit u: Irwin-Hall sum of twelve 16-bit uniforms drawn
 // from three splitmix64 outputs, z = (sum - 6*65536) / 65536 (variance 1,
-// exact in fp32), rounded once to fp16.
-__device__ __forceinline__ uint16_t kv_elem(uint64_t seed, uint64_t unit, uint32_t e) {
+// exact in fp32).
+__device__ __forceinline__ float kv_elem_f32(uint64_t seed, uint64_t unit, uint32_t e) {
   const uint64_t base = mix64(seed ^ mix64(unit * 4096ull + e));
   uint32_t acc = 0;
 #pragma unroll
@@ -16,8 +18,85 @@ __device__ __forceinline__ uint16_t kv_elem(uint64_t seed, uint64_t unit, uint32
     acc += (uint32_t)(h & 0xFFFF) + (uint32_t)((h >> 16) & 0xFFFF) +
            (uint32_t)((h >> 32) & 0xFFFF) + (uint32_t)(h >> 48);
   }
-  const float z = __fmul_rn((float)((int32_t)acc - 6 * 65536), 1.0f / 65536.0f);
-  return __half_as_ushort(__float2half_rn(z));
+  return __fmul_rn((float)((int32_t)acc - 6 * 65536), 1.0f / 65536.0f);
+}
+
+// fp16 pool: z rounded once to fp16
+__device__ __forceinline__ uint16_t kv_elem(uint64_t seed, uint64_t unit, uint32_t e) {
+  return __half_as_ushort(__float2half_rn(kv_elem_f32(seed, unit, e)));
+}
+
+// e4m3 pool: one warp per 4112-byte unit. For K (elements 0..2047) and V
+// (2048..4095): scale = amax / 448 of the unit's fp32 values (1 when all are
+// zero), q = e4m3(z / scale), round to nearest even with saturation to +-448
+// (cvt.rn.satfinite). Lane l owns 64 consecutive elements of each half.
+__global__ void __launch_bounds__(256) kv_generate_e4m3_kernel(uint64_t seed, uint64_t unit0,
+                                                               int64_t n_units, uint8_t* dst) {
+  const int t = threadIdx.x & 31;
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t u = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < n_units; u += nw) {
+    const uint64_t unit = unit0 + (uint64_t)u;
+    uint8_t* out = dst + (size_t)u * kUnitBytesF8;
+    float scales[2];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const uint32_t e0 = half * 2048 + t * 64;
+      float amax = 0.f;
+      for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(kv_elem_f32(seed, unit, e0 + i)));
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+      const float scale = amax > 0.f ? __fdiv_rn(amax, 448.0f) : 1.0f;
+      scales[half] = scale;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {  // 4 x 16 bytes
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t word = 0;
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const float z = kv_elem_f32(seed, unit, e0 + v * 16 + j * 4 + b);
+            const __nv_fp8_storage_t q = __nv_cvt_float_to_fp8(__fdiv_rn(z, scale), __NV_SATFINITE, __NV_E4M3);
+            word |= (uint32_t)q << (8 * b);
+          }
+          w[j] = word;
+        }
+        *reinterpret_cast<uint4*>(out + e0 + v * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    if (t == 0)
+      *reinterpret_cast<uint4*>(out + 4096) =
+          make_uint4(__float_as_uint(scales[0]), __float_as_uint(scales[1]), 0u, 0u);
+  }
+}
+
+// e4m3 summary: summary[d] = (k_0[d] + ... + k_15[d]) * (1/16) with
+// k_t[d] = float(e4m3) * k_scale (one rounding), in token order.
+__global__ void __launch_bounds__(256) summary_e4m3_kernel(const uint8_t* __restrict__ pool, int64_t unit0,
+                                                           int64_t n_units, float* __restrict__ summ) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t u = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < n_units; u += warps) {
+    const uint8_t* K = pool + (size_t)(unit0 + u) * kUnitBytesF8;
+    const float ks = *reinterpret_cast<const float*>(K + 4096);
+    float acc[4];
+#pragma unroll
+    for (int tt = 0; tt < kPageTokens; ++tt) {
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(K + tt * kHeadDim + lane * 4);
+      const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w & 0xFFFF), __NV_E4M3);
+      const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w >> 16), __NV_E4M3);
+      const float v[4] = {__half2float(__ushort_as_half(lo.x)), __half2float(__ushort_as_half(lo.y)),
+                          __half2float(__ushort_as_half(hi.x)), __half2float(__ushort_as_half(hi.y))};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float kv = __fmul_rn(v[j], ks);
+        acc[j] = tt == 0 ? kv : __fadd_rn(acc[j], kv);
+      }
+    }
+    reinterpret_cast<float4*>(summ + (size_t)(unit0 + u) * kHeadDim)[lane] =
+        make_float4(__fmul_rn(acc[0], 0.0625f), __fmul_rn(acc[1], 0.0625f), __fmul_rn(acc[2], 0.0625f),
+                    __fmul_rn(acc[3], 0.0625f));
+  }
 }
 
 // One thread writes 8 consecutive elements (one 16-byte store) so that
@@ -74,10 +153,10 @@ __global__ void __launch_bounds__(256) summary_kernel(const uint8_t* __restrict_
 }  // namespace
 
 int launch_kv_generate(cudaStream_t st, uint64_t seed, uint64_t unit0, int64_t n_units,
-                       void* dst) {
+                       void* dst, int kv_dtype) {
   if (n_units <= 0) return FERRY_OK;
-  if (!dst || ((uintptr_t)dst & 15)) {
-    set_error("ferry_kv_generate: dst must be non-null and 16-byte aligned");
+  if (!dst || ((uintptr_t)dst & 15) || (kv_dtype != FERRY_KV_F16 && kv_dtype != FERRY_KV_E4M3)) {
+    set_error("ferry_kv_generate: dst must be non-null and 16-byte aligned, dtype F16 or E4M3");
     return FERRY_E_INVAL;
   }
   // pinned host memory: write through its device-side alias
@@ -86,6 +165,12 @@ int launch_kv_generate(cudaStream_t st, uint64_t seed, uint64_t unit0, int64_t n
       attr.devicePointer)
     dst = attr.devicePointer;
   cudaGetLastError();
+  if (kv_dtype == FERRY_KV_E4M3) {
+    const int64_t blocks = std::min<int64_t>((n_units + 7) / 8, 148 * 16);
+    kv_generate_e4m3_kernel<<<(unsigned)blocks, 256, 0, st>>>(seed, unit0, n_units, (uint8_t*)dst);
+    FERRY_TRY(cudaGetLastError());
+    return FERRY_OK;
+  }
   const int64_t n_vec = n_units * (kUnitElems / 8);
   const int64_t blocks = std::min<int64_t>((n_vec + 255) / 256, 148 * 16);
   kv_generate_kernel<<<(unsigned)blocks, 256, 0, st>>>(seed, unit0, n_vec, (uint4*)dst);
@@ -94,10 +179,13 @@ int launch_kv_generate(cudaStream_t st, uint64_t seed, uint64_t unit0, int64_t n
 }
 
 int launch_summary(cudaStream_t st, const uint8_t* pool, int64_t unit0, int64_t n_units,
-                   float* summ) {
+                   float* summ, int kv_dtype) {
   if (n_units <= 0) return FERRY_OK;
   const int64_t blocks = std::min<int64_t>((n_units + 7) / 8, 148 * 16);
-  summary_kernel<<<(unsigned)blocks, 256, 0, st>>>(pool, unit0, n_units, summ);
+  if (kv_dtype == FERRY_KV_E4M3)
+    summary_e4m3_kernel<<<(unsigned)blocks, 256, 0, st>>>(pool, unit0, n_units, summ);
+  else
+    summary_kernel<<<(unsigned)blocks, 256, 0, st>>>(pool, unit0, n_units, summ);
   FERRY_TRY(cudaGetLastError());
   return FERRY_OK;
 }

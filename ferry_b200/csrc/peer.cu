@@ -64,6 +64,7 @@ struct MigArgs {
   int C;
   int N;
   int full;
+  int unit_bytes;
   unsigned long long* stats;
   uint32_t* err;
 };
@@ -121,18 +122,14 @@ __global__ void __launch_bounds__(256) migrate_pages_kernel(MigArgs A) {
     if (sr < 0 || sr >= A.R || dr < 0 || dr >= A.R) continue;
     const int64_t sl = (int64_t)sr * A.lanes_per_req + l, dl = (int64_t)dr * A.lanes_per_req + l;
     if (!A.full && s >= A.size[dl]) continue;  // delta: resident slots only
-    const uint8_t* src = A.p_cache + ((size_t)sl * A.C + s) * kUnitBytes;
-    uint8_t* dst = A.cache + ((size_t)dl * A.C + s) * kUnitBytes;
-    uint4 r[kUnitBytes / (32 * 16)];
-#pragma unroll
-    for (int j = 0; j < kUnitBytes / (32 * 16); ++j) r[j] = ld_nc_v4(src + (size_t)(t + 32 * j) * 16);
-#pragma unroll
-    for (int j = 0; j < kUnitBytes / (32 * 16); ++j) st_v4(dst + (size_t)(t + 32 * j) * 16, r[j]);
+    const uint8_t* src = A.p_cache + ((size_t)sl * A.C + s) * A.unit_bytes;
+    uint8_t* dst = A.cache + ((size_t)dl * A.C + s) * A.unit_bytes;
+    warp_copy_unit(src, dst, A.unit_bytes, t);
     ++copied;
   }
   if (t == 0 && copied && A.stats) {
     atomicAdd(&A.stats[2], (unsigned long long)copied);
-    atomicAdd(&A.stats[3], (unsigned long long)copied * kUnitBytes);
+    atomicAdd(&A.stats[3], (unsigned long long)copied * A.unit_bytes);
   }
 }
 
@@ -291,6 +288,7 @@ int ferry_migrate_requests(ferry_ctx* c, void* stream, int peer_slot, const int3
   A.C = c->cfg.cache_pages;
   A.N = c->cfg.max_pages;
   A.full = mode == FERRY_MIGRATE_FULL;
+  A.unit_bytes = c->unit_bytes;
   A.stats = c->stats;
   A.err = c->err;
   cudaStream_t st = (cudaStream_t)stream;

@@ -61,7 +61,6 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
     for (int j = threadIdx.x; j < k; j += kSelThreads) out[j] = -1;
     return;
   }
-  const int64_t gl = (int64_t)req * lanes_per_req + a % lanes_per_req;
   int np = ctx_pages[req];
   if (np < 0 || np > N) {
     if (threadIdx.x == 0) record_error(err, kErrRange);

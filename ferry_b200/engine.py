@@ -61,7 +61,8 @@ class Decoder:
         self.w = w
         self.device = device
         self.dev = torch.device("cuda", device)
-        cfg = _abi.Cfg(kv_dtype=_abi.KV_F16, **w.cfg_dict())
+        self.kv_dtype = _abi.KV_E4M3 if w.kv_dtype == "e4m3" else _abi.KV_F16
+        cfg = _abi.Cfg(kv_dtype=self.kv_dtype, **w.cfg_dict())
         h = C.c_void_p()
         call("ferry_ctx_create", device, C.byref(cfg), C.byref(h))
         self.ctx = h
@@ -84,10 +85,10 @@ class Decoder:
         every unit's page summary on the device."""
         w = self.w
         units = w.pool_units if units is None else units
-        pool = PinnedPool(units * UNIT_BYTES)
+        pool = PinnedPool(units * w.unit_bytes)
         s = _stream()
         call("ferry_kv_generate", s, C.c_uint64(w.seed if seed is None else seed), C.c_uint64(0),
-             C.c_int64(units), pool.ptr)
+             C.c_int64(units), pool.ptr, self.kv_dtype)
         torch.cuda.synchronize(self.dev)
         call("ferry_kv_register", self.ctx, pool.ptr, C.c_size_t(pool.nbytes))
         call("ferry_page_summary_update", self.ctx, s, C.c_int64(0), C.c_int64(units))

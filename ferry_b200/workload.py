@@ -35,6 +35,12 @@ class Workload:
     seed: int = 42
     head_dim: int = 128
     page_tokens: int = 16
+    kv_dtype: str = "f16"  # "f16" or "e4m3" (per-page fp32 scales)
+
+    @property
+    def unit_bytes(self) -> int:
+        """Bytes of one page unit (16 tokens of K and V for one kv head)."""
+        return 8192 if self.kv_dtype == "f16" else 4112
 
     @property
     def max_pages(self) -> int:
@@ -64,8 +70,9 @@ class Workload:
 
     # ---- bytes per decoded token (algorithmic roofline numerators)
     def attn_bytes_per_token(self) -> int:
-        """KV of the selected pages: L * Hkv * k * 16 * 128 * 2 (K,V) * 2 B."""
-        return self.num_layers * self.kv_heads * self.top_k * self.page_tokens * self.head_dim * 4
+        """KV of the selected pages: L * Hkv * k page units (8 KiB fp16:
+        16 * 128 * (K,V) * 2 B; 4112 B e4m3 with the two page scales)."""
+        return self.num_layers * self.kv_heads * self.top_k * self.unit_bytes
 
     def select_bytes_per_token(self) -> int:
         """fp32 page summaries read by selection: L * Hkv * N * 128 * 4 B."""

@@ -47,7 +47,9 @@ extern "C" {
 #define FERRY_E_STATE 5   /* call out of order (e.g. no host pool registered) */
 #define FERRY_E_RANGE 6   /* a kernel saw an out-of-range index and skipped it */
 
-#define FERRY_KV_F16 0
+#define FERRY_KV_F16 0  /* page unit 8192 B: K[16][128] f16 | V[16][128] f16 */
+#define FERRY_KV_E4M3 1 /* page unit 4112 B: K e4m3 | V e4m3 | k_scale f32 | v_scale f32 | 8 pad;
+                           attention runs on tcgen05 tensor cores */
 
 #define FERRY_LRU_DISTINCT 1 /* selections of a lane hold no duplicates */
 
@@ -61,7 +63,7 @@ typedef struct ferry_cfg {
   int max_pages;    /* N: pages per lane context (<= 16384) */
   int cache_pages;  /* C: HBM cache slots per lane */
   int top_k;        /* k: selected pages per lane, k <= C */
-  int kv_dtype;     /* FERRY_KV_F16 */
+  int kv_dtype;     /* FERRY_KV_F16 or FERRY_KV_E4M3 */
 } ferry_cfg;
 
 typedef struct ferry_ctx ferry_ctx;
@@ -96,11 +98,13 @@ int ferry_host_free(void* p);
 int ferry_kv_register(ferry_ctx* ctx, void* host_pool, size_t bytes);
 
 /* Fill n_units page units starting at unit0 of dst (device or mapped host
- * memory) with the seeded procedural KV (Irwin-Hall N(0,1) -> fp16). Input
- * generator for tests and benches; no reference counterpart (the reference
- * fills its slab from mt19937, src/runtime/wla_multigpu.cuh:535-543). */
+ * memory) with the seeded procedural KV: Irwin-Hall N(0,1) values, rounded to
+ * fp16 (FERRY_KV_F16) or quantised to e4m3 with per-page scale amax/448
+ * (FERRY_KV_E4M3). Input generator for tests and benches; no reference
+ * counterpart (the reference fills its slab from mt19937,
+ * src/runtime/wla_multigpu.cuh:535-543). */
 int ferry_kv_generate(void* stream, uint64_t seed, uint64_t unit0, int64_t n_units,
-                      void* dst);
+                      void* dst, int kv_dtype);
 
 /* Page summaries (fp32 mean of the 16 keys, token order) of pool units
  * [unit0, unit0 + n_units), read from the registered host pool. The reference

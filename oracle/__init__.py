@@ -78,6 +78,13 @@ def lib():
                                       C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
         L.orc_sparse_decode.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
                                         C.c_int, C.c_float, C.c_void_p]
+        L.orc_e4m3_encode.restype = C.c_uint8
+        L.orc_e4m3_encode.argtypes = [C.c_float]
+        L.orc_e4m3_decode.restype = C.c_float
+        L.orc_e4m3_decode.argtypes = [C.c_uint8]
+        L.orc_kv_gen_e4m3_mt.argtypes = [C.c_uint64, C.c_uint64, C.c_int64, C.c_void_p, C.c_int]
+        L.orc_e4m3_unit_dequant.argtypes = [C.c_void_p, C.c_int64, C.c_void_p]
+        L.orc_page_summary_e4m3.argtypes = [C.c_void_p, C.c_int64, C.c_void_p]
         L.orc_pipe_create.restype = C.c_void_p
         L.orc_pipe_create.argtypes = [C.c_int] * 5 + [C.c_void_p, C.c_void_p, C.c_int]
         L.orc_pipe_destroy.argtypes = [C.c_void_p]
@@ -219,6 +226,57 @@ UNIT_ELEMS = 2 * 16 * 128
 def kv_gen(seed: int, unit0: int, n_units: int, threads: int = 1) -> np.ndarray:
     out = np.zeros((n_units, UNIT_ELEMS), np.uint16)
     lib().orc_kv_gen_mt(seed, unit0, n_units, out.ctypes.data, threads)
+    return out
+
+
+UNIT_BYTES_E4M3 = 4112
+
+
+def e4m3_encode(x: np.ndarray) -> np.ndarray:
+    f = lib().orc_e4m3_encode
+    return np.array([f(float(v)) for v in np.asarray(x, np.float32).ravel()], np.uint8).reshape(np.shape(x))
+
+
+def e4m3_decode_table() -> np.ndarray:
+    return np.array([lib().orc_e4m3_decode(b) for b in range(256)], np.float32)
+
+
+def kv_gen_e4m3(seed: int, unit0: int, n_units: int, threads: int = 1) -> np.ndarray:
+    out = np.zeros((n_units, UNIT_BYTES_E4M3), np.uint8)
+    lib().orc_kv_gen_e4m3_mt(seed, unit0, n_units, out.ctypes.data, threads)
+    return out
+
+
+def e4m3_dequant(units: np.ndarray) -> np.ndarray:
+    """[n][4112] fp8 units -> [n][4096] fp32 (K then V, scales applied)."""
+    units = np.ascontiguousarray(units, np.uint8).reshape(-1, UNIT_BYTES_E4M3)
+    out = np.zeros((units.shape[0], 4096), np.float32)
+    lib().orc_e4m3_unit_dequant(units.ctypes.data, units.shape[0], out.ctypes.data)
+    return out
+
+
+def page_summary_e4m3(units: np.ndarray) -> np.ndarray:
+    units = np.ascontiguousarray(units, np.uint8).reshape(-1, UNIT_BYTES_E4M3)
+    out = np.zeros((units.shape[0], 128), np.float32)
+    lib().orc_page_summary_e4m3(units.ctypes.data, units.shape[0], out.ctypes.data)
+    return out
+
+
+def sparse_decode_f32(q_f16bits: np.ndarray, pages_f32: np.ndarray, n_sel, scale: float) -> np.ndarray:
+    """Attention in float64 over already-dequantised pages [lanes][k][4096]."""
+    q = np.asarray(q_f16bits, np.uint16).view(np.float16).astype(np.float64)
+    lanes, G, _ = q.shape
+    out = np.zeros((lanes, G, 128), np.float32)
+    for i in range(lanes):
+        n = int(n_sel[i])
+        K = pages_f32[i, :n, :2048].reshape(-1, 128).astype(np.float64)
+        V = pages_f32[i, :n, 2048:].reshape(-1, 128).astype(np.float64)
+        for g in range(G):
+            if n == 0:
+                continue
+            lg = K @ q[i, g] * scale
+            p = np.exp(lg - lg.max())
+            out[i, g] = (p / p.sum()) @ V
     return out
 
 

@@ -598,6 +598,126 @@ int64_t orc_pipe_step(void* h, int n_active, const int32_t* lane_ids, const uint
   return misses.load();
 }
 
-int orc_version(void) { return 1; }
+// ===========================================================================
+// 7. fp8 KV (benchmark definition: OCP e4m3 with a per-page fp32 scale).
+//    e4m3: 1 sign, 4 exponent bits (bias 7), 3 mantissa bits, no infinities,
+//    max finite 448, S.1111.111 = NaN. Encoding rounds to nearest, ties to
+//    even, and saturates to +-448 (what cvt.rn.satfinite.e4m3x2.f32 does).
+//    Page unit (4112 B): K[16][128] e4m3 | V[16][128] e4m3 | k_scale f32 |
+//    v_scale f32 | 8 pad bytes. scale = amax / 448 over the page's K (resp.
+//    V) values before quantisation; q = e4m3(z / scale).
+// ===========================================================================
+uint8_t orc_e4m3_encode(float x) {
+  uint32_t u;
+  std::memcpy(&u, &x, 4);
+  const uint8_t sign = (u >> 31) ? 0x80 : 0;
+  const float a = std::fabs(x);
+  if (std::isnan(x)) return 0x7F | sign;
+  if (a >= 448.0f) return sign | 0x7E;  // satfinite
+  // smallest subnormal 2^-9; values below 2^-10 (half of it) round to 0 or
+  // to 2^-9 by ties-to-even at exactly 2^-10
+  int e;
+  std::frexp(a, &e);  // a = m * 2^e, m in [0.5, 1)
+  int E = e - 1;      // a in [2^E, 2^(E+1))
+  if (E < -6) E = -6;  // subnormal range: spacing 2^-9
+  const float spacing = std::ldexp(1.0f, E - 3);
+  float q = a / spacing;           // exact (power-of-two scaling)
+  float r = std::nearbyint(q);     // ties to even (default rounding mode)
+  float v = r * spacing;
+  if (v >= 448.0f) return sign | 0x7E;
+  if (v == 0.0f) return sign;
+  int ev;
+  const float mv = std::frexp(v, &ev);  // v = mv * 2^ev
+  int Eb = ev - 1 + 7;
+  if (Eb <= 0) {  // subnormal: v = mant * 2^-9
+    const int mant = (int)std::ldexp(v, 9);
+    return sign | (uint8_t)mant;
+  }
+  const int mant = (int)((mv * 2.0f - 1.0f) * 8.0f);
+  return sign | (uint8_t)((Eb << 3) | mant);
+}
+
+float orc_e4m3_decode(uint8_t b) {
+  const int s = b >> 7, E = (b >> 3) & 0xF, m = b & 7;
+  if (E == 0xF && m == 7) return NAN;
+  const float v = E == 0 ? std::ldexp((float)m, -9) : std::ldexp(1.0f + m / 8.0f, E - 7);
+  return s ? -v : v;
+}
+
+static inline float kv_elem_f32(uint64_t seed, uint64_t unit, uint32_t e) {
+  const uint64_t base = mix64(seed ^ mix64(unit * 4096ull + e));
+  uint32_t acc = 0;
+  for (int j = 0; j < 3; ++j) {
+    const uint64_t h = mix64(base + (uint64_t)j);
+    acc += (uint32_t)(h & 0xFFFF) + (uint32_t)((h >> 16) & 0xFFFF) +
+           (uint32_t)((h >> 32) & 0xFFFF) + (uint32_t)(h >> 48);
+  }
+  return (float)((int32_t)acc - 6 * 65536) * (1.0f / 65536.0f);
+}
+
+constexpr int kUnitBytesF8 = 4112;
+
+// n_units page units of 4112 bytes each
+int orc_kv_gen_e4m3(uint64_t seed, uint64_t unit0, int64_t n_units, uint8_t* out) {
+  for (int64_t u = 0; u < n_units; ++u) {
+    uint8_t* dst = out + u * kUnitBytesF8;
+    float scales[2];
+    for (int half = 0; half < 2; ++half) {
+      const uint32_t e0 = half * 2048;
+      float amax = 0.f;
+      for (int i = 0; i < 2048; ++i)
+        amax = std::max(amax, std::fabs(kv_elem_f32(seed, unit0 + u, e0 + i)));
+      const float scale = amax > 0.f ? amax / 448.0f : 1.0f;
+      scales[half] = scale;
+      for (int i = 0; i < 2048; ++i)
+        dst[e0 + i] = orc_e4m3_encode(kv_elem_f32(seed, unit0 + u, e0 + i) / scale);
+    }
+    std::memcpy(dst + 4096, scales, 8);
+    std::memset(dst + 4104, 0, 8);
+  }
+  return 0;
+}
+
+int orc_kv_gen_e4m3_mt(uint64_t seed, uint64_t unit0, int64_t n_units, uint8_t* out, int threads) {
+  if (threads < 1) threads = 1;
+  std::vector<std::thread> th;
+  const int64_t per = (n_units + threads - 1) / threads;
+  for (int i = 0; i < threads; ++i) {
+    const int64_t b = i * per, e = std::min<int64_t>(n_units, b + per);
+    if (b >= e) break;
+    th.emplace_back([=] { orc_kv_gen_e4m3(seed, unit0 + (uint64_t)b, e - b, out + b * kUnitBytesF8); });
+  }
+  for (auto& x : th) x.join();
+  return 0;
+}
+
+// dequantised K/V of n units into fp32 [n][2][16][128]
+int orc_e4m3_unit_dequant(const uint8_t* units, int64_t n_units, float* out) {
+  for (int64_t u = 0; u < n_units; ++u) {
+    const uint8_t* p = units + u * kUnitBytesF8;
+    float sc[2];
+    std::memcpy(sc, p + 4096, 8);
+    for (int i = 0; i < 4096; ++i) out[u * 4096 + i] = orc_e4m3_decode(p[i]) * sc[i / 2048];
+  }
+  return 0;
+}
+
+// summary[d] = (k_0[d] + ... + k_15[d]) * (1/16) over dequantised keys
+// (each k_t[d] = float(e4m3) * k_scale, one rounding), token order.
+int orc_page_summary_e4m3(const uint8_t* units, int64_t n_units, float* summ) {
+  for (int64_t u = 0; u < n_units; ++u) {
+    const uint8_t* K = units + u * kUnitBytesF8;
+    float ks;
+    std::memcpy(&ks, K + 4096, 4);
+    for (int d = 0; d < kHeadDim; ++d) {
+      float acc = orc_e4m3_decode(K[d]) * ks;
+      for (int t = 1; t < kPageTokens; ++t) acc = acc + orc_e4m3_decode(K[t * kHeadDim + d]) * ks;
+      summ[u * kHeadDim + d] = acc * 0.0625f;
+    }
+  }
+  return 0;
+}
+
+int orc_version(void) { return 2; }
 
 }  // extern "C"

@@ -139,10 +139,11 @@ def main():
     torch.cuda.synchronize()
     dec.check()
     units = int(dec.n_miss.sum().item())
-    res = {"workload": w.name, "batch_requests": R}
+    res = {"workload": w.name, "batch_requests": R, "kv_dtype": w.kv_dtype}
     # gather re-copies the same miss list each launch (idempotent)
     t = _time(lambda: dec.gather(ids), max(3, args.iters // 5))
-    res["gather"] = {"us": t, "bytes": units * 8192, "GB_s": units * 8192 / t / 1e3}
+    ub = w.unit_bytes
+    res["gather"] = {"us": t, "units": units, "bytes": units * ub, "GB_s": units * ub / t / 1e3}
     dec.gather(ids)
     t = _time(lambda: dec.attention(q, ids, out), args.iters)
     b = R * w.attn_bytes_per_token() + R * w.qo_bytes_per_token()

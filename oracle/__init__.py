@@ -223,6 +223,17 @@ class LruLanes:
 UNIT_ELEMS = 2 * 16 * 128
 
 
+def _f16bits(x) -> np.ndarray:
+    """fp16 data as contiguous uint16 bit patterns: float16 arrays are
+    reinterpreted (never value-cast), integer arrays are taken as bits."""
+    x = np.asarray(x)
+    if x.dtype == np.float16:
+        return np.ascontiguousarray(x).view(np.uint16)
+    if x.dtype != np.uint16 and x.dtype.kind == "f":
+        raise TypeError(f"fp16 bits expected, got {x.dtype}")
+    return np.ascontiguousarray(x, np.uint16)
+
+
 def kv_gen(seed: int, unit0: int, n_units: int, threads: int = 1) -> np.ndarray:
     out = np.zeros((n_units, UNIT_ELEMS), np.uint16)
     lib().orc_kv_gen_mt(seed, unit0, n_units, out.ctypes.data, threads)
@@ -263,8 +274,9 @@ def page_summary_e4m3(units: np.ndarray) -> np.ndarray:
 
 
 def sparse_decode_f32(q_f16bits: np.ndarray, pages_f32: np.ndarray, n_sel, scale: float) -> np.ndarray:
-    """Attention in float64 over already-dequantised pages [lanes][k][4096]."""
-    q = np.asarray(q_f16bits, np.uint16).view(np.float16).astype(np.float64)
+    """Attention in float64 over already-dequantised pages [lanes][k][4096].
+    q: [lanes, G, 128] as float16 values or their uint16 bit patterns."""
+    q = _f16bits(q_f16bits).view(np.float16).astype(np.float64)
     lanes, G, _ = q.shape
     out = np.zeros((lanes, G, 128), np.float32)
     for i in range(lanes):
@@ -281,7 +293,7 @@ def sparse_decode_f32(q_f16bits: np.ndarray, pages_f32: np.ndarray, n_sel, scale
 
 
 def page_summary(units: np.ndarray) -> np.ndarray:
-    units = np.ascontiguousarray(units, np.uint16).reshape(-1, UNIT_ELEMS)
+    units = _f16bits(units).reshape(-1, UNIT_ELEMS)
     out = np.zeros((units.shape[0], 128), np.float32)
     lib().orc_page_summary(units.ctypes.data, units.shape[0], out.ctypes.data)
     return out
@@ -289,7 +301,7 @@ def page_summary(units: np.ndarray) -> np.ndarray:
 
 def select_topk(q_f16bits: np.ndarray, summ: np.ndarray, n_pages, k: int, return_scores=False):
     """q: [lanes, G, 128] uint16 (fp16 bits); summ: [lanes, N, 128] fp32."""
-    q = np.ascontiguousarray(q_f16bits, np.uint16)
+    q = _f16bits(q_f16bits)
     lanes, G, _ = q.shape
     summ = np.ascontiguousarray(summ, np.float32)
     N = summ.shape[1]
@@ -304,9 +316,9 @@ def select_topk(q_f16bits: np.ndarray, summ: np.ndarray, n_pages, k: int, return
 
 def sparse_decode(q_f16bits: np.ndarray, pages: np.ndarray, n_sel, scale: float) -> np.ndarray:
     """pages: [lanes, k, UNIT_ELEMS] uint16 -- the selected pages' contents."""
-    q = np.ascontiguousarray(q_f16bits, np.uint16)
+    q = _f16bits(q_f16bits)
     lanes, G, _ = q.shape
-    pages = np.ascontiguousarray(pages, np.uint16)
+    pages = _f16bits(pages)
     k = pages.shape[1]
     n_sel = np.ascontiguousarray(n_sel, np.int32)
     out = np.zeros((lanes, G, 128), np.float32)
@@ -319,7 +331,7 @@ class CpuPipeline:
     """Multi-threaded CPU path (select -> LRU -> memcpy gather -> fp32 attention)."""
 
     def __init__(self, lanes, N, C_, k, G, pool: np.ndarray, summ: np.ndarray, threads: int):
-        self.pool = np.ascontiguousarray(pool, np.uint16)
+        self.pool = _f16bits(pool)
         self.summ = np.ascontiguousarray(summ, np.float32)
         self.G = G
         self.h = lib().orc_pipe_create(lanes, N, C_, k, G, self.pool.ctypes.data,
@@ -334,7 +346,7 @@ class CpuPipeline:
         lane_ids = np.ascontiguousarray(lane_ids, np.int32)
         n = len(lane_ids)
         reset = np.zeros(n, np.uint8) if reset is None else np.ascontiguousarray(reset, np.uint8)
-        q = np.ascontiguousarray(q_f16bits, np.uint16)
+        q = _f16bits(q_f16bits)
         out = np.zeros((n, self.G, 128), np.float32)
         misses = lib().orc_pipe_step(self.h, n, lane_ids.ctypes.data, reset.ctypes.data,
                                      q.ctypes.data, C.c_float(scale), out.ctypes.data)

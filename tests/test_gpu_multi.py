@@ -267,6 +267,7 @@ def _cluster_worker(rank, world, port, devices, out):
     import torch
     import torch.distributed as dist
 
+    from ferry_b200 import _abi
     from ferry_b200.cluster import RankRunner
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -277,8 +278,11 @@ def _cluster_worker(rank, world, port, devices, out):
     total = 12
     home = np.zeros(total, np.int32)          # every request starts on rank 0
     join = np.zeros(total, np.int64)
+    # FULL migration: every stolen request carries all of its lanes' cache
+    # slots, so the unit count is deterministic (owners pop LIFO and thieves
+    # take the oldest tasks, which may not have run yet: DELTA could move 0)
     runner = RankRunner(w, total, world, rank, devices[rank], slots=total + 4, max_batch=4,
-                        steal_batch=4)
+                        steal_batch=4, migrate_mode=_abi.MIGRATE_FULL)
     try:
         stats = runner.run(home, join, epoch=2, max_ticks=400)
     finally:
@@ -313,5 +317,8 @@ def test_executor_two_ranks_steal_and_migrate(torch_cuda):
                 p.kill()
     (r0, tok0, st0, mig0, ticks0), (r1, tok1, st1, mig1, ticks1) = res
     assert tok0 + tok1 == 12 * 6
-    assert st1 > 0 and mig1 > 0 and tok1 > 0
+    assert st1 > 0 and tok1 > 0
+    w = _workload()
+    per_req = w.lanes_per_req * w.cache_pages
+    assert mig1 == st1 * per_req and mig0 == st0 * per_req
     assert ticks0 == ticks1

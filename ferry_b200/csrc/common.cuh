@@ -26,6 +26,16 @@ constexpr int kUnitBytes = kUnitElems * 2;              // fp16: 8192 bytes
 constexpr int kUnitBytesF8 = kUnitElems + 16;           // 4112 bytes
 constexpr int kMaxGroup = 8;
 constexpr int kMaxPages = 16384;
+// selection scores a lane in chunks of about this many pages (one CTA each)
+// once the lane is longer than two chunks
+constexpr int kSelChunk = 1024;
+__host__ __device__ constexpr int select_chunks(int max_pages) {
+  return max_pages <= 2 * kSelChunk ? 1 : (max_pages + kSelChunk - 1) / kSelChunk;
+}
+// pages per chunk: a multiple of 8 (the scoring batch)
+__host__ __device__ constexpr int select_chunk_pages(int max_pages, int nchunks) {
+  return (((max_pages + nchunks - 1) / nchunks) + 7) & ~7;
+}
 
 // Device-side error record bits (ctx->d_err); read by ferry_ctx_check.
 enum : uint32_t { kErrTimeout = 1u, kErrRange = 2u };
@@ -184,6 +194,10 @@ struct ferry_ctx {
   int32_t* ws = nullptr;
   int32_t *ws_sel = nullptr, *ws_nsel = nullptr, *ws_islot = nullptr, *ws_mpage = nullptr,
           *ws_mslot = nullptr, *ws_nmiss = nullptr;
+
+  // selection chunk scratch (select_chunks(max_pages) > 1 only)
+  uint32_t* sel_keys = nullptr;  // lanes * max_pages order keys
+  uint32_t* sel_done = nullptr;  // lanes chunk counters
 
   // attention scratch
   float* part = nullptr;          // attention_partial_slots * group * kPartStride

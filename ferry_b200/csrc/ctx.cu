@@ -87,6 +87,8 @@ void destroy_ctx(ferry_ctx* c) {
   cudaFree(c->ws);
   cudaFree(c->part);
   cudaFree(c->lane_done);
+  cudaFree(c->sel_keys);
+  cudaFree(c->sel_done);
   cudaFree(c->err);
   cudaFree(c->stats);
   delete c;
@@ -172,6 +174,10 @@ int ferry_ctx_create(int device, const ferry_cfg* cfg, ferry_ctx** out) {
   c->ws_nmiss = c->ws_nsel + R * LH;
   FERRY_CK(dev_alloc(&c->part, attention_partial_slots(c->lanes, c->num_sms) * c->group * kPartStride, 0));
   FERRY_CK(dev_alloc(&c->lane_done, (size_t)c->lanes, 0));
+  if (select_chunks(cfg->max_pages) > 1) {
+    FERRY_CK(dev_alloc(&c->sel_keys, (size_t)c->lanes * cfg->max_pages, 0));
+    FERRY_CK(dev_alloc(&c->sel_done, (size_t)c->lanes, 0));
+  }
 #undef FERRY_CK
   FERRY_TRY(cudaDeviceSynchronize());
   *out = c;
@@ -195,6 +201,7 @@ int ferry_ctx_check(ferry_ctx* c) {
   if (!e) return FERRY_OK;
   FERRY_TRY(cudaMemset(c->err, 0, 4));
   FERRY_TRY(cudaMemset(c->lane_done, 0, (size_t)c->lanes * 4));
+  if (c->sel_done) FERRY_TRY(cudaMemset(c->sel_done, 0, (size_t)c->lanes * 4));
   if (e & kErrTimeout) return set_error("a device wait timed out"), FERRY_E_TIMEOUT;
   return set_error("a kernel saw an out-of-range index"), FERRY_E_RANGE;
 }

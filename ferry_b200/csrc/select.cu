@@ -1,15 +1,24 @@
 // select.cu -- top-k page selection by q . mean-key page summary.
 //
-// One CTA per batch lane (request, layer, kv_head). Phase 1 scores every page
-// of the lane's context: a warp per page, lane l holding dims 4l..4l+3 of the
-// fp32 summary (one 16-byte load), dot product in the fixed order
-// q[4l]*s[4l] -> fma 4l+1..4l+3 -> butterfly add over 16,8,4,2,1, and the
-// maximum over the GQA group (first head wins ties). Phase 2 finds the k-th
-// largest order-preserving key with a 4-pass 8-bit radix select in shared
-// memory. Phase 3 emits, in ascending page order, every page whose key is
-// larger plus the lowest-id pages equal to it -- ties go to the lower page id.
-// Every fp32 operation and its order is fixed, so any IEEE-754 implementation
-// of the same steps reproduces the selection bit for bit.
+// Scoring (phase 1) splits a lane (request, layer, kv_head) into chunks of
+// kSelChunk pages, one CTA each, so the grid stays balanced however few lanes
+// are long. A warp scores 8 pages per batch: lane l loads dims 4l..4l+3 of
+// each fp32 summary row (one coalesced 512-byte row per warp load) and forms,
+// per (page, q head), the partial q[4l]*s[4l] -> fma 4l+1..4l+3. The 32
+// partials of up to 32 (page, head) values are summed together by one
+// transpose-reduce whose additions are exactly those of the xor butterfly
+// over 16, 8, 4, 2, 1 -- bit-identical to reducing each value alone, at one
+// shuffle per value instead of five. The maximum over the GQA group is a
+// lane tree in which the lower head wins ties (= the sequential scan "first
+// head wins"). Every fp32 operation and its order is fixed, so any IEEE-754
+// implementation of the same steps reproduces the selection bit for bit.
+//
+// The last CTA of a lane to finish (a per-lane counter; the sole CTA when the
+// lane fits one chunk) holds all keys in shared memory and runs phase 2, a
+// 4-pass 8-bit radix select of the k-th largest order-preserving key
+// (warp-aggregated histogram atomics), and phase 3, emission in ascending
+// page order of every page whose key is larger plus the lowest-id pages equal
+// to it -- ties go to the lower page id.
 #include "common.cuh"
 
 namespace ferry {
@@ -17,102 +26,161 @@ namespace {
 
 constexpr int kSelThreads = 256;
 constexpr int kSelWarps = kSelThreads / 32;
-
-__device__ __forceinline__ uint32_t block_excl_scan(bool flag, uint32_t* warp_tot,
-                                                    uint32_t* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t m = __ballot_sync(0xffffffffu, flag);
-  const uint32_t below = __popc(m & ((1u << lane) - 1u));
-  if (lane == 0) warp_tot[warp] = __popc(m);
-  __syncthreads();
-  uint32_t before = 0, all = 0;
-#pragma unroll
-  for (int w = 0; w < kSelWarps; ++w) {
-    const uint32_t t = warp_tot[w];
-    before += (w < warp) ? t : 0u;
-    all += t;
-  }
-  __syncthreads();  // warp_tot reusable after this
-  *total = all;
-  return before + below;
-}
+constexpr int kSelBatch = 8;  // pages per warp batch: 8 x 512 B of summaries in flight
 
 template <int G>
-__global__ void __launch_bounds__(kSelThreads) select_kernel(
-    const uint16_t* __restrict__ q, const int32_t* __restrict__ req_ids, int lanes_per_req,
-    const int32_t* __restrict__ ctx_pages, const int64_t* __restrict__ req_base,
-    const float* __restrict__ summ, uint64_t pool_units,
-    int N, int k, int num_requests, int32_t* __restrict__ sel_out,
-    int32_t* __restrict__ n_sel_out, uint32_t* err) {
+struct SelShape {
+  static constexpr int UR = (32 / G < kSelBatch) ? 32 / G : kSelBatch;  // pages per reduction
+  static constexpr int NR = kSelBatch / UR;                            // reductions per batch
+  static constexpr int V = UR * G;                                       // values per reduction
+  static constexpr int T = V == 32 ? 5 : V == 16 ? 4 : 3;                // transposing levels
+  static constexpr int S = 5 - T;  // lane l ends with value l >> S
+};
+
+// Sum over the 32 lanes of V independent values. Level j pairs lane l with
+// l ^ (16 >> j), as the xor butterfly does; while more than one value is
+// left the pair swaps halves (the lane with the level's bit set keeps the
+// upper half), afterwards it is a plain butterfly step. Each addition has the
+// same two operands as the butterfly's. Lane l returns value l >> (5 - log2 V).
+template <int V>
+__device__ __forceinline__ float transpose_reduce(float (&v)[V], int lane) {
+#pragma unroll
+  for (int j = 0; j < 5; ++j) {
+    const int o = 16 >> j;
+    const int n = V >> j;
+    if (n > 1) {
+      const bool up = (lane & o) != 0;
+#pragma unroll
+      for (int i = 0; i < n / 2; ++i) {
+        const float send = up ? v[i] : v[i + n / 2];
+        const float keep = up ? v[i + n / 2] : v[i];
+        v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
+      }
+    } else {
+      v[0] = __fadd_rn(v[0], __shfl_xor_sync(0xffffffffu, v[0], o));
+    }
+  }
+  return v[0];
+}
+
+__device__ __forceinline__ float lane_partial(const float (&q)[4], const float4 s) {
+  float v = __fmul_rn(q[0], s.x);
+  v = __fmaf_rn(q[1], s.y, v);
+  v = __fmaf_rn(q[2], s.z, v);
+  return __fmaf_rn(q[3], s.w, v);
+}
+
+__device__ __forceinline__ uint32_t lanemask_lt(int lane) { return (1u << lane) - 1u; }
+
+struct SelArgs {
+  const uint16_t* q;
+  const int32_t* req_ids;
+  int lanes_per_req;
+  const int32_t* ctx_pages;
+  const int64_t* req_base;
+  const float* summ;
+  uint64_t pool_units;
+  int N, k, num_requests, nchunks;
+  uint32_t* gkeys;  // [batch lanes][N] when nchunks > 1
+  uint32_t* done;   // [batch lanes] chunk counters, back to 0 after each launch
+  int32_t* sel_out;
+  int32_t* n_sel_out;
+  uint32_t* err;
+};
+
+template <int G>
+__global__ void __launch_bounds__(kSelThreads, 2) select_kernel(SelArgs A) {
+  using Sh = SelShape<G>;
   extern __shared__ uint32_t keys[];  // N entries
   __shared__ uint32_t hist[256];
-  __shared__ uint32_t warp_tot[kSelWarps];
-  __shared__ uint32_t s_prefix, s_krem;
+  __shared__ uint32_t wcnt[2][kSelWarps];
+  __shared__ uint32_t s_prefix, s_krem, s_last;
 
-  const int a = blockIdx.x;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int req = req_ids[a / lanes_per_req];
-  int32_t* out = sel_out + (size_t)a * k;
-  if (req < 0 || req >= num_requests) {
-    if (threadIdx.x == 0) {
-      record_error(err, kErrRange);
-      n_sel_out[a] = 0;
+  const int a = blockIdx.x / A.nchunks, chunk = blockIdx.x % A.nchunks;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int req = A.req_ids[a / A.lanes_per_req];
+  const int k = A.k, N = A.N;
+  int32_t* out = A.sel_out + (size_t)a * k;
+  if (req < 0 || req >= A.num_requests) {  // every chunk of the lane takes this path
+    if (tid == 0) {
+      record_error(A.err, kErrRange);
+      A.n_sel_out[a] = 0;
     }
-    for (int j = threadIdx.x; j < k; j += kSelThreads) out[j] = -1;
+    for (int j = tid; j < k; j += kSelThreads) out[j] = -1;
     return;
   }
-  int np = ctx_pages[req];
+  int np = A.ctx_pages[req];
   if (np < 0 || np > N) {
-    if (threadIdx.x == 0) record_error(err, kErrRange);
+    if (tid == 0) record_error(A.err, kErrRange);
     np = np < 0 ? 0 : N;
   }
 
-  // ---- phase 1: scores
-  float qv[G][4];
+  // ---- phase 1: scores of this chunk's pages
+  {
+    float qv[G][4];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const uint2 raw =
-        *reinterpret_cast<const uint2*>(q + ((size_t)a * G + g) * kHeadDim + lane * 4);
-    const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-    const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-    qv[g][0] = x.x; qv[g][1] = x.y; qv[g][2] = y.x; qv[g][3] = y.y;
+    for (int g = 0; g < G; ++g) {
+      const uint2 raw =
+          *reinterpret_cast<const uint2*>(A.q + ((size_t)a * G + g) * kHeadDim + lane * 4);
+      const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+      const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+      qv[g][0] = x.x; qv[g][1] = x.y; qv[g][2] = y.x; qv[g][3] = y.y;
+    }
+    // pool units of this lane: request home + lane-in-request * N (+ page)
+    const uint64_t unit0 =
+        (uint64_t)(A.req_base[req] + (int64_t)(a % A.lanes_per_req) * N) % A.pool_units;
+    const int cs = select_chunk_pages(N, A.nchunks);
+    const int c0 = chunk * cs, c1 = min(np, c0 + cs);
+    uint32_t* kdst = A.nchunks > 1 ? A.gkeys + (size_t)a * N : keys;
+    for (int p0 = c0 + warp * kSelBatch; p0 < c1; p0 += kSelWarps * kSelBatch) {  // warp-uniform
+      float4 s[kSelBatch];
+#pragma unroll
+      for (int u = 0; u < kSelBatch; ++u) {
+        const int p = p0 + u;
+        if (p < c1) {
+          uint64_t unit = unit0 + (uint64_t)p;
+          if (unit >= A.pool_units) unit %= A.pool_units;
+          s[u] = __ldg(reinterpret_cast<const float4*>(A.summ + unit * kHeadDim) + lane);
+        } else {
+          s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < Sh::NR; ++r) {
+        float v[Sh::V];
+#pragma unroll
+        for (int u = 0; u < Sh::UR; ++u)
+#pragma unroll
+          for (int g = 0; g < G; ++g) v[u * G + g] = lane_partial(qv[g], s[r * Sh::UR + u]);
+        float best = transpose_reduce<Sh::V>(v, lane);
+        const int x = lane >> Sh::S;  // value index held: page x / G, head x % G
+#pragma unroll
+        for (int b = 1; b < G; b <<= 1) {
+          const float other = __shfl_xor_sync(0xffffffffu, best, b << Sh::S);
+          const bool right = (x & b) != 0;  // this lane carries the higher heads
+          const float lo = right ? other : best, hi = right ? best : other;
+          best = hi > lo ? hi : lo;  // the lower head wins ties
+        }
+        const int p = p0 + r * Sh::UR + x / G;
+        if ((x % G) == 0 && (lane & ((1 << Sh::S) - 1)) == 0 && p < c1) kdst[p] = order_key(best);
+      }
+    }
   }
-  // pool units of this lane: request home + lane-in-request * N (+ page)
-  const uint64_t ubase = (uint64_t)(req_base[req] + (int64_t)(a % lanes_per_req) * N);
-  constexpr int U = 4;
-  for (int p0 = warp * U; p0 < np; p0 += kSelWarps * U) {
-    float4 s[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int p = p0 + u;
-      if (p < np) {
-        const uint64_t unit = (ubase + (uint64_t)p) % pool_units;
-        s[u] = __ldg(reinterpret_cast<const float4*>(summ + unit * kHeadDim) + lane);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int p = p0 + u;
-      if (p >= np) break;  // warp-uniform
-      float best = 0.f;
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        float v = __fmul_rn(qv[g][0], s[u].x);
-        v = __fmaf_rn(qv[g][1], s[u].y, v);
-        v = __fmaf_rn(qv[g][2], s[u].z, v);
-        v = __fmaf_rn(qv[g][3], s[u].w, v);
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
-        best = (g == 0 || v > best) ? v : best;
-      }
-      if (lane == 0) keys[p] = order_key(best);
-    }
+  if (A.nchunks > 1) {
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&A.done[a], 1u) == (uint32_t)(A.nchunks - 1);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (tid == 0) A.done[a] = 0;
+    for (int p = tid; p < np; p += kSelThreads) keys[p] = __ldcg(A.gkeys + (size_t)a * N + p);
   }
   __syncthreads();
 
   if (np <= k) {
-    for (int j = threadIdx.x; j < k; j += kSelThreads) out[j] = j < np ? j : -1;
-    if (threadIdx.x == 0) n_sel_out[a] = np;
+    for (int j = tid; j < k; j += kSelThreads) out[j] = j < np ? j : -1;
+    if (tid == 0) A.n_sel_out[a] = np;
     return;
   }
 
@@ -120,11 +188,15 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
   uint32_t prefix = 0, mask = 0, krem = (uint32_t)k;
 #pragma unroll 1
   for (int shift = 24; shift >= 0; shift -= 8) {
-    hist[threadIdx.x] = 0;  // kSelThreads == 256 bins
+    hist[tid] = 0;  // kSelThreads == 256 bins
     __syncthreads();
-    for (int p = threadIdx.x; p < np; p += kSelThreads) {
-      const uint32_t key = keys[p];
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    for (int base = 0; base < np; base += kSelThreads) {  // block-uniform
+      const int p = base + tid;
+      const uint32_t key = p < np ? keys[p] : 0u;
+      const bool act = p < np && (key & mask) == prefix;
+      const uint32_t bin = act ? (key >> shift) & 255u : 256u;
+      const uint32_t m = __match_any_sync(0xffffffffu, bin);
+      if (act && lane == __ffs(m) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(m));
     }
     __syncthreads();
     if (warp == 0) {
@@ -161,22 +233,39 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
   }
   const uint32_t T = prefix;
 
-  // ---- phase 3: ordered emission
-  uint32_t run_eq = 0, run_sel = 0;
-  for (int base = 0; base < np; base += kSelThreads) {
-    const int p = base + threadIdx.x;
-    const uint32_t key = p < np ? keys[p] : 0u;
-    const bool gt = p < np && key > T;
-    const bool eq = p < np && key == T;
-    uint32_t tot_eq, tot_sel;
-    const uint32_t eq_rank = run_eq + block_excl_scan(eq, warp_tot, &tot_eq);
-    const bool take = gt || (eq && eq_rank < krem);
-    const uint32_t pos = run_sel + block_excl_scan(take, warp_tot, &tot_sel);
-    if (take) out[pos] = p;
-    run_eq += tot_eq;
-    run_sel += tot_sel;
+  // ---- phase 3: ordered emission; warp w owns pages [w * span, (w + 1) * span)
+  const int span = ((np + kSelWarps * 32 - 1) / (kSelWarps * 32)) * 32;
+  const int lo = warp * span, hi = min(np, lo + span);
+  uint32_t ngt = 0, neq = 0;
+  for (int base = lo; base < hi; base += 32) {  // warp-uniform
+    const int p = base + lane;
+    const uint32_t key = p < hi ? keys[p] : 0u;
+    ngt += __popc(__ballot_sync(0xffffffffu, p < hi && key > T));
+    neq += __popc(__ballot_sync(0xffffffffu, p < hi && key == T));
   }
-  if (threadIdx.x == 0) n_sel_out[a] = k;
+  if (lane == 0) {
+    wcnt[0][warp] = ngt;
+    wcnt[1][warp] = neq;
+  }
+  __syncthreads();
+  uint32_t gt_before = 0, eq_before = 0;
+  for (int w = 0; w < warp; ++w) {
+    gt_before += wcnt[0][w];
+    eq_before += wcnt[1][w];
+  }
+  uint32_t pos = gt_before + min(eq_before, krem), eq_rank = eq_before;
+  for (int base = lo; base < hi; base += 32) {
+    const int p = base + lane;
+    const uint32_t key = p < hi ? keys[p] : 0u;
+    const bool gt = p < hi && key > T, eq = p < hi && key == T;
+    const uint32_t meq = __ballot_sync(0xffffffffu, eq);
+    const bool take = gt || (eq && eq_rank + __popc(meq & lanemask_lt(lane)) < krem);
+    const uint32_t mt = __ballot_sync(0xffffffffu, take);
+    if (take) out[pos + __popc(mt & lanemask_lt(lane))] = p;
+    pos += __popc(mt);
+    eq_rank += __popc(meq);
+  }
+  if (tid == 0) A.n_sel_out[a] = k;
 }
 
 }  // namespace
@@ -184,18 +273,36 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(
 int launch_select(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,
                   const int32_t* req_ids, int n_req, int32_t* sel, int32_t* n_sel) {
   if (n_req <= 0) return FERRY_OK;
-  const int N = c->cfg.max_pages, k = c->cfg.top_k;
-  const unsigned grid = (unsigned)(n_req * c->lanes_per_req);
-  const size_t smem = (size_t)N * sizeof(uint32_t);
+  SelArgs A{};
+  A.q = q;
+  A.req_ids = req_ids;
+  A.lanes_per_req = c->lanes_per_req;
+  A.ctx_pages = c->ctx_pages;
+  A.req_base = c->req_base;
+  A.summ = c->summ;
+  A.pool_units = c->pool_units;
+  A.N = c->cfg.max_pages;
+  A.k = c->cfg.top_k;
+  A.num_requests = c->cfg.num_requests;
+  A.nchunks = select_chunks(A.N);
+  A.gkeys = c->sel_keys;
+  A.done = c->sel_done;
+  A.sel_out = sel;
+  A.n_sel_out = n_sel;
+  A.err = c->err;
+  if (A.nchunks > 1 && (!A.gkeys || !A.done)) {
+    set_error("select: chunk scratch missing");
+    return FERRY_E_STATE;
+  }
+  const unsigned grid = (unsigned)((int64_t)n_req * c->lanes_per_req * A.nchunks);
+  const size_t smem = (size_t)A.N * sizeof(uint32_t);
 #define FERRY_SEL_CASE(GG)                                                                    \
   case GG: {                                                                                  \
     auto kern = select_kernel<GG>;                                                            \
     if (smem > 48 * 1024)                                                                     \
       FERRY_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,       \
                                      (int)smem));                                             \
-    kern<<<grid, kSelThreads, smem, st>>>(q, req_ids, c->lanes_per_req, c->ctx_pages, c->req_base, c->summ, \
-                                          c->pool_units, N, k, c->cfg.num_requests, sel,      \
-                                          n_sel, c->err);                                     \
+    kern<<<grid, kSelThreads, smem, st>>>(A);                                                 \
     break;                                                                                    \
   }
   switch (c->group) {

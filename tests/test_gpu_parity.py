@@ -152,6 +152,9 @@ def test_kvgen_and_summaries_bit_exact(torch_cuda):
     dict(),                                            # G=1, C=k
     dict(q_heads=8, kv_heads=2, cache_frac=0.5),       # GQA group 4, C=2k
     dict(q_heads=8, kv_heads=1, ctx_tokens=2048, top_k=32, cache_frac=0.25),  # group 8
+    # long lanes: selection scores them in several chunks (one CTA each)
+    dict(num_layers=1, q_heads=8, kv_heads=1, ctx_tokens=65536, top_k=64),  # N 4096, G 8
+    dict(num_layers=1, q_heads=4, kv_heads=2, ctx_tokens=40000, top_k=48),  # N 2500, G 2
 ])
 def test_decode_steps_match_oracle(torch_cuda, shape):
     from ferry_b200.workload import small
@@ -172,6 +175,34 @@ def test_decode_steps_match_oracle(torch_cuda, shape):
         h.check_step(_q(w, reqs, 4, job=1), reqs)
         # a partial batch in a different order
         h.check_step(_q(w, [2, 0], 5), [2, 0])
+    finally:
+        h.close()
+
+
+@pytest.mark.parametrize("ctx_tokens", [2048, 65536])
+def test_select_ties_and_signed_zeros(torch_cuda, ctx_tokens):
+    """All-zero queries score every page +-0 (ties everywhere, and -0 < +0 in
+    key order); identical q heads tie the GQA maximum on every page."""
+    from ferry_b200.workload import small
+
+    t = torch_cuda
+    w = small(num_requests=3, num_layers=1, q_heads=8, kv_heads=2, ctx_tokens=ctx_tokens, top_k=40)
+    h = Harness(t, w)
+    try:
+        reqs = [0, 1, 2]
+        h.begin(reqs)
+        q = _q(w, reqs, 0)
+        q[0] = 0                                   # request 0: zero queries
+        q[1, :, :, :] = q[1, :, :1, :]             # request 1: every head equal to head 0
+        q[2, :, 1::2, :] = -q[2, :, 0::2, :]       # request 2: heads mirrored in each group
+        ids = t.from_numpy(np.asarray(reqs, np.int32)).to(h.dev)
+        h.dec.select(t.from_numpy(q).to(h.dev), ids)
+        t.cuda.synchronize()
+        h.dec.check()
+        nl = len(reqs) * h.LH
+        sel_ref, ns_ref = h.oracle_select(q, reqs)
+        assert (h.dec.n_sel[:nl].cpu().numpy() == ns_ref).all()
+        assert (h.dec.sel[:nl].cpu().numpy() == sel_ref).all()
     finally:
         h.close()
 

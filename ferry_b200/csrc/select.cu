@@ -26,7 +26,13 @@ namespace {
 
 constexpr int kSelThreads = 256;
 constexpr int kSelWarps = kSelThreads / 32;
-constexpr int kSelBatch = 8;  // pages per warp batch: 8 x 512 B of summaries in flight
+constexpr int kSelBatch = 8;  // pages per warp per stage
+constexpr int kStagePages = kSelWarps * kSelBatch;  // 64 summary rows per ring stage
+constexpr int kSelStages = 3;
+constexpr int kRowBytes = kHeadDim * 4;                        // 512
+constexpr int kStageBytes = kStagePages * kRowBytes;           // 32 KiB
+constexpr int kRingBytes = kSelStages * kStageBytes;           // 96 KiB
+static_assert(kMaxPages * 4 <= kRingBytes, "keys of a lane must fit the ring");
 
 template <int G>
 struct SelShape {
@@ -39,28 +45,27 @@ struct SelShape {
 
 // Sum over the 32 lanes of V independent values. Level j pairs lane l with
 // l ^ (16 >> j), as the xor butterfly does; while more than one value is
-// left the pair swaps halves (the lane with the level's bit set keeps the
-// upper half), afterwards it is a plain butterfly step. Each addition has the
-// same two operands as the butterfly's. Lane l returns value l >> (5 - log2 V).
+// left the pair swaps halves, afterwards it is a plain butterfly step. Each
+// addition has the same two operands as the butterfly's.
+//
+// The half swap needs no selects: lane l holds its values permuted,
+// w[i] = value[i ^ m] with m = l >> (5 - log2 V), so at every level each lane
+// keeps the lower half and sends the upper one (the partner's upper half
+// holds the same values as this lane's lower half). Lane l returns value m.
 template <int V>
-__device__ __forceinline__ float transpose_reduce(float (&v)[V], int lane) {
+__device__ __forceinline__ float transpose_reduce(float (&w)[V]) {
 #pragma unroll
   for (int j = 0; j < 5; ++j) {
     const int o = 16 >> j;
     const int n = V >> j;
     if (n > 1) {
-      const bool up = (lane & o) != 0;
 #pragma unroll
-      for (int i = 0; i < n / 2; ++i) {
-        const float send = up ? v[i] : v[i + n / 2];
-        const float keep = up ? v[i + n / 2] : v[i];
-        v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
-      }
+      for (int i = 0; i < n / 2; ++i) w[i] = __fadd_rn(w[i], __shfl_xor_sync(0xffffffffu, w[i + n / 2], o));
     } else {
-      v[0] = __fadd_rn(v[0], __shfl_xor_sync(0xffffffffu, v[0], o));
+      w[0] = __fadd_rn(w[0], __shfl_xor_sync(0xffffffffu, w[0], o));
     }
   }
-  return v[0];
+  return w[0];
 }
 
 __device__ __forceinline__ float lane_partial(const float (&q)[4], const float4 s) {
@@ -91,7 +96,11 @@ struct SelArgs {
 template <int G>
 __global__ void __launch_bounds__(kSelThreads, 2) select_kernel(SelArgs A) {
   using Sh = SelShape<G>;
-  extern __shared__ uint32_t keys[];  // N entries
+  // dynamic: the summary ring; keys after it (one chunk) or in it (after scoring)
+  extern __shared__ __align__(128) uint8_t sel_smem[];
+  uint8_t* ring = sel_smem;
+  uint32_t* keys = reinterpret_cast<uint32_t*>(sel_smem + (A.nchunks > 1 ? 0 : kRingBytes));
+  __shared__ __align__(8) uint64_t bars[kSelStages];
   __shared__ uint32_t hist[256];
   __shared__ uint32_t wcnt[2][kSelWarps];
   __shared__ uint32_t s_prefix, s_krem, s_last;
@@ -115,13 +124,17 @@ __global__ void __launch_bounds__(kSelThreads, 2) select_kernel(SelArgs A) {
     np = np < 0 ? 0 : N;
   }
 
-  // ---- phase 1: scores of this chunk's pages
+  // ---- phase 1: scores of this chunk's pages. Summary rows stream through a
+  // kSelStages-deep ring of 64-row stages (cp.async.bulk, mbarrier-completed);
+  // warp w scores rows 8w..8w+7 of each stage.
   {
+    // this lane's value permutation (see transpose_reduce): page u ^ pm, head g ^ hm
+    const int m = lane >> Sh::S, pm = m / G, hm = m % G;
     float qv[G][4];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       const uint2 raw =
-          *reinterpret_cast<const uint2*>(A.q + ((size_t)a * G + g) * kHeadDim + lane * 4);
+          *reinterpret_cast<const uint2*>(A.q + ((size_t)a * G + (g ^ hm)) * kHeadDim + lane * 4);
       const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
       const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
       qv[g][0] = x.x; qv[g][1] = x.y; qv[g][2] = y.x; qv[g][3] = y.y;
@@ -131,39 +144,66 @@ __global__ void __launch_bounds__(kSelThreads, 2) select_kernel(SelArgs A) {
         (uint64_t)(A.req_base[req] + (int64_t)(a % A.lanes_per_req) * N) % A.pool_units;
     const int cs = select_chunk_pages(N, A.nchunks);
     const int c0 = chunk * cs, c1 = min(np, c0 + cs);
+    const int n_st = c1 > c0 ? (c1 - c0 + kStagePages - 1) / kStagePages : 0;
+    if (tid == 0) {
+      for (int i = 0; i < kSelStages; ++i) mbar_init(&bars[i], 1);
+      fence_mbar_init();
+    }
+    __syncthreads();
+    auto issue = [&](int it) {  // thread 0: stage `it` into buffer it % kSelStages
+      const int pb = c0 + it * kStagePages, cnt = min(kStagePages, c1 - pb);
+      uint8_t* dst = ring + (it % kSelStages) * kStageBytes;
+      uint64_t* bar = &bars[it % kSelStages];
+      mbar_arrive_expect_tx(bar, (uint32_t)(cnt * kRowBytes));
+      uint64_t u = (unit0 + (uint64_t)pb) % A.pool_units;
+      for (int d = 0; d < cnt;) {  // split where the pool wraps
+        const uint64_t room = A.pool_units - u;
+        const int run = (uint64_t)(cnt - d) < room ? cnt - d : (int)room;
+        bulk_load(dst + d * kRowBytes, A.summ + u * kHeadDim, (uint32_t)(run * kRowBytes), bar);
+        d += run;
+        u = 0;
+      }
+    };
+    if (tid == 0)
+      for (int i = 0; i < kSelStages && i < n_st; ++i) issue(i);
     uint32_t* kdst = A.nchunks > 1 ? A.gkeys + (size_t)a * N : keys;
-    for (int p0 = c0 + warp * kSelBatch; p0 < c1; p0 += kSelWarps * kSelBatch) {  // warp-uniform
-      float4 s[kSelBatch];
+    for (int it = 0; it < n_st; ++it) {
+      const int buf = it % kSelStages;
+      const bool got = __all_sync(0xffffffffu, mbar_wait(&bars[buf], (uint32_t)((it / kSelStages) & 1), A.err));
+      const int p0 = c0 + it * kStagePages + warp * kSelBatch;
+      if (got && p0 < c1) {  // warp-uniform
+        const uint8_t* rows = ring + buf * kStageBytes + warp * kSelBatch * kRowBytes + lane * 16;
 #pragma unroll
-      for (int u = 0; u < kSelBatch; ++u) {
-        const int p = p0 + u;
-        if (p < c1) {
-          uint64_t unit = unit0 + (uint64_t)p;
-          if (unit >= A.pool_units) unit %= A.pool_units;
-          s[u] = __ldg(reinterpret_cast<const float4*>(A.summ + unit * kHeadDim) + lane);
-        } else {
-          s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < Sh::NR; ++r) {
+          float v[Sh::V];
+#pragma unroll
+          for (int u = 0; u < Sh::UR; ++u) {
+            const float4 sv = *reinterpret_cast<const float4*>(rows + (r * Sh::UR + (u ^ pm)) * kRowBytes);
+#pragma unroll
+            for (int g = 0; g < G; ++g) v[u * G + g] = lane_partial(qv[g], sv);
+          }
+          float best = transpose_reduce<Sh::V>(v);
+          // lane holds value m: page m / G, head m % G
+#pragma unroll
+          for (int b = 1; b < G; b <<= 1) {
+            const float other = __shfl_xor_sync(0xffffffffu, best, b << Sh::S);
+            const bool right = (m & b) != 0;  // this lane carries the higher heads
+            const float lo = right ? other : best, hi = right ? best : other;
+            best = hi > lo ? hi : lo;  // the lower head wins ties
+          }
+          const int p = p0 + r * Sh::UR + pm;
+          if (hm == 0 && (lane & ((1 << Sh::S) - 1)) == 0 && p < c1) kdst[p] = order_key(best);
         }
       }
-#pragma unroll
-      for (int r = 0; r < Sh::NR; ++r) {
-        float v[Sh::V];
-#pragma unroll
-        for (int u = 0; u < Sh::UR; ++u)
-#pragma unroll
-          for (int g = 0; g < G; ++g) v[u * G + g] = lane_partial(qv[g], s[r * Sh::UR + u]);
-        float best = transpose_reduce<Sh::V>(v, lane);
-        const int x = lane >> Sh::S;  // value index held: page x / G, head x % G
-#pragma unroll
-        for (int b = 1; b < G; b <<= 1) {
-          const float other = __shfl_xor_sync(0xffffffffu, best, b << Sh::S);
-          const bool right = (x & b) != 0;  // this lane carries the higher heads
-          const float lo = right ? other : best, hi = right ? best : other;
-          best = hi > lo ? hi : lo;  // the lower head wins ties
-        }
-        const int p = p0 + r * Sh::UR + x / G;
-        if ((x % G) == 0 && (lane & ((1 << Sh::S) - 1)) == 0 && p < c1) kdst[p] = order_key(best);
+      if (__syncthreads_or(!got)) {
+        // a stage never completed: let the copies still in flight land, then leave
+        if (tid == 0)
+          for (int j = it; j < n_st && j < it + kSelStages; ++j)
+            mbar_wait(&bars[j % kSelStages], (uint32_t)((j / kSelStages) & 1), nullptr);
+        __syncthreads();
+        return;
       }
+      if (tid == 0 && it + kSelStages < n_st) issue(it + kSelStages);
     }
   }
   if (A.nchunks > 1) {
@@ -295,7 +335,7 @@ int launch_select(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,
     return FERRY_E_STATE;
   }
   const unsigned grid = (unsigned)((int64_t)n_req * c->lanes_per_req * A.nchunks);
-  const size_t smem = (size_t)A.N * sizeof(uint32_t);
+  const size_t smem = kRingBytes + (A.nchunks > 1 ? 0 : (size_t)A.N * sizeof(uint32_t));
 #define FERRY_SEL_CASE(GG)                                                                    \
   case GG: {                                                                                  \
     auto kern = select_kernel<GG>;                                                            \

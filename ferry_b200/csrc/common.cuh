@@ -181,6 +181,7 @@ struct ferry_ctx {
   int64_t lanes = 0;      // R * L * Hkv
 
   uint8_t* cache = nullptr;  // lanes * C units
+  alignas(64) unsigned char cache_map[128] = {};  // TMA tensor map of the e4m3 cache
   ferry_lru lru;             // page tables + LRU order, lanes x (C, N)
   int32_t* ctx_pages = nullptr;  // R
   int64_t* req_base = nullptr;   // R: pool unit of the request's (lane 0, page 0)
@@ -237,6 +238,7 @@ int launch_attention(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,
                      const int32_t* req_ids, int n_req, const int32_t* item_slot,
                      const int32_t* n_sel, float* out);
 // e4m3 KV path on tcgen05 tensor cores (attn_tc.cu)
+int make_cache_tensor_map(ferry_ctx* c);
 int launch_attention_tc(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,
                         const int32_t* req_ids, int n_req, const int32_t* item_slot,
                         const int32_t* n_sel, float* out);

@@ -110,6 +110,8 @@ def main():
     ap.add_argument("--device", type=int, default=0)
     ap.add_argument("--migrate", action="store_true", help="time request migration over NVLink")
     ap.add_argument("--probe", action="store_true", help="topology and link peaks")
+    ap.add_argument("--requests", type=int, default=0, help="override the batch (a smaller case to profile)")
+    ap.add_argument("--only", default="", help="comma list of kernels to time (gather,attention,select,detect)")
     args = ap.parse_args()
     if args.probe:
         print(json.dumps({"probe": probe()}))
@@ -118,6 +120,11 @@ def main():
         print(json.dumps({"migrate": migrate_bench(WORKLOADS[args.workload], args.iters)}))
         return
     w = WORKLOADS[args.workload]
+    if args.requests:
+        import dataclasses
+
+        w = dataclasses.replace(w, num_requests=args.requests)
+    only = set(args.only.split(",")) if args.only else {"gather", "attention", "select", "detect"}
     torch.cuda.set_device(args.device)
     dev = torch.device("cuda", args.device)
     dec = Decoder(w, args.device)
@@ -141,18 +148,22 @@ def main():
     units = int(dec.n_miss.sum().item())
     res = {"workload": w.name, "batch_requests": R, "kv_dtype": w.kv_dtype}
     # gather re-copies the same miss list each launch (idempotent)
-    t = _time(lambda: dec.gather(ids), max(3, args.iters // 5))
-    ub = w.unit_bytes
-    res["gather"] = {"us": t, "units": units, "bytes": units * ub, "GB_s": units * ub / t / 1e3}
+    if "gather" in only:
+        t = _time(lambda: dec.gather(ids), max(3, args.iters // 5))
+        ub = w.unit_bytes
+        res["gather"] = {"us": t, "units": units, "bytes": units * ub, "GB_s": units * ub / t / 1e3}
     dec.gather(ids)
-    t = _time(lambda: dec.attention(q, ids, out), args.iters)
-    b = R * w.attn_bytes_per_token() + R * w.qo_bytes_per_token()
-    res["attention"] = {"us": t, "bytes": b, "GB_s": b / t / 1e3}
-    t = _time(lambda: dec.select(q, ids), args.iters)
-    b = R * w.select_bytes_per_token()
-    res["select"] = {"us": t, "bytes": b, "GB_s": b / t / 1e3}
-    t = _time(lambda: dec.detect(ids), args.iters)  # all hits after the first launch
-    res["detect"] = {"us": t}
+    if "attention" in only:
+        t = _time(lambda: dec.attention(q, ids, out), args.iters)
+        b = R * w.attn_bytes_per_token() + R * w.qo_bytes_per_token()
+        res["attention"] = {"us": t, "bytes": b, "GB_s": b / t / 1e3}
+    if "select" in only:
+        t = _time(lambda: dec.select(q, ids), args.iters)
+        b = R * w.select_bytes_per_token()
+        res["select"] = {"us": t, "bytes": b, "GB_s": b / t / 1e3}
+    if "detect" in only:
+        t = _time(lambda: dec.detect(ids), args.iters)  # all hits after the first launch
+        res["detect"] = {"us": t}
     dec.check()
     dec.close()
     print(json.dumps(res))

@@ -34,7 +34,7 @@
 namespace ferry {
 namespace {
 
-constexpr int kTcThreads = 128;
+constexpr int kTcThreads = 192;  // warps 0-3 softmax (TMEM lanes), 4 TMA producer, 5 MMA issuer
 constexpr int kTcPages = 8;                       // pages per group: 128 tokens
 constexpr int kTcN = 32;                          // MMA N: 3 terms x 8 head rows, padded
 constexpr int kTcStages = 3;
@@ -45,11 +45,11 @@ constexpr int kScl = kTcPages * 16;               // 16 B per page: k_scale, v_s
 constexpr int kOffK = 0;                          // stage s: K at s * 2 * kTile, V after it
 constexpr int kOffQ = kTcStages * 2 * kTile;      // 98304
 constexpr int kOffP = kOffQ + kQP;
-constexpr int kOffScl = kOffP + kQP;
+constexpr int kOffScl = kOffP + 2 * kQP;          // P double-buffered
 constexpr int kTcSmemUsed = kOffScl + kTcStages * kScl;
 constexpr int kTcSmem = kTcSmemUsed + 1024;       // alignment slack
 static_assert(2 * (kTcSmem + 1024) <= 228 * 1024, "two CTAs per SM must fit");
-constexpr uint32_t kTmemCols = 64;                // S at cols [0,32), O at [32,64)
+constexpr uint32_t kTmemCols = 128;               // S[2] at cols 0, 32; O[2] at 64, 96
 
 // UMMA shared-memory descriptor without swizzle (layout type 0), version 1
 __device__ __forceinline__ uint64_t plain_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -94,22 +94,6 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// 32 consecutive f32 columns of this thread's TMEM lane
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
 
 // 3-D tensor copy global -> shared (no multicast), completion on the mbarrier
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
@@ -227,13 +211,50 @@ struct TcArgs {
 
 __device__ __forceinline__ int cta_of(int64_t x, int nc, int64_t T) { return (int)(((x + 1) * nc - 1) / T); }
 
+// 8 consecutive f32 columns of this thread's TMEM lane (column a multiple of 8)
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// barrier among the 128 softmax threads only (named barrier 1); true when
+// any of them passed `flag`
+__device__ __forceinline__ bool softmax_bar_or(bool flag) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)flag)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Walk of a CTA's flat range, shared by its three roles: lane segments in
+// order, each with its groups [glo, ghi) (pages present only).
+struct Seg {
+  int a, n, glo, ghi;
+  int64_t unit0;
+};
+
 template <int G>
 __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_constant__ CUtensorMap tmap, TcArgs A) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full[kTcStages];
-  __shared__ __align__(8) uint64_t bar_s, bar_o;
-  __shared__ float red[4][8];
-  __shared__ uint32_t tmem_slot, s_flag;
+  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages];
+  __shared__ __align__(8) uint64_t s_full[2], s_free[2], p_full[2], o_full[2], o_free[2], q_full;
+  __shared__ float red[2][4][8], qred[4][8];
+  __shared__ uint32_t tmem_slot, s_flag, s_abort;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = blockIdx.x;
@@ -245,9 +266,19 @@ __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_con
   uint8_t* scl = smem + kOffScl;
 
   if (tid == 0) {
-    for (int s = 0; s < kTcStages; ++s) mbar_init(&full[s], 1);
-    mbar_init(&bar_s, 1);
-    mbar_init(&bar_o, 1);
+    for (int i = 0; i < kTcStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&s_free[i], 4);  // one arrival per softmax warp
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_free[i], 4);
+    }
+    mbar_init(&q_full, 4);
+    s_abort = 0;
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -256,295 +287,331 @@ __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_con
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   // zero every tile once: rows the copies never fill (short groups, padded
-  // heads) must hold finite values
+  // heads and terms) must hold finite values, and zeros in P
   for (int i = tid; i < kTcSmemUsed / 16; i += kTcThreads) reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = tmem_slot, tmem_s = tmem, tmem_o = tmem + 32;
-  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-  constexpr uint32_t kIdQK = idesc_f8(false, false), kIdPV = idesc_f8(true, true);
+  const uint32_t tmem = tmem_slot;
   const int k = A.k;
 
-  // valid pages of lane a (0 when its request id or n_sel is out of range)
-  auto lane_pages = [&](int a, int64_t* unit0) -> int {
+  // segment of lane a (no pages when its request id or n_sel is out of range)
+  auto segment = [&](int a) {
+    Seg sg;
+    sg.a = a;
     const int64_t gl = (int64_t)A.req_ids[a / A.lanes_per_req] * A.lanes_per_req + a % A.lanes_per_req;
-    const int n = A.n_sel[a];
+    int n = A.n_sel[a];
     if (gl < 0 || gl >= A.lanes_total || n < 0 || n > k) {
       if (tid == 0) record_error(A.err, kErrRange);
-      return 0;
+      n = 0;
     }
-    *unit0 = gl * A.C;
-    return n;
-  };
-
-  // ---- producer (warp 0): a cursor over the same flat range, one group ahead
-  // of the copies it issues; lane p holds the cache slot of page p of the
-  // group under the cursor, loaded a group early so the copies never wait on it
-  int la = (int)(x_lo / A.gpl), lg = 0, lgend = 0, lnp = 0, nslot = 0;
-  int64_t lunit0 = 0;
-  bool more = false;
-  auto lane_begin = [&]() {
-    lnp = lane_pages(la, &lunit0);
-    const int64_t base = (int64_t)la * A.gpl;
-    lg = (int)(max(x_lo, base) - base);
-    const int64_t e = x_hi - base;
-    const int ng = (lnp + kTcPages - 1) / kTcPages;
-    lgend = (int)(e < ng ? e : ng);
-  };
-  auto advance = [&]() {  // to the next group with pages, then prefetch its slots
-    while ((int64_t)la * A.gpl < x_hi && lg >= lgend) {
-      ++la;
-      if ((int64_t)la * A.gpl < x_hi) lane_begin();
-    }
-    more = (int64_t)la * A.gpl < x_hi;
-    if (more) {
-      const int p0 = lg * kTcPages;
-      nslot = lane < min(kTcPages, lnp - p0) ? A.item_slot[(size_t)la * k + p0 + lane] : 0;
-    }
-  };
-  uint32_t it_load = 0, it_use = 0;
-  auto issue = [&]() {
-    if (warp != 0 || !more) return;
-    const int s = it_load % kTcStages;
-    const int np = min(kTcPages, lnp - lg * kTcPages);
-    uint8_t* Ks = smem + kOffK + s * 2 * kTile;
-    if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(np * (2 * 2048 + 16)));
-    __syncwarp();
-    if (lane < np) {
-      int slot = nslot;
-      if (slot < 0 || slot >= A.C) {
-        record_error(A.err, kErrRange);
-        slot = 0;
-      }
-      const int64_t unit = lunit0 + slot;
-      tma_load_3d(Ks + lane * 2048, &tmap, 0, 0, (int)unit, &full[s]);           // K rows
-      tma_load_3d(Ks + kTile + lane * 2048, &tmap, 0, 16, (int)unit, &full[s]);  // V rows
-      bulk_load(scl + s * kScl + lane * 16, A.cache + (size_t)unit * kUnitBytesF8 + 4096, 16, &full[s]);
-    }
-    ++lg;
-    ++it_load;
-    advance();
-  };
-  if (warp == 0) {
-    lane_begin();
-    advance();
-  }
-  for (int s = 0; s < kTcStages; ++s) issue();
-
-  uint32_t ph_s = 0, ph_o = 0;
-  bool ok = true, mma_pending_s = false, mma_pending_o = false;
-  const int t = tid;
-  for (int a = (int)(x_lo / A.gpl); (int64_t)a * A.gpl < x_hi && ok; ++a) {
-    int64_t unit0 = 0;
-    const int n = lane_pages(a, &unit0);
+    sg.n = n;
+    sg.unit0 = gl * A.C;
     const int64_t base = (int64_t)a * A.gpl;
-    const int glo = (int)(max(x_lo, base) - base);
+    sg.glo = (int)(max(x_lo, base) - base);
     const int ng = (n + kTcPages - 1) / kTcPages;
-    const int ghi = (int)min(x_hi - base, (int64_t)ng);
-    float m_run[G], l_thr[G], o_acc[G], qdiv[G];
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      m_run[h] = -INFINITY;
-      l_thr[h] = 0.f;
-      o_acc[h] = 0.f;
-      qdiv[h] = 0.f;
+    sg.ghi = (int)min(x_hi - base, (int64_t)ng);
+    return sg;
+  };
+  const int a_lo = (int)(x_lo / A.gpl);
+  auto in_range = [&](int a) { return (int64_t)a * A.gpl < x_hi; };
+
+  // what each role leaves in flight, drained only when a wait gave up
+  uint32_t prod_j = 0;           // producer: groups issued
+  uint64_t* mma_last = nullptr;  // MMA issuer: barrier of its last commit
+  uint32_t mma_par = 0;
+  if (warp == 4) {
+    // ================= producer: stage j of the group sequence into buffer j % 3
+    uint32_t& j = prod_j;
+    bool ok = true;
+    for (int a = a_lo; in_range(a) && ok; ++a) {
+      const Seg sg = segment(a);
+      for (int g = sg.glo; g < sg.ghi; ++g, ++j) {
+        const int s = j % kTcStages, np = min(kTcPages, sg.n - g * kTcPages);
+        int slot = lane < np ? A.item_slot[(size_t)a * k + g * kTcPages + lane] : 0;
+        if (j >= (uint32_t)kTcStages) ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], ((j / kTcStages) - 1) & 1u, A.err));
+        if (!ok) break;
+        uint8_t* Ks = smem + kOffK + s * 2 * kTile;
+        if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(np * (2 * 2048 + 16)));
+        __syncwarp();
+        if (lane < np) {
+          if (slot < 0 || slot >= A.C) {
+            record_error(A.err, kErrRange);
+            slot = 0;
+          }
+          const int64_t unit = sg.unit0 + slot;
+          tma_load_3d(Ks + lane * 2048, &tmap, 0, 0, (int)unit, &full[s]);           // K rows
+          tma_load_3d(Ks + kTile + lane * 2048, &tmap, 0, 16, (int)unit, &full[s]);  // V rows
+          bulk_load(scl + s * kScl + lane * 16, A.cache + (size_t)unit * kUnitBytesF8 + 4096, 16, &full[s]);
+        }
+      }
     }
-    if (glo < ghi) {
-      // ---- Q terms of this lane: thread t = dim t; per-head power-of-two scale
-      float qf[G];
+    if (!ok && lane == 0) atomicOr(&s_abort, 1u);
+    __syncwarp();
+  } else if (warp == 5) {
+    // ================= MMA issuer (one thread)
+    if (lane == 0) {
+      constexpr uint32_t kIdQK = idesc_f8(false, false), kIdPV = idesc_f8(true, true);
+      const uint32_t sQ = smem_addr(Qt);
+      bool ok = true;
+      uint64_t*& last_bar = mma_last;
+      uint32_t& last_par = mma_par;
+      auto issue_pv = [&](uint32_t i) {
+        const int bi = i & 1, si = i % kTcStages;
+        ok = ok && mbar_wait(&p_full[bi], (i >> 1) & 1u, A.err);
+        if (ok && i >= 2) ok = mbar_wait(&o_free[bi], ((i >> 1) - 1) & 1u, A.err);
+        if (!ok) return;
+        tc_fence_after();
+        const uint32_t sV = smem_addr(smem + kOffK + si * 2 * kTile) + kTile, sP = smem_addr(Pt + bi * kQP);
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        qf[h] = __half2float(__ushort_as_half(A.q[((size_t)a * G + h) * kHeadDim + t]));
-        float x = fabsf(qf[h]);
+        for (int jj = 0; jj < 4; ++jj)
+          mma_f8(tmem + 64 + bi * 32, sw128_desc(sV + jj * 4096, kTile, 1024), plain_desc(sP + jj * 1024, 256, 128),
+                 kIdPV, jj > 0);
+        mma_commit(&o_full[bi]);
+        mma_commit(&empty[si]);  // K and V of this stage are no longer read
+        last_bar = &o_full[bi];
+        last_par = (i >> 1) & 1u;
+      };
+      uint32_t j = 0, segs = 0;
+      for (int a = a_lo; in_range(a) && ok; ++a) {
+        const Seg sg = segment(a);
+        for (int g = sg.glo; g < sg.ghi && ok; ++g, ++j) {
+          const int s = j % kTcStages, b = j & 1;
+          if (g == sg.glo) {
+            if (j > 0) issue_pv(j - 1);  // the previous segment's last group first
+            ok = ok && mbar_wait(&q_full, segs & 1u, A.err);
+            ++segs;
+          }
+          ok = ok && mbar_wait(&full[s], (j / kTcStages) & 1u, A.err);
+          if (ok && j >= 2) ok = mbar_wait(&s_free[b], ((j >> 1) - 1) & 1u, A.err);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t sK = smem_addr(smem + kOffK + s * 2 * kTile);
 #pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, off));
-        if (lane == 0) red[warp][h] = x;
+          for (int jj = 0; jj < 4; ++jj)
+            mma_f8(tmem + b * 32, sw128_desc(sK + jj * 32, 16, 1024), sw128_desc(sQ + jj * 32, 16, 1024), kIdQK, jj > 0);
+          mma_commit(&s_full[b]);
+          last_bar = &s_full[b];
+          last_par = (j >> 1) & 1u;
+          if (g > sg.glo) issue_pv(j - 1);
+        }
       }
-      __syncthreads();
-#pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float am = fmaxf(fmaxf(red[0][h], red[1][h]), fmaxf(red[2][h], red[3][h]));
-        const float sc = pow2_scale(am);
-        qdiv[h] = A.qscale / sc;  // score = (S0 + S1/16 + S2/256) * k_scale * qdiv
-        uint8_t tt[3];
-        split3(qf[h] * sc, tt);
-#pragma unroll
-        for (int j = 0; j < 3; ++j) Qt[sw128(j * 8 + h, t)] = tt[j];
-      }
-      fence_proxy_async_smem();
-      __syncthreads();  // red reusable; Q tile complete
+      if (ok && j > 0) issue_pv(j - 1);
+      if (!ok) atomicOr(&s_abort, 1u);
     }
-    for (int g = glo; g < ghi; ++g) {
-      const int s = it_use % kTcStages;
-      const uint32_t par = (it_use / kTcStages) & 1u;
-      const int np = min(kTcPages, n - g * kTcPages);
-      ok = mbar_wait(&full[s], par, A.err);
-      if (__syncthreads_or(!ok)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t sK = smem_addr(smem + kOffK + s * 2 * kTile), sV = sK + kTile;
-      const uint32_t sQ = smem_addr(Qt), sP = smem_addr(Pt);
-      // ---- S = K Q^T (4 K-steps of 32 dims)
-      if (tid == 0) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          mma_f8(tmem_s, sw128_desc(sK + j * 32, 16, 1024), sw128_desc(sQ + j * 32, 16, 1024), kIdQK, j > 0);
-        mma_commit(&bar_s);
-      }
-      mma_pending_s = true;
-      ok = __all_sync(0xffffffffu, mbar_wait(&bar_s, ph_s, A.err));
-      float sv[32];
-      if (ok) {
-        ph_s ^= 1;
-        mma_pending_s = false;
-        tc_fence_after();
-        tmem_ld32(tmem_s + lane_off, sv);
-      }
-      const int pg = t >> 4;
-      const bool valid = pg < np;
-      const float ks = *reinterpret_cast<const float*>(scl + s * kScl + pg * 16);
-      const float vs = *reinterpret_cast<const float*>(scl + s * kScl + pg * 16 + 4);
-      float x[G], mx[G];
+    __syncwarp();
+  } else {
+    // ================= softmax warps 0-3: thread t = TMEM lane t = token t (S) / dim t (O)
+    const int t = tid;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    uint32_t j = 0;
+    bool ok = true;
+    for (int a = a_lo; in_range(a) && ok; ++a) {
+      const Seg sg = segment(a);
+      const int glo = sg.glo, ghi = sg.ghi, n = sg.n;
+      const int64_t base = (int64_t)a * A.gpl;
+      float m_run[G], l_thr[G], o_acc[G], qdiv[G], alpha_prev[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        x[h] = valid && ok ? (sv[h] + sv[8 + h] * 0.0625f + sv[16 + h] * 0.00390625f) * ks * qdiv[h] : -INFINITY;
-        mx[h] = x[h];
+        m_run[h] = -INFINITY;
+        l_thr[h] = 0.f;
+        o_acc[h] = 0.f;
+        qdiv[h] = 0.f;
+        alpha_prev[h] = 0.f;
       }
-      {
-        const float wm = warp_max_heads<G>(mx, lane);  // head (lane >> (5 - log2 G))
-        if ((lane & ((32 / G) - 1)) == 0) red[warp][lane / (32 / G)] = wm;
-      }
-      // power-of-two scale of the weights: p * v_scale * beta <= 448 in this group
-      float vmax = (lane & 31) < np ? *reinterpret_cast<const float*>(scl + s * kScl + (lane & 7) * 16 + 4) : 0.f;
-      vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
-      vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
-      vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 4));
-      const float beta = pow2_scale(__shfl_sync(0xffffffffu, vmax, 0));
-      if (__syncthreads_or(!ok)) {
-        ok = false;
-        break;
-      }
-      // block maximum per head: lane l takes warp l / 8's value of head l % 8
-      float gmx = red[lane >> 3][lane & 7];
-      gmx = fmaxf(gmx, __shfl_xor_sync(0xffffffffu, gmx, 8));
-      gmx = fmaxf(gmx, __shfl_xor_sync(0xffffffffu, gmx, 16));
-      float alpha[G], pw[G];
+      float beta_prev = 1.f;
+      if (glo < ghi) {
+        // ---- Q terms of this lane: thread t = dim t; per-head power-of-two scale
+        float qf[G];
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float mn = fmaxf(m_run[h], __shfl_sync(0xffffffffu, gmx, h));
-        alpha[h] = ex2(m_run[h] - mn);
-        const float p = valid ? ex2(x[h] - mn) : 0.f;
-        l_thr[h] = l_thr[h] * alpha[h] + p;
-        m_run[h] = mn;
-        pw[h] = p * vs * beta;
-      }
-      // this token's row of the P tile: byte j*8 + h = term j of head h
-      uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int h = 0; h < G; ++h) {
+          qf[h] = __half2float(__ushort_as_half(A.q[((size_t)a * G + h) * kHeadDim + t]));
+          float x = fabsf(qf[h]);
 #pragma unroll
-      for (int i = 0; i < (G + 1) / 2; ++i) {
-        uint32_t t0, t1, t2;
-        split3x2(make_float2(pw[2 * i], 2 * i + 1 < G ? pw[2 * i + 1] : 0.f), t0, t1, t2);
-        const int sh = 16 * (i & 1);
-        w[(i >> 1)] |= t0 << sh;
-        w[2 + (i >> 1)] |= t1 << sh;
-        w[4 + (i >> 1)] |= t2 << sh;
-      }
-      {
-        uint8_t* row = Pt + (t >> 3) * 256 + (t & 7) * 16;
-        *reinterpret_cast<uint4*>(row) = make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4*>(row + 128) = make_uint4(w[4], w[5], w[6], w[7]);
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncthreads();
-      tc_fence_after();
-      // ---- O^T = V^T P'^T (4 K-steps of 32 tokens)
-      if (tid == 0) {
+          for (int off = 16; off >= 1; off >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, off));
+          if (lane == 0) qred[warp][h] = x;
+        }
+        softmax_bar_or(false);
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          mma_f8(tmem_o, sw128_desc(sV + j * 4096, kTile, 1024), plain_desc(sP + j * 1024, 256, 128), kIdPV, j > 0);
-        mma_commit(&bar_o);
+        for (int h = 0; h < G; ++h) {
+          const float am = fmaxf(fmaxf(qred[0][h], qred[1][h]), fmaxf(qred[2][h], qred[3][h]));
+          const float sc = pow2_scale(am);
+          qdiv[h] = A.qscale / sc;  // score = (S0 + S1/16 + S2/256) * k_scale * qdiv
+          uint8_t tt[3];
+          split3(qf[h] * sc, tt);
+#pragma unroll
+          for (int jj = 0; jj < 3; ++jj) Qt[sw128(jj * 8 + h, t)] = tt[jj];
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&q_full);
       }
-      mma_pending_o = true;
-      ok = __all_sync(0xffffffffu, mbar_wait(&bar_o, ph_o, A.err));
-      if (ok) {
-        ph_o ^= 1;
-        mma_pending_o = false;
+      // fold of group i's PV (buffer i & 1) into o_acc
+      auto fold = [&](uint32_t i) {
+        const int bi = i & 1;
+        ok = __all_sync(0xffffffffu, mbar_wait(&o_full[bi], (i >> 1) & 1u, A.err));
+        if (!ok) return;
         tc_fence_after();
-        float ov[32];
-        tmem_ld32(tmem_o + lane_off, ov);  // thread t = head dim t
-        const float ib = __frcp_rn(beta);  // exact: beta is a power of two
+        float o0[8], o1[8], o2[8];
+        tmem_ld8(tmem + 64 + bi * 32 + lane_off, o0);  // thread t = head dim t
+        tmem_ld8(tmem + 64 + bi * 32 + lane_off + 8, o1);
+        tmem_ld8(tmem + 64 + bi * 32 + lane_off + 16, o2);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_free[bi]);
+        const float ib = __frcp_rn(beta_prev);  // exact: a power of two
 #pragma unroll
         for (int h = 0; h < G; ++h)
-          o_acc[h] = o_acc[h] * alpha[h] + (ov[h] + ov[8 + h] * 0.0625f + ov[16 + h] * 0.00390625f) * ib;
+          o_acc[h] = o_acc[h] * alpha_prev[h] + (o0[h] + o1[h] * 0.0625f + o2[h] * 0.00390625f) * ib;
+      };
+      for (int g = glo; g < ghi; ++g, ++j) {
+        const int s = j % kTcStages, b = j & 1;
+        const int np = min(kTcPages, n - g * kTcPages);
+        // ---- S of this group (its buffer is released as soon as it is read)
+        ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (j >> 1) & 1u, A.err));
+        float s0[8], s1[8], s2[8];
+        if (ok) {
+          tc_fence_after();
+          tmem_ld8(tmem + b * 32 + lane_off, s0);  // columns jj*8 + h: term jj of head h
+          tmem_ld8(tmem + b * 32 + lane_off + 8, s1);
+          tmem_ld8(tmem + b * 32 + lane_off + 16, s2);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_free[b]);
+          ok = mbar_wait(&full[s], (j / kTcStages) & 1u, A.err);  // the stage's scales
+        }
+        const int pg = t >> 4;
+        const bool valid = pg < np;
+        const float ks = *reinterpret_cast<const float*>(scl + s * kScl + pg * 16);
+        const float vs = *reinterpret_cast<const float*>(scl + s * kScl + pg * 16 + 4);
+        float x[G], mx[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          x[h] = valid && ok ? (s0[h] + s1[h] * 0.0625f + s2[h] * 0.00390625f) * ks * qdiv[h] : -INFINITY;
+          mx[h] = x[h];
+        }
+        {
+          const float wm = warp_max_heads<G>(mx, lane);  // head (lane >> (5 - log2 G))
+          if ((lane & ((32 / G) - 1)) == 0) red[b][warp][lane / (32 / G)] = wm;
+        }
+        // power-of-two scale of the weights: p * v_scale * beta <= 448 in this group
+        float vmax = lane < np ? *reinterpret_cast<const float*>(scl + s * kScl + (lane & 7) * 16 + 4) : 0.f;
+        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 4));
+        const float beta = pow2_scale(__shfl_sync(0xffffffffu, vmax, 0));
+        if (softmax_bar_or(!ok)) {
+          ok = false;
+          break;
+        }
+        // block maximum per head: lane l takes warp l / 8, head l % 8
+        float gmx = red[b][(lane >> 3) & 3][lane & 7];
+        gmx = fmaxf(gmx, __shfl_xor_sync(0xffffffffu, gmx, 8));
+        gmx = fmaxf(gmx, __shfl_xor_sync(0xffffffffu, gmx, 16));
+        float alpha[G], pw[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          const float mn = fmaxf(m_run[h], __shfl_sync(0xffffffffu, gmx, h));
+          alpha[h] = ex2(m_run[h] - mn);
+          const float p = valid ? ex2(x[h] - mn) : 0.f;
+          l_thr[h] = l_thr[h] * alpha[h] + p;
+          m_run[h] = mn;
+          pw[h] = p * vs * beta;
+        }
+        // this token's row of P[b] (MN-major, no swizzle): byte jj*8 + h =
+        // term jj of head h. P[b]'s last reader, the PV two groups back, was
+        // folded a group ago.
+        {
+          uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+          for (int i = 0; i < (G + 1) / 2; ++i) {
+            uint32_t t0, t1, t2;
+            split3x2(make_float2(pw[2 * i], 2 * i + 1 < G ? pw[2 * i + 1] : 0.f), t0, t1, t2);
+            const int sh = 16 * (i & 1);
+            w[(i >> 1)] |= t0 << sh;
+            w[2 + (i >> 1)] |= t1 << sh;
+            w[4 + (i >> 1)] |= t2 << sh;
+          }
+          uint8_t* row = Pt + b * kQP + (t >> 3) * 256 + (t & 7) * 16;
+          *reinterpret_cast<uint4*>(row) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(row + 128) = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[b]);
+        // ---- fold the previous group's PV (a failure here ends the loop at
+        // the next group's barrier, which every softmax warp reaches)
+        if (g > glo && ok) fold(j - 1);
+#pragma unroll
+        for (int h = 0; h < G; ++h) alpha_prev[h] = alpha[h];
+        beta_prev = beta;
       }
-      ++it_use;
-      tc_fence_before();
-      if (__syncthreads_or(!ok)) {  // stage, S/O TMEM, P tile and red reusable
+      if (ok && glo < ghi) fold(j - 1);
+      if (softmax_bar_or(!ok)) {
         ok = false;
         break;
       }
-      issue();
-    }
-    if (!ok) break;
-    // ---- partial of this lane segment: slot a + c
-    const int cf = cta_of(base, A.nc, A.T);
-    const int parts = cta_of(base + A.gpl - 1, A.nc, A.T) - cf + 1;
-    float* pc = A.part + ((size_t)a + c) * G * kPartStride;
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      float l = l_thr[h];
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-      if (lane == 0) red[warp][h] = l;
-      pc[h * kPartStride + t] = o_acc[h];
-    }
-    __syncthreads();
-    if (tid < G) {
-      pc[tid * kPartStride + 128] = m_run[tid];
-      pc[tid * kPartStride + 129] = red[0][tid] + red[1][tid] + red[2][tid] + red[3][tid];
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_flag = atomicAdd(&A.lane_done[a], 1u) == (uint32_t)(parts - 1);
-    __syncthreads();
-    if (s_flag) {
-      // combine: thread t = dim t of every head
-      __threadfence();
-      const float* pl = A.part + ((size_t)a + cf) * G * kPartStride;
+      // ---- partial of this lane segment: slot a + c
+      const int cf = cta_of(base, A.nc, A.T);
+      const int parts = cta_of(base + A.gpl - 1, A.nc, A.T) - cf + 1;
+      float* pc = A.part + ((size_t)a + c) * G * kPartStride;
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        float M = -INFINITY;
-        for (int j = 0; j < parts; ++j) M = fmaxf(M, __ldcg(pl + ((size_t)j * G + h) * kPartStride + 128));
-        float L = 0.f, O = 0.f;
-        for (int j = 0; j < parts; ++j) {
-          const float* pj = pl + ((size_t)j * G + h) * kPartStride;
-          const float mj = __ldcg(pj + 128);
-          const float wj = (M == -INFINITY || mj == -INFINITY) ? 0.f : exp2f(mj - M);
-          L = fmaf(__ldcg(pj + 129), wj, L);
-          O = fmaf(__ldcg(pj + t), wj, O);
-        }
-        A.out[((size_t)a * G + h) * kHeadDim + t] = L > 0.f ? O / L : 0.f;
+        float l = l_thr[h];
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+        if (lane == 0) qred[warp][h] = l;
+        pc[h * kPartStride + t] = o_acc[h];
       }
-      if (tid == 0) A.lane_done[a] = 0;
+      softmax_bar_or(false);
+      if (t < G) {
+        float mv = m_run[0];
+#pragma unroll
+        for (int h = 1; h < G; ++h) mv = t == h ? m_run[h] : mv;
+        pc[t * kPartStride + 128] = mv;
+        pc[t * kPartStride + 129] = qred[0][t] + qred[1][t] + qred[2][t] + qred[3][t];
+      }
+      __threadfence();
+      softmax_bar_or(false);
+      if (t == 0) s_flag = atomicAdd(&A.lane_done[a], 1u) == (uint32_t)(parts - 1);
+      softmax_bar_or(false);
+      if (s_flag) {
+        // combine: thread t = dim t of every head
+        __threadfence();
+        const float* pl = A.part + ((size_t)a + cf) * G * kPartStride;
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          float M = -INFINITY;
+          for (int jj = 0; jj < parts; ++jj) M = fmaxf(M, __ldcg(pl + ((size_t)jj * G + h) * kPartStride + 128));
+          float L = 0.f, O = 0.f;
+          for (int jj = 0; jj < parts; ++jj) {
+            const float* pj = pl + ((size_t)jj * G + h) * kPartStride;
+            const float mj = __ldcg(pj + 128);
+            const float wj = (M == -INFINITY || mj == -INFINITY) ? 0.f : exp2f(mj - M);
+            L = fmaf(__ldcg(pj + 129), wj, L);
+            O = fmaf(__ldcg(pj + t), wj, O);
+          }
+          A.out[((size_t)a * G + h) * kHeadDim + t] = L > 0.f ? O / L : 0.f;
+        }
+        if (t == 0) A.lane_done[a] = 0;
+      }
+      softmax_bar_or(false);  // qred / s_flag reusable
     }
-    __syncthreads();  // red / s_flag reusable
-  }
-  if (!ok && tid == 0) {
-    // let copies and MMAs still in flight land (bounded, results ignored)
-    while (it_use < it_load) {
-      mbar_wait(&full[it_use % kTcStages], (it_use / kTcStages) & 1u, nullptr);
-      ++it_use;
-    }
-    if (mma_pending_s) mbar_wait(&bar_s, ph_s, nullptr);
-    if (mma_pending_o) mbar_wait(&bar_o, ph_o, nullptr);
+    if (!ok && t == 0) atomicOr(&s_abort, 1u);
   }
   tc_fence_before();
   __syncthreads();
+  if (s_abort) {
+    // a wait gave up: let the copies and MMAs still in flight land (bounded)
+    if (warp == 4 && lane == 0)
+      for (uint32_t i = prod_j > (uint32_t)kTcStages ? prod_j - kTcStages : 0; i < prod_j; ++i)
+        mbar_wait(&full[i % kTcStages], (i / kTcStages) & 1u, nullptr);
+    if (warp == 5 && lane == 0 && mma_last) mbar_wait(mma_last, mma_par, nullptr);  // MMAs complete in order
+    __syncthreads();
+  }
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
 }

@@ -58,9 +58,17 @@ __device__ __forceinline__ float transpose_reduce(float (&w)[V]) {
   for (int j = 0; j < 5; ++j) {
     const int o = 16 >> j;
     const int n = V >> j;
-    if (n > 1) {
+    if (n > 2) {
 #pragma unroll
-      for (int i = 0; i < n / 2; ++i) w[i] = __fadd_rn(w[i], __shfl_xor_sync(0xffffffffu, w[i + n / 2], o));
+      for (int i = 0; i < n / 2; i += 2) {  // paired adds (same IEEE rounding per element)
+        const float2 r = make_float2(__shfl_xor_sync(0xffffffffu, w[i + n / 2], o),
+                                     __shfl_xor_sync(0xffffffffu, w[i + 1 + n / 2], o));
+        const float2 sum = __fadd2_rn(make_float2(w[i], w[i + 1]), r);
+        w[i] = sum.x;
+        w[i + 1] = sum.y;
+      }
+    } else if (n == 2) {
+      w[0] = __fadd_rn(w[0], __shfl_xor_sync(0xffffffffu, w[1], o));
     } else {
       w[0] = __fadd_rn(w[0], __shfl_xor_sync(0xffffffffu, w[0], o));
     }
@@ -68,12 +76,6 @@ __device__ __forceinline__ float transpose_reduce(float (&w)[V]) {
   return w[0];
 }
 
-__device__ __forceinline__ float lane_partial(const float (&q)[4], const float4 s) {
-  float v = __fmul_rn(q[0], s.x);
-  v = __fmaf_rn(q[1], s.y, v);
-  v = __fmaf_rn(q[2], s.z, v);
-  return __fmaf_rn(q[3], s.w, v);
-}
 
 __device__ __forceinline__ uint32_t lanemask_lt(int lane) { return (1u << lane) - 1u; }
 
@@ -176,11 +178,24 @@ __global__ void __launch_bounds__(kSelThreads, 2) select_kernel(SelArgs A) {
 #pragma unroll
         for (int r = 0; r < Sh::NR; ++r) {
           float v[Sh::V];
+          float4 sv[Sh::UR];
 #pragma unroll
-          for (int u = 0; u < Sh::UR; ++u) {
-            const float4 sv = *reinterpret_cast<const float4*>(rows + (r * Sh::UR + (u ^ pm)) * kRowBytes);
+          for (int u = 0; u < Sh::UR; ++u)
+            sv[u] = *reinterpret_cast<const float4*>(rows + (r * Sh::UR + (u ^ pm)) * kRowBytes);
+          // values x = 2i, 2i+1 in one paired FMA chain: heads g, g+1 of a
+          // page (G >= 2), or pages u, u+1 (G = 1)
 #pragma unroll
-            for (int g = 0; g < G; ++g) v[u * G + g] = lane_partial(qv[g], sv);
+          for (int i = 0; i < Sh::V / 2; ++i) {
+            const int x0 = 2 * i, x1 = 2 * i + 1;
+            const float4 sa = sv[x0 / G], sb = sv[x1 / G];
+            const float* qa = qv[x0 % G];
+            const float* qb = qv[x1 % G];
+            float2 acc = __fmul2_rn(make_float2(qa[0], qb[0]), make_float2(sa.x, sb.x));
+            acc = __ffma2_rn(make_float2(qa[1], qb[1]), make_float2(sa.y, sb.y), acc);
+            acc = __ffma2_rn(make_float2(qa[2], qb[2]), make_float2(sa.z, sb.z), acc);
+            acc = __ffma2_rn(make_float2(qa[3], qb[3]), make_float2(sa.w, sb.w), acc);
+            v[x0] = acc.x;
+            v[x1] = acc.y;
           }
           float best = transpose_reduce<Sh::V>(v);
           // lane holds value m: page m / G, head m % G

@@ -26,7 +26,8 @@ EXPORTS = [
     "ferry_kv_generate", "ferry_page_summary_update", "ferry_requests_begin",
     "ferry_select_topk", "ferry_detect_misses", "ferry_gather_misses", "ferry_sparse_decode",
     "ferry_sparse_decode_noalloc", "ferry_decode_step", "ferry_stats_read", "ferry_debug_read",
-    "ferry_ctx_export", "ferry_ctx_import", "ferry_ctx_link", "ferry_migrate_requests",
+    "ferry_ctx_export", "ferry_store_create", "ferry_store_fill", "ferry_gather_source",
+    "ferry_ctx_import", "ferry_ctx_link", "ferry_migrate_requests",
     "ferry_slot_states", "ferry_deque_create", "ferry_deque_destroy", "ferry_deque_push",
     "ferry_deque_pop", "ferry_deque_steal", "ferry_deque_size", "ferry_deque_export",
     "ferry_deque_import", "ferry_deque_peer_view", "ferry_deque_stress",
@@ -38,6 +39,8 @@ EXPORTS = [
 MAX_PEERS = 8
 CTX_HANDLE_BYTES = 1024
 MIGRATE_FULL, MIGRATE_DELTA = 0, 1
+SRC_HOST, SRC_OWNER = 0, 1
+NUM_STATS = 8
 
 
 class FerryError(RuntimeError):
@@ -90,6 +93,9 @@ _SIGS = {
     "ferry_stats_read": (I, [V, V, I]),
     "ferry_debug_read": (I, [V, I, C.c_size_t, C.c_size_t, V]),
     "ferry_ctx_export": (I, [V, V]),
+    "ferry_store_create": (I, [V, I, I, C.c_int64]),
+    "ferry_store_fill": (I, [V, V, C.c_uint64, C.c_uint64]),
+    "ferry_gather_source": (I, [V, I]),
     "ferry_ctx_import": (I, [V, I, V]),
     "ferry_ctx_link": (I, [V, I, V]),
     "ferry_migrate_requests": (I, [V, V, I, V, V, I, I]),

@@ -197,7 +197,7 @@ class RankRunner:
         e1.record(st)
         torch.cuda.synchronize(self.dev)
         self.dec.check()
-        g_units, g_bytes, m_units, m_bytes = self.dec.all_stats()
+        g_units, g_bytes, m_units, m_bytes = self.dec.all_stats()[:4]
         return ClusterStats(rank=self.rank, tokens=tokens, ticks=t, device_ms=e0.elapsed_time(e1),
                             steals=steals, stolen_tasks=stolen, migrated_units=m_units,
                             migrated_bytes=m_bytes, gathered_bytes=g_bytes, tick_ms=tick_ms,

@@ -170,6 +170,10 @@ struct ferry_peer {
   int32_t* ctx_pages = nullptr;
   int32_t* slot_state = nullptr;
   int64_t* req_base = nullptr;
+  // the peer's page-owner store (null when it has none)
+  uint8_t* store = nullptr;
+  int own_world = 0, own_rank = -1;
+  int64_t store_lanes = 0;
 };
 
 struct ferry_ctx {
@@ -206,10 +210,17 @@ struct ferry_ctx {
   uint32_t* grid_done = nullptr;  // 1
 
   uint32_t* err = nullptr;                // device error record
-  unsigned long long* stats = nullptr;    // [0,1] units/bytes gathered, [2,3] units/bytes migrated in
+  unsigned long long* stats = nullptr;    // FERRY_NUM_STATS counters (ferry_stats_read)
   int32_t* slot_state = nullptr;          // R: 2 = request migrated away by a peer
   ferry_peer peers[FERRY_MAX_PEERS];
   int num_sms = 148;
+
+  // page-owner store (store.cu): pages with page id % own_world == own_rank
+  int own_world = 0, own_rank = -1, own_np = 0;  // own_np = ceil(N / own_world)
+  int64_t store_lanes = 0;                        // global lanes covered
+  uint8_t* store = nullptr;
+  uint8_t* store_of[FERRY_MAX_PEERS + 1] = {};    // by owner rank (this GPU's own included)
+  int gather_src = FERRY_SRC_HOST;
 };
 
 namespace ferry {
@@ -232,6 +243,11 @@ int launch_lru_reset(const ferry_lru* L, cudaStream_t st, const int32_t* req_ids
 int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, int n_req,
                   const int32_t* miss_page, const int32_t* miss_slot, const int32_t* n_miss);
 void close_all_peers(ferry_ctx* c);
+// owner store of rank `rank` of `world` (kvgen.cu)
+int launch_store_fill(cudaStream_t st, uint64_t seed, int world, int rank, int N, int own_np, int64_t n_units,
+                      uint64_t pool_units, uint8_t* dst, int kv_dtype);
+// recompute store_of[] from the own store and the mapped peers (store.cu)
+void refresh_store_map(ferry_ctx* c);
 // partial slots the attention kernel needs for `lanes` lanes on `sms` SMs
 size_t attention_partial_slots(int64_t lanes, int sms);
 int launch_attention(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,

@@ -88,6 +88,7 @@ void destroy_ctx(ferry_ctx* c) {
   cudaFree(c->part);
   cudaFree(c->lane_done);
   cudaFree(c->sel_keys);
+  cudaFree(c->store);
   cudaFree(c->sel_done);
   cudaFree(c->err);
   cudaFree(c->stats);
@@ -150,7 +151,7 @@ int ferry_ctx_create(int device, const ferry_cfg* cfg, ferry_ctx** out) {
     return rc;             \
   }
   FERRY_CK(dev_alloc(&c->err, 1, 0));
-  FERRY_CK(dev_alloc(&c->stats, 4, 0));
+  FERRY_CK(dev_alloc(&c->stats, FERRY_NUM_STATS, 0));
   FERRY_CK(dev_alloc(&c->slot_state, (size_t)cfg->num_requests, 0));
   c->unit_bytes = cfg->kv_dtype == FERRY_KV_E4M3 ? kUnitBytesF8 : kUnitBytes;
   FERRY_CK(dev_alloc(&c->cache, (size_t)c->lanes * cfg->cache_pages * c->unit_bytes, 0));
@@ -345,8 +346,8 @@ int ferry_stats_read(ferry_ctx* c, uint64_t* stats, int reset) {
   if (!c || !stats) return set_error("bad arguments"), FERRY_E_INVAL;
   DeviceGuard guard(c->device);
   FERRY_TRY(cudaDeviceSynchronize());
-  FERRY_TRY(cudaMemcpy(stats, c->stats, 32, cudaMemcpyDeviceToHost));
-  if (reset) FERRY_TRY(cudaMemset(c->stats, 0, 32));
+  FERRY_TRY(cudaMemcpy(stats, c->stats, 8 * FERRY_NUM_STATS, cudaMemcpyDeviceToHost));
+  if (reset) FERRY_TRY(cudaMemset(c->stats, 0, 8 * FERRY_NUM_STATS));
   return FERRY_OK;
 }
 

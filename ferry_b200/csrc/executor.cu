@@ -385,7 +385,7 @@ int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out) {
   FERRY_TRY(cudaEventElapsedTime(&ms, x->ev0, x->ev1));
   if (ts.mig_ms < 0.f) {
     FERRY_TRY(cudaEventElapsedTime(&ts.mig_ms, x->ev2, x->ev3));
-    uint64_t st4[4];
+    uint64_t st4[FERRY_NUM_STATS];
     if ((rc = ferry_stats_read(x->ctx, st4, 0))) return rc;
     // the counter may have been zeroed by ferry_stats_read(reset) since the last steal
     ts.mig_bytes = (int64_t)(st4[3] >= x->mig_bytes_seen ? st4[3] - x->mig_bytes_seen : st4[3]);

@@ -14,16 +14,23 @@
 namespace ferry {
 namespace {
 
+// Owner stores by rank (FERRY_SRC_OWNER); world == 0 means host only.
+struct OwnerMap {
+  const uint8_t* store[FERRY_MAX_PEERS + 1];
+  int world, self, own_np;
+  int64_t store_lanes;
+};
+
 __global__ void __launch_bounds__(256) gather_kernel(
     const uint8_t* __restrict__ pool, uint64_t pool_units, uint8_t* __restrict__ cache, int N,
     int C, const int32_t* __restrict__ req_ids, int lanes_per_req, int64_t lanes_total,
     int n_lanes, const int32_t* __restrict__ miss_page, const int32_t* __restrict__ miss_slot,
     const int32_t* __restrict__ n_miss, int k, const int64_t* __restrict__ req_base, int unit_bytes,
-    unsigned long long* stats, uint32_t* err) {
+    const __grid_constant__ OwnerMap own, unsigned long long* stats, uint32_t* err) {
   const int t = threadIdx.x & 31;
   const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int64_t total = (int64_t)n_lanes * k;
-  uint32_t copied = 0;
+  uint32_t copied = 0, from_peer = 0, from_self = 0;
   for (int64_t f = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); f < total;
        f += nw) {
     const int a = (int)(f / k), i = (int)(f % k);
@@ -36,9 +43,22 @@ __global__ void __launch_bounds__(256) gather_kernel(
       if (t == 0) record_error(err, kErrRange);
       continue;
     }
-    const uint64_t unit =
-        (uint64_t)(req_base[req] + (int64_t)(a % lanes_per_req) * N + page) % pool_units;
-    const uint8_t* src = pool + unit * unit_bytes;
+    const int64_t home = req_base[req] + (int64_t)(a % lanes_per_req) * N;  // global lane * N
+    const uint8_t* src = nullptr;
+    if (own.world > 0) {
+      // the owner of page p is rank p % world; its store holds (lane, p) at
+      // lane * own_np + p / world
+      const int owner = page % own.world;
+      const int64_t glane = home / N;
+      if (glane >= 0 && glane < own.store_lanes && own.store[owner]) {
+        src = own.store[owner] + ((size_t)glane * own.own_np + page / own.world) * unit_bytes;
+        if (owner == own.self)
+          ++from_self;
+        else
+          ++from_peer;
+      }
+    }
+    if (!src) src = pool + ((uint64_t)(home + page) % pool_units) * unit_bytes;
     uint8_t* dst = cache + ((uint64_t)gl * C + slot) * unit_bytes;
     warp_copy_unit(src, dst, unit_bytes, t);
     ++copied;
@@ -46,6 +66,14 @@ __global__ void __launch_bounds__(256) gather_kernel(
   if (t == 0 && copied && stats) {
     atomicAdd(&stats[0], (unsigned long long)copied);
     atomicAdd(&stats[1], (unsigned long long)copied * unit_bytes);
+    if (from_peer) {
+      atomicAdd(&stats[4], (unsigned long long)from_peer);
+      atomicAdd(&stats[5], (unsigned long long)from_peer * unit_bytes);
+    }
+    if (from_self) {
+      atomicAdd(&stats[6], (unsigned long long)from_self);
+      atomicAdd(&stats[7], (unsigned long long)from_self * unit_bytes);
+    }
   }
 }
 
@@ -58,6 +86,14 @@ int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, i
     set_error("gather: no host pool registered");
     return FERRY_E_STATE;
   }
+  OwnerMap own{};
+  if (c->gather_src == FERRY_SRC_OWNER && c->store) {
+    own.world = c->own_world;
+    own.self = c->own_rank;
+    own.own_np = c->own_np;
+    own.store_lanes = c->store_lanes;
+    for (int r = 0; r <= FERRY_MAX_PEERS; ++r) own.store[r] = c->store_of[r];
+  }
   const int n_lanes = n_req * c->lanes_per_req;
   const int64_t items = (int64_t)n_lanes * c->cfg.top_k;
   // enough warps to keep the host link saturated, capped at 16 CTAs per SM
@@ -65,7 +101,7 @@ int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, i
   gather_kernel<<<(unsigned)blocks, 256, 0, st>>>(
       c->pool_dev, c->pool_units, c->cache, c->cfg.max_pages, c->cfg.cache_pages, req_ids,
       c->lanes_per_req, c->lanes, n_lanes, miss_page, miss_slot, n_miss, c->cfg.top_k, c->req_base,
-      c->unit_bytes, c->stats, c->err);
+      c->unit_bytes, own, c->stats, c->err);
   FERRY_TRY(cudaGetLastError());
   return FERRY_OK;
 }

@@ -4,7 +4,6 @@
 #include "common.cuh"
 
 namespace ferry {
-namespace {
 
 // Element e of page unit u: Irwin-Hall sum of twelve 16-bit uniforms drawn
 // from three splitmix64 outputs, z = (sum - 6*65536) / 65536 (variance 1,
@@ -21,22 +20,18 @@ __device__ __forceinline__ float kv_elem_f32(uint64_t seed, uint64_t unit, uint3
   return __fmul_rn((float)((int32_t)acc - 6 * 65536), 1.0f / 65536.0f);
 }
 
+namespace {
+
 // fp16 pool: z rounded once to fp16
 __device__ __forceinline__ uint16_t kv_elem(uint64_t seed, uint64_t unit, uint32_t e) {
   return __half_as_ushort(__float2half_rn(kv_elem_f32(seed, unit, e)));
 }
 
-// e4m3 pool: one warp per 4112-byte unit. For K (elements 0..2047) and V
+// e4m3 unit by one warp (lane t). For K (elements 0..2047) and V
 // (2048..4095): scale = amax / 448 of the unit's fp32 values (1 when all are
 // zero), q = e4m3(z / scale), round to nearest even with saturation to +-448
-// (cvt.rn.satfinite). Lane l owns 64 consecutive elements of each half.
-__global__ void __launch_bounds__(256) kv_generate_e4m3_kernel(uint64_t seed, uint64_t unit0,
-                                                               int64_t n_units, uint8_t* dst) {
-  const int t = threadIdx.x & 31;
-  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t u = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < n_units; u += nw) {
-    const uint64_t unit = unit0 + (uint64_t)u;
-    uint8_t* out = dst + (size_t)u * kUnitBytesF8;
+// (cvt.rn.satfinite). Lane t owns 64 consecutive elements of each half.
+__device__ __forceinline__ void gen_unit_e4m3(uint64_t seed, uint64_t unit, uint8_t* out, int t) {
     float scales[2];
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
@@ -67,7 +62,52 @@ __global__ void __launch_bounds__(256) kv_generate_e4m3_kernel(uint64_t seed, ui
     if (t == 0)
       *reinterpret_cast<uint4*>(out + 4096) =
           make_uint4(__float_as_uint(scales[0]), __float_as_uint(scales[1]), 0u, 0u);
+}
+
+// fp16 unit by one warp: lane t writes 16-byte vectors t, t + 32, ...
+__device__ __forceinline__ void gen_unit_f16(uint64_t seed, uint64_t unit, uint8_t* out, int t) {
+#pragma unroll 4
+  for (int v = t; v < kUnitElems / 8; v += 32) {
+    const uint32_t e0 = (uint32_t)v * 8;
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      w[j] = (uint32_t)__half_as_ushort(__float2half_rn(kv_elem_f32(seed, unit, e0 + 2 * j))) |
+             ((uint32_t)__half_as_ushort(__float2half_rn(kv_elem_f32(seed, unit, e0 + 2 * j + 1))) << 16);
+    reinterpret_cast<uint4*>(out)[v] = make_uint4(w[0], w[1], w[2], w[3]);
   }
+}
+
+// Owner store of rank `rank` of `world`: store index i holds page
+// p = (i % own_np) * world + rank of global lane i / own_np, i.e. procedural
+// unit (lane * N + p) mod pool_units; indices with p >= N stay zero.
+__global__ void __launch_bounds__(256) store_fill_kernel(uint64_t seed, int world, int rank, int N, int own_np,
+                                                         int64_t n_units, uint64_t pool_units, uint8_t* dst,
+                                                         int unit_bytes, int e4m3) {
+  const int t = threadIdx.x & 31;
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t i = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < n_units; i += nw) {
+    const int64_t lane = i / own_np;
+    const int p = (int)(i % own_np) * world + rank;
+    uint8_t* out = dst + (size_t)i * unit_bytes;
+    if (p >= N) {
+      for (int v = t; v < unit_bytes / 16; v += 32) reinterpret_cast<uint4*>(out)[v] = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    const uint64_t unit = ((uint64_t)lane * (uint64_t)N + (uint64_t)p) % pool_units;
+    if (e4m3)
+      gen_unit_e4m3(seed, unit, out, t);
+    else
+      gen_unit_f16(seed, unit, out, t);
+  }
+}
+
+__global__ void __launch_bounds__(256) kv_generate_e4m3_kernel(uint64_t seed, uint64_t unit0,
+                                                               int64_t n_units, uint8_t* dst) {
+  const int t = threadIdx.x & 31;
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t u = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < n_units; u += nw)
+    gen_unit_e4m3(seed, unit0 + (uint64_t)u, dst + (size_t)u * kUnitBytesF8, t);
 }
 
 // e4m3 summary: summary[d] = (k_0[d] + ... + k_15[d]) * (1/16) with
@@ -186,6 +226,17 @@ int launch_summary(cudaStream_t st, const uint8_t* pool, int64_t unit0, int64_t 
     summary_e4m3_kernel<<<(unsigned)blocks, 256, 0, st>>>(pool, unit0, n_units, summ);
   else
     summary_kernel<<<(unsigned)blocks, 256, 0, st>>>(pool, unit0, n_units, summ);
+  FERRY_TRY(cudaGetLastError());
+  return FERRY_OK;
+}
+
+int launch_store_fill(cudaStream_t st, uint64_t seed, int world, int rank, int N, int own_np, int64_t n_units,
+                      uint64_t pool_units, uint8_t* dst, int kv_dtype) {
+  if (n_units <= 0) return FERRY_OK;
+  const int ub = kv_dtype == FERRY_KV_E4M3 ? kUnitBytesF8 : kUnitBytes;
+  const int64_t blocks = std::min<int64_t>((n_units + 7) / 8, 148 * 16);
+  store_fill_kernel<<<(unsigned)blocks, 256, 0, st>>>(seed, world, rank, N, own_np, n_units, pool_units, dst, ub,
+                                                        kv_dtype == FERRY_KV_E4M3);
   FERRY_TRY(cudaGetLastError());
   return FERRY_OK;
 }

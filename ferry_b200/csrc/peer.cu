@@ -29,6 +29,10 @@ struct PeerHandle {  // what ferry_ctx_export writes (FERRY_CTX_HANDLE_BYTES)
   int32_t device;
   ferry_cfg cfg;
   cudaIpcMemHandle_t mem[kPeerBufs];
+  // page-owner store (has_store == 0: none)
+  int32_t has_store, own_world, own_rank, pad;
+  int64_t store_lanes;
+  cudaIpcMemHandle_t store_mem;
 };
 static_assert(sizeof(PeerHandle) <= FERRY_CTX_HANDLE_BYTES, "handle too large");
 constexpr uint32_t kPeerMagic = 0x46455259u;  // "FERY"
@@ -169,6 +173,7 @@ void close_peer(ferry_peer& p) {
                              p.size,  p.ctx_pages, p.slot_state, p.req_base};
     for (void* b : bufs)
       if (b) cudaIpcCloseMemHandle(b);
+    if (p.store) cudaIpcCloseMemHandle(p.store);
   }
   p = ferry_peer{};
 }
@@ -177,6 +182,7 @@ void close_peer(ferry_peer& p) {
 namespace ferry {
 void close_all_peers(ferry_ctx* c) {
   for (auto& p : c->peers) close_peer(p);
+  refresh_store_map(c);
 }
 }  // namespace ferry
 
@@ -192,6 +198,13 @@ int ferry_ctx_export(ferry_ctx* c, void* handle) {
   const void* bufs[kPeerBufs] = {c->cache,    c->lru.page_slot, c->lru.slot_page, c->lru.order,
                                  c->lru.size, c->ctx_pages,     c->slot_state,    c->req_base};
   for (int i = 0; i < kPeerBufs; ++i) FERRY_TRY(cudaIpcGetMemHandle(&h.mem[i], (void*)bufs[i]));
+  if (c->store) {
+    h.has_store = 1;
+    h.own_world = c->own_world;
+    h.own_rank = c->own_rank;
+    h.store_lanes = c->store_lanes;
+    FERRY_TRY(cudaIpcGetMemHandle(&h.store_mem, c->store));
+  }
   std::memset(handle, 0, FERRY_CTX_HANDLE_BYTES);
   std::memcpy(handle, &h, sizeof h);
   return FERRY_OK;
@@ -214,9 +227,21 @@ int ferry_ctx_import(ferry_ctx* c, int peer_slot, const void* handle) {
       return cuda_status(e, "cudaIpcOpenMemHandle");
     }
   }
+  void* st = nullptr;
+  if (h.has_store) {
+    cudaError_t e = cudaIpcOpenMemHandle(&st, h.store_mem, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int j = 0; j < kPeerBufs; ++j) cudaIpcCloseMemHandle(p[j]);
+      return cuda_status(e, "cudaIpcOpenMemHandle (store)");
+    }
+  }
   ferry_peer& q = c->peers[peer_slot];
   q.ipc = true;
   q.device = h.device;
+  q.store = (uint8_t*)st;
+  q.own_world = h.has_store ? h.own_world : 0;
+  q.own_rank = h.has_store ? h.own_rank : -1;
+  q.store_lanes = h.has_store ? h.store_lanes : 0;
   q.cache = (uint8_t*)p[0];
   q.page_slot = (int32_t*)p[1];
   q.slot_page = (int32_t*)p[2];
@@ -225,6 +250,7 @@ int ferry_ctx_import(ferry_ctx* c, int peer_slot, const void* handle) {
   q.ctx_pages = (int32_t*)p[5];
   q.slot_state = (int32_t*)p[6];
   q.req_base = (int64_t*)p[7];
+  refresh_store_map(c);
   return FERRY_OK;
 }
 
@@ -253,6 +279,11 @@ int ferry_ctx_link(ferry_ctx* c, int peer_slot, ferry_ctx* peer) {
   q.ctx_pages = peer->ctx_pages;
   q.slot_state = peer->slot_state;
   q.req_base = peer->req_base;
+  q.store = peer->store;
+  q.own_world = peer->own_world;
+  q.own_rank = peer->own_rank;
+  q.store_lanes = peer->store_lanes;
+  refresh_store_map(c);
   return FERRY_OK;
 }
 

@@ -134,11 +134,31 @@ class Decoder:
         """(page units gathered, gather bytes) since the last reset."""
         return self.all_stats(reset)[:2]
 
-    def all_stats(self, reset: bool = False) -> tuple[int, int, int, int]:
-        """(units gathered, gather bytes, units migrated in, migration bytes)."""
-        s = (C.c_uint64 * 4)()
+    def all_stats(self, reset: bool = False) -> tuple[int, ...]:
+        """(units gathered, gather bytes, units migrated in, migration bytes,
+        units / bytes gathered from peer owner stores, units / bytes gathered
+        from this GPU's own store)."""
+        s = (C.c_uint64 * _abi.NUM_STATS)()
         call("ferry_stats_read", self.ctx, s, int(reset))
-        return int(s[0]), int(s[1]), int(s[2]), int(s[3])
+        return tuple(int(v) for v in s)
+
+    # ------------------------------------------------------------------ page-owner stores
+    def store_create(self, world: int, rank: int, global_lanes: int | None = None):
+        """Keep the pages with page id % world == rank of global lanes
+        [0, global_lanes) in this GPU's HBM (default: this ctx's lanes)."""
+        gl = self.w.num_requests * self.w.lanes_per_req if global_lanes is None else global_lanes
+        call("ferry_store_create", self.ctx, world, rank, C.c_int64(gl))
+
+    def store_fill(self, seed: int | None = None, pool_units: int | None = None, stream=None):
+        """Procedural content of the owned units: the bytes of pool unit
+        (lane * N + p) mod pool_units (default: the registered pool's size)."""
+        if pool_units is None:
+            pool_units = self.pool.nbytes // self.w.unit_bytes if self.pool is not None else self.w.pool_units
+        call("ferry_store_fill", self.ctx, _stream(stream), C.c_uint64(self.w.seed if seed is None else seed),
+             C.c_uint64(pool_units))
+
+    def gather_source(self, source: int):
+        call("ferry_gather_source", self.ctx, source)
 
     def debug_read(self, which: int, dtype, count: int, offset_elems: int = 0) -> np.ndarray:
         out = np.empty(count, dtype)

@@ -68,7 +68,7 @@ def migrate_bench(w, iters: int) -> dict:
         dst.all_stats(reset=True)
         with torch.cuda.device(d0):
             t = _time(fn, iters)
-        units, _, mu, mb = dst.all_stats()
+        units, _, mu, mb = dst.all_stats()[:4]
         dst.check()
         per = mb / (iters + 3)
         return {"src_device": src_dev, "requests": R, "bytes_per_call": per, "us": t,

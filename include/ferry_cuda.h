@@ -189,9 +189,12 @@ int ferry_sparse_decode_noalloc(void* stream, const void* d_cache, int cache_pag
 int ferry_decode_step(ferry_ctx* ctx, void* stream, const uint16_t* d_q,
                       const int32_t* d_req_ids, int n_req, float* d_out);
 
-/* Read (and optionally zero) the ctx counters into stats[4]: [0] page units
- * gathered, [1] gather bytes, [2] page units migrated in, [3] migration bytes.
- * Synchronous. */
+/* Read (and optionally zero) the ctx counters into stats[FERRY_NUM_STATS]:
+ * [0] page units gathered (any source), [1] gather bytes, [2] page units
+ * migrated in, [3] migration bytes, [4] units gathered from peer GPUs' owner
+ * stores, [5] their bytes, [6] units gathered from this GPU's own store,
+ * [7] their bytes (host-pool units = [0] - [4] - [6]). Synchronous. */
+#define FERRY_NUM_STATS 8
 int ferry_stats_read(ferry_ctx* ctx, uint64_t* stats, int reset);
 
 /* Copy ctx device state to host for checking (synchronous).
@@ -218,6 +221,26 @@ int ferry_debug_read(ferry_ctx* ctx, int which, size_t offset, size_t bytes, voi
 #define FERRY_MIGRATE_FULL 0
 #define FERRY_MIGRATE_DELTA 1
 int ferry_ctx_export(ferry_ctx* ctx, void* handle /* FERRY_CTX_HANDLE_BYTES */);
+/* ---- page-owner stores
+ * Pages sharded by page id across the GPUs of a job: rank `rank` of `world`
+ * keeps in HBM every page unit (lane, p) with p % world == rank, for global
+ * lanes [0, global_lanes), at store index lane * ceil(N / world) + p / world.
+ * A lane's global id is req_base / N + its index in the request (the
+ * request's pool home; the default home of slot r is r * L * Hkv * N). The
+ * store holds the bytes of the procedural pool unit the host path would read,
+ * (lane * N + p) mod pool_units (ferry_kv_generate's content).
+ * ferry_gather_source selects where misses come from: FERRY_SRC_HOST (the
+ * registered pinned host pool) or FERRY_SRC_OWNER (the owning rank's store:
+ * this GPU's, or a peer's read over NVLink once mapped by ferry_ctx_link or
+ * ferry_ctx_import after the peer created its store; pages of unmapped owners
+ * or of lanes outside the store come from the host pool). Stores are created
+ * before ferry_ctx_export so that the handle carries them.
+ * No counterpart in the reference (it has no page ownership). */
+#define FERRY_SRC_HOST 0
+#define FERRY_SRC_OWNER 1
+int ferry_store_create(ferry_ctx* ctx, int world, int rank, int64_t global_lanes);
+int ferry_store_fill(ferry_ctx* ctx, void* stream, uint64_t seed, uint64_t pool_units);
+int ferry_gather_source(ferry_ctx* ctx, int source);
 int ferry_ctx_import(ferry_ctx* ctx, int peer_slot, const void* handle);
 int ferry_ctx_link(ferry_ctx* ctx, int peer_slot, ferry_ctx* peer);
 int ferry_migrate_requests(ferry_ctx* ctx, void* stream, int peer_slot, const int32_t* d_src_req,

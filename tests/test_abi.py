@@ -55,6 +55,9 @@ def test_null_arguments_rejected(cuda_lib):
     assert cuda_lib.ferry_ctx_check(None) == _abi.E_INVAL
     assert cuda_lib.ferry_ctx_destroy(None) == _abi.OK
     assert cuda_lib.ferry_kv_register(None, None, 0) == _abi.E_INVAL
+    assert cuda_lib.ferry_store_create(None, 2, 0, 16) == _abi.E_INVAL
+    assert cuda_lib.ferry_store_fill(None, None, 1, 16) == _abi.E_INVAL
+    assert cuda_lib.ferry_gather_source(None, _abi.SRC_OWNER) == _abi.E_INVAL
 
 
 def test_product_never_imports_oracle():

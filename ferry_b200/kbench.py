@@ -112,6 +112,8 @@ def main():
     ap.add_argument("--probe", action="store_true", help="topology and link peaks")
     ap.add_argument("--requests", type=int, default=0, help="override the batch (a smaller case to profile)")
     ap.add_argument("--only", default="", help="comma list of kernels to time (gather,attention,select,detect)")
+    ap.add_argument("--store-world", type=int, default=0,
+                    help="serve misses from page-owner stores of W ranks (rank r on GPU r mod count)")
     args = ap.parse_args()
     if args.probe:
         print(json.dumps({"probe": probe()}))
@@ -129,6 +131,24 @@ def main():
     dev = torch.device("cuda", args.device)
     dec = Decoder(w, args.device)
     dec.register_pool()
+    peers = []
+    if args.store_world:
+        from . import _abi
+
+        W = args.store_world
+        ndev = torch.cuda.device_count()
+        dec.store_create(W, 0)
+        dec.store_fill()
+        for r in range(1, W):
+            p = Decoder(w, (args.device + r) % ndev)
+            p.store_create(W, r)
+            p.store_fill(pool_units=w.pool_units)
+            peers.append(p)
+        for i, p in enumerate(peers):
+            _abi.call("ferry_ctx_link", dec.ctx, i, p.ctx)
+        for d in range(ndev):
+            torch.cuda.synchronize(d)
+        dec.gather_source(_abi.SRC_OWNER)
     R = w.num_requests
     ids = torch.arange(R, dtype=torch.int32, device=dev)
     dec.begin(ids, torch.full((R,), w.max_pages, dtype=torch.int32, device=dev))
@@ -149,9 +169,13 @@ def main():
     res = {"workload": w.name, "batch_requests": R, "kv_dtype": w.kv_dtype}
     # gather re-copies the same miss list each launch (idempotent)
     if "gather" in only:
+        dec.all_stats(reset=True)
         t = _time(lambda: dec.gather(ids), max(3, args.iters // 5))
         ub = w.unit_bytes
-        res["gather"] = {"us": t, "units": units, "bytes": units * ub, "GB_s": units * ub / t / 1e3}
+        st = dec.all_stats()
+        res["gather"] = {"us": t, "units": units, "bytes": units * ub, "GB_s": units * ub / t / 1e3,
+                         "source": ("owner stores, world %d" % args.store_world) if args.store_world else "host pool",
+                         "share_peer": st[4] / max(1, st[0]), "share_local_store": st[6] / max(1, st[0])}
     dec.gather(ids)
     if "attention" in only:
         t = _time(lambda: dec.attention(q, ids, out), args.iters)
@@ -166,6 +190,8 @@ def main():
         res["detect"] = {"us": t}
     dec.check()
     dec.close()
+    for p in peers:
+        p.close()
     print(json.dumps(res))
 
 

@@ -415,6 +415,8 @@ def main():
         ap.error("--warmup must be >= 3")
     from ferry_b200.workload import WORKLOADS
 
+    if args.workload == "cfg5s":
+        return run_owner(args)
     if args.workload == "skew":
         run_cluster(args)
         return
@@ -496,6 +498,116 @@ def run_cluster(args):
         print(json.dumps(line), flush=True)
     dist.barrier()
     dist.destroy_process_group()
+
+
+def run_owner(args):
+    """configs[4] slice on N ranks with page ownership: fp8 e4m3 KV with
+    per-page scales, 64 q / 8 kv heads, 131072-token contexts (8192 pages),
+    top-512, cache 15%, 2 of the 80 layers. The 32 requests are split evenly
+    over the ranks; page p of every lane lives in the HBM store of rank
+    p % N and misses are gathered from the owner (NVLink for a peer). A step
+    decodes one token of every request (steady decode). Strong scaling: the
+    job is the same at every N."""
+    import ctypes as C
+    import dataclasses
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from ferry_b200 import _abi
+    from ferry_b200.engine import Decoder
+    from ferry_b200.workload import CFG5S, q_stream
+
+    ws, rank, local = _dist()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    total = CFG5S.num_requests
+    if total % ws:
+        raise SystemExit(f"cfg5s: {total} requests do not split over {ws} ranks")
+    R = total // ws
+    w = dataclasses.replace(CFG5S, num_requests=R)
+    LH, N = w.lanes_per_req, w.max_pages
+    units = R * LH * N
+    dec = Decoder(w, local)
+    # this rank's requests in the pinned pool (summaries, and misses of pages
+    # whose owner is unreachable): global request g = rank * R + slot
+    dec.register_pool(units=units, unit0=rank * units)
+    dec.store_create(ws, rank, total * LH)
+    dec.store_fill(pool_units=total * LH * N)
+    torch.cuda.synchronize(dev)
+    if ws > 1:
+        h = (C.c_uint8 * _abi.CTX_HANDLE_BYTES)()
+        _abi.call("ferry_ctx_export", dec.ctx, h)
+        allh = [None] * ws
+        dist.all_gather_object(allh, bytes(h))
+        slot = 0
+        for p in range(ws):
+            if p != rank:
+                _abi.call("ferry_ctx_import", dec.ctx, slot,
+                          (C.c_uint8 * _abi.CTX_HANDLE_BYTES).from_buffer_copy(allh[p]))
+                slot += 1
+    dec.gather_source(_abi.SRC_OWNER)
+    g_ids = np.arange(rank * R, (rank + 1) * R)
+    ids = torch.arange(R, dtype=torch.int32, device=dev)
+    base = torch.from_numpy(g_ids.astype(np.int64) * LH * N).to(dev)
+    n_steps = args.warmup + args.steps
+    qs = torch.from_numpy(np.stack([q_stream(w, int(g), steps=n_steps) for g in g_ids], 1)).to(dev)
+    out = torch.empty((R, w.num_layers, w.q_heads, 128), dtype=torch.float32, device=dev)
+    st = torch.cuda.current_stream(dev)
+    dec.begin(ids, torch.full((R,), N, dtype=torch.int32, device=dev), pool_base=base)
+    for s in range(args.warmup):
+        dec.step(qs[s], ids, out)
+    dec.all_stats(reset=True)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    evs = []
+    with Clocks(local) as clocks:
+        e0.record(st)
+        for s in range(args.warmup, n_steps):
+            a = torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            dec.step(qs[s], ids, out)
+            evs.append(a)
+        e1.record(st)
+        torch.cuda.synchronize(dev)
+    dec.check()
+    ms = e0.elapsed_time(e1)
+    step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(len(evs) - 1)] + [evs[-1].elapsed_time(e1)]
+    stats = dec.all_stats()
+    t = torch.tensor([ms, float(np.percentile(step_ms, 99)), stats[1], stats[5], stats[7]],
+                     dtype=torch.float64, device=dev)
+    mx, sm = t.clone(), t.clone()
+    if ws > 1:
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+    if rank == 0:
+        ms = float(mx[0])
+        tokens = total * args.steps
+        gb, peer_b, self_b = float(sm[2]), float(sm[3]), float(sm[4])
+        line = {"metric": METRIC, "value": tokens / (ms / 1e3), "unit": UNIT, "n_gpus": ws,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+                "p99_step_ms": float(mx[1]), "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "e4m3-kv(per-page f32 scales)/fp32-acc",
+                "data": "synthetic (procedural KV, AR(1) queries, seeded)",
+                "config": {"workload": "configs[4] slice: 2 of 80 layers", "requests": total,
+                           "requests_per_gpu": R, "ctx_tokens": w.ctx_tokens, "heads": [w.q_heads, w.kv_heads],
+                           "top_k": w.top_k, "cache_pages": w.cache_pages, "kv_dtype": "e4m3",
+                           "page_owner": f"page id mod {ws}", "parallelism": f"{ws} ranks, owner-store gathers"},
+                "miss_gather": {"bytes_per_step": gb / args.steps,
+                                "share_from_peer_gpus": peer_b / gb if gb else 0.0,
+                                "share_from_own_hbm": self_b / gb if gb else 0.0,
+                                "share_from_host": 1.0 - (peer_b + self_b) / gb if gb else 0.0},
+                "clocks": clocks.summary()}
+        print(json.dumps(line), flush=True)
+    dec.close()
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -80,14 +80,15 @@ class Decoder:
         self.is_miss = torch.empty((n, k), dtype=torch.uint8, device=self.dev)
 
     # ------------------------------------------------------------------ setup
-    def register_pool(self, seed: int | None = None, units: int | None = None) -> PinnedPool:
-        """Allocate the pinned pool, fill it with the procedural KV and compute
-        every unit's page summary on the device."""
+    def register_pool(self, seed: int | None = None, units: int | None = None, unit0: int = 0) -> PinnedPool:
+        """Allocate the pinned pool, fill it with the procedural KV (content of
+        units unit0 .. unit0 + units - 1) and compute every unit's page summary
+        on the device."""
         w = self.w
         units = w.pool_units if units is None else units
         pool = PinnedPool(units * w.unit_bytes)
         s = _stream()
-        call("ferry_kv_generate", s, C.c_uint64(w.seed if seed is None else seed), C.c_uint64(0),
+        call("ferry_kv_generate", s, C.c_uint64(w.seed if seed is None else seed), C.c_uint64(unit0),
              C.c_int64(units), pool.ptr, self.kv_dtype)
         torch.cuda.synchronize(self.dev)
         call("ferry_kv_register", self.ctx, pool.ptr, C.c_size_t(pool.nbytes))

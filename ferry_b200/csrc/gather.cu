@@ -77,6 +77,124 @@ __global__ void __launch_bounds__(256) gather_kernel(
   }
 }
 
+// Owner-store gathers (FERRY_SRC_OWNER): units whose owner store is
+// mapped move by the TMA engine -- lane 0 of each warp streams them through
+// a 2-stage shared-memory ring with 1-D bulk copies (load from the owner's
+// store, this GPU's HBM or a peer's over NVLink; then a bulk store into the
+// cache slot), one unit's load in flight while the previous one is stored.
+// Units without a mapped owner fall back to the warp's register copy from
+// the host pool.
+constexpr int kGtWarps = 8;
+constexpr int kGtSmem = kGtWarps * 2 * kUnitBytes;
+
+__device__ __forceinline__ void bulk_store(void* dst_global, const void* src_smem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst_global),
+               "r"(smem_addr(src_smem)), "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// this thread's bulk stores have all finished reading shared memory
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__global__ void __launch_bounds__(kGtWarps * 32, 1) gather_store_kernel(
+    const uint8_t* __restrict__ pool, uint64_t pool_units, uint8_t* __restrict__ cache, int N,
+    int C, const int32_t* __restrict__ req_ids, int lanes_per_req, int64_t lanes_total,
+    int n_lanes, const int32_t* __restrict__ miss_page, const int32_t* __restrict__ miss_slot,
+    const int32_t* __restrict__ n_miss, int k, const int64_t* __restrict__ req_base, int unit_bytes,
+    const __grid_constant__ OwnerMap own, unsigned long long* stats, uint32_t* err) {
+  extern __shared__ __align__(128) uint8_t gsm[];
+  __shared__ __align__(8) uint64_t bars[kGtWarps][2];
+  const int t = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint8_t* ring = gsm + (size_t)warp * 2 * kUnitBytes;
+  if (t == 0) {
+    mbar_init(&bars[warp][0], 1);
+    mbar_init(&bars[warp][1], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  const int64_t nw = (int64_t)gridDim.x * kGtWarps;
+  const int64_t total = (int64_t)n_lanes * k;
+  uint32_t copied = 0, from_peer = 0, from_self = 0;
+  uint32_t it = 0;           // units this warp sent through the ring
+  int pend = -1;             // stage whose load is still to be stored
+  uint8_t* pend_dst = nullptr;
+  bool ok = true;
+  auto flush = [&]() {       // store the pending stage (lane 0)
+    if (pend < 0) return;
+    const uint32_t use = it - 1;  // the pending unit is the last one sent
+    if (mbar_wait(&bars[warp][pend], (use >> 1) & 1u, err))
+      bulk_store(pend_dst, ring + pend * kUnitBytes, (uint32_t)unit_bytes);
+    else
+      ok = false;
+    pend = -1;
+  };
+  for (int64_t f = (int64_t)blockIdx.x * kGtWarps + warp; f < total && ok; f += nw) {
+    const int a = (int)(f / k), i = (int)(f % k);
+    if (i >= n_miss[a]) continue;  // warp-uniform
+    const int page = miss_page[(size_t)a * k + i];
+    const int slot = miss_slot[(size_t)a * k + i];
+    const int req = req_ids[a / lanes_per_req];
+    const int64_t gl = (int64_t)req * lanes_per_req + a % lanes_per_req;
+    if (page < 0 || page >= N || slot < 0 || slot >= C || gl < 0 || gl >= lanes_total) {
+      if (t == 0) record_error(err, kErrRange);
+      continue;
+    }
+    const int64_t home = req_base[req] + (int64_t)(a % lanes_per_req) * N;  // global lane * N
+    const int owner = page % own.world;
+    const int64_t glane = home / N;
+    uint8_t* dst = cache + ((uint64_t)gl * C + slot) * unit_bytes;
+    ++copied;
+    if (glane >= 0 && glane < own.store_lanes && own.store[owner]) {
+      const uint8_t* src = own.store[owner] + ((size_t)glane * own.own_np + page / own.world) * unit_bytes;
+      if (owner == own.self)
+        ++from_self;
+      else
+        ++from_peer;
+      if (t == 0) {
+        const int s = it & 1;
+        bulk_wait_read();  // the store that last read stage s (the newest group) is done with it
+        mbar_arrive_expect_tx(&bars[warp][s], (uint32_t)unit_bytes);
+        bulk_load(ring + s * kUnitBytes, src, (uint32_t)unit_bytes, &bars[warp][s]);
+        ++it;
+        const int ps = pend;
+        uint8_t* pd = pend_dst;
+        if (ps >= 0) {  // store the previous unit while this one loads
+          if (mbar_wait(&bars[warp][ps], ((it - 2) >> 1) & 1u, err))
+            bulk_store(pd, ring + ps * kUnitBytes, (uint32_t)unit_bytes);
+          else
+            ok = false;
+        }
+        pend = s;
+        pend_dst = dst;
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+    } else {
+      warp_copy_unit(pool + ((uint64_t)(home + page) % pool_units) * unit_bytes, dst, unit_bytes, t);
+    }
+  }
+  if (t == 0) {
+    if (ok) flush();
+    // drain: loads still in flight land (bounded), stores complete
+    if (!ok)
+      for (uint32_t u = it >= 2 ? it - 2 : 0; u < it; ++u) mbar_wait(&bars[warp][u & 1], (u >> 1) & 1u, nullptr);
+    bulk_wait_all();
+  }
+  __syncwarp();
+  if (t == 0 && copied && stats) {
+    atomicAdd(&stats[0], (unsigned long long)copied);
+    atomicAdd(&stats[1], (unsigned long long)copied * unit_bytes);
+    if (from_peer) {
+      atomicAdd(&stats[4], (unsigned long long)from_peer);
+      atomicAdd(&stats[5], (unsigned long long)from_peer * unit_bytes);
+    }
+    if (from_self) {
+      atomicAdd(&stats[6], (unsigned long long)from_self);
+      atomicAdd(&stats[7], (unsigned long long)from_self * unit_bytes);
+    }
+  }
+}
+
 }  // namespace
 
 int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, int n_req,
@@ -96,6 +214,16 @@ int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, i
   }
   const int n_lanes = n_req * c->lanes_per_req;
   const int64_t items = (int64_t)n_lanes * c->cfg.top_k;
+  if (own.world > 0) {
+    FERRY_TRY(cudaFuncSetAttribute(gather_store_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGtSmem));
+    const int64_t blocks = std::min<int64_t>((items + kGtWarps - 1) / kGtWarps, (int64_t)c->num_sms);
+    gather_store_kernel<<<(unsigned)blocks, kGtWarps * 32, kGtSmem, st>>>(
+        c->pool_dev, c->pool_units, c->cache, c->cfg.max_pages, c->cfg.cache_pages, req_ids,
+        c->lanes_per_req, c->lanes, n_lanes, miss_page, miss_slot, n_miss, c->cfg.top_k, c->req_base,
+        c->unit_bytes, own, c->stats, c->err);
+    FERRY_TRY(cudaGetLastError());
+    return FERRY_OK;
+  }
   // enough warps to keep the host link saturated, capped at 16 CTAs per SM
   const int64_t blocks = std::min<int64_t>((items + 7) / 8, (int64_t)c->num_sms * 16);
   gather_kernel<<<(unsigned)blocks, 256, 0, st>>>(

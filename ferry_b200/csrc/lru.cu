@@ -137,9 +137,82 @@ __global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
     __syncwarp();
   }
 
-  // ---- sequential replay on shared memory (lane 0)
   int p = 0, qn = 0, nn = 0, sz = sz0, ne = 0;
-  if (t == 0) {
+  bool done = false;
+  // ---- distinct selections, warp-parallel: a hit keeps its slot, the r-th
+  // miss takes slot sz0 + r while free slots last, else the slot of old-order
+  // entry r - free. This is the sequential result whenever no page touched in
+  // this step is evicted within it, i.e. none of the first E entries of the
+  // old order (E = evictions) is touched; otherwise the serial replay runs.
+  if (A.distinct) {
+    int nv = 0, nmiss = 0;
+    for (int i0 = 0; i0 < n; i0 += 32) {
+      const int i = i0 + t;
+      const int x = i < n ? sel_s[i] : -1;
+      const int s = x >= 0 ? islot[i] : -1;
+      const bool valid = x >= 0, hit = valid && s >= 0 && s < C && spg[s] == x, miss = valid && !hit;
+      const uint32_t mv = __ballot_sync(0xffffffffu, valid), mm = __ballot_sync(0xffffffffu, miss);
+      if (i < n) {
+        if (!valid) {
+          islot[i] = -1;
+          mflag[i] = 0;
+        } else if (hit) {
+          seq[s] = nv + __popc(mv & lt);  // touched this step
+          mflag[i] = 0;
+        } else {
+          prev[i] = nmiss + __popc(mm & lt);  // rank among the misses
+          mflag[i] = 1;
+        }
+      }
+      nv += __popc(mv);
+      nmiss += __popc(mm);
+    }
+    __syncwarp();
+    const int f = max(0, C - sz0), E = max(0, nmiss - f);
+    bool clash = E > sz0;
+    for (int j = t; j < E && j < sz0; j += 32) clash |= seq[old[j]] != -1;
+    clash = __any_sync(0xffffffffu, clash);
+    if (!clash) {
+      for (int i = t; i < n; i += 32)
+        if (mflag[i]) {
+          const int r = prev[i];
+          int sl;
+          if (r < f) {
+            sl = sz0 + r;
+          } else {
+            sl = old[r - f];
+            evict[r - f] = spg[sl];
+          }
+          islot[i] = sl;
+        }
+      __syncwarp();
+      int nv2 = 0;
+      for (int i0 = 0; i0 < n; i0 += 32) {  // touch list in selection order
+        const int i = i0 + t;
+        const bool valid = i < n && sel_s[i] >= 0;
+        const uint32_t mv = __ballot_sync(0xffffffffu, valid);
+        if (valid) {
+          const int tr = nv2 + __popc(mv & lt), sl = islot[i];
+          newl[tr] = sl;
+          seq[sl] = tr;
+          if (mflag[i]) spg[sl] = sel_s[i];
+        }
+        nv2 += __popc(mv);
+      }
+      p = E;
+      nn = nv;
+      sz = sz0 + min(nmiss, f);
+      ne = E;
+      done = true;
+    } else {
+      for (int i = t; i < n; i += 32)  // undo the hit marks for the serial replay
+        if (sel_s[i] >= 0 && !mflag[i]) seq[islot[i]] = -1;
+    }
+    __syncwarp();
+  }
+
+  // ---- sequential replay on shared memory (lane 0)
+  if (t == 0 && !done) {
     for (int i = 0; i < n; ++i) {
       const int x = sel_s[i];
       if (x < 0) {

@@ -334,6 +334,49 @@ def test_lru_kernel_over_capacity_and_resets(torch_cuda):
         _abi.call("ferry_lru_destroy", h)
 
 
+@pytest.mark.parametrize("cap,k,ids,reuse", [
+    (48, 16, 200, 0.7),   # evictions reach only untouched pages: warp-parallel path
+    (16, 16, 60, 0.5),    # cache = k: touched pages at the LRU front, serial replay
+    (24, 16, 40, 0.9),    # mixed: some steps each way
+])
+def test_lru_distinct_selections_both_paths(torch_cuda, cap, k, ids, reuse):
+    """Distinct ascending selections (the decode step's case) against the
+    sequential oracle, step after step, with partial selections and resets."""
+    import oracle
+    from ferry_b200 import _abi
+
+    rng = np.random.default_rng(cap * 1000 + k)
+    lanes_n = 24
+    h = C.c_void_p()
+    _abi.call("ferry_lru_create", 0, lanes_n, cap, ids, C.byref(h))
+    mirror = oracle.LruLanes(lanes_n, cap, ids)
+    prev = [rng.choice(ids, k, replace=False) for _ in range(lanes_n)]
+    try:
+        for s in range(20):
+            lanes = rng.permutation(lanes_n)[:17].astype(np.int32)
+            sel = np.full((17, k), -1, np.int32)
+            for a, ln in enumerate(lanes):
+                keep = prev[ln][rng.random(k) < reuse]
+                fresh = rng.choice(np.setdiff1d(np.arange(ids), keep), k - len(keep), replace=False)
+                pages = np.sort(np.concatenate([keep, fresh]))
+                prev[ln] = pages
+                sel[a] = pages
+            n_sel = np.where(rng.random(17) < 0.8, k, rng.integers(0, k + 1, 17)).astype(np.int32)
+            reset = (rng.random(17) < 0.05).astype(np.uint8)
+            im, isl, mp, ms, nm = _lru_touch(torch_cuda, h, lanes, sel, n_sel, reset, distinct=True)
+            rim, risl, rmp, rms, rnm = mirror.step(lanes, sel, n_sel=n_sel, reset=reset)
+            for a in range(17):
+                n = n_sel[a]
+                assert nm[a] == rnm[a]
+                assert (im[a, :n] == rim[a, :n]).all() and (isl[a, :n] == risl[a, :n]).all()
+                assert (mp[a, : nm[a]] == rmp[a, : nm[a]]).all() and (ms[a, : nm[a]] == rms[a, : nm[a]]).all()
+        for lane in range(lanes_n):
+            g, r = _lru_state(h, lane, ids, cap), mirror.state(lane)
+            assert (g[0] == r[0]).all() and (g[1] == r[1]).all() and g[2] == r[2]
+    finally:
+        _abi.call("ferry_lru_destroy", h)
+
+
 def test_out_of_range_ids_are_reported_not_faulted(torch_cuda):
     from ferry_b200 import _abi
 

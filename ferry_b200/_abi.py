@@ -29,10 +29,11 @@ EXPORTS = [
     "ferry_ctx_export", "ferry_store_create", "ferry_store_fill", "ferry_gather_source",
     "ferry_ctx_import", "ferry_ctx_link", "ferry_migrate_requests",
     "ferry_slot_states", "ferry_deque_create", "ferry_deque_destroy", "ferry_deque_push",
-    "ferry_deque_pop", "ferry_deque_steal", "ferry_deque_size", "ferry_deque_export",
+    "ferry_deque_pop", "ferry_deque_steal", "ferry_deque_size", "ferry_deque_peek", "ferry_deque_export",
     "ferry_deque_import", "ferry_deque_peer_view", "ferry_deque_stress",
     "ferry_exec_create", "ferry_exec_destroy", "ferry_exec_link_peer", "ferry_exec_admit",
-    "ferry_exec_set_global", "ferry_exec_owned", "ferry_exec_tick",
+    "ferry_exec_set_global", "ferry_exec_owned", "ferry_exec_tick", "ferry_exec_policy",
+    "ferry_steal_filter",
     "ferry_trace_load", "ferry_probe_topology", "ferry_probe_link",
     "ferry_lru_create", "ferry_lru_destroy", "ferry_lru_touch", "ferry_lru_read",
 ]
@@ -60,6 +61,13 @@ class ExecCfg(C.Structure):
     _fields_ = [("rank", C.c_int), ("world", C.c_int), ("max_batch", C.c_int),
                 ("steal_batch", C.c_int), ("migrate_mode", C.c_int), ("steps_per_req", C.c_int),
                 ("total_requests", C.c_int)]
+
+
+class StealPolicy(C.Structure):
+    """ferry_steal_policy: cost_filter 0 = water-level steal (policy C),
+    1 = plus the value/cost filter (policy E)."""
+    _fields_ = [("cost_filter", C.c_int), ("margin", C.c_double), ("cost_scale", C.c_double),
+                ("link_gbs", C.c_double), ("fixed_ms", C.c_double)]
 
 
 class TickStats(C.Structure):
@@ -106,6 +114,7 @@ _SIGS = {
     "ferry_deque_pop": (I, [V, V, V, I, V]),
     "ferry_deque_steal": (I, [V, V, V, I, V]),
     "ferry_deque_size": (I, [V, V, V]),
+    "ferry_deque_peek": (I, [V, V, V, I, V]),
     "ferry_deque_export": (I, [V, V]),
     "ferry_deque_import": (I, [I, V, C.c_uint64, C.POINTER(V)]),
     "ferry_deque_peer_view": (I, [I, V, C.POINTER(V)]),
@@ -117,6 +126,8 @@ _SIGS = {
     "ferry_exec_set_global": (I, [V, C.c_int64]),
     "ferry_exec_owned": (I, [V, V, I, C.POINTER(I)]),
     "ferry_exec_tick": (I, [V, V, C.POINTER(TickStats)]),
+    "ferry_exec_policy": (I, [V, C.POINTER(StealPolicy)]),
+    "ferry_steal_filter": (I, [C.POINTER(StealPolicy), I, V, V, C.c_double, V, V, C.POINTER(I)]),
     "ferry_trace_load": (I, [C.c_char_p, I, I, I, I, I, I, V, C.c_int64, V, V]),
     "ferry_probe_topology": (I, [C.POINTER(I), V, V, I]),
     "ferry_probe_link": (I, [I, I, C.c_size_t, I, C.POINTER(C.c_double)]),

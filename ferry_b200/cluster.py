@@ -107,7 +107,8 @@ class RankRunner:
 
     def __init__(self, w: Workload, total_requests: int, world: int, rank: int, device: int,
                  slots: int, max_batch: int, steal_batch: int = 4,
-                 migrate_mode: int = _abi.MIGRATE_DELTA, pool_units: int | None = None):
+                 migrate_mode: int = _abi.MIGRATE_DELTA, pool_units: int | None = None,
+                 policy: "_abi.StealPolicy | None" = None):
         import torch
         import torch.distributed as dist
 
@@ -129,6 +130,8 @@ class RankRunner:
         self.exec = C.c_void_p()
         call("ferry_exec_create", self.dec.ctx, self.deque, C.byref(cfg),
              C.c_void_p(self.q_table.data_ptr()), C.byref(self.exec))
+        if policy is not None:
+            call("ferry_exec_policy", self.exec, C.byref(policy))
         self.slots = slots
         self.peer_deques = []
         if world > 1:

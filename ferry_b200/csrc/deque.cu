@@ -130,6 +130,20 @@ __global__ void steal_kernel(DequeHdr* h, unsigned long long* ring, uint64_t* ou
   }
 }
 
+// snapshot of up to max_n tasks at the top (what the next steals would take),
+// without taking them; concurrent pops and steals may change them afterwards
+__global__ void peek_kernel(DequeHdr* h, unsigned long long* ring, uint64_t* out, int max_n, int32_t* count) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    const unsigned long long t = ld_acquire_sys(&h->top);
+    const unsigned long long b = ld_acquire_sys(&h->bottom);
+    long long n = (long long)(b - t);
+    n = n < 0 ? 0 : (n > max_n ? max_n : n);
+    const unsigned long long cap = h->cap;
+    for (long long i = 0; i < n; ++i) out[i] = ld_relaxed_sys(&ring[(t + (unsigned long long)i) % cap]);
+    *count = (int32_t)n;
+  }
+}
+
 __global__ void size_kernel(const DequeHdr* h, int64_t* out) {
   if (threadIdx.x == 0 && blockIdx.x == 0) {
     const unsigned long long t = ld_acquire_sys(&h->top);
@@ -279,6 +293,13 @@ int ferry_deque_pop(ferry_deque* q, void* stream, uint64_t* d_out, int max_n, in
 int ferry_deque_steal(ferry_deque* q, void* stream, uint64_t* d_out, int max_n, int32_t* d_count) {
   if (!q || max_n < 0 || !d_out || !d_count) return set_error("deque_steal: bad arguments"), FERRY_E_INVAL;
   steal_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(q->hdr, q->ring, d_out, max_n, d_count);
+  FERRY_TRY(cudaGetLastError());
+  return FERRY_OK;
+}
+
+int ferry_deque_peek(ferry_deque* q, void* stream, uint64_t* d_out, int max_n, int32_t* d_count) {
+  if (!q || max_n < 0 || !d_out || !d_count) return set_error("deque_peek: bad arguments"), FERRY_E_INVAL;
+  peek_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(q->hdr, q->ring, d_out, max_n, d_count);
   FERRY_TRY(cudaGetLastError());
   return FERRY_OK;
 }

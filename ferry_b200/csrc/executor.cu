@@ -96,6 +96,10 @@ struct ferry_exec {
   std::vector<int32_t> slot_state;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr, ev3 = nullptr;
   uint64_t mig_bytes_seen = 0;
+  // steal policy (ferry_exec_policy)
+  ferry_steal_policy pol{0, 2.0, 3.0, 700.0, 0.06};
+  double step_ms_ema = 2.0;
+  int32_t* h_live = nullptr;  // steal_batch * lanes_per_req resident-page counts of candidates
 };
 
 using namespace ferry;
@@ -119,7 +123,7 @@ void free_exec(ferry_exec* x) {
   cudaFree(x->d_base); cudaFree(x->d_q); cudaFree(x->d_out);
   cudaFreeHost(x->h_tasks); cudaFreeHost(x->h_push); cudaFreeHost(x->h_admit);
   cudaFreeHost(x->h_cnt); cudaFreeHost(x->h_sizes); cudaFreeHost(x->h_ids); cudaFreeHost(x->h_mig);
-  cudaFreeHost(x->h_begin); cudaFreeHost(x->h_base);
+  cudaFreeHost(x->h_begin); cudaFreeHost(x->h_base); cudaFreeHost(x->h_live);
   for (cudaEvent_t e : {x->ev0, x->ev1, x->ev2, x->ev3})
     if (e) cudaEventDestroy(e);
   delete x;
@@ -219,6 +223,7 @@ int ferry_exec_create(ferry_ctx* ctx, ferry_deque* own, const ferry_exec_cfg* cf
   FX(cudaMallocHost(&x->h_mig, 2 * S * 4));
   FX(cudaMallocHost(&x->h_begin, (size_t)R * 2 * 4));
   FX(cudaMallocHost(&x->h_base, (size_t)R * 8));
+  FX(cudaMallocHost(&x->h_live, (size_t)S * ctx->lanes_per_req * 4));
   FX(cudaEventCreate(&x->ev0));
   FX(cudaEventCreate(&x->ev1));
   FX(cudaEventCreate(&x->ev2));
@@ -323,6 +328,36 @@ int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out) {
         int64_t take = std::min<int64_t>(x->cfg.steal_batch, std::min<int64_t>(cur - fair, cur / 2 + 1));
         take = std::min<int64_t>(take, B - n);
         take = std::min<int64_t>(take, (int64_t)x->free_slots.size());
+        const ferry_peer& vp = x->ctx->peers[x->peer_slot[victim]];
+        if (take > 0 && x->pol.cost_filter && vp.size) {
+          // price the tasks the steal would take: remaining steps x step time
+          // against moving their resident pages (policy E)
+          if ((rc = ferry_deque_peek(x->peer_deque[victim], st, x->d_tasks + n, (int)take, x->d_cnt + 3))) return rc;
+          FERRY_TRY(cudaMemcpyAsync(x->h_cnt, x->d_cnt, 16, cudaMemcpyDeviceToHost, st));
+          FERRY_TRY(cudaMemcpyAsync(x->h_tasks + n, x->d_tasks + n, (size_t)take * 8, cudaMemcpyDeviceToHost, st));
+          FERRY_TRY(cudaStreamSynchronize(st));
+          const int seen = std::min<int>(x->h_cnt[3], (int)take);
+          const int LH = x->ctx->lanes_per_req;
+          for (int i = 0; i < seen; ++i) {
+            const int vs = task_slot(x->h_tasks[n + i]);
+            if (vs < 0 || vs >= x->ctx->cfg.num_requests) return set_error("exec: peeked task slot out of range"), FERRY_E_RANGE;
+            FERRY_TRY(cudaMemcpyAsync(x->h_live + (size_t)i * LH, vp.size + (size_t)vs * LH, (size_t)LH * 4,
+                                      cudaMemcpyDeviceToHost, st));
+          }
+          FERRY_TRY(cudaStreamSynchronize(st));
+          int32_t remain[64];
+          int64_t live[64];
+          const int m = std::min(seen, 64);
+          for (int i = 0; i < m; ++i) {
+            remain[i] = x->cfg.steps_per_req - (int)task_step(x->h_tasks[n + i]);
+            int64_t units = 0;
+            for (int l = 0; l < LH; ++l) units += std::max(0, x->h_live[(size_t)i * LH + l]);
+            live[i] = units * x->ctx->unit_bytes;
+          }
+          int acc = 0;
+          if ((rc = ferry_steal_filter(&x->pol, m, remain, live, x->step_ms_ema, nullptr, nullptr, &acc))) return rc;
+          take = std::min<int64_t>(take, acc);
+        }
         if (take > 0) {
           if ((rc = ferry_deque_steal(x->peer_deque[victim], st, x->d_tasks + n, (int)take, x->d_cnt + 1))) return rc;
           FERRY_TRY(cudaMemcpyAsync(x->h_cnt, x->d_cnt, 16, cudaMemcpyDeviceToHost, st));
@@ -392,10 +427,40 @@ int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out) {
     x->mig_bytes_seen = st4[3];
   }
   x->finished += ts.finished;
+  if (n > 0) x->step_ms_ema = 0.9 * x->step_ms_ema + 0.1 * ms;  // one step of every decoded request
   ts.decoded = n;
   ts.tick_ms = ms;
   ts.queued = np;
   *out = ts;
+  return FERRY_OK;
+}
+
+int ferry_steal_filter(const ferry_steal_policy* pol, int n, const int32_t* remain_steps,
+                       const int64_t* live_bytes, double step_ms, double* value_ms, double* cost_ms,
+                       int* n_accept) {
+  if (!pol || !n_accept || n < 0 || (n && (!remain_steps || !live_bytes)) || !(pol->link_gbs > 0.0))
+    return set_error("steal_filter: bad arguments"), FERRY_E_INVAL;
+  const double ms_per_byte = 1e3 / (pol->link_gbs * 1e9);
+  int ok = 0;
+  bool open = true;
+  for (int i = 0; i < n; ++i) {
+    const double v = (double)remain_steps[i] * step_ms;
+    const double c = pol->cost_scale * (double)live_bytes[i] * ms_per_byte + pol->fixed_ms;
+    if (value_ms) value_ms[i] = v;
+    if (cost_ms) cost_ms[i] = c;
+    if (open && (!pol->cost_filter || v >= pol->margin * c))
+      ++ok;
+    else
+      open = false;  // the accepted candidates are a prefix
+  }
+  *n_accept = ok;
+  return FERRY_OK;
+}
+
+int ferry_exec_policy(ferry_exec* x, const ferry_steal_policy* pol) {
+  if (!x || !pol || !(pol->link_gbs > 0.0) || pol->margin < 0.0 || pol->cost_scale < 0.0 || pol->fixed_ms < 0.0)
+    return set_error("exec_policy: bad arguments"), FERRY_E_INVAL;
+  x->pol = *pol;
   return FERRY_OK;
 }
 

@@ -265,6 +265,10 @@ int ferry_deque_push(ferry_deque* q, void* stream, const uint64_t* d_tasks, int 
 int ferry_deque_pop(ferry_deque* q, void* stream, uint64_t* d_out, int max_n, int32_t* d_count);
 int ferry_deque_steal(ferry_deque* q, void* stream, uint64_t* d_out, int max_n, int32_t* d_count);
 int ferry_deque_size(ferry_deque* q, void* stream, int64_t* d_size);
+/* Copy up to max_n tasks at the top -- the ones the next steals would take --
+ * without taking them (a snapshot: concurrent pops and steals may change
+ * them). Owner or peer view. Used by the steal policy to price candidates. */
+int ferry_deque_peek(ferry_deque* q, void* stream, uint64_t* d_out, int max_n, int32_t* d_count);
 /* IPC export (64-byte handle) / import of an owner's deque, and a
  * same-process view from another device (enables peer access). */
 int ferry_deque_export(ferry_deque* q, void* handle64);
@@ -325,6 +329,30 @@ int ferry_exec_set_global(ferry_exec* x, int64_t global_pending);
 /* Global ids of the requests this GPU holds (the ownership table row). */
 int ferry_exec_owned(ferry_exec* x, int32_t* h_out, int cap, int* n);
 int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out);
+
+/* Steal policy. cost_filter = 0 is the water-level steal alone (the
+ * reference's policy C, wla_multigpu.cuh:1063-1506). cost_filter = 1 adds
+ * its value filter (policy E, cost_filter_ok, wla_multigpu.cuh:942-1061):
+ * candidates are the victim's next tasks (ferry_deque_peek), and the thief
+ * takes the longest prefix with
+ *     remaining_steps * step_ms >= margin * (cost_scale * live_bytes / link + fixed_ms)
+ * where live_bytes are the request's resident cache pages (delta migration),
+ * step_ms an EMA of this GPU's tick time (0.9 / 0.1, from 2 ms) and link the
+ * migration bandwidth in GB/s -- the measured NVLink peer copy instead of the
+ * reference's PCIe constant (kMigBWRefGbs = 16.6, :146). */
+typedef struct ferry_steal_policy {
+  int cost_filter;
+  double margin;      /* reference default 2.0 */
+  double cost_scale;  /* kappa, reference default 3.0 */
+  double link_gbs;    /* migration bandwidth */
+  double fixed_ms;    /* per-migration fixed cost (reference kMigDeltaFixedMs 0.06) */
+} ferry_steal_policy;
+int ferry_exec_policy(ferry_exec* x, const ferry_steal_policy* policy);
+/* The filter alone (host, no GPU): value_ms / cost_ms per candidate
+ * (nullable) and the length of the accepted prefix. */
+int ferry_steal_filter(const ferry_steal_policy* policy, int n, const int32_t* remain_steps,
+                       const int64_t* live_bytes, double step_ms, double* value_ms, double* cost_ms,
+                       int* n_accept);
 
 /* ---- real selection traces (FMT1) ----------------------------------------
  * Replaces load_miss_trace (src/workloads/miss_trace.cuh:75-185): reads the

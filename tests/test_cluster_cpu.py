@@ -62,3 +62,64 @@ def test_exchange_ownership_two_gloo_ranks():
         p.join(timeout=60)
     for rank, owner, fin, adm in res:
         assert owner == [0, 1, 0, 1, -1, -1] and fin == 3 and adm == 30
+
+
+# --------------------------------------------------------------------------- steal policy E
+
+
+def _filter(pol, remain, live, step_ms):
+    import ctypes as C
+
+    from ferry_b200 import _abi
+
+    n = len(remain)
+    r = np.ascontiguousarray(remain, np.int32)
+    lb = np.ascontiguousarray(live, np.int64)
+    v = np.zeros(n, np.float64)
+    c = np.zeros(n, np.float64)
+    acc = C.c_int()
+    _abi.call("ferry_steal_filter", C.byref(pol), n, r.ctypes.data_as(C.c_void_p),
+              lb.ctypes.data_as(C.c_void_p), C.c_double(step_ms), v.ctypes.data_as(C.c_void_p),
+              c.ctypes.data_as(C.c_void_p), C.byref(acc))
+    return acc.value, v, c
+
+
+def test_steal_filter_prices_candidates_like_policy_e():
+    """value = remaining steps x step time; cost = kappa x live bytes / link
+    + fixed; the accepted candidates are the longest prefix with value >=
+    margin x cost (cost_filter_ok, wla_multigpu.cuh:942-1061)."""
+    from ferry_b200 import _abi
+
+    pol = _abi.StealPolicy(cost_filter=1, margin=2.0, cost_scale=3.0, link_gbs=16.6, fixed_ms=0.06)
+    remain = [40, 5, 2, 30]
+    live = [24 << 20, 24 << 20, 24 << 20, 1 << 20]
+    acc, v, c = _filter(pol, remain, live, 1.5)
+    ms_per_b = 1e3 / (16.6e9)
+    exp_c = [3.0 * b * ms_per_b + 0.06 for b in live]
+    exp_v = [r * 1.5 for r in remain]
+    np.testing.assert_allclose(c, exp_c, rtol=1e-12)
+    np.testing.assert_allclose(v, exp_v, rtol=1e-12)
+    ok = [vv >= 2.0 * cc for vv, cc in zip(exp_v, exp_c)]
+    assert ok == [True, False, False, True]
+    assert acc == 1  # the prefix stops at the first rejection
+    # the NVLink link prices the same candidates as cheap
+    pol.link_gbs = 700.0
+    assert _filter(pol, remain, live, 1.5)[0] == 4
+    # margin 0 takes everything; without the filter every candidate passes
+    pol.link_gbs, pol.margin = 16.6, 0.0
+    assert _filter(pol, remain, live, 1.5)[0] == 4
+    pol.margin, pol.cost_filter = 2.0, 0
+    assert _filter(pol, remain, live, 1.5)[0] == 4
+
+
+def test_steal_filter_rejects_bad_policy():
+    import ctypes as C
+
+    from ferry_b200 import _abi
+
+    pol = _abi.StealPolicy(cost_filter=1, margin=2.0, cost_scale=3.0, link_gbs=0.0, fixed_ms=0.06)
+    acc = C.c_int()
+    lib = _abi.lib()
+    assert lib.ferry_steal_filter(C.byref(pol), 0, None, None, C.c_double(1.0), None, None,
+                                  C.byref(acc)) == _abi.E_INVAL
+    assert lib.ferry_exec_policy(None, C.byref(pol)) == _abi.E_INVAL

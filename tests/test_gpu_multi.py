@@ -69,6 +69,35 @@ def test_deque_owner_and_thief_ends(torch_cuda):
         _abi.call("ferry_deque_destroy", q)
 
 
+def test_deque_peek_takes_nothing(torch_cuda):
+    from ferry_b200 import _abi
+
+    t = torch_cuda
+    q = C.c_void_p()
+    _abi.call("ferry_deque_create", 0, 8, C.byref(q))
+    try:
+        st = C.c_void_p(t.cuda.current_stream().cuda_stream)
+        cnt = t.zeros(1, dtype=t.int32, device="cuda")
+        out = t.full((8,), -1, dtype=t.int64, device="cuda")
+        size = t.zeros(1, dtype=t.int64, device="cuda")
+        _abi.call("ferry_deque_peek", q, st, _p(out), 4, _p(cnt))
+        assert cnt.item() == 0
+        # wrap the ring: push 6, steal 5, push 5 -> tasks 5..10 with top at 5
+        _abi.call("ferry_deque_push", q, st, _p(t.arange(6, dtype=t.int64, device="cuda")), 6, _p(cnt))
+        _abi.call("ferry_deque_steal", q, st, _p(out), 5, _p(cnt))
+        _abi.call("ferry_deque_push", q, st, _p(t.arange(6, 11, dtype=t.int64, device="cuda")), 5, _p(cnt))
+        _abi.call("ferry_deque_peek", q, st, _p(out), 4, _p(cnt))
+        assert cnt.item() == 4 and out[:4].tolist() == [5, 6, 7, 8]
+        _abi.call("ferry_deque_peek", q, st, _p(out), 8, _p(cnt))
+        assert cnt.item() == 6 and out[:6].tolist() == [5, 6, 7, 8, 9, 10]
+        _abi.call("ferry_deque_size", q, st, _p(size))
+        assert size.item() == 6                       # nothing taken
+        _abi.call("ferry_deque_steal", q, st, _p(out), 2, _p(cnt))
+        assert out[:2].tolist() == [5, 6]             # the peeked ones are what a steal takes
+    finally:
+        _abi.call("ferry_deque_destroy", q)
+
+
 def test_deque_steal_from_peer_device(torch_cuda):
     from ferry_b200 import _abi
 
@@ -261,7 +290,7 @@ def test_migrate_over_cuda_ipc(torch_cuda):
 # --------------------------------------------------------------------------- executor
 
 
-def _cluster_worker(rank, world, port, devices, out):
+def _cluster_worker(rank, world, port, devices, out, policy=None):
     import os
 
     import torch
@@ -281,8 +310,10 @@ def _cluster_worker(rank, world, port, devices, out):
     # FULL migration: every stolen request carries all of its lanes' cache
     # slots, so the unit count is deterministic (owners pop LIFO and thieves
     # take the oldest tasks, which may not have run yet: DELTA could move 0)
+    pol = None if policy is None else _abi.StealPolicy(cost_filter=1, margin=policy, cost_scale=3.0,
+                                                        link_gbs=700.0, fixed_ms=0.06)
     runner = RankRunner(w, total, world, rank, devices[rank], slots=total + 4, max_batch=4,
-                        steal_batch=4, migrate_mode=_abi.MIGRATE_FULL)
+                        steal_batch=4, migrate_mode=_abi.MIGRATE_FULL, policy=pol)
     try:
         stats = runner.run(home, join, epoch=2, max_ticks=400)
     finally:
@@ -292,9 +323,12 @@ def _cluster_worker(rank, world, port, devices, out):
     dist.destroy_process_group()
 
 
-def test_executor_two_ranks_steal_and_migrate(torch_cuda):
+@pytest.mark.parametrize("policy", [None, 0.0, 1e12])
+def test_executor_two_ranks_steal_and_migrate(torch_cuda, policy):
     """Rank 1 starts idle, steals from rank 0's deque and migrates the stolen
-    requests over NVLink / IPC; every (request, step) decodes exactly once."""
+    requests over NVLink / IPC; every (request, step) decodes exactly once.
+    policy: None = water-level steal; a margin = plus the value/cost filter
+    (0 accepts every candidate, 1e12 rejects every one)."""
     import socket
 
     t = torch_cuda
@@ -305,7 +339,7 @@ def test_executor_two_ranks_steal_and_migrate(torch_cuda):
     s.close()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    ps = [ctx.Process(target=_cluster_worker, args=(r, 2, port, devices, q)) for r in range(2)]
+    ps = [ctx.Process(target=_cluster_worker, args=(r, 2, port, devices, q, policy)) for r in range(2)]
     for p in ps:
         p.start()
     try:
@@ -317,6 +351,9 @@ def test_executor_two_ranks_steal_and_migrate(torch_cuda):
                 p.kill()
     (r0, tok0, st0, mig0, ticks0), (r1, tok1, st1, mig1, ticks1) = res
     assert tok0 + tok1 == 12 * 6
+    if policy is not None and policy > 1e9:
+        assert st0 == st1 == 0 and tok1 == 0 and mig1 == 0   # every candidate priced out
+        return
     assert st1 > 0 and tok1 > 0
     w = _workload()
     per_req = w.lanes_per_req * w.cache_pages

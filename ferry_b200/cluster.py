@@ -59,8 +59,11 @@ def merge_ownership(rows: np.ndarray, total_requests: int):
     """rows: [world][cap + 3] gathered ownership rows -> (owner_of[total],
     finished_total, admitted_total). A request absent from every row is -1."""
     owner = np.full(total_requests, -1, np.int32)
+    cap = rows.shape[1] - 3
     for rank, row in enumerate(rows):
         n = int(row[2])
+        if not (0 <= n <= cap) or row[0] < 0 or row[1] < 0:
+            raise ValueError(f"ownership row of rank {rank} is corrupt (count {n}, cap {cap})")
         ids = row[3:3 + n]
         ids = ids[(ids >= 0) & (ids < total_requests)]
         owner[ids] = rank

@@ -27,6 +27,19 @@ int cuda_status(cudaError_t e, const char* what) {
 
 namespace {
 
+// one thread polls the flag (acquire, system scope) with a short sleep
+__global__ void wait_flag_kernel(const uint32_t* flag, uint32_t value, uint32_t max_polls, uint32_t* err) {
+  if (threadIdx.x != 0) return;
+  for (uint32_t i = 0; i < max_polls; ++i) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v == value) return;
+    __nanosleep(100);
+  }
+  record_error(err, kErrTimeout);
+}
+
+
 // Switch to a device for the duration of a call and restore the caller's.
 struct DeviceGuard {
   int prev = -1;
@@ -340,6 +353,14 @@ int ferry_decode_step(ferry_ctx* c, void* stream, const uint16_t* d_q, const int
   if (c->cfg.kv_dtype == FERRY_KV_E4M3)
     return launch_attention_tc(c, st, d_q, d_req_ids, n_req, c->ws_islot, c->ws_nsel, d_out);
   return launch_attention(c, st, d_q, d_req_ids, n_req, c->ws_islot, c->ws_nsel, d_out);
+}
+
+int ferry_wait_flag(ferry_ctx* c, void* stream, const uint32_t* d_flag, uint32_t value, uint32_t max_polls) {
+  if (!c || !d_flag) return set_error("wait_flag: bad arguments"), FERRY_E_INVAL;
+  DeviceGuard guard(c->device);
+  wait_flag_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(d_flag, value, max_polls, c->err);
+  FERRY_TRY(cudaGetLastError());
+  return FERRY_OK;
 }
 
 int ferry_stats_read(ferry_ctx* c, uint64_t* stats, int reset) {

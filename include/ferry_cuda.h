@@ -197,6 +197,14 @@ int ferry_decode_step(ferry_ctx* ctx, void* stream, const uint16_t* d_q,
 #define FERRY_NUM_STATS 8
 int ferry_stats_read(ferry_ctx* ctx, uint64_t* stats, int reset);
 
+/* Bounded wait on `stream` until *d_flag == value -- a flag another stream,
+ * a peer GPU (through a mapped pointer) or the host sets. At most max_polls
+ * polls about 100 ns apart; when they run out the ctx records
+ * FERRY_E_TIMEOUT (reported by ferry_ctx_check), the kernel returns and the
+ * stream and the ctx stay usable. No counterpart in the reference (its waits
+ * are host-side and unbounded). */
+int ferry_wait_flag(ferry_ctx* ctx, void* stream, const uint32_t* d_flag, uint32_t value, uint32_t max_polls);
+
 /* Copy ctx device state to host for checking (synchronous).
  * which: 0 cache bytes, 1 page_slot, 2 lru order, 3 lru size, 4 summaries,
  * 5 ctx pages, 6 decode-step workspace (sel | item_slot | miss_page |

@@ -4,6 +4,7 @@ import os
 import socket
 
 import numpy as np
+import pytest
 import torch.multiprocessing as mp
 
 
@@ -123,3 +124,63 @@ def test_steal_filter_rejects_bad_policy():
     assert lib.ferry_steal_filter(C.byref(pol), 0, None, None, C.c_double(1.0), None, None,
                                   C.byref(acc)) == _abi.E_INVAL
     assert lib.ferry_exec_policy(None, C.byref(pol)) == _abi.E_INVAL
+
+
+# --------------------------------------------------------------------------- failures on the host
+
+
+def test_merge_rejects_corrupt_rows():
+    from ferry_b200.cluster import merge_ownership, ownership_row
+
+    rows = np.stack([ownership_row(0, 2, np.array([0, 1]), 4), ownership_row(1, 2, np.array([2, 3]), 4)])
+    owner, fin, adm = merge_ownership(rows, 8)
+    assert owner.tolist() == [0, 0, 1, 1, -1, -1, -1, -1] and (fin, adm) == (1, 4)
+    bad = rows.copy()
+    bad[1, 2] = 99  # a garbled count
+    with pytest.raises(ValueError):
+        merge_ownership(bad, 8)
+    bad = rows.copy()
+    bad[0, 1] = -5
+    with pytest.raises(ValueError):
+        merge_ownership(bad, 8)
+
+
+def _leaving_rank(rank, port, out):
+    import datetime
+
+    import torch.distributed as dist
+
+    from ferry_b200.cluster import exchange_ownership
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:  # leaves between steps, before the exchange
+        out.put((1, "left"))
+        dist.destroy_process_group()
+        return
+    try:
+        exchange_ownership(0, 4, np.arange(4), 8, 8)
+        out.put((0, "no error"))
+    except Exception as e:  # the collective ends with an error instead of waiting for good
+        out.put((0, type(e).__name__))
+
+
+def test_a_rank_that_leaves_ends_the_exchange_with_an_error():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_leaving_rank, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    try:
+        res = dict(q.get(timeout=90) for _ in ps)
+    finally:
+        for p in ps:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert res[1] == "left" and res[0] != "no error"

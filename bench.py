@@ -373,6 +373,8 @@ def run_ferry(args, w):
             "roofline": {"bound": "hbm", "kernel": "attn_kernel", "achieved": achieved,
                          "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                          "peak_kind": peak_kind,
+                         "note": "the step's HBM-bound kernel; the step itself is bound by the host link "
+                                 "(gather_kernel, ~96% of step time: see miss_gather.frac)",
                          # ncu DRAM bytes of a full-batch launch, scaled by this
                          # run's algorithmic bytes per launch (profiles/ncu_traffic.json)
                          "traffic": (traffic["traffic_over_algorithmic"] * attn_bytes / max(1, n_launch)

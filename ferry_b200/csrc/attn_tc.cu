@@ -30,79 +30,58 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace ferry {
 namespace {
 
 constexpr int kTcThreads = 192;  // warps 0-3 softmax (TMEM lanes), 4 TMA producer, 5 MMA issuer
-constexpr int kTcPages = 8;                       // pages per group: 128 tokens
-constexpr int kTcN = 32;                          // MMA N: 3 terms x 8 head rows, padded
+constexpr int kTcPages = 8;      // pages per group: 128 tokens
 constexpr int kTcStages = 3;
-constexpr int kTile = 128 * 128;                  // 16 KiB: 128 rows x 128 B (e4m3)
-constexpr int kQP = kTcN * 128;                   // 4 KiB: 32 rows x 128 B
-constexpr int kScl = kTcPages * 16;               // 16 B per page: k_scale, v_scale, pad
-// dynamic shared memory, from a 1024-aligned base
-constexpr int kOffK = 0;                          // stage s: K at s * 2 * kTile, V after it
-constexpr int kOffQ = kTcStages * 2 * kTile;      // 98304
-constexpr int kOffP = kOffQ + kQP;
-constexpr int kOffScl = kOffP + 2 * kQP;          // P double-buffered
-constexpr int kTcSmemUsed = kOffScl + kTcStages * kScl;
-constexpr int kTcSmem = kTcSmemUsed + 1024;       // alignment slack
-static_assert(2 * (kTcSmem + 1024) <= 228 * 1024, "two CTAs per SM must fit");
-constexpr uint32_t kTmemCols = 128;               // S[2] at cols 0, 32; O[2] at 64, 96
+constexpr int kQP = 4096;            // the Q tile and each P tile
+constexpr int kScl = kTcPages * 16;  // e4m3: 16 B per page (k_scale, v_scale, pad)
+constexpr uint32_t kTmemCols = 128;  // S[2] at cols 0, 32; O[2] at 64, 96
 
-// UMMA shared-memory descriptor without swizzle (layout type 0), version 1
-__device__ __forceinline__ uint64_t plain_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
-  d |= (uint64_t)1 << 46;
-  return d;
-}
+// Shared-memory map for e4m3 (F8) or fp16 KV, from a 1024-aligned base. Stage
+// s holds the K tile at s * kStage and the V tile kHalf after it: e4m3 128
+// rows x 128 B each; fp16 two 64-dim blocks of 128 rows x 128 B each.
+template <bool F8>
+struct TcLayout {
+  static constexpr int kHalf = F8 ? 128 * 128 : 2 * 128 * 128;
+  static constexpr int kStage = 2 * kHalf;
+  static constexpr int kOffQ = kTcStages * kStage;
+  static constexpr int kOffP = kOffQ + kQP;
+  static constexpr int kOffScl = kOffP + 2 * kQP;  // P double-buffered
+  static constexpr int kUsed = kOffScl + (F8 ? kTcStages * kScl : 0);
+  static constexpr int kSmem = kUsed + 1024;       // alignment slack
+  static constexpr int kCtasPerSm = F8 ? 2 : 1;
+};
+static_assert(2 * (TcLayout<true>::kSmem + 1024) <= 228 * 1024, "two e4m3 CTAs per SM must fit");
+static_assert(TcLayout<false>::kSmem + 1024 <= 228 * 1024, "one fp16 CTA per SM must fit");
 
-// UMMA shared-memory descriptor, SWIZZLE_128B (layout type 2), version 1
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
-  return d;
-}
-
-// kind::f8f6f4 instruction descriptor: e4m3 A and B, f32 accumulate, M = 128, N = 32
-__host__ __device__ constexpr uint32_t idesc_f8(bool a_mn_major, bool b_mn_major) {
+// instruction descriptor, f32 accumulate, M = 128: kind::f8f6f4 e4m3 x e4m3
+// with N = 32 (3 terms x 8 head rows, padded), or kind::f16 f16 x f16 with
+// N = 16 (8 head rows, padded); the operand format codes are 0 in both
+__host__ __device__ constexpr uint32_t idesc_tc(bool f8, bool a_mn_major, bool b_mn_major) {
   return (1u << 4) | (a_mn_major ? (1u << 15) : 0u) | (b_mn_major ? (1u << 16) : 0u) |
-         ((uint32_t)(kTcN >> 3) << 17) | ((128u >> 4) << 24);
+         ((uint32_t)((f8 ? 32 : 16) >> 3) << 17) | ((128u >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+template <bool F8>
+__device__ __forceinline__ void mma_tc(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_addr(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// 3-D tensor copy global -> shared (no multicast), completion on the mbarrier
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
-          smem_addr(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
-      : "memory");
+  if constexpr (F8)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
 // byte offset of (row, col) in a K-major SWIZZLE_128B tile of 128-byte rows:
@@ -157,99 +136,11 @@ __device__ __forceinline__ float pow2_scale(float amax) {
   return __int_as_float((sh + 127) << 23);
 }
 
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 
-// maximum over the warp of G values per lane at once: levels pair lanes
-// l ^ 16, l ^ 8, ...; while more than one value is left each pair swaps
-// halves (the lane with the level's bit set keeps the upper half). Lane l
-// returns the maximum of value l >> (5 - log2 G).
-template <int G>
-__device__ __forceinline__ float warp_max_heads(float (&v)[G], int lane) {
-#pragma unroll
-  for (int j = 0; j < 5; ++j) {
-    const int o = 16 >> j;
-    const int n = G >> j;
-    if (n > 1) {
-      const bool up = (lane & o) != 0;
-#pragma unroll
-      for (int i = 0; i < n / 2; ++i) {
-        const float send = up ? v[i] : v[i + n / 2];
-        const float keep = up ? v[i + n / 2] : v[i];
-        v[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, o));
-      }
-    } else {
-      v[0] = fmaxf(v[0], __shfl_xor_sync(0xffffffffu, v[0], o));
-    }
-  }
-  return v[0];
-}
-
-struct TcArgs {
-  const uint16_t* q;
-  const int32_t* req_ids;
-  int lanes_per_req;
-  int n_lanes;
-  int64_t lanes_total;
-  const uint8_t* cache;
-  int C;
-  const int32_t* item_slot;
-  const int32_t* n_sel;
-  int k;
-  int gpl;     // groups per lane: ceil(k / 8)
-  int64_t T;   // n_lanes * gpl
-  int nc;      // CTAs sharing the flat range
-  float* part;
-  uint32_t* lane_done;
-  float* out;
-  uint32_t* err;
-  float qscale;  // log2(e) / sqrt(head_dim)
-};
-
-__device__ __forceinline__ int cta_of(int64_t x, int nc, int64_t T) { return (int)(((x + 1) * nc - 1) / T); }
-
-// 8 consecutive f32 columns of this thread's TMEM lane (column a multiple of 8)
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
-  uint32_t r[8];
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// barrier among the 128 softmax threads only (named barrier 1); true when
-// any of them passed `flag`
-__device__ __forceinline__ bool softmax_bar_or(bool flag) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, 128, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)flag)
-      : "memory");
-  return r != 0;
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-
-// Walk of a CTA's flat range, shared by its three roles: lane segments in
-// order, each with its groups [glo, ghi) (pages present only).
-struct Seg {
-  int a, n, glo, ghi;
-  int64_t unit0;
-};
-
-template <int G>
-__global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_constant__ CUtensorMap tmap, TcArgs A) {
+template <int G, bool F8>
+__global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmap, TcArgs A) {
+  using Lay = TcLayout<F8>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages];
   __shared__ __align__(8) uint64_t s_full[2], s_free[2], p_full[2], o_full[2], o_free[2], q_full;
@@ -261,9 +152,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_con
   const int64_t x_lo = (int64_t)c * A.T / A.nc, x_hi = (int64_t)(c + 1) * A.T / A.nc;
   if (x_lo >= x_hi) return;
   uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
-  uint8_t* Qt = smem + kOffQ;
-  uint8_t* Pt = smem + kOffP;
-  uint8_t* scl = smem + kOffScl;
+  uint8_t* Qt = smem + Lay::kOffQ;
+  uint8_t* Pt = smem + Lay::kOffP;
+  uint8_t* scl = smem + Lay::kOffScl;
 
   if (tid == 0) {
     for (int i = 0; i < kTcStages; ++i) {
@@ -288,7 +179,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_con
   }
   // zero every tile once: rows the copies never fill (short groups, padded
   // heads and terms) must hold finite values, and zeros in P
-  for (int i = tid; i < kTcSmemUsed / 16; i += kTcThreads) reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  for (int i = tid; i < Lay::kUsed / 16; i += kTcThreads) reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -332,8 +223,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_con
         int slot = lane < np ? A.item_slot[(size_t)a * k + g * kTcPages + lane] : 0;
         if (j >= (uint32_t)kTcStages) ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], ((j / kTcStages) - 1) & 1u, A.err));
         if (!ok) break;
-        uint8_t* Ks = smem + kOffK + s * 2 * kTile;
-        if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(np * (2 * 2048 + 16)));
+        uint8_t* Ks = smem + s * Lay::kStage;
+        if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(np * (F8 ? 2 * 2048 + 16 : 4 * 2048)));
         __syncwarp();
         if (lane < np) {
           if (slot < 0 || slot >= A.C) {
@@ -341,9 +232,16 @@ __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_con
             slot = 0;
           }
           const int64_t unit = sg.unit0 + slot;
-          tma_load_3d(Ks + lane * 2048, &tmap, 0, 0, (int)unit, &full[s]);           // K rows
-          tma_load_3d(Ks + kTile + lane * 2048, &tmap, 0, 16, (int)unit, &full[s]);  // V rows
-          bulk_load(scl + s * kScl + lane * 16, A.cache + (size_t)unit * kUnitBytesF8 + 4096, 16, &full[s]);
+          if constexpr (F8) {
+            tma_load_3d(Ks + lane * 2048, &tmap, 0, 0, (int)unit, &full[s]);                 // K rows
+            tma_load_3d(Ks + Lay::kHalf + lane * 2048, &tmap, 0, 16, (int)unit, &full[s]);   // V rows
+            bulk_load(scl + s * kScl + lane * 16, A.cache + (size_t)unit * kUnitBytesF8 + 4096, 16, &full[s]);
+          } else {  // dims 0-63 and 64-127 of the K rows, then of the V rows
+            tma_load_3d(Ks + lane * 2048, &tmap, 0, 0, (int)unit, &full[s]);
+            tma_load_3d(Ks + 128 * 128 + lane * 2048, &tmap, 64, 0, (int)unit, &full[s]);
+            tma_load_3d(Ks + Lay::kHalf + lane * 2048, &tmap, 0, 16, (int)unit, &full[s]);
+            tma_load_3d(Ks + Lay::kHalf + 128 * 128 + lane * 2048, &tmap, 64, 16, (int)unit, &full[s]);
+          }
         }
       }
     }
@@ -352,7 +250,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_con
   } else if (warp == 5) {
     // ================= MMA issuer (one thread)
     if (lane == 0) {
-      constexpr uint32_t kIdQK = idesc_f8(false, false), kIdPV = idesc_f8(true, true);
+      constexpr uint32_t kIdQK = idesc_tc(F8, false, false), kIdPV = idesc_tc(F8, true, true);
       const uint32_t sQ = smem_addr(Qt);
       bool ok = true;
       uint64_t*& last_bar = mma_last;
@@ -363,11 +261,14 @@ __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_con
         if (ok && i >= 2) ok = mbar_wait(&o_free[bi], ((i >> 1) - 1) & 1u, A.err);
         if (!ok) return;
         tc_fence_after();
-        const uint32_t sV = smem_addr(smem + kOffK + si * 2 * kTile) + kTile, sP = smem_addr(Pt + bi * kQP);
+        const uint32_t sV = smem_addr(smem + si * Lay::kStage) + Lay::kHalf, sP = smem_addr(Pt + bi * kQP);
+        // A = V read MN-major (dims contiguous; fp16: two 64-dim blocks 16 KiB
+        // apart), B = P MN-major unswizzled; K steps of 32 (e4m3) / 16 (f16) tokens
+        constexpr int kSteps = F8 ? 4 : 8;
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj)
-          mma_f8(tmem + 64 + bi * 32, sw128_desc(sV + jj * 4096, kTile, 1024), plain_desc(sP + jj * 1024, 256, 128),
-                 kIdPV, jj > 0);
+        for (int jj = 0; jj < kSteps; ++jj)
+          mma_tc<F8>(tmem + 64 + bi * 32, sw128_desc(sV + jj * (F8 ? 4096 : 2048), 128 * 128, 1024),
+                     plain_desc(sP + jj * (F8 ? 1024 : 512), 256, 128), kIdPV, jj > 0);
         mma_commit(&o_full[bi]);
         mma_commit(&empty[si]);  // K and V of this stage are no longer read
         last_bar = &o_full[bi];
@@ -387,10 +288,15 @@ __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_con
           if (ok && j >= 2) ok = mbar_wait(&s_free[b], ((j >> 1) - 1) & 1u, A.err);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t sK = smem_addr(smem + kOffK + s * 2 * kTile);
+          const uint32_t sK = smem_addr(smem + s * Lay::kStage);
+          // K steps of 32 B along the 128-B rows: 4 x K=32 (e4m3), or 2 dim
+          // blocks x 4 x K=16 (f16, blocks 16 KiB apart in K and 2 KiB in Q)
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj)
-            mma_f8(tmem + b * 32, sw128_desc(sK + jj * 32, 16, 1024), sw128_desc(sQ + jj * 32, 16, 1024), kIdQK, jj > 0);
+          for (int kb = 0; kb < (F8 ? 1 : 2); ++kb)
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj)
+              mma_tc<F8>(tmem + b * 32, sw128_desc(sK + kb * 128 * 128 + jj * 32, 16, 1024),
+                         sw128_desc(sQ + kb * 2048 + jj * 32, 16, 1024), kIdQK, (kb | jj) > 0);
           mma_commit(&s_full[b]);
           last_bar = &s_full[b];
           last_par = (j >> 1) & 1u;
@@ -421,7 +327,20 @@ __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_con
         alpha_prev[h] = 0.f;
       }
       float beta_prev = 1.f;
-      if (glo < ghi) {
+      if (glo < ghi && !F8) {
+        // ---- Q of this lane as f16 rows (K-major, SWIZZLE_128B, two 64-dim
+        // blocks 2 KiB apart): thread t = dim t
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          *reinterpret_cast<uint16_t*>(Qt + (t >> 6) * 2048 + sw128(h, (t & 63) * 2)) =
+              A.q[((size_t)a * G + h) * kHeadDim + t];
+          qdiv[h] = A.qscale;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&q_full);
+      }
+      if (glo < ghi && F8) {
         // ---- Q terms of this lane: thread t = dim t; per-head power-of-two scale
         float qf[G];
 #pragma unroll
@@ -455,8 +374,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_con
         tc_fence_after();
         float o0[8], o1[8], o2[8];
         tmem_ld8(tmem + 64 + bi * 32 + lane_off, o0);  // thread t = head dim t
-        tmem_ld8(tmem + 64 + bi * 32 + lane_off + 8, o1);
-        tmem_ld8(tmem + 64 + bi * 32 + lane_off + 16, o2);
+        if constexpr (F8) {
+          tmem_ld8(tmem + 64 + bi * 32 + lane_off + 8, o1);
+          tmem_ld8(tmem + 64 + bi * 32 + lane_off + 16, o2);
+        }
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
@@ -464,7 +385,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_con
         const float ib = __frcp_rn(beta_prev);  // exact: a power of two
 #pragma unroll
         for (int h = 0; h < G; ++h)
-          o_acc[h] = o_acc[h] * alpha_prev[h] + (o0[h] + o1[h] * 0.0625f + o2[h] * 0.00390625f) * ib;
+          o_acc[h] = o_acc[h] * alpha_prev[h] + (F8 ? (o0[h] + o1[h] * 0.0625f + o2[h] * 0.00390625f) * ib : o0[h]);
       };
       for (int g = glo; g < ghi; ++g, ++j) {
         const int s = j % kTcStages, b = j & 1;
@@ -475,8 +396,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_con
         if (ok) {
           tc_fence_after();
           tmem_ld8(tmem + b * 32 + lane_off, s0);  // columns jj*8 + h: term jj of head h
-          tmem_ld8(tmem + b * 32 + lane_off + 8, s1);
-          tmem_ld8(tmem + b * 32 + lane_off + 16, s2);
+          if constexpr (F8) {
+            tmem_ld8(tmem + b * 32 + lane_off + 8, s1);
+            tmem_ld8(tmem + b * 32 + lane_off + 16, s2);
+          }
           tmem_wait_ld();
           tc_fence_before();
           __syncwarp();
@@ -485,12 +408,13 @@ __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_con
         }
         const int pg = t >> 4;
         const bool valid = pg < np;
-        const float ks = *reinterpret_cast<const float*>(scl + s * kScl + pg * 16);
-        const float vs = *reinterpret_cast<const float*>(scl + s * kScl + pg * 16 + 4);
+        const float ks = F8 ? *reinterpret_cast<const float*>(scl + s * kScl + pg * 16) : 1.f;
+        const float vs = F8 ? *reinterpret_cast<const float*>(scl + s * kScl + pg * 16 + 4) : 1.f;
         float x[G], mx[G];
 #pragma unroll
         for (int h = 0; h < G; ++h) {
-          x[h] = valid && ok ? (s0[h] + s1[h] * 0.0625f + s2[h] * 0.00390625f) * ks * qdiv[h] : -INFINITY;
+          const float sc = F8 ? (s0[h] + s1[h] * 0.0625f + s2[h] * 0.00390625f) * ks : s0[h];
+          x[h] = valid && ok ? sc * qdiv[h] : -INFINITY;
           mx[h] = x[h];
         }
         {
@@ -498,11 +422,14 @@ __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_con
           if ((lane & ((32 / G) - 1)) == 0) red[b][warp][lane / (32 / G)] = wm;
         }
         // power-of-two scale of the weights: p * v_scale * beta <= 448 in this group
-        float vmax = lane < np ? *reinterpret_cast<const float*>(scl + s * kScl + (lane & 7) * 16 + 4) : 0.f;
-        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
-        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
-        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 4));
-        const float beta = pow2_scale(__shfl_sync(0xffffffffu, vmax, 0));
+        float beta = 1.f;
+        if constexpr (F8) {
+          float vmax = lane < np ? *reinterpret_cast<const float*>(scl + s * kScl + (lane & 7) * 16 + 4) : 0.f;
+          vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+          vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+          vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 4));
+          beta = pow2_scale(__shfl_sync(0xffffffffu, vmax, 0));
+        }
         if (softmax_bar_or(!ok)) {
           ok = false;
           break;
@@ -524,7 +451,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_con
         // this token's row of P[b] (MN-major, no swizzle): byte jj*8 + h =
         // term jj of head h. P[b]'s last reader, the PV two groups back, was
         // folded a group ago.
-        {
+        uint8_t* row = Pt + b * kQP + (t >> 3) * 256 + (t & 7) * 16;
+        if constexpr (F8) {
           uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
           for (int i = 0; i < (G + 1) / 2; ++i) {
@@ -535,9 +463,16 @@ __global__ void __launch_bounds__(kTcThreads, 2) attn_tc_kernel(const __grid_con
             w[2 + (i >> 1)] |= t1 << sh;
             w[4 + (i >> 1)] |= t2 << sh;
           }
-          uint8_t* row = Pt + b * kQP + (t >> 3) * 256 + (t & 7) * 16;
           *reinterpret_cast<uint4*>(row) = make_uint4(w[0], w[1], w[2], w[3]);
           *reinterpret_cast<uint4*>(row + 128) = make_uint4(w[4], w[5], w[6], w[7]);
+        } else {  // f16 weights of heads 0-7 (the second chunk, heads 8-15, stays zero)
+          uint32_t w[4] = {0, 0, 0, 0};
+#pragma unroll
+          for (int i = 0; i < (G + 1) / 2; ++i) {
+            const __half2 hv = __floats2half2_rn(pw[2 * i], 2 * i + 1 < G ? pw[2 * i + 1] : 0.f);
+            w[i] = *reinterpret_cast<const uint32_t*>(&hv);
+          }
+          *reinterpret_cast<uint4*>(row) = make_uint4(w[0], w[1], w[2], w[3]);
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -632,20 +567,23 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 }  // namespace
 
-// Tensor map over the e4m3 cache: (128 B, 32 rows, units) with unit stride
-// 4112 B; rows 0-15 of a unit are K, rows 16-31 V. Boxes of 128 B x 16 rows
-// land SWIZZLE_128B in shared memory.
+// Tensor map over the cache as (dims, 32 rows, units): rows 0-15 of a unit
+// are K, rows 16-31 V. e4m3: 128 B rows, unit stride 4112 B, boxes of 128 B x
+// 16 rows; fp16: 256 B rows, unit stride 8192 B, boxes of 64 elements (128 B)
+// x 16 rows. Boxes land SWIZZLE_128B in shared memory.
 int make_cache_tensor_map(ferry_ctx* c) {
   auto fn = encode_fn();
   if (!fn) return set_error("cuTensorMapEncodeTiled unavailable"), FERRY_E_CUDA;
   const uint64_t units = (uint64_t)c->lanes * c->cfg.cache_pages;
   if (units == 0 || units > 0x7fffffffull) return set_error("cache too large for a tensor map"), FERRY_E_INVAL;
+  const bool f8 = c->cfg.kv_dtype == FERRY_KV_E4M3;
   cuuint64_t dims[3] = {128, 32, units};
-  cuuint64_t strides[2] = {128, (cuuint64_t)kUnitBytesF8};
-  cuuint32_t box[3] = {128, 16, 1};
+  cuuint64_t strides[2] = {f8 ? 128u : 256u, (cuuint64_t)(f8 ? kUnitBytesF8 : kUnitBytes)};
+  cuuint32_t box[3] = {f8 ? 128u : 64u, 16, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   static_assert(sizeof(CUtensorMap) <= sizeof(c->cache_map), "tensor map storage");
-  const CUresult r = fn(reinterpret_cast<CUtensorMap*>(c->cache_map), CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, c->cache, dims,
+  const CUresult r = fn(reinterpret_cast<CUtensorMap*>(c->cache_map),
+                        f8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, c->cache, dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error("cuTensorMapEncodeTiled failed (%d)", (int)r), FERRY_E_CUDA;
@@ -668,8 +606,10 @@ int launch_attention_tc(const ferry_ctx* c, cudaStream_t st, const uint16_t* q, 
   A.k = c->cfg.top_k;
   A.gpl = (A.k + kTcPages - 1) / kTcPages;
   A.T = (int64_t)A.n_lanes * A.gpl;
+  const bool f8 = c->cfg.kv_dtype == FERRY_KV_E4M3;
   // resident CTAs, >= 2 groups each, <= 31 per lane (a lane combines <= 32 partials)
-  int64_t nc = std::min<int64_t>((int64_t)c->num_sms * 2, std::max<int64_t>(1, A.T / 2));
+  int64_t nc = std::min<int64_t>((int64_t)c->num_sms * (f8 ? TcLayout<true>::kCtasPerSm : TcLayout<false>::kCtasPerSm),
+                                 std::max<int64_t>(1, A.T / 2));
   nc = std::min<int64_t>(nc, 31 * (int64_t)A.n_lanes);
   if ((size_t)A.n_lanes + (size_t)nc > attention_partial_slots(c->lanes, c->num_sms))
     return set_error("attention: partial scratch too small"), FERRY_E_STATE;
@@ -680,10 +620,17 @@ int launch_attention_tc(const ferry_ctx* c, cudaStream_t st, const uint16_t* q, 
   A.err = c->err;
   A.qscale = 1.4426950408889634f / sqrtf((float)kHeadDim);
   const CUtensorMap* map = reinterpret_cast<const CUtensorMap*>(c->cache_map);
-#define FERRY_TC_CASE(GG)                                                                                  \
-  case GG:                                                                                                 \
-    FERRY_TRY(cudaFuncSetAttribute(attn_tc_kernel<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem)); \
-    attn_tc_kernel<GG><<<(unsigned)nc, kTcThreads, kTcSmem, st>>>(*map, A);                               \
+#define FERRY_TC_CASE(GG)                                                                                   \
+  case GG:                                                                                                  \
+    if (f8) {                                                                                               \
+      FERRY_TRY(cudaFuncSetAttribute(attn_tc_kernel<GG, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                     TcLayout<true>::kSmem));                                               \
+      attn_tc_kernel<GG, true><<<(unsigned)nc, kTcThreads, TcLayout<true>::kSmem, st>>>(*map, A);           \
+    } else {                                                                                                \
+      FERRY_TRY(cudaFuncSetAttribute(attn_tc_kernel<GG, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                     TcLayout<false>::kSmem));                                              \
+      attn_tc_kernel<GG, false><<<(unsigned)nc, kTcThreads, TcLayout<false>::kSmem, st>>>(*map, A);         \
+    }                                                                                                       \
     break;
   switch (c->group) {
     FERRY_TC_CASE(1)

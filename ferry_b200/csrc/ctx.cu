@@ -27,6 +27,17 @@ int cuda_status(cudaError_t e, const char* what) {
 
 namespace {
 
+// Attention kernel choice: with one q head per kv head (G = 1) every loaded
+// fp16 K/V element feeds a single multiply-add, so the CUDA-core kernel
+// (attn.cu) is the faster one; with a GQA group, or fp8 KV, the tcgen05
+// kernel (attn_tc.cu) runs the dense QK / PV tiles on the tensor cores.
+int launch_attention_any(const ferry_ctx* c, cudaStream_t st, const uint16_t* q, const int32_t* req_ids, int n_req,
+                         const int32_t* item_slot, const int32_t* n_sel, float* out) {
+  if (c->cfg.kv_dtype == FERRY_KV_F16 && c->group == 1)
+    return launch_attention(c, st, q, req_ids, n_req, item_slot, n_sel, out);
+  return launch_attention_tc(c, st, q, req_ids, n_req, item_slot, n_sel, out);
+}
+
 // one thread polls the flag (acquire, system scope) with a short sleep
 __global__ void wait_flag_kernel(const uint32_t* flag, uint32_t value, uint32_t max_polls, uint32_t* err) {
   if (threadIdx.x != 0) return;
@@ -168,7 +179,7 @@ int ferry_ctx_create(int device, const ferry_cfg* cfg, ferry_ctx** out) {
   FERRY_CK(dev_alloc(&c->slot_state, (size_t)cfg->num_requests, 0));
   c->unit_bytes = cfg->kv_dtype == FERRY_KV_E4M3 ? kUnitBytesF8 : kUnitBytes;
   FERRY_CK(dev_alloc(&c->cache, (size_t)c->lanes * cfg->cache_pages * c->unit_bytes, 0));
-  if (cfg->kv_dtype == FERRY_KV_E4M3) FERRY_CK(make_cache_tensor_map(c));
+  FERRY_CK(make_cache_tensor_map(c));
   FERRY_CK(alloc_lru_state(&c->lru, c->lanes, cfg->cache_pages, cfg->max_pages, c->err));
   c->lru.device = device;
   FERRY_CK(dev_alloc(&c->ctx_pages, R, 0));
@@ -330,10 +341,7 @@ int ferry_sparse_decode(ferry_ctx* c, void* stream, const uint16_t* d_q, const i
   if (n_req && (!d_q || !d_item_slot || !d_n_sel || !d_out))
     return set_error("sparse_decode: NULL buffer"), FERRY_E_INVAL;
   DeviceGuard guard(c->device);
-  if (c->cfg.kv_dtype == FERRY_KV_E4M3)
-    return launch_attention_tc(c, (cudaStream_t)stream, d_q, d_req_ids, n_req, d_item_slot, d_n_sel, d_out);
-  return launch_attention(c, (cudaStream_t)stream, d_q, d_req_ids, n_req, d_item_slot, d_n_sel,
-                          d_out);
+  return launch_attention_any(c, (cudaStream_t)stream, d_q, d_req_ids, n_req, d_item_slot, d_n_sel, d_out);
 }
 
 int ferry_decode_step(ferry_ctx* c, void* stream, const uint16_t* d_q, const int32_t* d_req_ids,
@@ -350,9 +358,7 @@ int ferry_decode_step(ferry_ctx* c, void* stream, const uint16_t* d_q, const int
                        c->ws_islot, c->ws_mpage, c->ws_mslot, c->ws_nmiss)))
     return rc;
   if ((rc = launch_gather(c, st, d_req_ids, n_req, c->ws_mpage, c->ws_mslot, c->ws_nmiss))) return rc;
-  if (c->cfg.kv_dtype == FERRY_KV_E4M3)
-    return launch_attention_tc(c, st, d_q, d_req_ids, n_req, c->ws_islot, c->ws_nsel, d_out);
-  return launch_attention(c, st, d_q, d_req_ids, n_req, c->ws_islot, c->ws_nsel, d_out);
+  return launch_attention_any(c, st, d_q, d_req_ids, n_req, c->ws_islot, c->ws_nsel, d_out);
 }
 
 int ferry_wait_flag(ferry_ctx* c, void* stream, const uint32_t* d_flag, uint32_t value, uint32_t max_polls) {

@@ -95,7 +95,13 @@ CFG5S = Workload(name="cfg5s", num_requests=32, num_layers=2, q_heads=64, kv_hea
                  ctx_tokens=131072, top_k=512, cache_frac=0.15, steps=64, arrival_rate=50.0,
                  kv_dtype="e4m3")
 
-WORKLOADS = {"cfg1": CFG1, "cfg5s": CFG5S}
+# the same GQA shape with fp16 KV (16 requests, a 17 GB pinned pool): the
+# fp16 path of the tensor-core attention kernel at G = 8
+CFG5S_F16 = Workload(name="cfg5s_f16", num_requests=16, num_layers=2, q_heads=64, kv_heads=8,
+                     ctx_tokens=131072, top_k=512, cache_frac=0.15, steps=64, arrival_rate=50.0,
+                     kv_dtype="f16")
+
+WORKLOADS = {"cfg1": CFG1, "cfg5s": CFG5S, "cfg5s_f16": CFG5S_F16}
 
 
 def small(name: str = "tiny", **kw) -> Workload:

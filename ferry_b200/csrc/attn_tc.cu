@@ -1,13 +1,16 @@
-// attn_tc.cu -- fp8 (e4m3) KV sparse decode attention on the 5th-generation
-// tensor cores (tcgen05.mma kind::f8f6f4, accumulators in TMEM).
+// attn_tc.cu -- sparse decode attention on the 5th-generation tensor cores
+// (tcgen05.mma, accumulators in TMEM): e4m3 KV with per-page scales
+// (kind::f8f6f4), and fp16 KV with a GQA group (kind::f16).
 //
-// K and V bytes never pass through registers: per selected page a 3-D TMA
-// tensor copy (box 128 B x 16 rows, SWIZZLE_128B) drops the page's K rows and
-// V rows straight into the canonical UMMA layouts, and the MMAs read them as
-// e4m3. Only queries and softmax weights are re-encoded, each as three e4m3
-// terms with a power-of-two scale: x*a = t0 + t1/16 + t2/256 carries 12
-// significant bits (f16 has 11), so the products are as exact as with f16
-// operands; the terms are extra MMA columns (N = 3 x 8 rows, padded to 32).
+// K and V bytes never pass through registers: per selected page 3-D TMA
+// tensor copies (boxes of 128 B x 16 rows, SWIZZLE_128B) drop the page's K
+// rows and V rows straight into the canonical UMMA layouts (fp16: two 64-dim
+// blocks per tile), and the MMAs read them as they are. fp16 queries and
+// softmax weights enter the f16 MMAs directly. For e4m3 they are re-encoded,
+// each as three e4m3 terms with a power-of-two scale: x*a = t0 + t1/16 +
+// t2/256 carries 12 significant bits (f16 has 11), so the products are as
+// exact as with f16 operands; the terms are extra MMA columns (N = 3 x 8 rows,
+// padded to 32).
 //
 // Work split. The batch's groups of 8 selected pages are laid out flat,
 // x = lane * gpl + g (gpl = ceil(k / 8)); CTA c of nc owns the contiguous
@@ -15,14 +18,18 @@
 // (o[128], m, l) per q head in scratch slot lane + c; the CTA completing a
 // lane's last segment (atomic count) combines them into out.
 //
-// Per group (128 tokens; thread t = TMEM lane t = token t for S, dim t for O):
-//   S = K Qt^T     A = K tile [128 tok][128 B] K-major, B = Q terms, 4 x K=32
-//   softmax        base 2, per head; k_scale applied to the scores
-//   P' = p*v_scale as three e4m3 terms (rows = head x term) -> P tile
-//   O^T = V^T P'^T A = V tile read MN-major (dims contiguous), B = P tile
-// A CTA keeps kTcStages groups in flight on mbarriers; every wait is bounded
-// (on timeout the kernel records FERRY_E_TIMEOUT, lets its copies and MMAs
-// land and frees its TMEM).
+// A CTA is warp-specialized: warp 4 issues the TMA copies of a 3-stage ring
+// (mbarrier full / empty per stage), warp 5 issues the MMAs, and warps 0-3 --
+// thread t = TMEM lane t = token t for S, dim t for O -- run the softmax. Per
+// group of 128 tokens:
+//   S = K Q^T      A = K tile K-major, B = Q (e4m3 terms or f16) K-major
+//   softmax        base 2, per head; e4m3: k_scale applied to the scores
+//   P              f16 weights, or p * v_scale as three e4m3 terms
+//   O^T = V^T P^T  A = V tile read MN-major (dims contiguous), B = P MN-major
+// S, P and O are double-buffered so the QK of the next group and the PV of
+// the last one overlap the softmax. Every wait is bounded (on timeout the
+// kernel records FERRY_E_TIMEOUT, lets its copies and MMAs land and frees its
+// TMEM).
 #include <cuda.h>
 #include <cuda_fp8.h>
 #include <cudaTypedefs.h>

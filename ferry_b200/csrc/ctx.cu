@@ -179,7 +179,8 @@ int ferry_ctx_create(int device, const ferry_cfg* cfg, ferry_ctx** out) {
   FERRY_CK(dev_alloc(&c->slot_state, (size_t)cfg->num_requests, 0));
   c->unit_bytes = cfg->kv_dtype == FERRY_KV_E4M3 ? kUnitBytesF8 : kUnitBytes;
   FERRY_CK(dev_alloc(&c->cache, (size_t)c->lanes * cfg->cache_pages * c->unit_bytes, 0));
-  FERRY_CK(make_cache_tensor_map(c));
+  // the tensor-core attention kernel reads the cache through a TMA tensor map
+  if (cfg->kv_dtype == FERRY_KV_E4M3 || c->group > 1) FERRY_CK(make_cache_tensor_map(c));
   FERRY_CK(alloc_lru_state(&c->lru, c->lanes, cfg->cache_pages, cfg->max_pages, c->err));
   c->lru.device = device;
   FERRY_CK(dev_alloc(&c->ctx_pages, R, 0));

@@ -33,6 +33,7 @@ EXPORTS = [
     "ferry_deque_import", "ferry_deque_peer_view", "ferry_deque_stress",
     "ferry_exec_create", "ferry_exec_destroy", "ferry_exec_link_peer", "ferry_exec_admit",
     "ferry_exec_set_global", "ferry_exec_owned", "ferry_exec_tick", "ferry_exec_policy",
+    "ferry_exec_usage", "ferry_exec_rebalance",
     "ferry_steal_filter",
     "ferry_trace_load", "ferry_probe_topology", "ferry_probe_link",
     "ferry_lru_create", "ferry_lru_destroy", "ferry_lru_touch", "ferry_lru_read",
@@ -128,6 +129,8 @@ _SIGS = {
     "ferry_exec_owned": (I, [V, V, I, C.POINTER(I)]),
     "ferry_exec_tick": (I, [V, V, C.POINTER(TickStats)]),
     "ferry_exec_policy": (I, [V, C.POINTER(StealPolicy)]),
+    "ferry_exec_usage": (I, [V, C.POINTER(C.c_int64), C.POINTER(C.c_int32)]),
+    "ferry_exec_rebalance": (I, [V, I, I]),
     "ferry_steal_filter": (I, [C.POINTER(StealPolicy), I, V, V, C.c_double, V, V, C.POINTER(I)]),
     "ferry_trace_load": (I, [C.c_char_p, I, I, I, I, I, I, V, C.c_int64, V, V]),
     "ferry_probe_topology": (I, [C.POINTER(I), V, V, I]),

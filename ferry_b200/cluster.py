@@ -48,42 +48,68 @@ def assign_ranks(n_req: int, world: int, policy: str = "rr", seed: int = 42,
     raise ValueError(f"unknown policy {policy!r}")
 
 
-def ownership_row(finished: int, admitted: int, owned: np.ndarray, cap: int) -> np.ndarray:
-    row = np.full(cap + 3, -1, np.int64)
-    row[0], row[1], row[2] = finished, admitted, len(owned)
-    row[3:3 + len(owned)] = owned[:cap]
+ROW_HEAD = 4  # finished, admitted, count, remaining steps (usage)
+
+
+def ownership_row(finished: int, admitted: int, owned: np.ndarray, cap: int, usage: int = 0) -> np.ndarray:
+    row = np.full(cap + ROW_HEAD, -1, np.int64)
+    row[0], row[1], row[2], row[3] = finished, admitted, len(owned), usage
+    row[ROW_HEAD:ROW_HEAD + len(owned)] = owned[:cap]
     return row
 
 
 def merge_ownership(rows: np.ndarray, total_requests: int):
-    """rows: [world][cap + 3] gathered ownership rows -> (owner_of[total],
+    """rows: [world][cap + 4] gathered ownership rows -> (owner_of[total],
     finished_total, admitted_total). A request absent from every row is -1."""
     owner = np.full(total_requests, -1, np.int32)
-    cap = rows.shape[1] - 3
+    cap = rows.shape[1] - ROW_HEAD
     for rank, row in enumerate(rows):
         n = int(row[2])
-        if not (0 <= n <= cap) or row[0] < 0 or row[1] < 0:
+        if not (0 <= n <= cap) or row[0] < 0 or row[1] < 0 or row[3] < 0:
             raise ValueError(f"ownership row of rank {rank} is corrupt (count {n}, cap {cap})")
-        ids = row[3:3 + n]
+        ids = row[ROW_HEAD:ROW_HEAD + n]
         ids = ids[(ids >= 0) & (ids < total_requests)]
         owner[ids] = rank
     return owner, int(rows[:, 0].sum()), int(rows[:, 1].sum())
 
 
+def llx_plan(usage: np.ndarray, counts: np.ndarray, threshold: float = 0.25, cap: int = 4):
+    """The rebalancer's decision (rebalance_llumnix, wla_multigpu.cuh:2084-2112):
+    usage[g] = remaining decode steps on GPU g, counts[g] = its requests.
+    Act when the max-min spread exceeds `threshold` x the mean: the least
+    loaded GPU pulls k requests from the most loaded one, k = the excess over
+    the mean divided by the source's mean steps per request (+1), clamped to
+    [1, cap]. Returns (src, dst, k) or None."""
+    usage = np.asarray(usage, np.int64)
+    counts = np.asarray(counts, np.int64)
+    n = len(usage)
+    if n < 2:
+        return None
+    src, dst = int(np.argmax(usage)), int(np.argmin(usage))
+    mean = float(usage.sum()) / n
+    if src == dst or mean == 0.0 or (usage[src] - usage[dst]) / mean <= threshold:
+        return None
+    over = int(usage[src] - int(mean))
+    per = int(mean / max(1, counts[src])) + 1 if mean > 0 else 1
+    k = max(1, min(over // max(per, 1), cap))
+    return src, dst, k
+
+
 def exchange_ownership(finished: int, admitted: int, owned: np.ndarray, cap: int, total_requests: int,
-                       device=None):
+                       device=None, usage: int = 0, with_rows: bool = False):
     """The page-ownership exchange: one all_gather of fixed-size rows (NCCL
     when ``device`` is a CUDA device, else the default group's backend)."""
     import torch
     import torch.distributed as dist
 
-    row = torch.from_numpy(ownership_row(finished, admitted, owned, cap))
+    row = torch.from_numpy(ownership_row(finished, admitted, owned, cap, usage))
     if device is not None:
         row = row.to(device)
     out = [torch.empty_like(row) for _ in range(dist.get_world_size())]
     dist.all_gather(out, row)
     rows = torch.stack(out).cpu().numpy()
-    return merge_ownership(rows, total_requests)
+    merged = merge_ownership(rows, total_requests)
+    return (merged, rows) if with_rows else merged
 
 
 @dataclasses.dataclass
@@ -100,6 +126,7 @@ class ClusterStats:
     tick_ms: list
     mig_ms: float = 0.0          # device time of the migration kernels
     mig_event_bytes: int = 0     # bytes those kernels moved
+    rebalances: int = 0          # rebalance orders this rank executed (LLX)
 
 
 # ---------------------------------------------------------------- per-rank runner (GPU)
@@ -158,7 +185,7 @@ class RankRunner:
                 slot += 1
 
     def run(self, home: np.ndarray, join: np.ndarray, epoch: int = 4, max_ticks: int = 100000,
-            exchange_device=None) -> ClusterStats:
+            exchange_device=None, llx: float | None = None) -> ClusterStats:
         """Tick until every request of the job finished on some GPU. home/join:
         each request's home rank and arrival tick."""
         import torch
@@ -172,6 +199,8 @@ class RankRunner:
         s = _abi.TickStats()
         owned = np.zeros(self.slots, np.int32)
         n_owned = C.c_int()
+        u_steps, u_reqs = C.c_int64(), C.c_int32()
+        rebalances = 0
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
         t = 0
@@ -195,9 +224,16 @@ class RankRunner:
             if t % epoch == 0:
                 call("ferry_exec_owned", self.exec, owned.ctypes.data_as(C.c_void_p), self.slots,
                      C.byref(n_owned))
-                _, fin_all, adm_all = exchange_ownership(finished, admitted, owned[:n_owned.value],
-                                                         self.slots, self.total, exchange_device)
+                call("ferry_exec_usage", self.exec, C.byref(u_steps), C.byref(u_reqs))
+                (_, fin_all, adm_all), rows = exchange_ownership(
+                    finished, admitted, owned[:n_owned.value], self.slots, self.total, exchange_device,
+                    usage=u_steps.value, with_rows=True)
                 call("ferry_exec_set_global", self.exec, adm_all - fin_all)
+                if llx is not None and fin_all < self.total:
+                    plan = llx_plan(rows[:, 3], rows[:, 2], llx)
+                    if plan is not None and plan[1] == self.rank:
+                        call("ferry_exec_rebalance", self.exec, plan[0], plan[2])
+                        rebalances += 1
                 if fin_all >= self.total:
                     break
         e1.record(st)
@@ -207,7 +243,7 @@ class RankRunner:
         return ClusterStats(rank=self.rank, tokens=tokens, ticks=t, device_ms=e0.elapsed_time(e1),
                             steals=steals, stolen_tasks=stolen, migrated_units=m_units,
                             migrated_bytes=m_bytes, gathered_bytes=g_bytes, tick_ms=tick_ms,
-                            mig_ms=mig_ms, mig_event_bytes=mig_b)
+                            mig_ms=mig_ms, mig_event_bytes=mig_b, rebalances=rebalances)
 
     def close(self):
         for pq in self.peer_deques:

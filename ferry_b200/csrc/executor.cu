@@ -68,6 +68,8 @@ struct ferry_exec {
   // slots
   std::vector<int> free_slots;
   std::vector<int> slot_req;  // global request in each slot (-1 free)
+  std::vector<int> slot_step; // next decode step of the request in each slot
+  int force_victim = -1, force_take = 0;  // a rebalance order for the next tick
   std::vector<std::pair<int, int>> pending_admit;  // (global request, n_pages)
   int64_t global_pending = 0;
   int64_t finished = 0;
@@ -150,6 +152,7 @@ int admit_pending(ferry_exec* x, cudaStream_t st) {
     const auto gp = x->pending_admit.front();
     x->pending_admit.erase(x->pending_admit.begin());
     const int s = alloc_slot(x, gp.first);
+    x->slot_step[s] = 0;
     x->h_begin[n] = s;
     x->h_begin[x->ctx->cfg.num_requests + n] = gp.second;
     x->h_base[n] = (int64_t)gp.first * LH * N;  // the request's home in the (replicated) host pool
@@ -191,6 +194,7 @@ int ferry_exec_create(ferry_ctx* ctx, ferry_deque* own, const ferry_exec_cfg* cf
   x->peer_deque.assign(cfg->world, nullptr);
   x->peer_slot.assign(cfg->world, -1);
   x->slot_req.assign(R, -1);
+  x->slot_step.assign(R, 0);
   x->slot_state.assign(R, 0);
   for (int s = R - 1; s >= 0; --s) x->free_slots.push_back(s);
   const size_t B = cfg->max_batch, W = cfg->world, S = std::max(1, cfg->steal_batch);
@@ -301,7 +305,8 @@ int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out) {
   FERRY_TRY(cudaMemcpyAsync(x->h_tasks, x->d_tasks, (size_t)B * 8, cudaMemcpyDeviceToHost, st));
   FERRY_TRY(cudaStreamSynchronize(st));
   int n = x->h_cnt[0];
-  // 3. water-level steal
+  // 3. steal: a rebalance order (ferry_exec_rebalance), else the water-level rule
+  const bool forced = x->force_take > 0;
   if (x->cfg.world > 1 && x->cfg.steal_batch > 0 && n < B && !x->free_slots.empty()) {
     const int64_t fair = (x->global_pending + x->cfg.world - 1) / x->cfg.world;
     FERRY_TRY(cudaMemcpyAsync(x->h_sizes + x->cfg.rank, x->d_sizes + x->cfg.rank, 8,
@@ -312,24 +317,30 @@ int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out) {
     FERRY_TRY(cudaMemcpyAsync(x->h_sizes, x->d_sizes, (size_t)x->cfg.world * 8, cudaMemcpyDeviceToHost, st));
     FERRY_TRY(cudaStreamSynchronize(st));
     const int64_t occ = n + x->h_sizes[x->cfg.rank];
-    if (occ < fair) {
+    if (forced || occ < fair) {
       int victim = -1;
       int64_t best = 0;
-      for (int r = 0; r < x->cfg.world; ++r) {
-        if (!x->peer_deque[r]) continue;
-        const int64_t ex = x->h_sizes[r] - fair;
-        if (ex > best) {
-          best = ex;
-          victim = r;
+      if (forced) {
+        if (x->force_victim >= 0 && x->force_victim < x->cfg.world && x->peer_deque[x->force_victim])
+          victim = x->force_victim;
+      } else {
+        for (int r = 0; r < x->cfg.world; ++r) {
+          if (!x->peer_deque[r]) continue;
+          const int64_t ex = x->h_sizes[r] - fair;
+          if (ex > best) {
+            best = ex;
+            victim = r;
+          }
         }
       }
       if (victim >= 0) {
         const int64_t cur = x->h_sizes[victim];
-        int64_t take = std::min<int64_t>(x->cfg.steal_batch, std::min<int64_t>(cur - fair, cur / 2 + 1));
+        int64_t take = forced ? std::min<int64_t>(std::min<int64_t>(x->force_take, x->cfg.steal_batch), cur)
+                              : std::min<int64_t>(x->cfg.steal_batch, std::min<int64_t>(cur - fair, cur / 2 + 1));
         take = std::min<int64_t>(take, B - n);
         take = std::min<int64_t>(take, (int64_t)x->free_slots.size());
         const ferry_peer& vp = x->ctx->peers[x->peer_slot[victim]];
-        if (take > 0 && x->pol.cost_filter && vp.size) {
+        if (take > 0 && !forced && x->pol.cost_filter && vp.size) {
           // price the tasks the steal would take: remaining steps x step time
           // against moving their resident pages (policy E)
           if ((rc = ferry_deque_peek(x->peer_deque[victim], st, x->d_tasks + n, (int)take, x->d_cnt + 3))) return rc;
@@ -368,6 +379,7 @@ int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out) {
           for (int i = 0; i < got; ++i) {
             const uint64_t t = x->h_tasks[n + i];
             const int s = alloc_slot(x, task_req(t));
+            x->slot_step[s] = (int)task_step(t);
             x->h_mig[i] = task_slot(t);
             x->h_mig[S + i] = s;
             x->h_tasks[n + i] = task_pack((uint64_t)task_req(t), (uint64_t)s, (uint64_t)task_step(t));
@@ -389,6 +401,7 @@ int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out) {
       }
     }
   }
+  x->force_take = 0;  // an order lasts one tick
   // 4. decode the batch
   if (n > 0) {
     for (int i = 0; i < n; ++i) x->h_ids[i] = task_slot(x->h_tasks[i]);
@@ -405,6 +418,7 @@ int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out) {
     const uint64_t t = x->h_tasks[i];
     if (task_step(t) + 1 < x->cfg.steps_per_req) {
       x->h_push[np++] = task_pack((uint64_t)task_req(t), (uint64_t)task_slot(t), (uint64_t)task_step(t) + 1);
+      x->slot_step[task_slot(t)] = (int)task_step(t) + 1;
     } else {
       release_slot(x, task_slot(t));
       ++ts.finished;
@@ -454,6 +468,28 @@ int ferry_steal_filter(const ferry_steal_policy* pol, int n, const int32_t* rema
       open = false;  // the accepted candidates are a prefix
   }
   *n_accept = ok;
+  return FERRY_OK;
+}
+
+int ferry_exec_usage(ferry_exec* x, int64_t* remaining_steps, int32_t* requests) {
+  if (!x || !remaining_steps || !requests) return set_error("exec_usage: bad arguments"), FERRY_E_INVAL;
+  int64_t u = 0;
+  int32_t n = 0;
+  for (size_t s = 0; s < x->slot_req.size(); ++s)
+    if (x->slot_req[s] >= 0) {
+      u += std::max(0, x->cfg.steps_per_req - x->slot_step[s]);
+      ++n;
+    }
+  *remaining_steps = u;
+  *requests = n;
+  return FERRY_OK;
+}
+
+int ferry_exec_rebalance(ferry_exec* x, int victim_rank, int k) {
+  if (!x || victim_rank < 0 || victim_rank >= x->cfg.world || victim_rank == x->cfg.rank || k < 0)
+    return set_error("exec_rebalance: bad arguments"), FERRY_E_INVAL;
+  x->force_victim = victim_rank;
+  x->force_take = k;
   return FERRY_OK;
 }
 

@@ -356,6 +356,14 @@ typedef struct ferry_steal_policy {
   double fixed_ms;    /* per-migration fixed cost (reference kMigDeltaFixedMs 0.06) */
 } ferry_steal_policy;
 int ferry_exec_policy(ferry_exec* x, const ferry_steal_policy* policy);
+/* Load of this GPU: remaining decode steps summed over its requests, and the
+ * request count (the rebalancer's usage, rebalance_llumnix,
+ * wla_multigpu.cuh:2084-2112). */
+int ferry_exec_usage(ferry_exec* x, int64_t* remaining_steps, int32_t* requests);
+/* A rebalance order: at the next tick steal up to k (<= steal_batch) tasks
+ * from victim_rank and migrate their requests, whatever the water level and
+ * without the cost filter (the reference's rebalancer path). */
+int ferry_exec_rebalance(ferry_exec* x, int victim_rank, int k);
 /* The filter alone (host, no GPU): value_ms / cost_ms per candidate
  * (nullable) and the length of the accepted prefix. */
 int ferry_steal_filter(const ferry_steal_policy* policy, int n, const int32_t* remain_steps,

@@ -184,3 +184,23 @@ def test_a_rank_that_leaves_ends_the_exchange_with_an_error():
             if p.is_alive():
                 p.kill()
     assert res[1] == "left" and res[0] != "no error"
+
+
+def test_llx_plan_matches_the_rebalancer_rule():
+    """rebalance_llumnix (wla_multigpu.cuh:2084-2112): spread / mean > thr ->
+    the least loaded pulls clamp((usage[src] - mean) // (mean // n_src + 1), 1, 4)."""
+    from ferry_b200.cluster import llx_plan
+
+    # usage 120 / 0 / 60, mean 60, spread 2.0 > 0.25; per = 60 // 4 + 1 = 16; k = 60 // 16 = 3
+    assert llx_plan([120, 0, 60], [4, 0, 2]) == (0, 1, 3)
+    # balanced within the threshold: nothing to do
+    assert llx_plan([100, 90, 95], [5, 5, 5]) is None
+    # the pull is capped at 4 and floored at 1
+    assert llx_plan([1000, 0], [40, 0]) == (0, 1, 4)   # per = 500 // 40 + 1 = 13, 500 // 13 = 38
+    assert llx_plan([1000, 0], [2, 0]) == (0, 1, 1)    # per = 251, 500 // 251 = 1
+    assert llx_plan([10, 0], [10, 0]) == (0, 1, 4)     # per = 1, k = 5 -> 4
+    assert llx_plan([3, 1], [1, 1]) == (0, 1, 1)       # over 1 < per 3: floored at 1
+    # idle job, single GPU
+    assert llx_plan([0, 0], [0, 0]) is None and llx_plan([50], [3]) is None
+    # ties: the first maximum and the first minimum, as the reference's strict comparisons
+    assert llx_plan([80, 80, 0, 0], [2, 2, 0, 0])[:2] == (0, 2)

@@ -290,7 +290,7 @@ def test_migrate_over_cuda_ipc(torch_cuda):
 # --------------------------------------------------------------------------- executor
 
 
-def _cluster_worker(rank, world, port, devices, out, policy=None):
+def _cluster_worker(rank, world, port, devices, out, policy=None, llx=None):
     import os
 
     import torch
@@ -315,10 +315,10 @@ def _cluster_worker(rank, world, port, devices, out, policy=None):
     runner = RankRunner(w, total, world, rank, devices[rank], slots=total + 4, max_batch=4,
                         steal_batch=4, migrate_mode=_abi.MIGRATE_FULL, policy=pol)
     try:
-        stats = runner.run(home, join, epoch=2, max_ticks=400)
+        stats = runner.run(home, join, epoch=2, max_ticks=400, llx=llx)
     finally:
         runner.close()
-    out.put((rank, stats.tokens, stats.stolen_tasks, stats.migrated_units, stats.ticks))
+    out.put((rank, stats.tokens, stats.stolen_tasks, stats.migrated_units, stats.ticks, stats.rebalances))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -349,7 +349,7 @@ def test_executor_two_ranks_steal_and_migrate(torch_cuda, policy):
             p.join(timeout=120)
             if p.is_alive():
                 p.kill()
-    (r0, tok0, st0, mig0, ticks0), (r1, tok1, st1, mig1, ticks1) = res
+    (r0, tok0, st0, mig0, ticks0, _), (r1, tok1, st1, mig1, ticks1, _) = res
     assert tok0 + tok1 == 12 * 6
     if policy is not None and policy > 1e9:
         assert st0 == st1 == 0 and tok1 == 0 and mig1 == 0   # every candidate priced out
@@ -359,3 +359,32 @@ def test_executor_two_ranks_steal_and_migrate(torch_cuda, policy):
     per_req = w.lanes_per_req * w.cache_pages
     assert mig1 == st1 * per_req and mig0 == st0 * per_req
     assert ticks0 == ticks1
+
+
+def test_executor_rebalance_orders_move_work(torch_cuda):
+    """The cost filter rejects every water-level candidate; only the
+    rebalancer's orders (usage exchanged with the ownership rows) move
+    requests to the idle rank, bypassing the filter as the reference's does."""
+    import socket
+
+    t = torch_cuda
+    devices = [0, 1] if t.cuda.device_count() > 1 else [0, 0]
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_cluster_worker, args=(r, 2, port, devices, q, 1e12, 0.25)) for r in range(2)]
+    for p in ps:
+        p.start()
+    try:
+        res = sorted(q.get(timeout=300) for _ in ps)
+    finally:
+        for p in ps:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    (r0, tok0, st0, mig0, ticks0, rb0), (r1, tok1, st1, mig1, ticks1, rb1) = res
+    assert tok0 + tok1 == 12 * 6
+    assert rb1 > 0 and st1 > 0 and tok1 > 0 and rb0 == 0

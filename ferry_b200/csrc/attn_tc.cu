@@ -42,7 +42,8 @@
 namespace ferry {
 namespace {
 
-constexpr int kTcThreads = 192;  // warps 0-3 softmax (TMEM lanes), 4 TMA producer, 5 MMA issuer
+constexpr int kTcThreads = 320;  // warps 0-7 softmax (two warpgroups on the TMEM lanes), 8 TMA producer, 9 MMA issuer
+constexpr int kSoftmaxWarps = 8;
 constexpr int kTcPages = 8;      // pages per group: 128 tokens
 constexpr int kTcStages = 3;
 constexpr int kQP = 4096;            // the Q tile and each P tile
@@ -151,7 +152,7 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages];
   __shared__ __align__(8) uint64_t s_full[2], s_free[2], p_full[2], o_full[2], o_free[2], q_full;
-  __shared__ float red[2][4][8], qred[4][8];
+  __shared__ float red[2][kSoftmaxWarps][8], qred[kSoftmaxWarps][8];
   __shared__ uint32_t tmem_slot, s_flag, s_abort;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -171,11 +172,11 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&o_full[i], 1);
-      mbar_init(&s_free[i], 4);  // one arrival per softmax warp
-      mbar_init(&p_full[i], 4);
-      mbar_init(&o_free[i], 4);
+      mbar_init(&s_free[i], kSoftmaxWarps);  // one arrival per softmax warp
+      mbar_init(&p_full[i], kSoftmaxWarps);
+      mbar_init(&o_free[i], kSoftmaxWarps);
     }
-    mbar_init(&q_full, 4);
+    mbar_init(&q_full, kSoftmaxWarps);
     s_abort = 0;
     fence_mbar_init();
   }
@@ -219,7 +220,7 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
   uint32_t prod_j = 0;           // producer: groups issued
   uint64_t* mma_last = nullptr;  // MMA issuer: barrier of its last commit
   uint32_t mma_par = 0;
-  if (warp == 4) {
+  if (warp == kSoftmaxWarps) {
     // ================= producer: stage j of the group sequence into buffer j % 3
     uint32_t& j = prod_j;
     bool ok = true;
@@ -254,7 +255,7 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
     }
     if (!ok && lane == 0) atomicOr(&s_abort, 1u);
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == kSoftmaxWarps + 1) {
     // ================= MMA issuer (one thread)
     if (lane == 0) {
       constexpr uint32_t kIdQK = idesc_tc(F8, false, false), kIdPV = idesc_tc(F8, true, true);
@@ -315,59 +316,65 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
     }
     __syncwarp();
   } else {
-    // ================= softmax warps 0-3: thread t = TMEM lane t = token t (S) / dim t (O)
-    const int t = tid;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    // ================= softmax: warps 0-7, two warpgroups over the same 128
+    // TMEM lanes (thread t = TMEM lane t = token t for S, dim t for O); each
+    // warpgroup handles half of the q heads, h0 .. h0 + HG - 1
+    constexpr int HG = (G + 1) / 2;
+    const int wg = tid >> 7, t = tid & 127, h0 = wg * HG;
+    const bool wg_on = h0 < G;  // false only for G == 1, warpgroup 1
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     uint32_t j = 0;
     bool ok = true;
     for (int a = a_lo; in_range(a) && ok; ++a) {
       const Seg sg = segment(a);
       const int glo = sg.glo, ghi = sg.ghi, n = sg.n;
       const int64_t base = (int64_t)a * A.gpl;
-      float m_run[G], l_thr[G], o_acc[G], qdiv[G], alpha_prev[G];
+      float m_run[HG], l_thr[HG], o_acc[HG], qdiv[HG], alpha_prev[HG];
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        m_run[h] = -INFINITY;
-        l_thr[h] = 0.f;
-        o_acc[h] = 0.f;
-        qdiv[h] = 0.f;
-        alpha_prev[h] = 0.f;
+      for (int hh = 0; hh < HG; ++hh) {
+        m_run[hh] = -INFINITY;
+        l_thr[hh] = 0.f;
+        o_acc[hh] = 0.f;
+        qdiv[hh] = A.qscale;
+        alpha_prev[hh] = 0.f;
       }
       float beta_prev = 1.f;
       if (glo < ghi && !F8) {
         // ---- Q of this lane as f16 rows (K-major, SWIZZLE_128B, two 64-dim
         // blocks 2 KiB apart): thread t = dim t
+        if (wg_on)
 #pragma unroll
-        for (int h = 0; h < G; ++h) {
-          *reinterpret_cast<uint16_t*>(Qt + (t >> 6) * 2048 + sw128(h, (t & 63) * 2)) =
-              A.q[((size_t)a * G + h) * kHeadDim + t];
-          qdiv[h] = A.qscale;
-        }
+          for (int hh = 0; hh < HG; ++hh)
+            *reinterpret_cast<uint16_t*>(Qt + (t >> 6) * 2048 + sw128(h0 + hh, (t & 63) * 2)) =
+                A.q[((size_t)a * G + h0 + hh) * kHeadDim + t];
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&q_full);
       }
       if (glo < ghi && F8) {
         // ---- Q terms of this lane: thread t = dim t; per-head power-of-two scale
-        float qf[G];
+        float qf[HG];
 #pragma unroll
-        for (int h = 0; h < G; ++h) {
-          qf[h] = __half2float(__ushort_as_half(A.q[((size_t)a * G + h) * kHeadDim + t]));
-          float x = fabsf(qf[h]);
+        for (int hh = 0; hh < HG; ++hh) {
+          qf[hh] = wg_on ? __half2float(__ushort_as_half(A.q[((size_t)a * G + h0 + hh) * kHeadDim + t])) : 0.f;
+          float x = fabsf(qf[hh]);
 #pragma unroll
           for (int off = 16; off >= 1; off >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, off));
-          if (lane == 0) qred[warp][h] = x;
+          if (lane == 0) qred[warp][hh] = x;
         }
         softmax_bar_or(false);
 #pragma unroll
-        for (int h = 0; h < G; ++h) {
-          const float am = fmaxf(fmaxf(qred[0][h], qred[1][h]), fmaxf(qred[2][h], qred[3][h]));
+        for (int hh = 0; hh < HG; ++hh) {
+          const float am = fmaxf(fmaxf(qred[wg * 4][hh], qred[wg * 4 + 1][hh]),
+                                 fmaxf(qred[wg * 4 + 2][hh], qred[wg * 4 + 3][hh]));
           const float sc = pow2_scale(am);
-          qdiv[h] = A.qscale / sc;  // score = (S0 + S1/16 + S2/256) * k_scale * qdiv
-          uint8_t tt[3];
-          split3(qf[h] * sc, tt);
+          qdiv[hh] = A.qscale / sc;  // score = (S0 + S1/16 + S2/256) * k_scale * qdiv
+          if (wg_on) {
+            uint8_t tt[3];
+            split3(qf[hh] * sc, tt);
 #pragma unroll
-          for (int jj = 0; jj < 3; ++jj) Qt[sw128(jj * 8 + h, t)] = tt[jj];
+            for (int jj = 0; jj < 3; ++jj) Qt[sw128(jj * 8 + h0 + hh, t)] = tt[jj];
+          }
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -379,11 +386,12 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
         ok = __all_sync(0xffffffffu, mbar_wait(&o_full[bi], (i >> 1) & 1u, A.err));
         if (!ok) return;
         tc_fence_after();
-        float o0[8], o1[8], o2[8];
-        tmem_ld8(tmem + 64 + bi * 32 + lane_off, o0);  // thread t = head dim t
+        // thread t = head dim t; this warpgroup's heads only
+        float o0[HG], o1[HG], o2[HG];
+        tmem_ld_n<HG>(tmem + 64 + bi * 32 + lane_off + h0, o0);
         if constexpr (F8) {
-          tmem_ld8(tmem + 64 + bi * 32 + lane_off + 8, o1);
-          tmem_ld8(tmem + 64 + bi * 32 + lane_off + 16, o2);
+          tmem_ld_n<HG>(tmem + 64 + bi * 32 + lane_off + 8 + h0, o1);
+          tmem_ld_n<HG>(tmem + 64 + bi * 32 + lane_off + 16 + h0, o2);
         }
         tmem_wait_ld();
         tc_fence_before();
@@ -391,21 +399,24 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
         if (lane == 0) mbar_arrive(&o_free[bi]);
         const float ib = __frcp_rn(beta_prev);  // exact: a power of two
 #pragma unroll
-        for (int h = 0; h < G; ++h)
-          o_acc[h] = o_acc[h] * alpha_prev[h] + (F8 ? (o0[h] + o1[h] * 0.0625f + o2[h] * 0.00390625f) * ib : o0[h]);
+        for (int hh = 0; hh < HG; ++hh) {
+          const float v = F8 ? (o0[hh] + o1[hh] * 0.0625f + o2[hh] * 0.00390625f) * ib : o0[hh];
+          o_acc[hh] = o_acc[hh] * alpha_prev[hh] + v;
+        }
       };
       for (int g = glo; g < ghi; ++g, ++j) {
         const int s = j % kTcStages, b = j & 1;
         const int np = min(kTcPages, n - g * kTcPages);
         // ---- S of this group (its buffer is released as soon as it is read)
-        ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (j >> 1) & 1u, A.err));
-        float s0[8], s1[8], s2[8];
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (j >> 1) & 1u, A.err));  // a failed fold stays failed
+        float s0[HG], s1[HG], s2[HG];
         if (ok) {
           tc_fence_after();
-          tmem_ld8(tmem + b * 32 + lane_off, s0);  // columns jj*8 + h: term jj of head h
+          // columns jj*8 + h: term jj of head h; this warpgroup's heads only
+          tmem_ld_n<HG>(tmem + b * 32 + lane_off + h0, s0);
           if constexpr (F8) {
-            tmem_ld8(tmem + b * 32 + lane_off + 8, s1);
-            tmem_ld8(tmem + b * 32 + lane_off + 16, s2);
+            tmem_ld_n<HG>(tmem + b * 32 + lane_off + 8 + h0, s1);
+            tmem_ld_n<HG>(tmem + b * 32 + lane_off + 16 + h0, s2);
           }
           tmem_wait_ld();
           tc_fence_before();
@@ -417,16 +428,16 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
         const bool valid = pg < np;
         const float ks = F8 ? *reinterpret_cast<const float*>(scl + s * kScl + pg * 16) : 1.f;
         const float vs = F8 ? *reinterpret_cast<const float*>(scl + s * kScl + pg * 16 + 4) : 1.f;
-        float x[G], mx[G];
+        float x[HG], mx[HG];
 #pragma unroll
-        for (int h = 0; h < G; ++h) {
-          const float sc = F8 ? (s0[h] + s1[h] * 0.0625f + s2[h] * 0.00390625f) * ks : s0[h];
-          x[h] = valid && ok ? sc * qdiv[h] : -INFINITY;
-          mx[h] = x[h];
+        for (int hh = 0; hh < HG; ++hh) {
+          const float sc = F8 ? (s0[hh] + s1[hh] * 0.0625f + s2[hh] * 0.00390625f) * ks : s0[hh];
+          x[hh] = valid && ok && wg_on ? sc * qdiv[hh] : -INFINITY;
+          mx[hh] = x[hh];
         }
         {
-          const float wm = warp_max_heads<G>(mx, lane);  // head (lane >> (5 - log2 G))
-          if ((lane & ((32 / G) - 1)) == 0) red[b][warp][lane / (32 / G)] = wm;
+          const float wm = warp_max_heads<HG>(mx, lane);  // head (lane >> (5 - log2 HG)) of the group
+          if ((lane & ((32 / HG) - 1)) == 0) red[b][warp][lane / (32 / HG)] = wm;
         }
         // power-of-two scale of the weights: p * v_scale * beta <= 448 in this group
         float beta = 1.f;
@@ -441,45 +452,56 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
           ok = false;
           break;
         }
-        // block maximum per head: lane l takes warp l / 8, head l % 8
-        float gmx = red[b][(lane >> 3) & 3][lane & 7];
+        // block maximum per head of this warpgroup: lane l takes warp l / 8
+        // of the group, head l % 8
+        float gmx = red[b][wg * 4 + ((lane >> 3) & 3)][lane & 7];
         gmx = fmaxf(gmx, __shfl_xor_sync(0xffffffffu, gmx, 8));
         gmx = fmaxf(gmx, __shfl_xor_sync(0xffffffffu, gmx, 16));
-        float alpha[G], pw[G];
+        float alpha[HG], pw[HG];
 #pragma unroll
-        for (int h = 0; h < G; ++h) {
-          const float mn = fmaxf(m_run[h], __shfl_sync(0xffffffffu, gmx, h));
-          alpha[h] = ex2(m_run[h] - mn);
-          const float p = valid ? ex2(x[h] - mn) : 0.f;
-          l_thr[h] = l_thr[h] * alpha[h] + p;
-          m_run[h] = mn;
-          pw[h] = p * vs * beta;
+        for (int hh = 0; hh < HG; ++hh) {
+          const float mn = fmaxf(m_run[hh], __shfl_sync(0xffffffffu, gmx, hh));
+          alpha[hh] = ex2(m_run[hh] - mn);
+          const float p = valid && wg_on ? ex2(x[hh] - mn) : 0.f;
+          l_thr[hh] = l_thr[hh] * alpha[hh] + p;
+          m_run[hh] = mn;
+          pw[hh] = p * vs * beta;
         }
-        // this token's row of P[b] (MN-major, no swizzle): byte jj*8 + h =
-        // term jj of head h. P[b]'s last reader, the PV two groups back, was
-        // folded a group ago.
+        // this token's row of P[b] (MN-major, no swizzle). e4m3: byte jj*8 + h
+        // = term jj of head h; f16: element h. Each warpgroup writes its heads'
+        // bytes; the rest of the row stays zero. P[b]'s last reader, the PV
+        // two groups back, was folded a group ago.
         uint8_t* row = Pt + b * kQP + (t >> 3) * 256 + (t & 7) * 16;
-        if constexpr (F8) {
-          uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (wg_on) {
+          if constexpr (F8) {
+            uint32_t tw[3] = {0, 0, 0};
 #pragma unroll
-          for (int i = 0; i < (G + 1) / 2; ++i) {
-            uint32_t t0, t1, t2;
-            split3x2(make_float2(pw[2 * i], 2 * i + 1 < G ? pw[2 * i + 1] : 0.f), t0, t1, t2);
-            const int sh = 16 * (i & 1);
-            w[(i >> 1)] |= t0 << sh;
-            w[2 + (i >> 1)] |= t1 << sh;
-            w[4 + (i >> 1)] |= t2 << sh;
-          }
-          *reinterpret_cast<uint4*>(row) = make_uint4(w[0], w[1], w[2], w[3]);
-          *reinterpret_cast<uint4*>(row + 128) = make_uint4(w[4], w[5], w[6], w[7]);
-        } else {  // f16 weights of heads 0-7 (the second chunk, heads 8-15, stays zero)
-          uint32_t w[4] = {0, 0, 0, 0};
+            for (int i = 0; i < (HG + 1) / 2; ++i) {
+              uint32_t t0, t1, t2;
+              split3x2(make_float2(pw[2 * i], 2 * i + 1 < HG ? pw[2 * i + 1] : 0.f), t0, t1, t2);
+              tw[0] |= t0 << (16 * i);
+              tw[1] |= t1 << (16 * i);
+              tw[2] |= t2 << (16 * i);
+            }
 #pragma unroll
-          for (int i = 0; i < (G + 1) / 2; ++i) {
-            const __half2 hv = __floats2half2_rn(pw[2 * i], 2 * i + 1 < G ? pw[2 * i + 1] : 0.f);
-            w[i] = *reinterpret_cast<const uint32_t*>(&hv);
+            for (int jj = 0; jj < 3; ++jj) {
+              uint8_t* dst = row + (jj >> 1) * 128 + (jj & 1) * 8 + h0;
+              if (HG == 4) *reinterpret_cast<uint32_t*>(dst) = tw[jj];
+              else if (HG == 2) *reinterpret_cast<uint16_t*>(dst) = (uint16_t)tw[jj];
+              else *dst = (uint8_t)tw[jj];
+            }
+          } else {
+            uint32_t w[2] = {0, 0};
+#pragma unroll
+            for (int i = 0; i < (HG + 1) / 2; ++i) {
+              const __half2 hv = __floats2half2_rn(pw[2 * i], 2 * i + 1 < HG ? pw[2 * i + 1] : 0.f);
+              w[i] = *reinterpret_cast<const uint32_t*>(&hv);
+            }
+            uint8_t* dst = row + h0 * 2;
+            if (HG == 4) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+            else if (HG == 2) *reinterpret_cast<uint32_t*>(dst) = w[0];
+            else *reinterpret_cast<uint16_t*>(dst) = (uint16_t)w[0];
           }
-          *reinterpret_cast<uint4*>(row) = make_uint4(w[0], w[1], w[2], w[3]);
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -488,7 +510,7 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
         // the next group's barrier, which every softmax warp reaches)
         if (g > glo && ok) fold(j - 1);
 #pragma unroll
-        for (int h = 0; h < G; ++h) alpha_prev[h] = alpha[h];
+        for (int hh = 0; hh < HG; ++hh) alpha_prev[hh] = alpha[hh];
         beta_prev = beta;
       }
       if (ok && glo < ghi) fold(j - 1);
@@ -501,31 +523,33 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
       const int parts = cta_of(base + A.gpl - 1, A.nc, A.T) - cf + 1;
       float* pc = A.part + ((size_t)a + c) * G * kPartStride;
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        float l = l_thr[h];
+      for (int hh = 0; hh < HG; ++hh) {
+        float l = l_thr[hh];
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-        if (lane == 0) qred[warp][h] = l;
-        pc[h * kPartStride + t] = o_acc[h];
+        if (lane == 0) qred[warp][hh] = l;
+        if (wg_on) pc[(h0 + hh) * kPartStride + t] = o_acc[hh];
       }
       softmax_bar_or(false);
-      if (t < G) {
+      if (wg_on && t < HG) {
+        const int h = h0 + t;
         float mv = m_run[0];
 #pragma unroll
-        for (int h = 1; h < G; ++h) mv = t == h ? m_run[h] : mv;
-        pc[t * kPartStride + 128] = mv;
-        pc[t * kPartStride + 129] = qred[0][t] + qred[1][t] + qred[2][t] + qred[3][t];
+        for (int hh = 1; hh < HG; ++hh) mv = t == hh ? m_run[hh] : mv;
+        pc[h * kPartStride + 128] = mv;
+        pc[h * kPartStride + 129] = qred[wg * 4][t] + qred[wg * 4 + 1][t] + qred[wg * 4 + 2][t] + qred[wg * 4 + 3][t];
       }
       __threadfence();
       softmax_bar_or(false);
-      if (t == 0) s_flag = atomicAdd(&A.lane_done[a], 1u) == (uint32_t)(parts - 1);
+      if (tid == 0) s_flag = atomicAdd(&A.lane_done[a], 1u) == (uint32_t)(parts - 1);
       softmax_bar_or(false);
-      if (s_flag) {
-        // combine: thread t = dim t of every head
+      if (s_flag && wg_on) {
+        // combine: thread t = dim t of this warpgroup's heads
         __threadfence();
         const float* pl = A.part + ((size_t)a + cf) * G * kPartStride;
 #pragma unroll
-        for (int h = 0; h < G; ++h) {
+        for (int hh = 0; hh < HG; ++hh) {
+          const int h = h0 + hh;
           float M = -INFINITY;
           for (int jj = 0; jj < parts; ++jj) M = fmaxf(M, __ldcg(pl + ((size_t)jj * G + h) * kPartStride + 128));
           float L = 0.f, O = 0.f;
@@ -538,20 +562,20 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
           }
           A.out[((size_t)a * G + h) * kHeadDim + t] = L > 0.f ? O / L : 0.f;
         }
-        if (t == 0) A.lane_done[a] = 0;
       }
+      if (s_flag && tid == 0) A.lane_done[a] = 0;
       softmax_bar_or(false);  // qred / s_flag reusable
     }
-    if (!ok && t == 0) atomicOr(&s_abort, 1u);
+    if (!ok && tid == 0) atomicOr(&s_abort, 1u);
   }
   tc_fence_before();
   __syncthreads();
   if (s_abort) {
     // a wait gave up: let the copies and MMAs still in flight land (bounded)
-    if (warp == 4 && lane == 0)
+    if (warp == kSoftmaxWarps && lane == 0)
       for (uint32_t i = prod_j > (uint32_t)kTcStages ? prod_j - kTcStages : 0; i < prod_j; ++i)
         mbar_wait(&full[i % kTcStages], (i / kTcStages) & 1u, nullptr);
-    if (warp == 5 && lane == 0 && mma_last) mbar_wait(mma_last, mma_par, nullptr);  // MMAs complete in order
+    if (warp == kSoftmaxWarps + 1 && lane == 0 && mma_last) mbar_wait(mma_last, mma_par, nullptr);  // MMAs complete in order
     __syncthreads();
   }
   if (warp == 0)

@@ -113,16 +113,40 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
+// N consecutive f32 columns (N = 1, 2, 4 or 8) of this thread's TMEM lane
+template <int N>
+__device__ __forceinline__ void tmem_ld_n(uint32_t taddr, float* v) {
+  if constexpr (N == 8) {
+    tmem_ld8(taddr, v);
+  } else if constexpr (N == 4) {
+    uint32_t r[4];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
+  } else if constexpr (N == 2) {
+    uint32_t r[2];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(taddr));
+    v[0] = __uint_as_float(r[0]);
+    v[1] = __uint_as_float(r[1]);
+  } else {
+    static_assert(N == 1, "tmem_ld_n: N is 1, 2, 4 or 8");
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+    v[0] = __uint_as_float(r);
+  }
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// barrier among the 128 softmax threads only (named barrier 1); true when
+// barrier among the 256 softmax threads only (named barrier 1); true when
 // any of them passed `flag`
 __device__ __forceinline__ bool softmax_bar_or(bool flag) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, 128, p;\n\t"
+      "bar.red.or.pred q, 1, 256, p;\n\t"
       "selp.u32 %0, 1, 0, q;\n\t}"
       : "=r"(r)
       : "r"((uint32_t)flag)

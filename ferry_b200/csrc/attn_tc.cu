@@ -428,16 +428,17 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
         const bool valid = pg < np;
         const float ks = F8 ? *reinterpret_cast<const float*>(scl + s * kScl + pg * 16) : 1.f;
         const float vs = F8 ? *reinterpret_cast<const float*>(scl + s * kScl + pg * 16 + 4) : 1.f;
-        float x[HG], mx[HG];
+        // weights against the running max of each head, taken as final when
+        // no score of the group exceeds it: then the block update gives the
+        // same max and alpha = ex2(0) = 1, bit for bit
+        float x[HG], pf[HG];
+        bool raise = false;
 #pragma unroll
         for (int hh = 0; hh < HG; ++hh) {
           const float sc = F8 ? (s0[hh] + s1[hh] * 0.0625f + s2[hh] * 0.00390625f) * ks : s0[hh];
           x[hh] = valid && ok && wg_on ? sc * qdiv[hh] : -INFINITY;
-          mx[hh] = x[hh];
-        }
-        {
-          const float wm = warp_max_heads<HG>(mx, lane);  // head (lane >> (5 - log2 HG)) of the group
-          if ((lane & ((32 / HG) - 1)) == 0) red[b][warp][lane / (32 / HG)] = wm;
+          raise |= x[hh] > m_run[hh];
+          pf[hh] = valid && wg_on ? ex2(x[hh] - m_run[hh]) : 0.f;
         }
         // power-of-two scale of the weights: p * v_scale * beta <= 448 in this group
         float beta = 1.f;
@@ -448,24 +449,38 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
           vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 4));
           beta = pow2_scale(__shfl_sync(0xffffffffu, vmax, 0));
         }
-        if (softmax_bar_or(!ok)) {
-          ok = false;
-          break;
-        }
-        // block maximum per head of this warpgroup: lane l takes warp l / 8
-        // of the group, head l % 8
-        float gmx = red[b][wg * 4 + ((lane >> 3) & 3)][lane & 7];
-        gmx = fmaxf(gmx, __shfl_xor_sync(0xffffffffu, gmx, 8));
-        gmx = fmaxf(gmx, __shfl_xor_sync(0xffffffffu, gmx, 16));
         float alpha[HG], pw[HG];
+        if (softmax_bar_or(!ok || raise)) {
+          // some score raises a running max (or a wait gave up): block
+          // maximum per head of this warpgroup, lane l takes warp l / 8 of
+          // the group, head l % 8
+          float mx[HG];
+#pragma unroll
+          for (int hh = 0; hh < HG; ++hh) mx[hh] = x[hh];
+          const float wm = warp_max_heads<HG>(mx, lane);  // head (lane >> (5 - log2 HG)) of the group
+          if ((lane & ((32 / HG) - 1)) == 0) red[b][warp][lane / (32 / HG)] = wm;
+          if (softmax_bar_or(!ok)) {
+            ok = false;
+            break;
+          }
+          float gmx = red[b][wg * 4 + ((lane >> 3) & 3)][lane & 7];
+          gmx = fmaxf(gmx, __shfl_xor_sync(0xffffffffu, gmx, 8));
+          gmx = fmaxf(gmx, __shfl_xor_sync(0xffffffffu, gmx, 16));
+#pragma unroll
+          for (int hh = 0; hh < HG; ++hh) {
+            const float mn = fmaxf(m_run[hh], __shfl_sync(0xffffffffu, gmx, hh));
+            alpha[hh] = ex2(m_run[hh] - mn);
+            pf[hh] = valid && wg_on ? ex2(x[hh] - mn) : 0.f;
+            m_run[hh] = mn;
+          }
+        } else {
+#pragma unroll
+          for (int hh = 0; hh < HG; ++hh) alpha[hh] = 1.f;
+        }
 #pragma unroll
         for (int hh = 0; hh < HG; ++hh) {
-          const float mn = fmaxf(m_run[hh], __shfl_sync(0xffffffffu, gmx, hh));
-          alpha[hh] = ex2(m_run[hh] - mn);
-          const float p = valid && wg_on ? ex2(x[hh] - mn) : 0.f;
-          l_thr[hh] = l_thr[hh] * alpha[hh] + p;
-          m_run[hh] = mn;
-          pw[hh] = p * vs * beta;
+          l_thr[hh] = l_thr[hh] * alpha[hh] + pf[hh];
+          pw[hh] = pf[hh] * vs * beta;
         }
         // this token's row of P[b] (MN-major, no swizzle). e4m3: byte jj*8 + h
         // = term jj of head h; f16: element h. Each warpgroup writes its heads'

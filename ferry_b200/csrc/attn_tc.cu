@@ -46,6 +46,9 @@ constexpr int kTcThreads = 320;  // warps 0-7 softmax (two warpgroups on the TME
 constexpr int kSoftmaxWarps = 8;
 constexpr int kTcPages = 8;      // pages per group: 128 tokens
 constexpr int kTcStages = 3;
+// each mbarrier probe may suspend a waiting warp this long (it wakes when the
+// phase completes): idle roles stop taking issue slots from the softmax warps
+constexpr uint32_t kWaitHintNs = 20000;
 constexpr int kQP = 4096;            // the Q tile and each P tile
 constexpr int kScl = kTcPages * 16;  // e4m3: 16 B per page (k_scale, v_scale, pad)
 constexpr uint32_t kTmemCols = 128;  // S[2] at cols 0, 32; O[2] at 64, 96
@@ -229,7 +232,7 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
       for (int g = sg.glo; g < sg.ghi; ++g, ++j) {
         const int s = j % kTcStages, np = min(kTcPages, sg.n - g * kTcPages);
         int slot = lane < np ? A.item_slot[(size_t)a * k + g * kTcPages + lane] : 0;
-        if (j >= (uint32_t)kTcStages) ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], ((j / kTcStages) - 1) & 1u, A.err));
+        if (j >= (uint32_t)kTcStages) ok = __all_sync(0xffffffffu, mbar_wait_sleep<kWaitHintNs>(&empty[s], ((j / kTcStages) - 1) & 1u, A.err));
         if (!ok) break;
         uint8_t* Ks = smem + s * Lay::kStage;
         if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(np * (F8 ? 2 * 2048 + 16 : 4 * 2048)));
@@ -265,8 +268,8 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
       uint32_t& last_par = mma_par;
       auto issue_pv = [&](uint32_t i) {
         const int bi = i & 1, si = i % kTcStages;
-        ok = ok && mbar_wait(&p_full[bi], (i >> 1) & 1u, A.err);
-        if (ok && i >= 2) ok = mbar_wait(&o_free[bi], ((i >> 1) - 1) & 1u, A.err);
+        ok = ok && mbar_wait_sleep<kWaitHintNs>(&p_full[bi], (i >> 1) & 1u, A.err);
+        if (ok && i >= 2) ok = mbar_wait_sleep<kWaitHintNs>(&o_free[bi], ((i >> 1) - 1) & 1u, A.err);
         if (!ok) return;
         tc_fence_after();
         const uint32_t sV = smem_addr(smem + si * Lay::kStage) + Lay::kHalf, sP = smem_addr(Pt + bi * kQP);
@@ -289,11 +292,11 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
           const int s = j % kTcStages, b = j & 1;
           if (g == sg.glo) {
             if (j > 0) issue_pv(j - 1);  // the previous segment's last group first
-            ok = ok && mbar_wait(&q_full, segs & 1u, A.err);
+            ok = ok && mbar_wait_sleep<kWaitHintNs>(&q_full, segs & 1u, A.err);
             ++segs;
           }
-          ok = ok && mbar_wait(&full[s], (j / kTcStages) & 1u, A.err);
-          if (ok && j >= 2) ok = mbar_wait(&s_free[b], ((j >> 1) - 1) & 1u, A.err);
+          ok = ok && mbar_wait_sleep<kWaitHintNs>(&full[s], (j / kTcStages) & 1u, A.err);
+          if (ok && j >= 2) ok = mbar_wait_sleep<kWaitHintNs>(&s_free[b], ((j >> 1) - 1) & 1u, A.err);
           if (!ok) break;
           tc_fence_after();
           const uint32_t sK = smem_addr(smem + s * Lay::kStage);
@@ -383,7 +386,7 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
       // fold of group i's PV (buffer i & 1) into o_acc
       auto fold = [&](uint32_t i) {
         const int bi = i & 1;
-        ok = __all_sync(0xffffffffu, mbar_wait(&o_full[bi], (i >> 1) & 1u, A.err));
+        ok = __all_sync(0xffffffffu, mbar_wait_sleep<kWaitHintNs>(&o_full[bi], (i >> 1) & 1u, A.err));
         if (!ok) return;
         tc_fence_after();
         // thread t = head dim t; this warpgroup's heads only
@@ -408,7 +411,7 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
         const int s = j % kTcStages, b = j & 1;
         const int np = min(kTcPages, n - g * kTcPages);
         // ---- S of this group (its buffer is released as soon as it is read)
-        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (j >> 1) & 1u, A.err));  // a failed fold stays failed
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait_sleep<kWaitHintNs>(&s_full[b], (j >> 1) & 1u, A.err));  // a failed fold stays failed
         float s0[HG], s1[HG], s2[HG];
         if (ok) {
           tc_fence_after();
@@ -422,7 +425,7 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&s_free[b]);
-          ok = mbar_wait(&full[s], (j / kTcStages) & 1u, A.err);  // the stage's scales
+          ok = mbar_wait_sleep<kWaitHintNs>(&full[s], (j / kTcStages) & 1u, A.err);  // the stage's scales
         }
         const int pg = t >> 4;
         const bool valid = pg < np;
@@ -589,8 +592,8 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
     // a wait gave up: let the copies and MMAs still in flight land (bounded)
     if (warp == kSoftmaxWarps && lane == 0)
       for (uint32_t i = prod_j > (uint32_t)kTcStages ? prod_j - kTcStages : 0; i < prod_j; ++i)
-        mbar_wait(&full[i % kTcStages], (i / kTcStages) & 1u, nullptr);
-    if (warp == kSoftmaxWarps + 1 && lane == 0 && mma_last) mbar_wait(mma_last, mma_par, nullptr);  // MMAs complete in order
+        mbar_wait_sleep<kWaitHintNs>(&full[i % kTcStages], (i / kTcStages) & 1u, nullptr);
+    if (warp == kSoftmaxWarps + 1 && lane == 0 && mma_last) mbar_wait_sleep<kWaitHintNs>(mma_last, mma_par, nullptr);  // MMAs complete in order
     __syncthreads();
   }
   if (warp == 0)

@@ -106,6 +106,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   return false;
 }
 
+// Bounded wait on an mbarrier phase in which each probe may suspend the warp
+// in hardware for up to hint_ns (woken early when the phase completes), so
+// that waiting warps leave their issue slots to the working ones. The probe
+// count is capped so the whole wait stays near a second.
+template <uint32_t kHintNs>
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t* err) {
+  constexpr uint32_t kProbes = (uint32_t)(1000000000ull / kHintNs);
+  for (uint32_t i = 0; i < kProbes; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(kHintNs)
+        : "memory");
+    if (ok) return true;
+  }
+  record_error(err, kErrTimeout);
+  return false;
+}
+
 // 1-D bulk async copy global -> shared (TMA engine), completion signalled on
 // the mbarrier as transaction bytes. dst, src 16-byte aligned; bytes % 16 == 0.
 __device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, uint32_t bytes,

@@ -82,10 +82,16 @@ __global__ void __launch_bounds__(256) gather_kernel(
 // a 2-stage shared-memory ring with 1-D bulk copies (load from the owner's
 // store, this GPU's HBM or a peer's over NVLink; then a bulk store into the
 // cache slot), one unit's load in flight while the previous one is stored.
-// Units without a mapped owner fall back to the warp's register copy from
-// the host pool.
-constexpr int kGtWarps = 8;
-constexpr int kGtSmem = kGtWarps * 2 * kUnitBytes;
+// Units without a mapped owner fall back to a plain copy from the host pool
+// (one 16-byte chunk per lane at a time: few registers, so that more warps,
+// each an independent bulk-copy issuer, fit on an SM).
+constexpr int kGtMaxWarps = 16;
+constexpr int kGtSmemBudget = 200 * 1024;
+
+// bytes of one ring stage: the unit rounded up to 128
+__host__ __device__ constexpr int gt_stride(int unit_bytes) { return (unit_bytes + 127) / 128 * 128; }
+// shared memory of one warp: two stages and their barriers
+constexpr int gt_warp_smem(int unit_bytes) { return 2 * gt_stride(unit_bytes) + 16; }
 
 __device__ __forceinline__ void bulk_store(void* dst_global, const void* src_smem, uint32_t bytes) {
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst_global),
@@ -97,23 +103,24 @@ __device__ __forceinline__ void bulk_store(void* dst_global, const void* src_sme
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-__global__ void __launch_bounds__(kGtWarps * 32, 1) gather_store_kernel(
+__global__ void __launch_bounds__(kGtMaxWarps * 32, 1) gather_store_kernel(
     const uint8_t* __restrict__ pool, uint64_t pool_units, uint8_t* __restrict__ cache, int N,
     int C, const int32_t* __restrict__ req_ids, int lanes_per_req, int64_t lanes_total,
     int n_lanes, const int32_t* __restrict__ miss_page, const int32_t* __restrict__ miss_slot,
     const int32_t* __restrict__ n_miss, int k, const int64_t* __restrict__ req_base, int unit_bytes,
     const __grid_constant__ OwnerMap own, unsigned long long* stats, uint32_t* err) {
   extern __shared__ __align__(128) uint8_t gsm[];
-  __shared__ __align__(8) uint64_t bars[kGtWarps][2];
-  const int t = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  uint8_t* ring = gsm + (size_t)warp * 2 * kUnitBytes;
+  const int t = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int stride = gt_stride(unit_bytes);
+  uint8_t* ring = gsm + (size_t)warp * 2 * stride;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gsm + (size_t)nwarps * 2 * stride) + warp * 2;
   if (t == 0) {
-    mbar_init(&bars[warp][0], 1);
-    mbar_init(&bars[warp][1], 1);
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
     fence_mbar_init();
   }
   __syncwarp();
-  const int64_t nw = (int64_t)gridDim.x * kGtWarps;
+  const int64_t nw = (int64_t)gridDim.x * nwarps;
   const int64_t total = (int64_t)n_lanes * k;
   uint32_t copied = 0, from_peer = 0, from_self = 0;
   uint32_t it = 0;           // units this warp sent through the ring
@@ -123,13 +130,13 @@ __global__ void __launch_bounds__(kGtWarps * 32, 1) gather_store_kernel(
   auto flush = [&]() {       // store the pending stage (lane 0)
     if (pend < 0) return;
     const uint32_t use = it - 1;  // the pending unit is the last one sent
-    if (mbar_wait(&bars[warp][pend], (use >> 1) & 1u, err))
-      bulk_store(pend_dst, ring + pend * kUnitBytes, (uint32_t)unit_bytes);
+    if (mbar_wait(&bars[pend], (use >> 1) & 1u, err))
+      bulk_store(pend_dst, ring + pend * stride, (uint32_t)unit_bytes);
     else
       ok = false;
     pend = -1;
   };
-  for (int64_t f = (int64_t)blockIdx.x * kGtWarps + warp; f < total && ok; f += nw) {
+  for (int64_t f = (int64_t)blockIdx.x * nwarps + warp; f < total && ok; f += nw) {
     const int a = (int)(f / k), i = (int)(f % k);
     if (i >= n_miss[a]) continue;  // warp-uniform
     const int page = miss_page[(size_t)a * k + i];
@@ -154,14 +161,14 @@ __global__ void __launch_bounds__(kGtWarps * 32, 1) gather_store_kernel(
       if (t == 0) {
         const int s = it & 1;
         bulk_wait_read();  // the store that last read stage s (the newest group) is done with it
-        mbar_arrive_expect_tx(&bars[warp][s], (uint32_t)unit_bytes);
-        bulk_load(ring + s * kUnitBytes, src, (uint32_t)unit_bytes, &bars[warp][s]);
+        mbar_arrive_expect_tx(&bars[s], (uint32_t)unit_bytes);
+        bulk_load(ring + s * stride, src, (uint32_t)unit_bytes, &bars[s]);
         ++it;
         const int ps = pend;
         uint8_t* pd = pend_dst;
         if (ps >= 0) {  // store the previous unit while this one loads
-          if (mbar_wait(&bars[warp][ps], ((it - 2) >> 1) & 1u, err))
-            bulk_store(pd, ring + ps * kUnitBytes, (uint32_t)unit_bytes);
+          if (mbar_wait(&bars[ps], ((it - 2) >> 1) & 1u, err))
+            bulk_store(pd, ring + ps * stride, (uint32_t)unit_bytes);
           else
             ok = false;
         }
@@ -170,14 +177,15 @@ __global__ void __launch_bounds__(kGtWarps * 32, 1) gather_store_kernel(
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
     } else {
-      warp_copy_unit(pool + ((uint64_t)(home + page) % pool_units) * unit_bytes, dst, unit_bytes, t);
+      const uint8_t* src = pool + ((uint64_t)(home + page) % pool_units) * unit_bytes;
+      for (int v = t; v < (unit_bytes >> 4); v += 32) st_v4(dst + (size_t)v * 16, ld_nc_v4(src + (size_t)v * 16));
     }
   }
   if (t == 0) {
     if (ok) flush();
     // drain: loads still in flight land (bounded), stores complete
     if (!ok)
-      for (uint32_t u = it >= 2 ? it - 2 : 0; u < it; ++u) mbar_wait(&bars[warp][u & 1], (u >> 1) & 1u, nullptr);
+      for (uint32_t u = it >= 2 ? it - 2 : 0; u < it; ++u) mbar_wait(&bars[u & 1], (u >> 1) & 1u, nullptr);
     bulk_wait_all();
   }
   __syncwarp();
@@ -215,9 +223,11 @@ int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, i
   const int n_lanes = n_req * c->lanes_per_req;
   const int64_t items = (int64_t)n_lanes * c->cfg.top_k;
   if (own.world > 0) {
-    FERRY_TRY(cudaFuncSetAttribute(gather_store_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGtSmem));
-    const int64_t blocks = std::min<int64_t>((items + kGtWarps - 1) / kGtWarps, (int64_t)c->num_sms);
-    gather_store_kernel<<<(unsigned)blocks, kGtWarps * 32, kGtSmem, st>>>(
+    const int warps = std::max(1, std::min(kGtMaxWarps, kGtSmemBudget / gt_warp_smem(c->unit_bytes)));
+    const int smem = warps * gt_warp_smem(c->unit_bytes);
+    FERRY_TRY(cudaFuncSetAttribute(gather_store_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    const int64_t blocks = std::min<int64_t>((items + warps - 1) / warps, (int64_t)c->num_sms);
+    gather_store_kernel<<<(unsigned)blocks, warps * 32, smem, st>>>(
         c->pool_dev, c->pool_units, c->cache, c->cfg.max_pages, c->cfg.cache_pages, req_ids,
         c->lanes_per_req, c->lanes, n_lanes, miss_page, miss_slot, n_miss, c->cfg.top_k, c->req_base,
         c->unit_bytes, own, c->stats, c->err);

@@ -54,17 +54,68 @@ def _ncu_traffic():
 
 
 class Clocks:
-    """Sample SM clocks and throttle reasons during the timed region."""
+    """Sample SM clocks and clock-event (throttle) reasons during the timed region.
+
+    NVML is read from a background thread every 5 ms (read-only queries: no GPU
+    setting is touched); the first sample is taken before the region starts and
+    a last one when it ends, so even a region of a few ms is covered. Falls
+    back to `nvidia-smi -lms 200` when NVML is not importable."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    PERIOD_S = 0.005
 
     def __init__(self, device_index: int):
         self.dev = device_index
         self.proc = None
+        self.thread = None
+        self.rows = []  # (sm_mhz, max_mhz, power_w, reason names)
+        self.out = ""
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        try:
+            pr = torch.cuda.get_device_properties(self.dev)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.dev)
+
+    def _sample(self, nv, h):
+        bits = (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)
+        r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        self.rows.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                          float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)),
+                          nv.nvmlDeviceGetPowerUsage(h) / 1e3,
+                          [n for n, bit in zip(self.NAMES, bits) if r & bit]))
 
     def __enter__(self):
+        import threading
+
+        try:
+            nv, h = self._nvml_handle()
+            self._sample(nv, h)
+            self.stop = threading.Event()
+
+            def loop():
+                while not self.stop.wait(self.PERIOD_S):
+                    try:
+                        self._sample(nv, h)
+                    except Exception:
+                        return
+
+            self.nv, self.h = nv, h
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.Q}",
@@ -75,7 +126,13 @@ class Clocks:
         return self
 
     def __exit__(self, *exc):
-        self.out = ""
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
+            try:
+                self._sample(self.nv, self.h)
+            except Exception:
+                pass
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -85,16 +142,24 @@ class Clocks:
         return False
 
     def summary(self):
-        rows = [r.split(",") for r in (self.out or "").strip().splitlines() if r.count(",") >= 8]
+        rows = list(self.rows)
+        for r in (self.out or "").strip().splitlines():
+            f = r.split(",")
+            if len(f) >= 9 and f[1].strip().replace(".", "").isdigit():
+                rows.append((float(f[1]), float(f[2]) if f[2].strip().replace(".", "").isdigit() else None,
+                             None, [n for i, n in enumerate(self.NAMES) if f[5 + i].strip() == "Active"]))
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
-        return {"sm_mhz": float(np.median(sm)) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
+        sm = [r[0] for r in rows]
+        mx = [r[1] for r in rows if r[1] is not None]
+        pw = [r[2] for r in rows if r[2] is not None]
+        reasons = sorted({n for r in rows for n in r[3]})
+        out = {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx) if mx else None,
+               "reasons": reasons, "samples": len(rows),
+               "source": "nvml" if self.rows else "nvidia-smi"}
+        if pw:
+            out["power_w_median"] = float(np.median(pw))
+        return out
 
 
 def _dist():
@@ -473,7 +538,8 @@ def run_cluster(args):
         return st, home
 
     job(args.warmup)
-    st, home = job(args.steps)
+    with Clocks(local) as clk:
+        st, home = job(args.steps)
     t = torch.tensor([st.device_ms, st.tokens, st.migrated_bytes, st.mig_ms, st.mig_event_bytes,
                       st.stolen_tasks, st.gathered_bytes], dtype=torch.float64, device=dev)
     mx, sm = t.clone(), t.clone()
@@ -496,7 +562,7 @@ def run_cluster(args):
                 "steal": {"stolen_tasks": int(sm[5]), "migrated_bytes": float(sm[2]),
                           "migration_GB_s": mig_gbs, "nvlink_peak_GB_s": 770.0,
                           "migration_frac": mig_gbs / 770.0 if mig_gbs else None},
-                "gathered_bytes": float(sm[6]), "ticks": st.ticks}
+                "gathered_bytes": float(sm[6]), "ticks": st.ticks, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     dist.barrier()
     dist.destroy_process_group()

@@ -44,6 +44,9 @@ struct LruArgs {
   int warp_ints;  // shared-memory ints per warp
 };
 
+constexpr int kLoadBatch = 8;
+constexpr int kLruRounds = 8;  // fixpoint rounds before the serial replay takes over
+
 __global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
   extern __shared__ int32_t smem_i[];
   const int t = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -86,20 +89,34 @@ __global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
   }
   const bool rst = A.reset && A.reset[a];
 
+  // the lane's tables arrive in batches of kLoadBatch loads per thread in
+  // flight (the tables are usually cold in L2 right after the selection)
   bool corrupt = false;
-  for (int j = t; j < sz0; j += 32) {
-    int o = od[j];
-    if (o < 0 || o >= C) {
-      corrupt = true;
-      o = 0;
+  for (int j0 = t; j0 < C; j0 += 32 * kLoadBatch) {
+    int vo[kLoadBatch], vs[kLoadBatch];
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int j = j0 + 32 * u;
+      vo[u] = j < sz0 ? __ldcg(od + j) : 0;
+      vs[u] = j < sz0 ? __ldcg(sp + j) : -1;
     }
-    old[j] = o;
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int j = j0 + 32 * u;
+      if (j < C) {
+        if (j < sz0) {
+          if (vo[u] < 0 || vo[u] >= C) {
+            corrupt = true;
+            vo[u] = 0;
+          }
+          old[j] = vo[u];
+        }
+        spg[j] = vs[u];
+        seq[j] = -1;
+      }
+    }
   }
   if (__any_sync(0xffffffffu, corrupt) && t == 0) record_error(A.err, kErrRange);
-  for (int s = t; s < C; s += 32) {
-    spg[s] = s < sz0 ? sp[s] : -1;
-    seq[s] = -1;
-  }
   __syncwarp();
   if (rst) {
     for (int s = t; s < sz0; s += 32) {
@@ -111,14 +128,30 @@ __global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
   }
   __syncwarp();
   bool bad = false;
-  for (int i = t; i < n; i += 32) {
-    int x = A.sel[(size_t)a * k + i];
-    if (x < 0 || x >= A.ids) {
-      bad = true;
-      x = -1;
+  for (int i0 = t; i0 < n; i0 += 32 * kLoadBatch) {
+    int vx[kLoadBatch], vp[kLoadBatch];
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int i = i0 + 32 * u;
+      vx[u] = i < n ? __ldcg(A.sel + (size_t)a * k + i) : -1;
     }
-    sel_s[i] = x;
-    islot[i] = (x >= 0 && !rst) ? ps[x] : -1;
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int i = i0 + 32 * u;
+      if (i < n && (vx[u] < 0 || vx[u] >= A.ids)) {
+        bad = true;
+        vx[u] = -1;
+      }
+      vp[u] = (vx[u] >= 0 && !rst) ? __ldcg(ps + vx[u]) : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int i = i0 + 32 * u;
+      if (i < n) {
+        sel_s[i] = vx[u];
+        islot[i] = vp[u];
+      }
+    }
   }
   if (__any_sync(0xffffffffu, bad) && t == 0) record_error(A.err, kErrRange);
   __syncwarp();
@@ -139,40 +172,115 @@ __global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
 
   int p = 0, qn = 0, nn = 0, sz = sz0, ne = 0;
   bool done = false;
-  // ---- distinct selections, warp-parallel: a hit keeps its slot, the r-th
-  // miss takes slot sz0 + r while free slots last, else the slot of old-order
-  // entry r - free. This is the sequential result whenever no page touched in
-  // this step is evicted within it, i.e. none of the first E entries of the
-  // old order (E = evictions) is touched; otherwise the serial replay runs.
+  // ---- distinct selections, warp-parallel. Times are ranks among the valid
+  // items. Once the f free slots are used a miss evicts: eviction e happens
+  // at the miss of rank f + e and takes the first old-order entry neither
+  // evicted nor touched before that miss (a touched entry moved to MRU). An
+  // old page evicted before its own touch in this step misses at that touch;
+  // K, the set of such pages, is found by iteration. With K's misses added,
+  // eviction e takes the e-th old entry that is untouched or in K; a round
+  // then adds every touched entry the evictions reach before its touch,
+  // drops every K entry touched no later than the eviction reaching it, and
+  // drops K entries no eviction reaches. A round that changes nothing leaves
+  // an assignment that agrees with every step of the sequential process (by
+  // induction over time), so a hit keeps its slot and the r-th miss takes
+  // slot sz0 + r while free slots last, else the slot of eviction r - f.
+  // Evictions that would reach this step's touch list, or no fixed point
+  // within kLruRounds, run the serial replay instead.
+  // seq[s] = touch time of old slot s; -1 untouched; -(time + 2) in K.
   if (A.distinct) {
-    int nv = 0, nmiss = 0;
+    int nv = 0;
     for (int i0 = 0; i0 < n; i0 += 32) {
       const int i = i0 + t;
       const int x = i < n ? sel_s[i] : -1;
       const int s = x >= 0 ? islot[i] : -1;
-      const bool valid = x >= 0, hit = valid && s >= 0 && s < C && spg[s] == x, miss = valid && !hit;
-      const uint32_t mv = __ballot_sync(0xffffffffu, valid), mm = __ballot_sync(0xffffffffu, miss);
+      const bool valid = x >= 0, hit = valid && s >= 0 && s < C && spg[s] == x;
+      const uint32_t mv = __ballot_sync(0xffffffffu, valid);
       if (i < n) {
-        if (!valid) {
-          islot[i] = -1;
-          mflag[i] = 0;
-        } else if (hit) {
-          seq[s] = nv + __popc(mv & lt);  // touched this step
-          mflag[i] = 0;
-        } else {
-          prev[i] = nmiss + __popc(mm & lt);  // rank among the misses
-          mflag[i] = 1;
-        }
+        if (!valid) islot[i] = -1;
+        if (hit) seq[s] = nv + __popc(mv & lt);  // touched this step
+        mflag[i] = valid && !hit;                // a page not resident before the step
       }
       nv += __popc(mv);
-      nmiss += __popc(mm);
     }
     __syncwarp();
-    const int f = max(0, C - sz0), E = max(0, nmiss - f);
-    bool clash = E > sz0;
-    for (int j = t; j < E && j < sz0; j += 32) clash |= seq[old[j]] != -1;
-    clash = __any_sync(0xffffffffu, clash);
-    if (!clash) {
+    const int f = max(0, C - sz0);
+    int nmiss = 0, E = 0, jlast = -1;  // jlast: old position of eviction E - 1
+    int kcount = 0;                    // entries in K
+    bool ok = false;
+    for (int round = 0; round < kLruRounds; ++round) {
+      nmiss = 0;  // miss ranks (prev) and times (newl, scratch until the touch list)
+      int tv = 0;
+      for (int i0 = 0; i0 < n; i0 += 32) {
+        const int i = i0 + t;
+        const bool valid = i < n && sel_s[i] >= 0;
+        const bool ism = valid && (mflag[i] || seq[islot[i]] <= -2);
+        const uint32_t mv = __ballot_sync(0xffffffffu, valid), mm = __ballot_sync(0xffffffffu, ism);
+        if (ism) {
+          const int r = nmiss + __popc(mm & lt);
+          prev[i] = r;
+          newl[r] = tv + __popc(mv & lt);
+        }
+        nmiss += __popc(mm);
+        tv += __popc(mv);
+      }
+      __syncwarp();
+      E = max(0, nmiss - f);
+      int ucount = 0, kseen = 0, kadd = 0, kdrop = 0;  // kseen, kadd, kdrop: this thread's
+      jlast = -1;
+      for (int j0 = 0; j0 < sz0 && ucount < E; j0 += 32) {  // warp-uniform
+        const int j = j0 + t;
+        const int sl = j < sz0 ? old[j] : 0;
+        const int tt = j < sz0 ? seq[sl] : 0;
+        const bool cand = j < sz0 && (tt == -1 || tt <= -2);  // untouched or in K
+        const uint32_t mu = __ballot_sync(0xffffffffu, cand);
+        const int u = ucount + __popc(mu & lt);  // evictions ahead of j
+        if (j < sz0 && u < E) {
+          const int me = newl[f + u];  // time of the miss making eviction u
+          if (cand) {
+            evict[u] = sl;
+            if (u == E - 1) jlast = j;
+            if (tt <= -2) {
+              ++kseen;
+              if (-tt - 2 <= me) {  // touched before its eviction: a hit after all
+                seq[sl] = -tt - 2;
+                ++kdrop;
+              }
+            }
+          } else if (tt > me) {  // evicted before its touch: joins K
+            seq[sl] = -tt - 2;
+            ++kadd;
+          }
+        }
+        ucount += __popc(mu);
+      }
+      if (__any_sync(0xffffffffu, ucount < E)) break;  // evictions would reach the touch list
+      jlast = __reduce_max_sync(0xffffffffu, jlast);
+      kseen = __reduce_add_sync(0xffffffffu, kseen);
+      kadd = __reduce_add_sync(0xffffffffu, kadd);
+      kdrop = __reduce_add_sync(0xffffffffu, kdrop);
+      if (kseen < kcount) {  // K entries past the last eviction are not evicted
+        int d = 0;
+        for (int j = jlast + 1 + t; j < sz0; j += 32) {
+          const int sl = old[j], tt = seq[sl];
+          if (tt <= -2) {
+            seq[sl] = -tt - 2;
+            ++d;
+          }
+        }
+        kdrop += __reduce_add_sync(0xffffffffu, d);
+      }
+      kcount += kadd - kdrop;
+      __syncwarp();
+      if (kadd == 0 && kdrop == 0) {
+        ok = true;
+        break;
+      }
+    }
+    if (ok) {
+      for (int i = t; i < n; i += 32)  // K pages miss at their touch
+        if (sel_s[i] >= 0 && !mflag[i] && seq[islot[i]] <= -2) mflag[i] = 1;
+      __syncwarp();
       for (int i = t; i < n; i += 32)
         if (mflag[i]) {
           const int r = prev[i];
@@ -180,7 +288,7 @@ __global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
           if (r < f) {
             sl = sz0 + r;
           } else {
-            sl = old[r - f];
+            sl = evict[r - f];
             evict[r - f] = spg[sl];
           }
           islot[i] = sl;
@@ -199,7 +307,7 @@ __global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
         }
         nv2 += __popc(mv);
       }
-      p = E;
+      p = E > 0 ? jlast + 1 : 0;  // old entries ahead of p are evicted or touched
       nn = nv;
       sz = sz0 + min(nmiss, f);
       ne = E;

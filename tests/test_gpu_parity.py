@@ -338,6 +338,7 @@ def test_lru_kernel_over_capacity_and_resets(torch_cuda):
     (48, 16, 200, 0.7),   # evictions reach only untouched pages: warp-parallel path
     (16, 16, 60, 0.5),    # cache = k: touched pages at the LRU front, serial replay
     (24, 16, 40, 0.9),    # mixed: some steps each way
+    (300, 128, 2000, 0.5),  # decode-step shape: touched pages interleave the evicted front
 ])
 def test_lru_distinct_selections_both_paths(torch_cuda, cap, k, ids, reuse):
     """Distinct ascending selections (the decode step's case) against the

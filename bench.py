@@ -621,8 +621,9 @@ def run_owner(args):
     g_ids = np.arange(rank * R, (rank + 1) * R)
     ids = torch.arange(R, dtype=torch.int32, device=dev)
     base = torch.from_numpy(g_ids.astype(np.int64) * LH * N).to(dev)
+    n_kb = 10  # steps of the per-kernel pass after the timed region
     n_steps = args.warmup + args.steps
-    qs = torch.from_numpy(np.stack([q_stream(w, int(g), steps=n_steps) for g in g_ids], 1)).to(dev)
+    qs = torch.from_numpy(np.stack([q_stream(w, int(g), steps=n_steps + n_kb) for g in g_ids], 1)).to(dev)
     out = torch.empty((R, w.num_layers, w.q_heads, 128), dtype=torch.float32, device=dev)
     st = torch.cuda.current_stream(dev)
     dec.begin(ids, torch.full((R,), N, dtype=torch.int32, device=dev), pool_base=base)
@@ -647,7 +648,25 @@ def run_owner(args):
     ms = e0.elapsed_time(e1)
     step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(len(evs) - 1)] + [evs[-1].elapsed_time(e1)]
     stats = dec.all_stats()
-    t = torch.tensor([ms, float(np.percentile(step_ms, 99)), stats[1], stats[5], stats[7]],
+    # per-kernel pass (untimed for value): the four stages as separate calls,
+    # CUDA events between them on the launching stream
+    kev = []
+    for s in range(n_steps, n_steps + n_kb):
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        e[0].record(st)
+        dec.select(qs[s], ids, stream=st)
+        e[1].record(st)
+        dec.detect(ids, stream=st)
+        e[2].record(st)
+        dec.gather(ids, stream=st)
+        e[3].record(st)
+        dec.attention(qs[s], ids, out, stream=st)
+        e[4].record(st)
+        kev.append(e)
+    torch.cuda.synchronize(dev)
+    dec.check()
+    k_ms = np.mean([[e[j].elapsed_time(e[j + 1]) for j in range(4)] for e in kev], axis=0)
+    t = torch.tensor([ms, float(np.percentile(step_ms, 99)), stats[1], stats[5], stats[7], *k_ms],
                      dtype=torch.float64, device=dev)
     mx, sm = t.clone(), t.clone()
     if ws > 1:
@@ -657,6 +676,12 @@ def run_owner(args):
         ms = float(mx[0])
         tokens = total * args.steps
         gb, peer_b, self_b = float(sm[2]), float(sm[3]), float(sm[4])
+        kms = [float(x) for x in mx[5:9]]  # max over ranks, per kernel
+        hbm_peak, peak_kind = _peaks()
+        lanes = R * LH
+        sel_bytes = lanes * N * 128 * 4  # fp32 page summaries
+        attn_bytes = lanes * w.top_k * w.unit_bytes + lanes * (w.q_heads // w.kv_heads) * 128 * (2 + 4)
+        gat_bytes = 2 * (gb / args.steps) / ws  # read + write of this rank's share, HBM side
         line = {"metric": METRIC, "value": tokens / (ms / 1e3), "unit": UNIT, "n_gpus": ws,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
                 "p99_step_ms": float(mx[1]), "higher_is_better": True, "scaling": "strong",
@@ -670,6 +695,24 @@ def run_owner(args):
                                 "share_from_peer_gpus": peer_b / gb if gb else 0.0,
                                 "share_from_own_hbm": self_b / gb if gb else 0.0,
                                 "share_from_host": 1.0 - (peer_b + self_b) / gb if gb else 0.0},
+                "kernel_ms_per_step": dict(zip(["select", "detect", "gather", "attention"], kms)),
+                "kernel_time_share": dict(zip(["select", "detect", "gather", "attention"],
+                                              [round(x / sum(kms), 4) for x in kms])),
+                "roofline": {"bound": "hbm", "kernel": "select_kernel", "achieved": sel_bytes / kms[0] / 1e6,
+                             "peak": hbm_peak, "unit": "GB/s", "frac": sel_bytes / kms[0] / 1e6 / hbm_peak,
+                             "peak_kind": peak_kind, "traffic": None, "bytes_per_launch": sel_bytes,
+                             "note": "rank 0's bytes over the slowest rank's time; the dominant kernel "
+                                     "(fp32 page summaries, bit-exact scoring)"},
+                "roofline_attention": {"bound": "hbm", "kernel": "attn_tc_kernel",
+                                       "achieved": attn_bytes / kms[3] / 1e6, "peak": hbm_peak,
+                                       "frac": attn_bytes / kms[3] / 1e6 / hbm_peak, "bytes_per_launch": attn_bytes},
+                "roofline_gather": {"bound": "hbm" if ws == 1 else "nvlink", "kernel": "gather_store_kernel",
+                                    "achieved": gat_bytes / kms[2] / 1e6,
+                                    "peak": hbm_peak if ws == 1 else 770.0,
+                                    "note": "HBM read + write of the gathered units" if ws == 1 else
+                                            "peer share of the units over the measured 770 GB/s peer-copy peak",
+                                    "frac": (gat_bytes / kms[2] / 1e6 / hbm_peak) if ws == 1 else
+                                            ((gb / args.steps / ws) * (peer_b / gb if gb else 0) / kms[2] / 1e6 / 770.0)},
                 "clocks": clocks.summary()}
         print(json.dumps(line), flush=True)
     dec.close()

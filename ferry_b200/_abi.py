@@ -35,11 +35,13 @@ EXPORTS = [
     "ferry_exec_set_global", "ferry_exec_owned", "ferry_exec_tick", "ferry_exec_policy",
     "ferry_exec_usage", "ferry_exec_rebalance",
     "ferry_steal_filter",
+    "ferry_comm_unique_id", "ferry_comm_create", "ferry_comm_destroy", "ferry_exchange_ownership",
     "ferry_trace_load", "ferry_probe_topology", "ferry_probe_link",
     "ferry_lru_create", "ferry_lru_destroy", "ferry_lru_touch", "ferry_lru_read",
 ]
 MAX_PEERS = 8
 CTX_HANDLE_BYTES = 1024
+COMM_ID_BYTES = 128
 MIGRATE_FULL, MIGRATE_DELTA = 0, 1
 SRC_HOST, SRC_OWNER = 0, 1
 NUM_STATS = 8
@@ -132,6 +134,10 @@ _SIGS = {
     "ferry_exec_usage": (I, [V, C.POINTER(C.c_int64), C.POINTER(C.c_int32)]),
     "ferry_exec_rebalance": (I, [V, I, I]),
     "ferry_steal_filter": (I, [C.POINTER(StealPolicy), I, V, V, C.c_double, V, V, C.POINTER(I)]),
+    "ferry_comm_unique_id": (I, [V]),
+    "ferry_comm_create": (I, [I, I, I, V, C.POINTER(V)]),
+    "ferry_comm_destroy": (I, [V]),
+    "ferry_exchange_ownership": (I, [V, V, V, I, V]),
     "ferry_trace_load": (I, [C.c_char_p, I, I, I, I, I, I, V, C.c_int64, V, V]),
     "ferry_probe_topology": (I, [C.POINTER(I), V, V, I]),
     "ferry_probe_link": (I, [I, I, C.c_size_t, I, C.POINTER(C.c_double)]),

@@ -95,19 +95,62 @@ def llx_plan(usage: np.ndarray, counts: np.ndarray, threshold: float = 0.25, cap
     return src, dst, k
 
 
-def exchange_ownership(finished: int, admitted: int, owned: np.ndarray, cap: int, total_requests: int,
-                       device=None, usage: int = 0, with_rows: bool = False):
-    """The page-ownership exchange: one all_gather of fixed-size rows (NCCL
-    when ``device`` is a CUDA device, else the default group's backend)."""
-    import torch
-    import torch.distributed as dist
+class OwnershipComm:
+    """The ownership exchange's own NCCL communicator, through the C ABI
+    (ferry_comm_create / ferry_exchange_ownership). Collective: every rank of
+    the default process group constructs it (ranks on distinct GPUs); rank 0's
+    NCCL id reaches the others through that process group."""
 
-    row = torch.from_numpy(ownership_row(finished, admitted, owned, cap, usage))
-    if device is not None:
-        row = row.to(device)
-    out = [torch.empty_like(row) for _ in range(dist.get_world_size())]
-    dist.all_gather(out, row)
-    rows = torch.stack(out).cpu().numpy()
+    def __init__(self, device: int):
+        import torch
+        import torch.distributed as dist
+
+        self.world, self.rank = dist.get_world_size(), dist.get_rank()
+        self.dev = torch.device("cuda", device)
+        uid = (C.c_uint8 * _abi.COMM_ID_BYTES)()
+        if self.rank == 0:
+            call("ferry_comm_unique_id", uid)
+        box = [bytes(uid)]
+        dist.broadcast_object_list(box, src=0)
+        uid = (C.c_uint8 * _abi.COMM_ID_BYTES).from_buffer_copy(box[0])
+        self.h = C.c_void_p()
+        call("ferry_comm_create", device, self.world, self.rank, uid, C.byref(self.h))
+
+    def all_gather(self, row: np.ndarray) -> np.ndarray:
+        """[world][len(row)] int32 rows of every rank (returns after the copy back)."""
+        import torch
+
+        d_row = torch.from_numpy(np.ascontiguousarray(row, np.int32)).to(self.dev)
+        d_all = torch.empty((self.world, len(row)), dtype=torch.int32, device=self.dev)
+        st = torch.cuda.current_stream(self.dev)
+        call("ferry_exchange_ownership", self.h, C.c_void_p(st.cuda_stream), C.c_void_p(d_row.data_ptr()),
+             len(row), C.c_void_p(d_all.data_ptr()))
+        return d_all.cpu().numpy()
+
+    def close(self):
+        if self.h:
+            call("ferry_comm_destroy", self.h)
+            self.h = None
+
+
+def exchange_ownership(finished: int, admitted: int, owned: np.ndarray, cap: int, total_requests: int,
+                       device=None, usage: int = 0, with_rows: bool = False, comm: "OwnershipComm | None" = None):
+    """The page-ownership exchange: one all_gather of fixed-size rows -- over
+    ``comm`` (the C ABI's NCCL exchange) when given, else the default process
+    group (NCCL when ``device`` is a CUDA device, else its backend)."""
+    row = ownership_row(finished, admitted, owned, cap, usage)
+    if comm is not None:
+        rows = comm.all_gather(row).astype(np.int64)
+    else:
+        import torch
+        import torch.distributed as dist
+
+        t = torch.from_numpy(row)
+        if device is not None:
+            t = t.to(device)
+        out = [torch.empty_like(t) for _ in range(dist.get_world_size())]
+        dist.all_gather(out, t)
+        rows = torch.stack(out).cpu().numpy()
     merged = merge_ownership(rows, total_requests)
     return (merged, rows) if with_rows else merged
 
@@ -164,6 +207,7 @@ class RankRunner:
             call("ferry_exec_policy", self.exec, C.byref(policy))
         self.slots = slots
         self.peer_deques = []
+        self.comm = None
         if world > 1:
             h = (C.c_uint8 * _abi.CTX_HANDLE_BYTES)()
             call("ferry_ctx_export", self.dec.ctx, h)
@@ -187,9 +231,14 @@ class RankRunner:
     def run(self, home: np.ndarray, join: np.ndarray, epoch: int = 4, max_ticks: int = 100000,
             exchange_device=None, llx: float | None = None) -> ClusterStats:
         """Tick until every request of the job finished on some GPU. home/join:
-        each request's home rank and arrival tick."""
+        each request's home rank and arrival tick. With ``exchange_device`` set
+        (ranks on distinct GPUs) the ownership exchange runs over the C ABI's
+        NCCL communicator, created here before the timed region."""
         import torch
 
+        if exchange_device is not None and self.comm is None:
+            self.comm = OwnershipComm(self.dev.index)
+        comm = self.comm if exchange_device is not None else None
         st = torch.cuda.current_stream(self.dev)
         mine = np.nonzero(home == self.rank)[0]
         admitted = finished = tokens = ticks = steals = stolen = 0
@@ -227,7 +276,7 @@ class RankRunner:
                 call("ferry_exec_usage", self.exec, C.byref(u_steps), C.byref(u_reqs))
                 (_, fin_all, adm_all), rows = exchange_ownership(
                     finished, admitted, owned[:n_owned.value], self.slots, self.total, exchange_device,
-                    usage=u_steps.value, with_rows=True)
+                    usage=u_steps.value, with_rows=True, comm=comm)
                 call("ferry_exec_set_global", self.exec, adm_all - fin_all)
                 if llx is not None and fin_all < self.total:
                     plan = llx_plan(rows[:, 3], rows[:, 2], llx)
@@ -246,6 +295,9 @@ class RankRunner:
                             mig_ms=mig_ms, mig_event_bytes=mig_b, rebalances=rebalances)
 
     def close(self):
+        if self.comm is not None:
+            self.comm.close()
+            self.comm = None
         for pq in self.peer_deques:
             call("ferry_deque_destroy", pq)
         self.peer_deques = []

@@ -8,13 +8,16 @@
 // -1), slot_page[cap], order[cap] (slots, LRU front first), size.
 //
 // One warp per lane. The warp loads the lane's order and slot table plus the
-// selection's page-table entries into shared memory (coalesced / gathered),
+// selection's page-table entries into shared memory (coalesced / gathered,
+// several loads per thread in flight). A selection without duplicates (the
+// decode step) is resolved warp-parallel and exactly, with ballot scans over
+// the selection and the old order (see the comment at that path). Otherwise
 // lane 0 replays the selection sequentially on shared memory only -- O(1) per
 // item using two lazily-deleted queues: the old order (pointer p, an entry is
 // live while its slot has not been touched this step) and this step's touch
-// list (pointer q, an entry is live while it is its slot's latest touch) --
-// and the warp then writes back the compacted order, slot table, page-table
-// deltas (evictions first, then final residents), and the miss list.
+// list (pointer q, an entry is live while it is its slot's latest touch). The
+// warp then writes back the compacted order, slot table, page-table deltas
+// (evictions first, then final residents), and the miss list.
 #include "common.cuh"
 
 namespace ferry {

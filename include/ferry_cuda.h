@@ -289,6 +289,26 @@ int ferry_deque_peer_view(int device, ferry_deque* owner, ferry_deque** out);
 int ferry_deque_stress(int device, uint64_t capacity, int n_tasks, int thieves, int batch,
                        uint64_t* taken, int32_t* dup_or_missing);
 
+/* ---- page-ownership exchange between ranks (one process per GPU) ----
+ * Replaces the reference's host-shared ownership state: the fair share's
+ * global pending count read under the context mutex
+ * (src/runtime/wla_multigpu.cuh:1518-1526, refreshed at tick boundaries
+ * :829-864) and the LLX rebalancer's per-GPU load (:2084-2112). Each rank
+ * contributes one fixed-size int32 row; ferry_exchange_ownership all-gathers
+ * the rows of every rank (NCCL, loaded at run time: without libnccl.so.2 these
+ * calls return FERRY_E_STATE). The path's only collective. */
+#define FERRY_COMM_ID_BYTES 128
+typedef struct ferry_comm ferry_comm;
+/* Rank 0 makes the id and hands it to the other ranks out of band. */
+int ferry_comm_unique_id(void* id /* FERRY_COMM_ID_BYTES */);
+/* Collective over the `world` ranks: blocks until all of them call it. */
+int ferry_comm_create(int device, int world, int rank, const void* id, ferry_comm** out);
+int ferry_comm_destroy(ferry_comm* comm);
+/* d_all[world][row_ints] <- every rank's d_row[row_ints]; device memory on the
+ * comm's device; asynchronous on `stream`. */
+int ferry_exchange_ownership(ferry_comm* comm, void* stream, const int32_t* d_row, int row_ints,
+                             int32_t* d_all);
+
 /* ---- per-GPU executor with work stealing ----------------------------------
  * The host runtime of one GPU: the counterpart of the reference's exec thread
  * and WlaMultiGpuCtx tick/steal protocol (src/runtime/wla_multigpu.cuh:829-864

@@ -58,6 +58,10 @@ def test_null_arguments_rejected(cuda_lib):
     assert cuda_lib.ferry_store_create(None, 2, 0, 16) == _abi.E_INVAL
     assert cuda_lib.ferry_store_fill(None, None, 1, 16) == _abi.E_INVAL
     assert cuda_lib.ferry_gather_source(None, _abi.SRC_OWNER) == _abi.E_INVAL
+    assert cuda_lib.ferry_comm_unique_id(None) == _abi.E_INVAL
+    assert cuda_lib.ferry_comm_create(0, 0, 0, None, None) == _abi.E_INVAL
+    assert cuda_lib.ferry_comm_destroy(None) == _abi.OK
+    assert cuda_lib.ferry_exchange_ownership(None, None, None, 4, None) == _abi.E_INVAL
 
 
 def test_product_never_imports_oracle():

@@ -290,7 +290,7 @@ def test_migrate_over_cuda_ipc(torch_cuda):
 # --------------------------------------------------------------------------- executor
 
 
-def _cluster_worker(rank, world, port, devices, out, policy=None, llx=None):
+def _cluster_worker(rank, world, port, devices, out, policy=None, llx=None, nccl_exchange=False):
     import os
 
     import torch
@@ -315,7 +315,8 @@ def _cluster_worker(rank, world, port, devices, out, policy=None, llx=None):
     runner = RankRunner(w, total, world, rank, devices[rank], slots=total + 4, max_batch=4,
                         steal_batch=4, migrate_mode=_abi.MIGRATE_FULL, policy=pol)
     try:
-        stats = runner.run(home, join, epoch=2, max_ticks=400, llx=llx)
+        stats = runner.run(home, join, epoch=2, max_ticks=400, llx=llx,
+                           exchange_device=devices[rank] if nccl_exchange else None)
     finally:
         runner.close()
     out.put((rank, stats.tokens, stats.stolen_tasks, stats.migrated_units, stats.ticks, stats.rebalances))
@@ -358,6 +359,37 @@ def test_executor_two_ranks_steal_and_migrate(torch_cuda, policy):
     w = _workload()
     per_req = w.lanes_per_req * w.cache_pages
     assert mig1 == st1 * per_req and mig0 == st0 * per_req
+    assert ticks0 == ticks1
+
+
+def test_executor_ownership_over_nccl_comm(torch_cuda):
+    """The same two-rank job with the ownership exchange on the C ABI's NCCL
+    communicator (ferry_exchange_ownership) instead of the process group:
+    the job ends on both ranks together and every (request, step) decodes
+    exactly once."""
+    import socket
+
+    t = torch_cuda
+    if t.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs (one NCCL rank per GPU)")
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_cluster_worker, args=(r, 2, port, [0, 1], q, None, None, True)) for r in range(2)]
+    for p in ps:
+        p.start()
+    try:
+        res = sorted(q.get(timeout=300) for _ in ps)
+    finally:
+        for p in ps:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    (_, tok0, st0, _, ticks0, _), (_, tok1, st1, _, ticks1, _) = res
+    assert tok0 + tok1 == 12 * 6 and st1 > 0 and tok1 > 0
     assert ticks0 == ticks1
 
 

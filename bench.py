@@ -637,11 +637,13 @@ def run_owner(args):
     evs = []
     with Clocks(local) as clocks:
         e0.record(st)
+        h0 = time.perf_counter()
         for s in range(args.warmup, n_steps):
             a = torch.cuda.Event(enable_timing=True)
             a.record(st)
             dec.step(qs[s], ids, out)
             evs.append(a)
+        host_ms = (time.perf_counter() - h0) * 1e3  # issuing the steps, no sync inside
         e1.record(st)
         torch.cuda.synchronize(dev)
     dec.check()
@@ -666,7 +668,7 @@ def run_owner(args):
     torch.cuda.synchronize(dev)
     dec.check()
     k_ms = np.mean([[e[j].elapsed_time(e[j + 1]) for j in range(4)] for e in kev], axis=0)
-    t = torch.tensor([ms, float(np.percentile(step_ms, 99)), stats[1], stats[5], stats[7], *k_ms],
+    t = torch.tensor([ms, float(np.percentile(step_ms, 99)), stats[1], stats[5], stats[7], *k_ms, host_ms],
                      dtype=torch.float64, device=dev)
     mx, sm = t.clone(), t.clone()
     if ws > 1:
@@ -696,6 +698,8 @@ def run_owner(args):
                                 "share_from_own_hbm": self_b / gb if gb else 0.0,
                                 "share_from_host": 1.0 - (peer_b + self_b) / gb if gb else 0.0},
                 "kernel_ms_per_step": dict(zip(["select", "detect", "gather", "attention"], kms)),
+                # host time to issue one step (max over ranks): near ms_per_step means launch-bound
+                "host_ms_per_step": float(mx[9]) / args.steps,
                 "kernel_time_share": dict(zip(["select", "detect", "gather", "attention"],
                                               [round(x / sum(kms), 4) for x in kms])),
                 "roofline": {"bound": "hbm", "kernel": "select_kernel", "achieved": sel_bytes / kms[0] / 1e6,

@@ -35,7 +35,8 @@ EXPORTS = [
     "ferry_exec_set_global", "ferry_exec_owned", "ferry_exec_tick", "ferry_exec_policy",
     "ferry_exec_usage", "ferry_exec_rebalance",
     "ferry_steal_filter",
-    "ferry_comm_unique_id", "ferry_comm_create", "ferry_comm_destroy", "ferry_exchange_ownership",
+    "ferry_comm_unique_id", "ferry_comm_create", "ferry_comm_destroy", "ferry_comm_abort",
+    "ferry_exchange_ownership",
     "ferry_trace_load", "ferry_probe_topology", "ferry_probe_link",
     "ferry_lru_create", "ferry_lru_destroy", "ferry_lru_touch", "ferry_lru_read",
 ]
@@ -137,6 +138,7 @@ _SIGS = {
     "ferry_comm_unique_id": (I, [V]),
     "ferry_comm_create": (I, [I, I, I, V, C.POINTER(V)]),
     "ferry_comm_destroy": (I, [V]),
+    "ferry_comm_abort": (I, [V]),
     "ferry_exchange_ownership": (I, [V, V, V, I, V]),
     "ferry_trace_load": (I, [C.c_char_p, I, I, I, I, I, I, V, C.c_int64, V, V]),
     "ferry_probe_topology": (I, [C.POINTER(I), V, V, I]),

@@ -116,8 +116,13 @@ class OwnershipComm:
         self.h = C.c_void_p()
         call("ferry_comm_create", device, self.world, self.rank, uid, C.byref(self.h))
 
-    def all_gather(self, row: np.ndarray) -> np.ndarray:
-        """[world][len(row)] int32 rows of every rank (returns after the copy back)."""
+    def all_gather(self, row: np.ndarray, timeout_s: float = 60.0) -> np.ndarray:
+        """[world][len(row)] int32 rows of every rank (returns after the copy
+        back). A collective not done within timeout_s (a peer rank gone) is
+        aborted -- the communicator with it -- and raises TimeoutError, the
+        way a process group's timeout ends its collective."""
+        import time
+
         import torch
 
         d_row = torch.from_numpy(np.ascontiguousarray(row, np.int32)).to(self.dev)
@@ -125,6 +130,14 @@ class OwnershipComm:
         st = torch.cuda.current_stream(self.dev)
         call("ferry_exchange_ownership", self.h, C.c_void_p(st.cuda_stream), C.c_void_p(d_row.data_ptr()),
              len(row), C.c_void_p(d_all.data_ptr()))
+        done = torch.cuda.Event()
+        done.record(st)
+        deadline = time.monotonic() + timeout_s
+        while not done.query():
+            if time.monotonic() > deadline:
+                call("ferry_comm_abort", self.h)
+                raise TimeoutError(f"ownership exchange on rank {self.rank} not done within {timeout_s} s")
+            time.sleep(5e-5)
         return d_all.cpu().numpy()
 
     def close(self):

@@ -31,6 +31,7 @@ struct NcclApi {
   ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
   bool ok = false;
 };
@@ -46,8 +47,9 @@ const NcclApi& nccl() {
     api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
     api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
     api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(dlsym(h, "ncclCommAbort"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
-    api.ok = api.get_unique_id && api.comm_init_rank && api.all_gather && api.comm_destroy;
+    api.ok = api.get_unique_id && api.comm_init_rank && api.all_gather && api.comm_destroy && api.comm_abort;
   });
   return api;
 }
@@ -123,9 +125,20 @@ int ferry_comm_destroy(ferry_comm* c) {
   return rc;
 }
 
+int ferry_comm_abort(ferry_comm* c) {
+  if (!c) return ferry::set_error("comm_abort: NULL comm"), FERRY_E_INVAL;
+  if (!c->comm) return FERRY_OK;
+  const auto& a = ferry::nccl();
+  if (!a.ok) return ferry::nccl_missing();
+  const int rc = ferry::on_device(c->device, [&] { return ferry::nccl_status(a.comm_abort(c->comm), "ncclCommAbort"); });
+  c->comm = nullptr;  // destroy only frees the handle now
+  return rc;
+}
+
 int ferry_exchange_ownership(ferry_comm* c, void* stream, const int32_t* d_row, int row_ints, int32_t* d_all) {
   if (!c || !d_row || !d_all || row_ints < 1)
     return ferry::set_error("exchange_ownership: bad arguments"), FERRY_E_INVAL;
+  if (!c->comm) return ferry::set_error("exchange_ownership: communicator was aborted"), FERRY_E_STATE;
   const auto& a = ferry::nccl();
   if (!a.ok) return ferry::nccl_missing();
   return ferry::on_device(c->device, [&] {

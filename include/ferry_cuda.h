@@ -304,6 +304,11 @@ int ferry_comm_unique_id(void* id /* FERRY_COMM_ID_BYTES */);
 /* Collective over the `world` ranks: blocks until all of them call it. */
 int ferry_comm_create(int device, int world, int rank, const void* id, ferry_comm** out);
 int ferry_comm_destroy(ferry_comm* comm);
+/* Ends every collective of `comm` still in flight (e.g. when a peer rank is
+ * gone and the caller's deadline for an exchange passed); the comm is then
+ * unusable: exchanges return FERRY_E_STATE, destroy frees the handle. May be
+ * called from another host thread while an exchange is pending. */
+int ferry_comm_abort(ferry_comm* comm);
 /* d_all[world][row_ints] <- every rank's d_row[row_ints]; device memory on the
  * comm's device; asynchronous on `stream`. */
 int ferry_exchange_ownership(ferry_comm* comm, void* stream, const int32_t* d_row, int row_ints,

@@ -61,6 +61,7 @@ def test_null_arguments_rejected(cuda_lib):
     assert cuda_lib.ferry_comm_unique_id(None) == _abi.E_INVAL
     assert cuda_lib.ferry_comm_create(0, 0, 0, None, None) == _abi.E_INVAL
     assert cuda_lib.ferry_comm_destroy(None) == _abi.OK
+    assert cuda_lib.ferry_comm_abort(None) == _abi.E_INVAL
     assert cuda_lib.ferry_exchange_ownership(None, None, None, 4, None) == _abi.E_INVAL
 
 

@@ -40,6 +40,11 @@ def test_exchange_single_rank(torch_cuda):
             _abi.call("ferry_exchange_ownership", h, None, C.c_void_p(row.data_ptr()), 0, C.c_void_p(out.data_ptr()))
         with pytest.raises(_abi.FerryError):
             _abi.call("ferry_comm_create", 0, 2, 2, uid, C.byref(C.c_void_p()))  # rank outside world
+        t.cuda.synchronize(dev)
+        _abi.call("ferry_comm_abort", h)  # nothing in flight: the comm just becomes unusable
+        with pytest.raises(_abi.FerryError):
+            _abi.call("ferry_exchange_ownership", h, C.c_void_p(st.cuda_stream), C.c_void_p(row.data_ptr()), 37,
+                      C.c_void_p(out.data_ptr()))
     finally:
         _abi.call("ferry_comm_destroy", h)
 

@@ -18,16 +18,18 @@
 // (o[128], m, l) per q head in scratch slot lane + c; the CTA completing a
 // lane's last segment (atomic count) combines them into out.
 //
-// A CTA is warp-specialized: warp 4 issues the TMA copies of a 3-stage ring
-// (mbarrier full / empty per stage), warp 5 issues the MMAs, and warps 0-3 --
-// thread t = TMEM lane t = token t for S, dim t for O -- run the softmax. Per
-// group of 128 tokens:
+// A CTA is warp-specialized: warp 8 issues the TMA copies of a 3-stage ring
+// (mbarrier full / empty per stage), warp 9 issues the MMAs, and warps 0-7 --
+// two warpgroups over the same TMEM lanes, thread t of each = TMEM lane t =
+// token t for S, dim t for O, each warpgroup taking half of the q heads --
+// run the softmax. Per group of 128 tokens:
 //   S = K Q^T      A = K tile K-major, B = Q (e4m3 terms or f16) K-major
 //   softmax        base 2, per head; e4m3: k_scale applied to the scores
 //   P              f16 weights, or p * v_scale as three e4m3 terms
 //   O^T = V^T P^T  A = V tile read MN-major (dims contiguous), B = P MN-major
 // S, P and O are double-buffered so the QK of the next group and the PV of
-// the last one overlap the softmax. Every wait is bounded (on timeout the
+// the last one overlap the softmax. Every wait is bounded (probes suspend in
+// hardware up to kWaitHintNs each, about a second in all; on timeout the
 // kernel records FERRY_E_TIMEOUT, lets its copies and MMAs land and frees its
 // TMEM).
 #include <cuda.h>

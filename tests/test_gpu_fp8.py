@@ -55,6 +55,7 @@ def test_e4m3_pool_and_summaries_bit_exact(torch_cuda):
 @pytest.mark.parametrize("shape", [
     dict(q_heads=32, kv_heads=4),                    # GQA group 8 (the long-context config)
     dict(q_heads=8, kv_heads=2, cache_frac=0.5),     # group 4
+    dict(q_heads=4, kv_heads=2),                     # group 2: one head per softmax warpgroup
     dict(q_heads=4, kv_heads=4),                     # group 1
 ])
 def test_e4m3_decode_matches_oracle(torch_cuda, shape):

@@ -115,6 +115,9 @@ class OwnershipComm:
         uid = (C.c_uint8 * _abi.COMM_ID_BYTES).from_buffer_copy(box[0])
         self.h = C.c_void_p()
         call("ferry_comm_create", device, self.world, self.rank, uid, C.byref(self.h))
+        # NCCL connects the ranks on a communicator's first collective (hundreds
+        # of ms): do that here, outside any timed region
+        self.all_gather(np.zeros(ROW_HEAD, np.int32))
 
     def all_gather(self, row: np.ndarray, timeout_s: float = 60.0) -> np.ndarray:
         """[world][len(row)] int32 rows of every rank (returns after the copy

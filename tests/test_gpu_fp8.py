@@ -57,6 +57,7 @@ def test_e4m3_pool_and_summaries_bit_exact(torch_cuda):
     dict(q_heads=8, kv_heads=2, cache_frac=0.5),     # group 4
     dict(q_heads=4, kv_heads=2),                     # group 2: one head per softmax warpgroup
     dict(q_heads=4, kv_heads=4),                     # group 1
+    dict(q_heads=32, kv_heads=4, n_pages="edge"),    # no page, one page, k - 1, full
 ])
 def test_e4m3_decode_matches_oracle(torch_cuda, shape):
     import oracle
@@ -64,6 +65,8 @@ def test_e4m3_decode_matches_oracle(torch_cuda, shape):
     from ferry_b200.workload import small
 
     t = torch_cuda
+    shape = dict(shape)
+    edge = shape.pop("n_pages", None) == "edge"
     w = small(kv_dtype="e4m3", ctx_tokens=2048, top_k=40, **shape)
     dec = Decoder(w, 0)
     try:
@@ -72,7 +75,7 @@ def test_e4m3_decode_matches_oracle(torch_cuda, shape):
         units = pool.numpy(np.uint8).reshape(U, UB)
         summ = oracle.page_summary_e4m3(units)
         dq = oracle.e4m3_dequant(units)
-        n_pages = np.array([N, N - 7, k - 9, k], np.int32)[: w.num_requests]
+        n_pages = np.array([0, 1, k - 1, N] if edge else [N, N - 7, k - 9, k], np.int32)[: w.num_requests]
         reqs = np.arange(w.num_requests, dtype=np.int32)
         dev = t.device("cuda", 0)
         dec.begin(t.from_numpy(reqs).to(dev), t.from_numpy(n_pages).to(dev))

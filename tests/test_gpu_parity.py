@@ -179,6 +179,44 @@ def test_decode_steps_match_oracle(torch_cuda, shape):
         h.close()
 
 
+@pytest.mark.parametrize("shape", [dict(), dict(q_heads=8, kv_heads=2, cache_frac=0.5)])
+def test_empty_and_single_page_contexts(torch_cuda, shape):
+    """Requests with no page, one page and k - 1 pages beside a full one: the
+    empty request's lanes select nothing, miss nothing and decode to exact
+    zeros, and every other intermediate matches the oracle."""
+    from ferry_b200.workload import small
+
+    w = small(**shape)
+    k, N = w.top_k, w.max_pages
+    reqs = list(range(w.num_requests))
+    h = Harness(torch_cuda, w, n_pages=[0, 1, k - 1, N][: w.num_requests])
+    try:
+        h.begin(reqs)
+        for s in range(3):
+            out, _ = h.check_step(_q(w, reqs, s), reqs)
+            assert (out[0] == 0).all()
+            assert (h.dec.n_sel[: h.LH].cpu().numpy() == 0).all()
+    finally:
+        h.close()
+
+
+def test_longest_lane(torch_cuda):
+    """Lanes of the maximum 16384 pages (16 selection chunks of 1024, the
+    keys of a lane filling the shared-memory ring), GQA group 8."""
+    from ferry_b200.workload import small
+
+    w = small(num_requests=2, num_layers=1, q_heads=8, kv_heads=1, ctx_tokens=16384 * 16, top_k=64)
+    assert w.max_pages == 16384
+    reqs = [0, 1]
+    h = Harness(torch_cuda, w, n_pages=[w.max_pages, w.max_pages - 3])
+    try:
+        h.begin(reqs)
+        for s in range(2):
+            h.check_step(_q(w, reqs, s), reqs)
+    finally:
+        h.close()
+
+
 @pytest.mark.parametrize("ctx_tokens", [2048, 65536])
 def test_select_ties_and_signed_zeros(torch_cuda, ctx_tokens):
     """All-zero queries score every page +-0 (ties everywhere, and -0 < +0 in

@@ -26,6 +26,11 @@ constexpr int kUnitBytes = kUnitElems * 2;              // fp16: 8192 bytes
 constexpr int kUnitBytesF8 = kUnitElems + 16;           // 4112 bytes
 constexpr int kMaxGroup = 8;
 constexpr int kMaxPages = 16384;
+// Shared memory of one LRU lane (one warp of the miss-detect kernel): old
+// order, slot table, touch marks (cap ints each), five k-int work lists and k
+// flag bytes. A lane must fit one block's 227 KiB.
+constexpr size_t kLruLaneSmemMax = 227 * 1024;
+inline int lru_lane_ints(int cap, int k) { return ((3 * cap + 5 * k) + (k + 3) / 4 + 3) & ~3; }
 // selection scores a lane in chunks of about this many pages (one CTA each)
 // once the lane is longer than two chunks
 constexpr int kSelChunk = 1024;

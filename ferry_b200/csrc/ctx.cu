@@ -136,6 +136,12 @@ int validate_cfg(const ferry_cfg* cfg) {
     return set_error("max_pages must be in [1, %d]", kMaxPages), FERRY_E_INVAL;
   if (cfg->cache_pages < 1 || cfg->top_k < 1 || cfg->top_k > cfg->cache_pages)
     return set_error("need 1 <= top_k <= cache_pages"), FERRY_E_INVAL;
+  if ((size_t)lru_lane_ints(cfg->cache_pages, cfg->top_k) * 4 > kLruLaneSmemMax)
+    return set_error("cache_pages %d with top_k %d need %zu bytes of shared memory per lane for miss "
+                     "detection (max %zu)",
+                     cfg->cache_pages, cfg->top_k, (size_t)lru_lane_ints(cfg->cache_pages, cfg->top_k) * 4,
+                     kLruLaneSmemMax),
+           FERRY_E_INVAL;
   return FERRY_OK;
 }
 

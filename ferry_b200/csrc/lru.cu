@@ -493,11 +493,11 @@ int launch_lru(const ferry_lru* L, cudaStream_t st, const int32_t* lane_ids,
   A.n_miss = n_miss;
   A.err = L->err;
   // old, spg, seq (cap each) + sel, islot, prev, newl, evict (k each) + k flag bytes
-  A.warp_ints = ((3 * L->cap + 5 * k) + (k + 3) / 4 + 3) & ~3;
+  A.warp_ints = lru_lane_ints(L->cap, k);
   const size_t per_warp = (size_t)A.warp_ints * 4;
   int warps = (int)std::min<size_t>(8, std::max<size_t>(1, (96 * 1024) / per_warp));
   const size_t smem = per_warp * warps;
-  if (smem > 227 * 1024) {
+  if (smem > kLruLaneSmemMax) {
     set_error("lru: capacity %d / k %d need %zu bytes of shared memory per lane", L->cap, k,
               per_warp);
     return FERRY_E_INVAL;

@@ -37,7 +37,8 @@ def test_invalid_configs_rejected_without_gpu(cuda_lib):
                 max_pages=64, cache_pages=16, top_k=8, kv_dtype=0)
     bad = [dict(head_dim=64), dict(page_tokens=8), dict(q_heads=6), dict(q_heads=48, kv_heads=4),
            dict(top_k=17), dict(top_k=0), dict(max_pages=20000), dict(kv_dtype=3),
-           dict(num_requests=0)]
+           dict(num_requests=0),
+           dict(max_pages=16384, cache_pages=16384, top_k=8192)]  # LRU lane past 227 KiB of smem
     for b in bad:
         cfg = _abi.Cfg(**{**base, **b})
         h = C.c_void_p()

@@ -204,3 +204,25 @@ def test_llx_plan_matches_the_rebalancer_rule():
     assert llx_plan([0, 0], [0, 0]) is None and llx_plan([50], [3]) is None
     # ties: the first maximum and the first minimum, as the reference's strict comparisons
     assert llx_plan([80, 80, 0, 0], [2, 2, 0, 0])[:2] == (0, 2)
+
+
+def test_exchange_over_a_communicator_merges_its_int32_rows():
+    """The runner's exchange through the C ABI's communicator: the rows come
+    back as int32 (the NCCL all_gather's type) and merge exactly like the
+    process group's int64 rows. A stand-in communicator plays the other rank."""
+    from ferry_b200.cluster import exchange_ownership, llx_plan, ownership_row
+
+    other = ownership_row(3, 9, np.array([1, 4, 6], np.int32), cap=8, usage=40)
+
+    class TwoRanks:
+        def all_gather(self, row):
+            assert row.dtype == np.int64 and len(row) == len(other)
+            return np.stack([np.asarray(row, np.int32), other.astype(np.int32)])
+
+    (owner, fin, adm), rows = exchange_ownership(2, 5, np.array([0, 2, 5], np.int32), 8, 8,
+                                                 usage=7, with_rows=True, comm=TwoRanks())
+    assert rows.dtype == np.int64 and rows.shape == (2, 12)
+    assert fin == 5 and adm == 14
+    assert owner.tolist() == [0, 1, 0, -1, 1, 0, 1, -1]
+    # loads 7 and 40, 3 requests each: mean 23.5, rank 0 pulls (40 - 23) // (23.5 // 3 + 1) = 2
+    assert llx_plan(rows[:, 3], rows[:, 2], 0.25) == (1, 0, 2)

@@ -25,7 +25,7 @@ EXPORTS = [
     "ferry_ctx_check", "ferry_host_alloc", "ferry_host_free", "ferry_kv_register",
     "ferry_kv_generate", "ferry_page_summary_update", "ferry_requests_begin",
     "ferry_select_topk", "ferry_detect_misses", "ferry_gather_misses", "ferry_sparse_decode",
-    "ferry_sparse_decode_noalloc", "ferry_decode_step", "ferry_wait_flag", "ferry_stats_read", "ferry_debug_read",
+    "ferry_sparse_decode_noalloc", "ferry_sparse_decode_noalloc_status", "ferry_decode_step", "ferry_wait_flag", "ferry_stats_read", "ferry_debug_read",
     "ferry_ctx_export", "ferry_store_create", "ferry_store_fill", "ferry_gather_source",
     "ferry_ctx_import", "ferry_ctx_link", "ferry_migrate_requests",
     "ferry_slot_states", "ferry_deque_create", "ferry_deque_destroy", "ferry_deque_push",
@@ -101,6 +101,7 @@ _SIGS = {
     "ferry_gather_misses": (I, [V, V, V, I, V, V, V]),
     "ferry_sparse_decode": (I, [V, V, V, V, I, V, V, V]),
     "ferry_sparse_decode_noalloc": (I, [V, V, I, I, I, I, I, V, V, I, V, V, V]),
+    "ferry_sparse_decode_noalloc_status": (I, [V]),
     "ferry_decode_step": (I, [V, V, V, V, I, V]),
     "ferry_wait_flag": (I, [V, V, V, C.c_uint32, C.c_uint32]),
     "ferry_stats_read": (I, [V, V, I]),

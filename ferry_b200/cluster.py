@@ -128,13 +128,18 @@ class OwnershipComm:
 
         import torch
 
-        d_row = torch.from_numpy(np.ascontiguousarray(row, np.int32)).to(self.dev)
-        d_all = torch.empty((self.world, len(row)), dtype=torch.int32, device=self.dev)
-        st = torch.cuda.current_stream(self.dev)
-        call("ferry_exchange_ownership", self.h, C.c_void_p(st.cuda_stream), C.c_void_p(d_row.data_ptr()),
-             len(row), C.c_void_p(d_all.data_ptr()))
-        done = torch.cuda.Event()
-        done.record(st)
+        # the copy, the collective and the completion event all on this
+        # communicator's device and its current stream, whatever device the
+        # caller has current
+        with torch.cuda.device(self.dev):
+            st = torch.cuda.current_stream(self.dev)
+            with torch.cuda.stream(st):
+                d_row = torch.from_numpy(np.ascontiguousarray(row, np.int32)).to(self.dev)
+                d_all = torch.empty((self.world, len(row)), dtype=torch.int32, device=self.dev)
+            call("ferry_exchange_ownership", self.h, C.c_void_p(st.cuda_stream), C.c_void_p(d_row.data_ptr()),
+                 len(row), C.c_void_p(d_all.data_ptr()))
+            done = torch.cuda.Event()
+            done.record(st)
         deadline = time.monotonic() + timeout_s
         while not done.query():
             if time.monotonic() > deadline:

@@ -369,11 +369,16 @@ int launch_attention(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,
 // to its own KV arena or caching allocator at start-up (an extra cudaMalloc
 // fails or fragments that pool), and a decode loop on the latency-critical
 // path, where cudaMalloc's implicit device synchronisation would stall every
-// stream. ferry_sparse_decode_noalloc serves them: it runs the same attention
-// kernel, but its split-K partials and per-lane counters live in the
-// fixed-size array below instead of a ctx allocation, and the call allocates
-// nothing. The array is a file-scope __device__ object, so every GPU that
-// loads this library holds its 4 MiB until the process exits.
+// stream. ferry_sparse_decode_noalloc serves them: it runs the fp16 CUDA-core
+// attention kernel, but its split-K partials, per-lane counters and error word
+// live in the fixed-size array below instead of a ctx allocation, and the call
+// allocates nothing. The array is a file-scope __device__ object, so every GPU
+// that loads this library holds its 4 MiB until the process exits.
+//
+// Layout of the array: [0, 64 KiB) per-lane completion counters (16384 lanes),
+// [64 KiB, 4 MiB - 256) split-K partials, [4 MiB - 256, 4 MiB) the error word
+// (kErrTimeout / kErrRange bits, sticky until ferry_sparse_decode_noalloc_status
+// reads and clears it).
 //
 // Host code never passes g_noalloc_scratch itself to a kernel -- in host code
 // that name is only a host-side stand-in for the symbol. The device address is
@@ -389,6 +394,7 @@ namespace {
 
 constexpr size_t kNoAllocScratchBytes = 4u << 20;
 constexpr size_t kNoAllocCounterBytes = 64u << 10;  // up to 16384 lanes of counters
+constexpr size_t kNoAllocErrOffset = kNoAllocScratchBytes - 256;  // the error word
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -443,7 +449,7 @@ extern "C" int ferry_sparse_decode_noalloc(void* stream, const void* d_cache, in
   FERRY_TRY(cudaGetDevice(&dev));
   FERRY_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   // partial slots = lanes + warps; use fewer warps when the array is the limit
-  const size_t part_cap = kNoAllocScratchBytes - kNoAllocCounterBytes;
+  const size_t part_cap = kNoAllocErrOffset - kNoAllocCounterBytes;
   const size_t slot_bytes = (size_t)group * kPartStride * sizeof(float);
   const int64_t T = n_lanes * top_k;
   int nw = attn_warps(T, n_lanes, resident_warps(sms));
@@ -479,7 +485,30 @@ extern "C" int ferry_sparse_decode_noalloc(void* stream, const void* d_cache, in
   A.part = part;
   A.lane_done = lane_done;
   A.out = d_out;
-  A.err = nullptr;  // no error word here: out-of-range ids are skipped, not reported
+  // timed-out waits and out-of-range ids / n_sel / slots land in the array's
+  // error word (ferry_sparse_decode_noalloc_status)
+  A.err = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(base) + kNoAllocErrOffset);
   A.qscale = 1.4426950408889634f / sqrtf((float)kHeadDim);
   return launch_attn(A, group, st);
+}
+
+extern "C" int ferry_sparse_decode_noalloc_status(void* stream) {
+  using namespace ferry;
+  int dev = 0;
+  FERRY_TRY(cudaGetDevice(&dev));
+  void* base = nullptr;
+  int rc = noalloc_scratch(dev, &base);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  uint32_t* err = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(base) + kNoAllocErrOffset);
+  uint32_t e = 0;
+  FERRY_TRY(cudaStreamSynchronize(st));
+  FERRY_TRY(cudaMemcpyAsync(&e, err, 4, cudaMemcpyDeviceToHost, st));
+  FERRY_TRY(cudaStreamSynchronize(st));
+  if (!e) return FERRY_OK;
+  FERRY_TRY(cudaMemsetAsync(err, 0, 4, st));
+  FERRY_TRY(cudaStreamSynchronize(st));
+  if (e & kErrTimeout) return set_error("sparse_decode_noalloc: a device wait timed out"), FERRY_E_TIMEOUT;
+  return set_error("sparse_decode_noalloc: an out-of-range request id, n_sel or slot was seen"),
+         FERRY_E_RANGE;
 }

@@ -170,18 +170,30 @@ int ferry_sparse_decode(ferry_ctx* ctx, void* stream, const uint16_t* d_q,
  * the caller passes the page cache (d_cache, num_requests * lanes_per_req *
  * cache_pages page units, lane-major) and its geometry (group = q heads per kv
  * head) plus the same q / req_ids / item_slot / n_sel / out as
- * ferry_sparse_decode, on the current device. Scratch is a fixed 4 MiB
- * __device__ array inside the library (held by every GPU that loads it until
- * exit): at most 16384 lanes per call, and batches whose split-K partials do
- * not fit are rejected with FERRY_E_INVAL. The first call on a device looks up
- * the array's address (call it once before any stream capture). Calls share
- * the array, so calls that overlap on the GPU race; out-of-range ids are
- * skipped, not reported. */
+ * ferry_sparse_decode, on the current device.
+ * The cache must hold fp16 page units of 8192 bytes (FERRY_KV_F16): the call
+ * has no dtype argument and reads 8192 bytes per slot, so an e4m3 cache is
+ * not supported. It runs the CUDA-core kernel at every group (1, 2, 4, 8);
+ * ferry_sparse_decode uses tensor cores for groups above 1 and is ~3x faster
+ * at group 8.
+ * Scratch is a fixed 4 MiB __device__ array inside the library (held by every
+ * GPU that loads it until exit): at most 16384 lanes per call, and batches
+ * whose split-K partials do not fit are rejected with FERRY_E_INVAL (large
+ * batches run with fewer warps so that they fit). The first call on a device
+ * looks up the array's address (call it once before any stream capture).
+ * Calls share the array, so calls that overlap on the GPU race.
+ * Errors the kernel sees -- a timed-out copy wait, an out-of-range request id
+ * or n_sel (that lane is skipped and its rows are zero), an out-of-range slot
+ * (read as slot 0 of its lane) -- are recorded in an error word inside the
+ * array; ferry_sparse_decode_noalloc_status synchronises `stream`, returns
+ * FERRY_E_TIMEOUT / FERRY_E_RANGE for any error recorded since its last call
+ * (FERRY_OK otherwise) and clears the word. It allocates nothing either. */
 int ferry_sparse_decode_noalloc(void* stream, const void* d_cache, int cache_pages,
                                 int num_requests, int lanes_per_req, int group, int top_k,
                                 const uint16_t* d_q, const int32_t* d_req_ids, int n_req,
                                 const int32_t* d_item_slot, const int32_t* d_n_sel,
                                 float* d_out);
+int ferry_sparse_decode_noalloc_status(void* stream);
 
 /* One decode step = select -> detect -> gather -> attention on ctx-owned
  * workspace. Replaces exec_step mode C (src/runtime/wla_multigpu.cuh:2527-2604)

@@ -169,11 +169,13 @@ def _dist():
     return ws, rank, local
 
 
-def cpu_baseline(w, seconds: float = 15.0, threads: int | None = None, ticks: int | None = None):
+def cpu_baseline(w, seconds: float = 15.0, threads: int | None = None, ticks: int | None = None,
+                 keep: int = 0):
     """The reference path restated on host cores (oracle pipeline: select ->
     LRU -> memcpy gather -> fp32 attention), all host threads, over a bounded
     sample of the job's ticks. Returns (tokens/s, threads, sample text,
-    per-tick [(ms, tokens)])."""
+    per-tick [(ms, tokens, misses, output of the first `keep` ticks or None)]);
+    the kept outputs let the caller check its own outputs of the same ticks."""
     import oracle
     from ferry_b200.workload import Schedule, q_stream
 
@@ -188,11 +190,11 @@ def cpu_baseline(w, seconds: float = 15.0, threads: int | None = None, ticks: in
     qs = [q_stream(w, r) for r in range(w.num_requests)]
     tok, t_used, i, per_tick = 0, 0.0, 0, []
     limit = sch.length if ticks is None else ticks
-    while i < limit and (ticks is not None or t_used < seconds):
+    while i < limit and (ticks is not None or t_used < seconds or i < keep):
         active, steps, job = sch.tick(i)
         i += 1
         if len(active) == 0:
-            per_tick.append((0.0, 0))
+            per_tick.append((0.0, 0, 0, None))
             continue
         if job:
             qs = [q_stream(w, r, job=job) for r in range(w.num_requests)]
@@ -200,12 +202,36 @@ def cpu_baseline(w, seconds: float = 15.0, threads: int | None = None, ticks: in
         reset = np.repeat((steps == 0).astype(np.uint8), LH)
         q = np.stack([qs[r][s] for r, s in zip(active, steps)]).view(np.uint16)
         t0 = time.perf_counter()
-        pipe.step(lanes, q.reshape(len(lanes), w.group, 128), reset=reset)
+        out, misses = pipe.step(lanes, q.reshape(len(lanes), w.group, 128), reset=reset)
         dt = time.perf_counter() - t0
         t_used += dt
-        per_tick.append((dt * 1e3, len(active)))
+        per_tick.append((dt * 1e3, len(active), misses, out if i <= keep else None))
         tok += len(active)
     return tok / t_used, threads, f"first {i} ticks of the {w.name} job ({tok} tokens)", per_tick
+
+
+def parity_vs_cpu(w, gpu_out, gpu_units, per_tick, rtol: float = 2e-3) -> dict:
+    """Compare the GPU's outputs of ticks 0..len(gpu_out)-1 (host arrays
+    [n][L][Hq][128], None for empty ticks) and its gathered page units over
+    those ticks with the CPU pipeline's (the oracle restatement run by
+    cpu_baseline on the same job). Attention within rtol relative error per
+    output row; the miss count (= units gathered) exact."""
+    n = min(len(gpu_out), len(per_tick))
+    worst, rows, cpu_misses = 0.0, 0, 0
+    for i in range(n):
+        g, (_, ntok, miss, ref) = gpu_out[i], per_tick[i]
+        cpu_misses += miss
+        if g is None or ref is None:
+            continue
+        a = g.reshape(-1, 128).astype(np.float64)
+        b = ref.reshape(-1, 128).astype(np.float64)
+        worst = max(worst, float((np.abs(a - b).max(1) / np.maximum(np.abs(b).max(1), 1e-30)).max()))
+        rows += a.shape[0]
+    ok = worst <= rtol and (n < len(gpu_out) or cpu_misses == gpu_units)
+    return {"status": "ok" if ok else "FAIL", "ticks": n, "rows": rows, "attn_max_rel_err": worst,
+            "tolerance": rtol, "units_gathered_gpu": gpu_units,
+            "units_missed_oracle": cpu_misses if n == len(gpu_out) else None,
+            "against": "the oracle pipeline (cpu_baseline) on the same job ticks"}
 
 
 def run_reference(args, w):
@@ -215,8 +241,8 @@ def run_reference(args, w):
         return
     _, threads, _, per_tick = cpu_baseline(w, ticks=args.warmup + args.steps)
     timed = per_tick[args.warmup:]
-    t_ms = sum(m for m, _ in timed)
-    tok = sum(n for _, n in timed)
+    t_ms = sum(x[0] for x in timed)
+    tok = sum(x[1] for x in timed)
     v = tok / (t_ms / 1e3) if t_ms > 0 else 0.0
     sample = f"ticks {args.warmup}..{args.warmup + args.steps - 1} of the {w.name} job ({tok} tokens)"
     line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
@@ -345,7 +371,11 @@ def run_ferry(args, w):
     dec.register_pool()
     pin_q = [None if tk["q"] is None else tk["q"].pin_memory() for tk in ticks]
     pin_ids = [torch.from_numpy(tk["active"]).pin_memory() for tk in ticks]
-    host_out = torch.empty_like(out, device="cpu").pin_memory()
+    # one pinned output buffer per tick (the same bytes per step as a single
+    # reused buffer), kept for the parity check after the timed region
+    host_outs = [None if tk["q"] is None else
+                 torch.empty((len(tk["active"]),) + tuple(out.shape[1:]), dtype=out.dtype).pin_memory()
+                 for tk in ticks]
     qbuf = torch.empty((w.num_requests, w.num_layers, w.q_heads, 128), dtype=torch.float16, device=dev)
     ibuf = torch.empty(w.num_requests, dtype=torch.int32, device=dev)
     h2d = d2h = 0
@@ -361,7 +391,7 @@ def run_ferry(args, w):
         qbuf[:n].copy_(pin_q[i], non_blocking=True)
         ibuf[:n].copy_(pin_ids[i], non_blocking=True)
         dec.step(qbuf[:n], ibuf[:n], out[:n], stream=st)
-        host_out[:n].copy_(out[:n], non_blocking=True)
+        host_outs[i].copy_(out[:n], non_blocking=True)
         h2d += pin_q[i].numel() * 2 + n * 4
         d2h += n * w.num_layers * w.q_heads * 128 * 4
         return n
@@ -381,6 +411,7 @@ def run_ferry(args, w):
     torch.cuda.synchronize(dev)
     e2e_ms = t0.elapsed_time(t1)
     dec.check()
+    e2e_units = dec.stats()[0]  # page units gathered over every tick of the pass
     if ws > 1:
         t = torch.tensor([e2e_ms, float(e2e_tokens)], dtype=torch.float64, device=dev)
         mx = t.clone()
@@ -456,9 +487,11 @@ def run_ferry(args, w):
         }
         line["clocks"] = clk.summary()
         if ws == 1 and not args.no_cpu_baseline:
-            v, threads, sample, _ = cpu_baseline(w, seconds=args.cpu_seconds)
+            v, threads, sample, per_tick = cpu_baseline(w, seconds=args.cpu_seconds, keep=n_ticks)
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
                                     "sample": sample}
+            line["parity"] = parity_vs_cpu(w, [None if h is None else h.numpy() for h in host_outs],
+                                           e2e_units, per_tick)
         print(json.dumps(line), flush=True)
     if ws > 1:
         dist.barrier()

@@ -49,3 +49,25 @@ def test_peaks_come_from_the_measured_file_when_present(bench):
     assert peak > 1000.0
     if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")):
         assert kind == "measured"
+
+
+def test_parity_check_against_the_cpu_pipeline(bench):
+    """The bench's parity field: the CPU pipeline's own outputs pass, a
+    planted error in one row (on the CPU side) fails, and the gathered-unit
+    count must equal the pipeline's misses."""
+    import numpy as np
+
+    from ferry_b200.workload import small
+
+    w = small(num_requests=3, num_layers=1, q_heads=4, kv_heads=2, ctx_tokens=512, top_k=8, steps=4)
+    _, _, _, per_tick = bench.cpu_baseline(w, threads=2, ticks=6, keep=6)
+    outs = [None if x[3] is None else x[3].reshape(-1, w.num_layers, w.q_heads, 128).copy() for x in per_tick]
+    misses = sum(x[2] for x in per_tick)
+    assert misses > 0 and any(o is not None for o in outs)
+    p = bench.parity_vs_cpu(w, outs, misses, per_tick)
+    assert p["status"] == "ok" and p["attn_max_rel_err"] == 0.0 and p["ticks"] == 6
+    bad = [None if o is None else o.copy() for o in outs]
+    j = next(i for i, o in enumerate(bad) if o is not None)
+    bad[j].reshape(-1, 128)[0, 5] += 1.0
+    assert bench.parity_vs_cpu(w, bad, misses, per_tick)["status"] == "FAIL"
+    assert bench.parity_vs_cpu(w, outs, misses + 1, per_tick)["status"] == "FAIL"

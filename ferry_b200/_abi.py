@@ -18,13 +18,14 @@ KV_F16 = 0
 KV_E4M3 = 1
 UNIT_BYTES = {KV_F16: 8192, KV_E4M3: 4112}
 LRU_DISTINCT = 1
+SELECT_MEAN, SELECT_QUEST = 0, 1
 
 # every symbol include/ferry_cuda.h declares
 EXPORTS = [
     "ferry_last_error", "ferry_version", "ferry_ctx_create", "ferry_ctx_destroy",
     "ferry_ctx_check", "ferry_host_alloc", "ferry_host_free", "ferry_kv_register",
     "ferry_kv_generate", "ferry_page_summary_update", "ferry_requests_begin",
-    "ferry_select_topk", "ferry_detect_misses", "ferry_gather_misses", "ferry_sparse_decode",
+    "ferry_select_mode", "ferry_select_topk", "ferry_detect_misses", "ferry_gather_misses", "ferry_sparse_decode",
     "ferry_sparse_decode_noalloc", "ferry_sparse_decode_noalloc_status", "ferry_decode_step", "ferry_wait_flag", "ferry_stats_read", "ferry_debug_read",
     "ferry_ctx_export", "ferry_store_create", "ferry_store_fill", "ferry_gather_source",
     "ferry_ctx_import", "ferry_ctx_link", "ferry_migrate_requests",
@@ -96,6 +97,7 @@ _SIGS = {
     "ferry_kv_generate": (I, [V, C.c_uint64, C.c_uint64, C.c_int64, V, I]),
     "ferry_page_summary_update": (I, [V, V, C.c_int64, C.c_int64]),
     "ferry_requests_begin": (I, [V, V, V, V, V, I]),
+    "ferry_select_mode": (I, [V, I]),
     "ferry_select_topk": (I, [V, V, V, V, I, V, V]),
     "ferry_detect_misses": (I, [V, V, V, I, V, V, V, V, V, V, V]),
     "ferry_gather_misses": (I, [V, V, V, I, V, V, V]),

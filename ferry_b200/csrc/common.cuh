@@ -220,7 +220,11 @@ struct ferry_ctx {
   // host pool
   uint8_t* pool_dev = nullptr;  // device-visible address of the pinned pool
   uint64_t pool_units = 0;
-  float* summ = nullptr;  // pool_units * 128
+  float* summ = nullptr;  // pool_units * summ_row: mean rows (128) or Quest [kmin | kmax] rows (256)
+  int summ_row = ferry::kHeadDim;
+  int select_mode = FERRY_SELECT_MEAN;
+  uint32_t* quest_keys = nullptr;  // R * L * max_pages order keys (Quest mode)
+  uint32_t* quest_done = nullptr;  // R * L chunk counters (Quest mode)
 
   // decode-step workspace (sized for R requests)
   int32_t* ws = nullptr;
@@ -260,6 +264,11 @@ int launch_summary(cudaStream_t st, const uint8_t* pool, int64_t unit0, int64_t 
                    float* summ, int kv_dtype);
 int launch_select(const ferry_ctx* c, cudaStream_t st, const uint16_t* q, const int32_t* req_ids,
                   int n_req, int32_t* sel, int32_t* n_sel);
+// Quest page bounds [kmin | kmax] of pool units (kvgen.cu)
+int launch_minmax(cudaStream_t st, const uint8_t* pool, int64_t unit0, int64_t n_units, float* mm,
+                  int kv_dtype);
+// dynamic shared memory of the Quest selection kernel (select.cu)
+size_t select_quest_smem(int q_heads, int max_pages);
 int launch_lru(const ferry_lru* L, cudaStream_t st, const int32_t* lane_ids, const int32_t* req_ids,
                int lanes_per_req, const uint8_t* reset, int n, const int32_t* sel, int k,
                const int32_t* n_sel, int distinct, uint8_t* is_miss, int32_t* item_slot,

@@ -114,6 +114,8 @@ void destroy_ctx(ferry_ctx* c) {
   cudaFree(c->sel_keys);
   cudaFree(c->store);
   cudaFree(c->sel_done);
+  cudaFree(c->quest_keys);
+  cudaFree(c->quest_done);
   cudaFree(c->err);
   cudaFree(c->stats);
   delete c;
@@ -235,6 +237,8 @@ int ferry_ctx_check(ferry_ctx* c) {
   FERRY_TRY(cudaMemset(c->err, 0, 4));
   FERRY_TRY(cudaMemset(c->lane_done, 0, (size_t)c->lanes * 4));
   if (c->sel_done) FERRY_TRY(cudaMemset(c->sel_done, 0, (size_t)c->lanes * 4));
+  if (c->quest_done)
+    FERRY_TRY(cudaMemset(c->quest_done, 0, (size_t)c->cfg.num_requests * c->cfg.num_layers * 4));
   if (e & kErrTimeout) return set_error("a device wait timed out"), FERRY_E_TIMEOUT;
   return set_error("a kernel saw an out-of-range index"), FERRY_E_RANGE;
 }
@@ -267,7 +271,7 @@ int ferry_kv_register(ferry_ctx* c, void* host_pool, size_t bytes) {
   }
   const uint64_t units = bytes / c->unit_bytes;
   float* summ = nullptr;
-  int rc = dev_alloc(&summ, (size_t)units * kHeadDim, 0);
+  int rc = dev_alloc(&summ, (size_t)units * c->summ_row, 0);
   if (rc) return rc;
   cudaFree(c->summ);
   c->summ = summ;
@@ -287,7 +291,36 @@ int ferry_page_summary_update(ferry_ctx* c, void* stream, int64_t unit0, int64_t
   if (unit0 < 0 || n_units < 0 || (uint64_t)(unit0 + n_units) > c->pool_units)
     return set_error("summary range outside the pool"), FERRY_E_INVAL;
   DeviceGuard guard(c->device);
+  if (c->select_mode == FERRY_SELECT_QUEST)
+    return launch_minmax((cudaStream_t)stream, c->pool_dev, unit0, n_units, c->summ, c->cfg.kv_dtype);
   return launch_summary((cudaStream_t)stream, c->pool_dev, unit0, n_units, c->summ, c->cfg.kv_dtype);
+}
+
+int ferry_select_mode(ferry_ctx* c, int mode) {
+  if (!c) return set_error("ctx is NULL"), FERRY_E_INVAL;
+  if (mode != FERRY_SELECT_MEAN && mode != FERRY_SELECT_QUEST)
+    return set_error("select_mode: unknown mode %d", mode), FERRY_E_INVAL;
+  if (c->pool_dev) return set_error("select_mode: set it before ferry_kv_register"), FERRY_E_STATE;
+  if (mode == FERRY_SELECT_QUEST) {
+    if (select_quest_smem(c->cfg.q_heads, c->cfg.max_pages) > 200 * 1024)
+      return set_error("select_mode: %d q heads and %d pages exceed the Quest kernel's shared memory",
+                       c->cfg.q_heads, c->cfg.max_pages),
+             FERRY_E_INVAL;
+    DeviceGuard guard(c->device);
+    const size_t groups = (size_t)c->cfg.num_requests * c->cfg.num_layers;
+    if (!c->quest_keys) {
+      int rc = dev_alloc(&c->quest_keys, groups * c->cfg.max_pages, 0);
+      if (!rc) rc = dev_alloc(&c->quest_done, groups, 0);
+      if (rc) {
+        cudaFree(c->quest_keys);
+        c->quest_keys = nullptr;
+        return rc;
+      }
+    }
+  }
+  c->select_mode = mode;
+  c->summ_row = mode == FERRY_SELECT_QUEST ? 2 * kHeadDim : kHeadDim;
+  return FERRY_OK;
 }
 
 int ferry_requests_begin(ferry_ctx* c, void* stream, const int32_t* d_req_ids,
@@ -395,7 +428,7 @@ int ferry_debug_read(ferry_ctx* c, int which, size_t offset, size_t bytes, void*
     case 1: base = (uint8_t*)c->lru.page_slot; size = (size_t)c->lanes * c->cfg.max_pages * 4; break;
     case 2: base = (uint8_t*)c->lru.order; size = (size_t)c->lanes * c->cfg.cache_pages * 4; break;
     case 3: base = (uint8_t*)c->lru.size; size = (size_t)c->lanes * 4; break;
-    case 4: base = (uint8_t*)c->summ; size = (size_t)c->pool_units * kHeadDim * 4; break;
+    case 4: base = (uint8_t*)c->summ; size = (size_t)c->pool_units * c->summ_row * 4; break;
     case 5: base = (uint8_t*)c->ctx_pages; size = R * 4; break;
     case 6: base = (uint8_t*)c->ws; size = R * LH * (4 * k + 2) * 4; break;
     case 7: base = (uint8_t*)c->req_base; size = R * 8; break;

@@ -190,6 +190,55 @@ __global__ void __launch_bounds__(256) summary_kernel(const uint8_t* __restrict_
   }
 }
 
+
+// Quest page bounds: per dim the min and max of the page's 16 keys, rows
+// [kmin[128] | kmax[128]] fp32 (e4m3: dequantised keys, value * k_scale with
+// one rounding). Tokens in order; a later token replaces only when strictly
+// smaller / larger. One warp per unit; lane l owns dims 4l..4l+3.
+template <bool F8>
+__global__ void __launch_bounds__(256) minmax_kernel(const uint8_t* __restrict__ pool, int64_t unit0,
+                                                     int64_t n_units, float* __restrict__ mm) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t u = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < n_units; u += warps) {
+    float lo[4], hi[4];
+    if (F8) {
+      const uint8_t* K = pool + (size_t)(unit0 + u) * kUnitBytesF8;
+      const float ks = *reinterpret_cast<const float*>(K + 4096);
+#pragma unroll
+      for (int tt = 0; tt < kPageTokens; ++tt) {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(K + tt * kHeadDim + lane * 4);
+        const __half2_raw a = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w & 0xFFFF), __NV_E4M3);
+        const __half2_raw b = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w >> 16), __NV_E4M3);
+        const float v[4] = {__half2float(__ushort_as_half(a.x)), __half2float(__ushort_as_half(a.y)),
+                            __half2float(__ushort_as_half(b.x)), __half2float(__ushort_as_half(b.y))};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float kv = __fmul_rn(v[j], ks);
+          lo[j] = (tt == 0 || kv < lo[j]) ? kv : lo[j];
+          hi[j] = (tt == 0 || kv > hi[j]) ? kv : hi[j];
+        }
+      }
+    } else {
+      const uint8_t* K = pool + (size_t)(unit0 + u) * kUnitBytes;
+#pragma unroll
+      for (int tt = 0; tt < kPageTokens; ++tt) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(K + tt * kHeadDim * 2 + lane * 8);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+        const float v[4] = {a.x, a.y, b.x, b.y};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          lo[j] = (tt == 0 || v[j] < lo[j]) ? v[j] : lo[j];
+          hi[j] = (tt == 0 || v[j] > hi[j]) ? v[j] : hi[j];
+        }
+      }
+    }
+    float4* row = reinterpret_cast<float4*>(mm + (size_t)(unit0 + u) * 2 * kHeadDim);
+    row[lane] = make_float4(lo[0], lo[1], lo[2], lo[3]);
+    row[32 + lane] = make_float4(hi[0], hi[1], hi[2], hi[3]);
+  }
+}
 }  // namespace
 
 int launch_kv_generate(cudaStream_t st, uint64_t seed, uint64_t unit0, int64_t n_units,
@@ -226,6 +275,18 @@ int launch_summary(cudaStream_t st, const uint8_t* pool, int64_t unit0, int64_t 
     summary_e4m3_kernel<<<(unsigned)blocks, 256, 0, st>>>(pool, unit0, n_units, summ);
   else
     summary_kernel<<<(unsigned)blocks, 256, 0, st>>>(pool, unit0, n_units, summ);
+  FERRY_TRY(cudaGetLastError());
+  return FERRY_OK;
+}
+
+int launch_minmax(cudaStream_t st, const uint8_t* pool, int64_t unit0, int64_t n_units, float* mm,
+                  int kv_dtype) {
+  if (n_units <= 0) return FERRY_OK;
+  const int64_t blocks = std::min<int64_t>((n_units + 7) / 8, 148 * 16);
+  if (kv_dtype == FERRY_KV_E4M3)
+    minmax_kernel<true><<<(unsigned)blocks, 256, 0, st>>>(pool, unit0, n_units, mm);
+  else
+    minmax_kernel<false><<<(unsigned)blocks, 256, 0, st>>>(pool, unit0, n_units, mm);
   FERRY_TRY(cudaGetLastError());
   return FERRY_OK;
 }

@@ -79,6 +79,106 @@ __device__ __forceinline__ float transpose_reduce(float (&w)[V]) {
 
 __device__ __forceinline__ uint32_t lanemask_lt(int lane) { return (1u << lane) - 1u; }
 
+// Shared state of topk_emit.
+struct TopkSmem {
+  uint32_t hist[256];
+  uint32_t wcnt[2][kSelWarps];
+  uint32_t s_prefix, s_krem;
+};
+
+// Top-k of np > k order keys in shared memory by one block of kSelThreads:
+// phase 2, a 4-pass 8-bit radix select of the k-th largest key (warp-aggregated
+// histogram atomics); phase 3, emission in ascending page order of every page
+// whose key is larger plus the lowest-id pages equal to it (ties go to the
+// lower page id). Writes out[0, k).
+__device__ __forceinline__ void topk_emit(const uint32_t* keys, int np, int k, int32_t* out,
+                                          TopkSmem& S) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t* hist = S.hist;
+  auto& wcnt = S.wcnt;
+  // ---- phase 2: radix select of the k-th largest key
+  uint32_t prefix = 0, mask = 0, krem = (uint32_t)k;
+#pragma unroll 1
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    hist[tid] = 0;  // kSelThreads == 256 bins
+    __syncthreads();
+    for (int base = 0; base < np; base += kSelThreads) {  // block-uniform
+      const int p = base + tid;
+      const uint32_t key = p < np ? keys[p] : 0u;
+      const bool act = p < np && (key & mask) == prefix;
+      const uint32_t bin = act ? (key >> shift) & 255u : 256u;
+      const uint32_t m = __match_any_sync(0xffffffffu, bin);
+      if (act && lane == __ffs(m) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(m));
+    }
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t c[8], tot = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = hist[255 - (lane * 8 + j)];
+        tot += c[j];
+      }
+      uint32_t incl = tot;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t v = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += v;
+      }
+      const uint32_t excl = incl - tot;
+      if (excl < krem && krem <= incl) {
+        uint32_t run = excl;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (run + c[j] >= krem) {
+            S.s_prefix = prefix | ((uint32_t)(255 - (lane * 8 + j)) << shift);
+            S.s_krem = krem - run;
+            break;
+          }
+          run += c[j];
+        }
+      }
+    }
+    __syncthreads();
+    prefix = S.s_prefix;
+    krem = S.s_krem;
+    mask |= 255u << shift;
+  }
+  const uint32_t T = prefix;
+
+  // ---- phase 3: ordered emission; warp w owns pages [w * span, (w + 1) * span)
+  const int span = ((np + kSelWarps * 32 - 1) / (kSelWarps * 32)) * 32;
+  const int lo = warp * span, hi = min(np, lo + span);
+  uint32_t ngt = 0, neq = 0;
+  for (int base = lo; base < hi; base += 32) {  // warp-uniform
+    const int p = base + lane;
+    const uint32_t key = p < hi ? keys[p] : 0u;
+    ngt += __popc(__ballot_sync(0xffffffffu, p < hi && key > T));
+    neq += __popc(__ballot_sync(0xffffffffu, p < hi && key == T));
+  }
+  if (lane == 0) {
+    wcnt[0][warp] = ngt;
+    wcnt[1][warp] = neq;
+  }
+  __syncthreads();
+  uint32_t gt_before = 0, eq_before = 0;
+  for (int w = 0; w < warp; ++w) {
+    gt_before += wcnt[0][w];
+    eq_before += wcnt[1][w];
+  }
+  uint32_t pos = gt_before + min(eq_before, krem), eq_rank = eq_before;
+  for (int base = lo; base < hi; base += 32) {
+    const int p = base + lane;
+    const uint32_t key = p < hi ? keys[p] : 0u;
+    const bool gt = p < hi && key > T, eq = p < hi && key == T;
+    const uint32_t meq = __ballot_sync(0xffffffffu, eq);
+    const bool take = gt || (eq && eq_rank + __popc(meq & lanemask_lt(lane)) < krem);
+    const uint32_t mt = __ballot_sync(0xffffffffu, take);
+    if (take) out[pos + __popc(mt & lanemask_lt(lane))] = p;
+    pos += __popc(mt);
+    eq_rank += __popc(meq);
+  }
+}
+
 struct SelArgs {
   const uint16_t* q;
   const int32_t* req_ids;
@@ -103,9 +203,8 @@ __global__ void __launch_bounds__(kSelThreads, 2) select_kernel(SelArgs A) {
   uint8_t* ring = sel_smem;
   uint32_t* keys = reinterpret_cast<uint32_t*>(sel_smem + (A.nchunks > 1 ? 0 : kRingBytes));
   __shared__ __align__(8) uint64_t bars[kSelStages];
-  __shared__ uint32_t hist[256];
-  __shared__ uint32_t wcnt[2][kSelWarps];
-  __shared__ uint32_t s_prefix, s_krem, s_last;
+  __shared__ TopkSmem tk;
+  __shared__ uint32_t s_last;
 
   const int a = blockIdx.x / A.nchunks, chunk = blockIdx.x % A.nchunks;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -239,95 +338,162 @@ __global__ void __launch_bounds__(kSelThreads, 2) select_kernel(SelArgs A) {
     return;
   }
 
-  // ---- phase 2: radix select of the k-th largest key
-  uint32_t prefix = 0, mask = 0, krem = (uint32_t)k;
-#pragma unroll 1
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    hist[tid] = 0;  // kSelThreads == 256 bins
-    __syncthreads();
-    for (int base = 0; base < np; base += kSelThreads) {  // block-uniform
-      const int p = base + tid;
-      const uint32_t key = p < np ? keys[p] : 0u;
-      const bool act = p < np && (key & mask) == prefix;
-      const uint32_t bin = act ? (key >> shift) & 255u : 256u;
-      const uint32_t m = __match_any_sync(0xffffffffu, bin);
-      if (act && lane == __ffs(m) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(m));
-    }
-    __syncthreads();
-    if (warp == 0) {
-      uint32_t c[8], tot = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        c[j] = hist[255 - (lane * 8 + j)];
-        tot += c[j];
-      }
-      uint32_t incl = tot;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const uint32_t v = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += v;
-      }
-      const uint32_t excl = incl - tot;
-      if (excl < krem && krem <= incl) {
-        uint32_t run = excl;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (run + c[j] >= krem) {
-            s_prefix = prefix | ((uint32_t)(255 - (lane * 8 + j)) << shift);
-            s_krem = krem - run;
-            break;
-          }
-          run += c[j];
-        }
-      }
-    }
-    __syncthreads();
-    prefix = s_prefix;
-    krem = s_krem;
-    mask |= 255u << shift;
-  }
-  const uint32_t T = prefix;
-
-  // ---- phase 3: ordered emission; warp w owns pages [w * span, (w + 1) * span)
-  const int span = ((np + kSelWarps * 32 - 1) / (kSelWarps * 32)) * 32;
-  const int lo = warp * span, hi = min(np, lo + span);
-  uint32_t ngt = 0, neq = 0;
-  for (int base = lo; base < hi; base += 32) {  // warp-uniform
-    const int p = base + lane;
-    const uint32_t key = p < hi ? keys[p] : 0u;
-    ngt += __popc(__ballot_sync(0xffffffffu, p < hi && key > T));
-    neq += __popc(__ballot_sync(0xffffffffu, p < hi && key == T));
-  }
-  if (lane == 0) {
-    wcnt[0][warp] = ngt;
-    wcnt[1][warp] = neq;
-  }
-  __syncthreads();
-  uint32_t gt_before = 0, eq_before = 0;
-  for (int w = 0; w < warp; ++w) {
-    gt_before += wcnt[0][w];
-    eq_before += wcnt[1][w];
-  }
-  uint32_t pos = gt_before + min(eq_before, krem), eq_rank = eq_before;
-  for (int base = lo; base < hi; base += 32) {
-    const int p = base + lane;
-    const uint32_t key = p < hi ? keys[p] : 0u;
-    const bool gt = p < hi && key > T, eq = p < hi && key == T;
-    const uint32_t meq = __ballot_sync(0xffffffffu, eq);
-    const bool take = gt || (eq && eq_rank + __popc(meq & lanemask_lt(lane)) < krem);
-    const uint32_t mt = __ballot_sync(0xffffffffu, take);
-    if (take) out[pos + __popc(mt & lanemask_lt(lane))] = p;
-    pos += __popc(mt);
-    eq_rank += __popc(meq);
-  }
+  topk_emit(keys, np, k, out, tk);
   if (tid == 0) A.n_sel_out[a] = k;
 }
 
+
+// ---------------------------------------------------------------------------
+// Quest selection (the reference's Selector.on_layer method "quest",
+// tools/capture_miss_trace.py:139-147, 158-159): one page set per (request,
+// layer) -- a "group lane" of Hkv kv-head lanes -- scored by
+//   score(p) = max over kv heads h, group heads g of
+//              sum_d max(q[h,g,d] * kmax[h,p,d], q[h,g,d] * kmin[h,p,d])
+// over per-page key bounds (pool rows [kmin[128] | kmax[128]] fp32). Fixed
+// arithmetic (the oracle's): products rounded to fp32, a >= b ? a : b with
+// a = q*kmax, lane l sums dims 4l..4l+3 in order, the lanes combine by the
+// xor butterfly 16, 8, 4, 2, 1; heads kv-head major, the first wins ties.
+// A CTA scores kQuestChunk pages of one group lane, one page per warp at a
+// time (all Hkv x G bounds of that page); the last CTA of the group lane runs
+// topk_emit and copies the page set into the rows of all Hkv lanes.
+constexpr int kQuestChunk = 64;
+
+struct QuestArgs {
+  const uint16_t* q;
+  const int32_t* req_ids;
+  int L, Hkv, G;
+  const int32_t* ctx_pages;
+  const int64_t* req_base;
+  const float* mm;
+  uint64_t pool_units;
+  int N, k, num_requests, nchunks;
+  uint32_t* gkeys;  // [batch group lanes][N]
+  uint32_t* done;   // [batch group lanes], back to 0 after each launch
+  int32_t* sel_out;
+  int32_t* n_sel_out;
+  uint32_t* err;
+};
+
+__device__ __forceinline__ float quest_term(float q, float lo, float hi) {
+  const float a = __fmul_rn(q, hi), b = __fmul_rn(q, lo);
+  return a >= b ? a : b;
+}
+
+__global__ void __launch_bounds__(kSelThreads) select_quest_kernel(QuestArgs A) {
+  extern __shared__ __align__(16) uint8_t quest_smem[];
+  const int Hq = A.Hkv * A.G;
+  float* qs = reinterpret_cast<float*>(quest_smem);                          // Hq x 128
+  uint32_t* keys = reinterpret_cast<uint32_t*>(quest_smem + (size_t)Hq * kHeadDim * 4);  // N
+  __shared__ TopkSmem tk;
+  __shared__ uint32_t s_last;
+  const int ag = blockIdx.x / A.nchunks, chunk = blockIdx.x % A.nchunks;
+  const int i = ag / A.L, layer = ag % A.L;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int k = A.k, N = A.N;
+  int32_t* out0 = A.sel_out + (size_t)ag * A.Hkv * k;
+  const int req = A.req_ids[i];
+  if (req < 0 || req >= A.num_requests) {  // every chunk of the group lane takes this path
+    if (tid == 0) record_error(A.err, kErrRange);
+    for (int x = tid; x < A.Hkv * k; x += kSelThreads) out0[x] = -1;
+    for (int h = tid; h < A.Hkv; h += kSelThreads) A.n_sel_out[(size_t)ag * A.Hkv + h] = 0;
+    return;
+  }
+  int np = A.ctx_pages[req];
+  if (np < 0 || np > N) {
+    if (tid == 0) record_error(A.err, kErrRange);
+    np = np < 0 ? 0 : N;
+  }
+  for (int x = tid; x < Hq * kHeadDim; x += kSelThreads)
+    qs[x] = __half2float(__ushort_as_half(A.q[(size_t)ag * Hq * kHeadDim + x]));
+  __syncthreads();
+  const int c0 = chunk * kQuestChunk, c1 = min(np, c0 + kQuestChunk);
+  uint32_t* kd = A.gkeys + (size_t)ag * N;
+  const int64_t lane0 = A.req_base[req] + (int64_t)layer * A.Hkv * N;  // pool unit of (h = 0, p = 0)
+  for (int p = c0 + warp; p < c1; p += kSelWarps) {  // warp-uniform
+    float best = 0.f;
+#pragma unroll 1
+    for (int h = 0; h < A.Hkv; ++h) {
+      const uint64_t unit = (uint64_t)(lane0 + (int64_t)h * N + p) % A.pool_units;
+      const float4 lo = __ldg(reinterpret_cast<const float4*>(A.mm + unit * 2 * kHeadDim) + lane);
+      const float4 hi = __ldg(reinterpret_cast<const float4*>(A.mm + unit * 2 * kHeadDim + kHeadDim) + lane);
+#pragma unroll 1
+      for (int g = 0; g < A.G; ++g) {
+        const float4 qv = reinterpret_cast<const float4*>(qs + (size_t)(h * A.G + g) * kHeadDim)[lane];
+        float v = quest_term(qv.x, lo.x, hi.x);
+        v = __fadd_rn(v, quest_term(qv.y, lo.y, hi.y));
+        v = __fadd_rn(v, quest_term(qv.z, lo.z, hi.z));
+        v = __fadd_rn(v, quest_term(qv.w, lo.w, hi.w));
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+        if ((h == 0 && g == 0) || v > best) best = v;
+      }
+    }
+    if (lane == 0) kd[p] = order_key(best);
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&A.done[ag], 1u) == (uint32_t)(A.nchunks - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (tid == 0) A.done[ag] = 0;
+  for (int p = tid; p < np; p += kSelThreads) keys[p] = __ldcg(kd + p);
+  __syncthreads();
+  if (np <= k) {
+    for (int j = tid; j < k; j += kSelThreads) out0[j] = j < np ? j : -1;
+  } else {
+    topk_emit(keys, np, k, out0, tk);
+  }
+  __syncthreads();  // out0 (global) written by this block is visible to the block
+  for (int x = tid; x < (A.Hkv - 1) * k; x += kSelThreads) out0[k + x] = out0[x % k];
+  for (int h = tid; h < A.Hkv; h += kSelThreads) A.n_sel_out[(size_t)ag * A.Hkv + h] = min(np, k);
+}
 }  // namespace
+
+size_t select_quest_smem(int q_heads, int max_pages) {
+  return (size_t)q_heads * kHeadDim * 4 + (size_t)max_pages * 4;
+}
+
+static int launch_select_quest(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,
+                               const int32_t* req_ids, int n_req, int32_t* sel, int32_t* n_sel) {
+  QuestArgs A{};
+  A.q = q;
+  A.req_ids = req_ids;
+  A.L = c->cfg.num_layers;
+  A.Hkv = c->cfg.kv_heads;
+  A.G = c->group;
+  A.ctx_pages = c->ctx_pages;
+  A.req_base = c->req_base;
+  A.mm = c->summ;
+  A.pool_units = c->pool_units;
+  A.N = c->cfg.max_pages;
+  A.k = c->cfg.top_k;
+  A.num_requests = c->cfg.num_requests;
+  A.nchunks = (A.N + kQuestChunk - 1) / kQuestChunk;
+  A.gkeys = c->quest_keys;
+  A.done = c->quest_done;
+  A.sel_out = sel;
+  A.n_sel_out = n_sel;
+  A.err = c->err;
+  if (!A.gkeys || !A.done) {
+    set_error("select: Quest scratch missing");
+    return FERRY_E_STATE;
+  }
+  const size_t smem = select_quest_smem(c->cfg.q_heads, A.N);
+  if (smem > 48 * 1024)
+    FERRY_TRY(cudaFuncSetAttribute(select_quest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)smem));
+  const unsigned grid = (unsigned)((int64_t)n_req * A.L * A.nchunks);
+  select_quest_kernel<<<grid, kSelThreads, smem, st>>>(A);
+  FERRY_TRY(cudaGetLastError());
+  return FERRY_OK;
+}
 
 int launch_select(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,
                   const int32_t* req_ids, int n_req, int32_t* sel, int32_t* n_sel) {
   if (n_req <= 0) return FERRY_OK;
+  if (c->select_mode == FERRY_SELECT_QUEST)
+    return launch_select_quest(c, st, q, req_ids, n_req, sel, n_sel);
   SelArgs A{};
   A.q = q;
   A.req_ids = req_ids;

@@ -57,7 +57,7 @@ class PinnedPool:
 
 
 class Decoder:
-    def __init__(self, w: Workload, device: int = 0):
+    def __init__(self, w: Workload, device: int = 0, select_mode: int = _abi.SELECT_MEAN):
         self.w = w
         self.device = device
         self.dev = torch.device("cuda", device)
@@ -66,6 +66,9 @@ class Decoder:
         h = C.c_void_p()
         call("ferry_ctx_create", device, C.byref(cfg), C.byref(h))
         self.ctx = h
+        if select_mode != _abi.SELECT_MEAN:
+            call("ferry_select_mode", h, select_mode)
+        self.select_mode = select_mode
         self.pool: PinnedPool | None = None
         LH, k = w.lanes_per_req, w.top_k
         n = w.num_requests * LH

@@ -126,9 +126,23 @@ int ferry_requests_begin(ferry_ctx* ctx, void* stream, const int32_t* d_req_ids,
 
 /* ---- the four hot-path steps --------------------------------------------- */
 
-/* Top-k page selection: score = q . mean-key summary per kv head (max over
- * the GQA group), top-k descending with ties to the lower page id, output
- * ascending by page id. d_sel: [n_req*L*Hkv][k]; d_n_sel: [n_req*L*Hkv].
+/* Selection rule of the ctx (set before ferry_kv_register; FERRY_E_STATE after).
+ * FERRY_SELECT_MEAN (default): per lane (request, layer, kv head), score =
+ *   q . mean-key page summary, max over the GQA group -- the benchmark's rule.
+ * FERRY_SELECT_QUEST: the reference's Quest method, Selector.on_layer
+ *   (tools/capture_miss_trace.py:139-147, 158-159): per-page key min/max,
+ *   bound = sum_d max(q_d * kmax_d, q_d * kmin_d), max over the GQA group and
+ *   then over the kv heads, top-k, ascending -- ONE page set per (request,
+ *   layer), written to the rows of all its kv-head lanes. Page summaries then
+ *   hold [kmin[128] | kmax[128]] fp32 rows (1 KiB per pool unit).
+ * Both: ties to the lower page id; a lane with n <= k pages selects all. */
+#define FERRY_SELECT_MEAN 0
+#define FERRY_SELECT_QUEST 1
+int ferry_select_mode(ferry_ctx* ctx, int mode);
+
+/* Top-k page selection under the ctx's selection rule (ferry_select_mode;
+ * default: score = q . mean-key summary per kv head, max over the GQA group),
+ * top-k descending with ties to the lower page id, output ascending by page id. d_sel: [n_req*L*Hkv][k]; d_n_sel: [n_req*L*Hkv].
  * Replaces Selector.on_layer (tools/capture_miss_trace.py:128-159) and the
  * synthetic selector of replay_miss_stream (src/workloads/missstream.cuh:118-133). */
 int ferry_select_topk(ferry_ctx* ctx, void* stream, const uint16_t* d_q,

@@ -85,6 +85,10 @@ def lib():
         L.orc_kv_gen_e4m3_mt.argtypes = [C.c_uint64, C.c_uint64, C.c_int64, C.c_void_p, C.c_int]
         L.orc_e4m3_unit_dequant.argtypes = [C.c_void_p, C.c_int64, C.c_void_p]
         L.orc_page_summary_e4m3.argtypes = [C.c_void_p, C.c_int64, C.c_void_p]
+        L.orc_page_minmax.argtypes = [C.c_void_p, C.c_int64, C.c_void_p]
+        L.orc_page_minmax_e4m3.argtypes = [C.c_void_p, C.c_int64, C.c_void_p]
+        L.orc_select_quest.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
+                                       C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
         L.orc_pipe_create.restype = C.c_void_p
         L.orc_pipe_create.argtypes = [C.c_int] * 5 + [C.c_void_p, C.c_void_p, C.c_int]
         L.orc_pipe_destroy.argtypes = [C.c_void_p]
@@ -325,6 +329,40 @@ def sparse_decode(q_f16bits: np.ndarray, pages: np.ndarray, n_sel, scale: float)
     lib().orc_sparse_decode(q.ctypes.data, G, pages.ctypes.data, n_sel.ctypes.data, lanes, k,
                             C.c_float(scale), out.ctypes.data)
     return out
+
+
+def page_minmax(units: np.ndarray) -> np.ndarray:
+    """Quest page bounds of fp16 units: rows [kmin[128] | kmax[128]] fp32."""
+    units = _f16bits(units).reshape(-1, UNIT_ELEMS)
+    out = np.zeros((units.shape[0], 256), np.float32)
+    lib().orc_page_minmax(units.ctypes.data, units.shape[0], out.ctypes.data)
+    return out
+
+
+def page_minmax_e4m3(units: np.ndarray) -> np.ndarray:
+    """Quest page bounds of e4m3 units (dequantised keys)."""
+    units = np.ascontiguousarray(units, np.uint8).reshape(-1, UNIT_BYTES_E4M3)
+    out = np.zeros((units.shape[0], 256), np.float32)
+    lib().orc_page_minmax_e4m3(units.ctypes.data, units.shape[0], out.ctypes.data)
+    return out
+
+
+def select_quest(q_f16bits: np.ndarray, kv_heads: int, mm: np.ndarray, n_pages, k: int,
+                 return_scores=False):
+    """The reference's Quest selection (one page set per request and layer).
+    q: [n_grp, Hkv * G, 128] fp16 (bits or values); mm: [n_grp, Hkv, N, 256]."""
+    q = _f16bits(q_f16bits)
+    n_grp, Hq, _ = q.shape
+    G = Hq // kv_heads
+    mm = np.ascontiguousarray(mm, np.float32)
+    N = mm.shape[2]
+    n_pages = np.ascontiguousarray(n_pages, np.int32)
+    sel = np.full((n_grp, k), -1, np.int32)
+    ns = np.zeros(n_grp, np.int32)
+    sc = np.zeros((n_grp, N), np.float32)
+    lib().orc_select_quest(q.ctypes.data, kv_heads, G, mm.ctypes.data, N, n_pages.ctypes.data, n_grp, k,
+                           sel.ctypes.data, ns.ctypes.data, sc.ctypes.data)
+    return (sel, ns, sc) if return_scores else (sel, ns)
 
 
 class CpuPipeline:

@@ -718,6 +718,111 @@ int orc_page_summary_e4m3(const uint8_t* units, int64_t n_units, float* summ) {
   return 0;
 }
 
+// ===========================================================================
+// 4b. Quest selection, the reference's Selector.on_layer method "quest"
+//     (tools/capture_miss_trace.py:139-147, 158-159): per page and dim the min
+//     and max of its keys; bound(head, page) = sum_d max(q_d*kmax_d, q_d*kmin_d);
+//     score(page) = max over the GQA group, then over the kv heads (one page set
+//     per layer); top-k by score, ascending output. Fixed arithmetic: products
+//     rounded to fp32, max(a = q*kmax, b = q*kmin) = a >= b ? a : b, lane l sums
+//     dims 4l..4l+3 in order, the 32 lane sums combine by the xor butterfly
+//     (16, 8, 4, 2, 1); heads scanned kv head major, the first head wins ties;
+//     top-k ties to the lower page id. min/max over tokens in token order
+//     (a later token replaces only when strictly smaller / larger).
+// ===========================================================================
+static void minmax_rows(const float* K /* 16 x 128 */, float* mm) {
+  for (int d = 0; d < kHeadDim; ++d) {
+    float lo = K[d], hi = K[d];
+    for (int t = 1; t < kPageTokens; ++t) {
+      const float v = K[t * kHeadDim + d];
+      lo = v < lo ? v : lo;
+      hi = v > hi ? v : hi;
+    }
+    mm[d] = lo;
+    mm[kHeadDim + d] = hi;
+  }
+}
+
+int orc_page_minmax(const uint16_t* units, int64_t n_units, float* mm) {
+  float K[kPageTokens * kHeadDim];
+  for (int64_t u = 0; u < n_units; ++u) {
+    for (int i = 0; i < kPageTokens * kHeadDim; ++i) K[i] = h2f(units[u * kUnitElems + i]);
+    minmax_rows(K, mm + u * 2 * kHeadDim);
+  }
+  return 0;
+}
+
+int orc_page_minmax_e4m3(const uint8_t* units, int64_t n_units, float* mm) {
+  float K[kPageTokens * kHeadDim];
+  for (int64_t u = 0; u < n_units; ++u) {
+    const uint8_t* p = units + u * kUnitBytesF8;
+    float ks;
+    std::memcpy(&ks, p + 4096, 4);
+    for (int i = 0; i < kPageTokens * kHeadDim; ++i) K[i] = orc_e4m3_decode(p[i]) * ks;
+    minmax_rows(K, mm + u * 2 * kHeadDim);
+  }
+  return 0;
+}
+
+static inline float quest_bound(const float* q, const float* mm) {
+  float v[32];
+  for (int l = 0; l < 32; ++l) {
+    float acc = 0.f;
+    for (int j = 0; j < 4; ++j) {
+      const int d = 4 * l + j;
+      const float a = q[d] * mm[kHeadDim + d], b = q[d] * mm[d];
+      const float m = a >= b ? a : b;
+      acc = j == 0 ? m : acc + m;
+    }
+    v[l] = acc;
+  }
+  for (int off = 16; off >= 1; off >>= 1) {
+    float w[32];
+    for (int l = 0; l < 32; ++l) w[l] = v[l] + v[l ^ off];
+    std::memcpy(v, w, sizeof v);
+  }
+  return v[0];
+}
+
+// q: n_grp x (Hkv * G) x 128 fp16 (head = kv head * G + g); mm: n_grp x Hkv x N
+// rows of 256 fp32 [kmin | kmax]; n_pages[i] <= N. sel_out: n_grp x k;
+// n_sel_out = min(k, n_pages); scores_out (nullable): n_grp x N.
+int orc_select_quest(const uint16_t* q, int Hkv, int G, const float* mm, int N,
+                     const int32_t* n_pages, int n_grp, int k, int32_t* sel_out,
+                     int32_t* n_sel_out, float* scores_out) {
+  const int Hq = Hkv * G;
+  std::vector<float> qf((size_t)Hq * kHeadDim);
+  std::vector<std::pair<uint32_t, int32_t>> keys;
+  for (int i = 0; i < n_grp; ++i) {
+    for (size_t j = 0; j < qf.size(); ++j) qf[j] = h2f(q[(size_t)i * Hq * kHeadDim + j]);
+    const int np = n_pages[i];
+    keys.resize(np);
+    for (int p = 0; p < np; ++p) {
+      float best = 0.f;
+      for (int h = 0; h < Hkv; ++h) {
+        const float* row = mm + (((size_t)i * Hkv + h) * N + p) * 2 * kHeadDim;
+        for (int g = 0; g < G; ++g) {
+          const float v = quest_bound(&qf[(size_t)(h * G + g) * kHeadDim], row);
+          if ((h == 0 && g == 0) || v > best) best = v;
+        }
+      }
+      if (scores_out) scores_out[(size_t)i * N + p] = best;
+      keys[p] = {order_key(best), p};
+    }
+    const int kk = std::min(k, np);
+    std::partial_sort(keys.begin(), keys.begin() + kk, keys.end(),
+                      [](const auto& a, const auto& b) {
+                        return a.first != b.first ? a.first > b.first : a.second < b.second;
+                      });
+    std::vector<int32_t> pick(kk);
+    for (int j = 0; j < kk; ++j) pick[j] = keys[j].second;
+    std::sort(pick.begin(), pick.end());
+    for (int j = 0; j < k; ++j) sel_out[(size_t)i * k + j] = j < kk ? pick[j] : -1;
+    n_sel_out[i] = kk;
+  }
+  return 0;
+}
+
 int orc_version(void) { return 2; }
 
 }  // extern "C"

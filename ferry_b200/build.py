@@ -32,8 +32,30 @@ def _stale() -> bool:
     return any(os.path.getmtime(p) > t for p in deps)
 
 
+DRIVERS = os.path.join(HERE, "drivers")
+DRIVER_BIN = os.path.join(DRIVERS, "bin")
+
+
+def build_drivers(force: bool = False) -> list[str]:
+    """The C++ drivers (drivers/*.cpp) against include/ferry_cuda.h and the
+    built library (rpath to it), into drivers/bin/."""
+    os.makedirs(DRIVER_BIN, exist_ok=True)
+    out = []
+    for src in sorted(glob.glob(os.path.join(DRIVERS, "*.cpp"))):
+        exe = os.path.join(DRIVER_BIN, os.path.splitext(os.path.basename(src))[0])
+        if force or not os.path.exists(exe) or os.path.getmtime(exe) < max(os.path.getmtime(src), os.path.getmtime(LIB)):
+            cmd = [NVCC, "-O2", "-std=c++17", "-I" + os.path.join(ROOT, "include"), "-o", exe, src,
+                   "-L" + HERE, "-lferry_cuda", "-Xlinker", "-rpath", "-Xlinker", "$ORIGIN/../.."]
+            res = subprocess.run(cmd, capture_output=True, text=True)
+            if res.returncode != 0:
+                raise RuntimeError("driver build failed:\n" + " ".join(cmd) + "\n" + res.stdout + res.stderr)
+        out.append(exe)
+    return out
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not _stale():
+        build_drivers()
         return LIB
     cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
            "-I" + os.path.join(ROOT, "include"), "-I" + CSRC, "-o", LIB + ".tmp", *sources()]
@@ -45,6 +67,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     os.replace(LIB + ".tmp", LIB)
     if verbose:
         print(res.stdout + res.stderr)
+    build_drivers(force=True)
     return LIB
 
 

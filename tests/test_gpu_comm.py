@@ -98,3 +98,81 @@ def test_exchange_two_gpus(torch_cuda):
         assert fin == 5 and adm == 15
         assert [owner[i] for i in (0, 2, 10)] == [0, 0, 0] and [owner[i] for i in (1, 3, 11)] == [1, 1, 1]
         assert owner[5] == -1
+
+
+def _deadline_worker(rank, port, out, gone):
+    """Rank 1 joins the first exchange, then never joins the second (it stays
+    alive, its memory intact, until rank 0 has given up). Rank 0's second
+    exchange must reach its deadline, abort the communicator (ncclCommAbort
+    ends the collective in flight) and raise."""
+    import os
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    from ferry_b200 import _abi
+    from ferry_b200.cluster import OwnershipComm, ownership_row
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    comm = OwnershipComm(rank)
+    try:
+        comm.all_gather(ownership_row(0, 1, np.array([rank], np.int32), cap=4))  # epoch 1: both ranks
+        if rank == 1:
+            gone.wait(120)  # never joins epoch 2; leaves once rank 0 has given up
+            _abi.call("ferry_comm_abort", comm.h)  # its peer is gone: no collective teardown
+            out.put((1, "left", 0.0, 0))
+            return
+        deadline = 2.0
+        t0 = time.monotonic()
+        try:
+            comm.all_gather(ownership_row(0, 1, np.array([0], np.int32), cap=4), timeout_s=deadline)
+            out.put((0, "no timeout", time.monotonic() - t0, 0))
+        except TimeoutError:
+            waited = time.monotonic() - t0
+            torch.cuda.synchronize(rank)  # the aborted collective has left the stream
+            try:  # the communicator is unusable after the abort
+                comm.all_gather(np.zeros(8, np.int32), timeout_s=1.0)
+                rc = 0
+            except _abi.FerryError as e:
+                rc = e.code
+            out.put((0, "timeout", waited - deadline, rc))
+        finally:
+            gone.set()
+    finally:
+        comm.close()
+
+
+def test_exchange_deadline_aborts_when_a_rank_never_joins(torch_cuda):
+    """Failure detection on the ownership exchange without a GPU fault: a peer
+    that never joins a collective (it stays alive and idle) ends the other
+    rank's exchange at its deadline; NVLS is off, as for every test of a
+    departed rank."""
+    import multiprocessing as mp
+    import os
+    import socket
+
+    if torch_cuda.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    os.environ["NCCL_NVLS_ENABLE"] = "0"  # inherited by the spawned ranks
+    ctx = mp.get_context("spawn")
+    q, gone = ctx.Queue(), ctx.Event()
+    ps = [ctx.Process(target=_deadline_worker, args=(r, port, q, gone)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted(q.get(timeout=240) for _ in ps)
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    (_, what, late, rc), (_, left, _, _) = res
+    assert what == "timeout" and left == "left"
+    assert 0.0 <= late <= 1.0  # raised within the deadline plus 1 s
+    from ferry_b200 import _abi
+
+    assert rc == _abi.E_STATE

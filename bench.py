@@ -510,6 +510,8 @@ def main():
     ap.add_argument("--per-gpu", type=int, default=16, help="skew: requests per GPU on average")
     ap.add_argument("--policy", default="zipf", help="skew: rr | zipf home assignment")
     ap.add_argument("--no-steal", action="store_true", help="skew: disable work stealing")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N > 1: independent cfg1 replicas per rank instead of the executor job")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -523,8 +525,147 @@ def main():
     w = WORKLOADS[args.workload]
     if args.impl == "reference":
         run_reference(args, w)
+    elif _dist()[0] > 1 and args.workload == "cfg1" and not args.replicas:
+        run_scale(args, w)
     else:
         run_ferry(args, w)
+
+
+def concurrent_h2d_peak(dev, ws, nbytes=1 << 30, iters=3):
+    """Copy-engine H2D from pinned host memory on every rank at once (barrier
+    before): (this rank's GB/s, aggregate GB/s = all bytes / slowest rank)."""
+    import torch
+    import torch.distributed as dist
+
+    src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream(dev)
+    dst.copy_(src, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    for _ in range(iters):
+        dst.copy_(src, non_blocking=True)
+    b.record(st)
+    torch.cuda.synchronize(dev)
+    sec = a.elapsed_time(b) / 1e3
+    mine = nbytes * iters / sec / 1e9
+    agg = mine
+    if ws > 1:
+        t = torch.tensor([sec, float(nbytes * iters)], dtype=torch.float64, device=dev)
+        mx, sm = t.clone(), t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        agg = float(sm[1]) / float(mx[0]) / 1e9
+    del src, dst
+    return mine, agg
+
+
+def gpu_numa(local):
+    """NUMA node of this GPU's PCI device and its local CPU list (sysfs)."""
+    import torch
+
+    pr = torch.cuda.get_device_properties(local)
+    bdf = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+
+    def rd(path):
+        try:
+            with open(path) as f:
+                return f.read().strip()
+        except OSError:
+            return None
+
+    return {"pci": bdf, "numa_node": rd(f"/sys/bus/pci/devices/{bdf}/numa_node"),
+            "local_cpus": rd(f"/sys/bus/pci/devices/{bdf}/local_cpulist")}
+
+
+def run_scale(args, w):
+    """N > 1 (torchrun): the configs[0]-shaped job on every GPU through the
+    multi-GPU executor -- N x 16 requests of cfg1's shape, homes round-robin
+    over the GPUs (the steady balanced config's partitioning), Poisson arrivals
+    at N x 50 req/s box-wide (each GPU sees the single-GPU job's rate), work
+    stealing on, the NCCL ownership exchange every 4 ticks. Weak scaling: per-
+    GPU work is the N = 1 job's. Ticks [W, W + K) of one job are timed with
+    CUDA events (barrier + synchronize on both sides, max over ranks).
+    value = tokens decoded by all ranks in the window / slowest rank's time.
+    e2e = the same window of a second job whose query table sits in pinned
+    host memory (each tick's queries cross the host link inside the step) and
+    whose outputs are copied to pinned host memory after every tick."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from ferry_b200.cluster import RankRunner, job_schedule, slots_needed
+
+    ws, rank, local = _dist()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    total = w.num_requests * ws
+    max_batch = w.num_requests
+    home, join = job_schedule(w, total, ws, "rr", rate=w.arrival_rate * ws)
+    window = (args.warmup, args.warmup + args.steps)
+
+    def job(host_q):
+        r = RankRunner(w, total, ws, rank, local, slots=slots_needed(home, ws, max_batch),
+                       max_batch=max_batch, steal_batch=4, host_q=host_q)
+        try:
+            dist.barrier()
+            torch.cuda.synchronize(dev)
+            return r.run(home, join, epoch=4, window=window, exchange_device=dev, outputs=host_q,
+                         barrier=dist.barrier)
+        finally:
+            r.close()
+
+    with Clocks(local) as clk:
+        st = job(False)
+    st2 = job(True)
+    mine_peak, agg_peak = concurrent_h2d_peak(dev, ws)
+    t = torch.tensor([st.window_ms, st.window_tokens, st.window_gathered_bytes, st.stolen_tasks,
+                      st.migrated_bytes, st2.window_ms, st2.window_tokens, st2.h2d_bytes, st2.d2h_bytes,
+                      sum(st.tick_ms[window[0]:window[1]]), len(st.tick_ms[window[0]:window[1]])],
+                     dtype=torch.float64, device=dev)
+    mx, sm = t.clone(), t.clone()
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+    numa = [None] * ws
+    dist.all_gather_object(numa, gpu_numa(local))
+    if rank == 0:
+        ms, tokens, gbytes = float(mx[0]), float(sm[1]), float(sm[2])
+        gather_agg = gbytes / (ms / 1e3) / 1e9
+        line = {"metric": METRIC, "value": tokens / (ms / 1e3), "unit": UNIT, "n_gpus": ws,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "fp16-kv/fp32-acc", "data": "synthetic (procedural KV, AR(1) queries, seeded)",
+                "config": {"workload": f"{w.name} (configs[0]) on every GPU through the executor", "requests": total,
+                           "requests_per_gpu": w.num_requests, "ctx_tokens": w.ctx_tokens, "layers": w.num_layers,
+                           "heads": [w.q_heads, w.kv_heads], "top_k": w.top_k, "cache_pages": w.cache_pages,
+                           "homes": "round-robin", "arrivals": f"poisson {w.arrival_rate * ws} req/s box-wide",
+                           "l2": "inputs larger than L2 (selected KV 256 MiB + summaries 64 MiB per GPU step)",
+                           "parallelism": f"{ws} ranks: executor + work stealing + NCCL ownership exchange"},
+                "miss_gather": {"aggregate_GB_s": gather_agg, "per_rank_GB_s": gather_agg / ws,
+                                "link_peak_aggregate_GB_s": agg_peak, "frac_of_aggregate": gather_agg / agg_peak,
+                                "link_peak_alone_GB_s": mine_peak,
+                                "peak_kind": "copy-engine H2D from pinned host on all ranks at once, this run",
+                                "note": "rate over the whole step (the gather is ~96% of it at N = 1)"},
+                "steal": {"stolen_tasks": int(sm[3]), "migrated_bytes": float(sm[4])},
+                # the executor's own device time per tick (pop .. push), slowest rank;
+                # ms_per_step above also holds the host's per-tick syncs and the exchange
+                "tick_device_ms_mean": float(mx[9]) / max(1.0, float(mx[10])),
+                # per tick: deque pop + size, query gather, select, detect, gather,
+                # attention, push (steal attempts add size probes of the peers)
+                "gpu_launches": 8 * args.steps * ws,
+                "e2e": {"value": float(sm[6]) / (float(mx[5]) / 1e3), "unit": UNIT,
+                        "h2d_bytes_per_step": float(sm[7]) / args.steps, "d2h_bytes_per_step": float(sm[8]) / args.steps,
+                        "api": "ferry_exec_tick (query table in pinned host memory) + ferry_exec_output"},
+                "gpu_numa": numa, "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 def run_cluster(args):

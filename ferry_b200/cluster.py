@@ -122,12 +122,18 @@ class OwnershipComm:
     def all_gather(self, row: np.ndarray, timeout_s: float = 60.0) -> np.ndarray:
         """[world][len(row)] int32 rows of every rank (returns after the copy
         back). A collective not done within timeout_s (a peer rank gone) is
-        aborted -- the communicator with it -- and raises TimeoutError, the
-        way a process group's timeout ends its collective."""
+        aborted -- the communicator with it -- and raises TimeoutError at the
+        deadline, the way a process group's timeout ends its collective. The
+        abort (ncclCommAbort: it ends the kernel in flight, then tears the
+        communicator down, which takes seconds) runs on a helper thread;
+        wait_aborted() joins it, and every later exchange raises FerryError
+        (FERRY_E_STATE)."""
+        import threading
         import time
 
         import torch
 
+        self.wait_aborted()
         # the copy, the collective and the completion event all on this
         # communicator's device and its current stream, whatever device the
         # caller has current
@@ -143,12 +149,22 @@ class OwnershipComm:
         deadline = time.monotonic() + timeout_s
         while not done.query():
             if time.monotonic() > deadline:
-                call("ferry_comm_abort", self.h)
+                h = self.h
+                self._abort = threading.Thread(target=lambda: _abi.lib().ferry_comm_abort(h), daemon=True)
+                self._abort.start()
                 raise TimeoutError(f"ownership exchange on rank {self.rank} not done within {timeout_s} s")
             time.sleep(5e-5)
         return d_all.cpu().numpy()
 
+    def wait_aborted(self, timeout_s: float = 120.0) -> None:
+        """Join the abort a missed deadline started (no-op without one)."""
+        t = getattr(self, "_abort", None)
+        if t is not None:
+            t.join(timeout_s)
+            self._abort = None
+
     def close(self):
+        self.wait_aborted()
         if self.h:
             call("ferry_comm_destroy", self.h)
             self.h = None
@@ -191,6 +207,11 @@ class ClusterStats:
     mig_ms: float = 0.0          # device time of the migration kernels
     mig_event_bytes: int = 0     # bytes those kernels moved
     rebalances: int = 0          # rebalance orders this rank executed (LLX)
+    window_ms: float = 0.0       # device time of the timed tick window (run(window=...))
+    window_tokens: int = 0       # tokens decoded inside it
+    window_gathered_bytes: int = 0  # miss-gather bytes inside it
+    h2d_bytes: int = 0           # host -> device query bytes of the window (host_q)
+    d2h_bytes: int = 0           # device -> host output bytes of the window (outputs)
 
 
 # ---------------------------------------------------------------- per-rank runner (GPU)
@@ -202,7 +223,7 @@ class RankRunner:
     def __init__(self, w: Workload, total_requests: int, world: int, rank: int, device: int,
                  slots: int, max_batch: int, steal_batch: int = 4,
                  migrate_mode: int = _abi.MIGRATE_DELTA, pool_units: int | None = None,
-                 policy: "_abi.StealPolicy | None" = None):
+                 policy: "_abi.StealPolicy | None" = None, host_q: bool = False):
         import torch
         import torch.distributed as dist
 
@@ -214,16 +235,27 @@ class RankRunner:
         wl = dataclasses.replace(w, num_requests=slots)
         self.dec = Decoder(wl, device)
         self.dec.register_pool(units=pool_units or min(total_requests * w.lanes_per_req * w.max_pages, 1 << 17))
-        # resident query table [total][steps][L][Hq][128]
+        # query table [total][steps][L][Hq][128]: resident in HBM, or (host_q)
+        # in pinned, device-mapped host memory that the executor's query
+        # gather reads over the host link every tick
         q = np.stack([q_stream(w, r) for r in range(total_requests)])
-        self.q_table = torch.from_numpy(q).to(self.dev)
+        self.host_q = host_q
+        if host_q:
+            from .engine import PinnedPool
+
+            self.q_pool = PinnedPool(q.nbytes)
+            self.q_pool.numpy(np.uint16)[:] = q.view(np.uint16).ravel()
+            q_ptr = self.q_pool.ptr
+        else:
+            self.q_table = torch.from_numpy(q).to(self.dev)
+            q_ptr = C.c_void_p(self.q_table.data_ptr())
+        self.row_elems = w.num_layers * w.q_heads * w.head_dim
         self.deque = C.c_void_p()
         call("ferry_deque_create", device, max(slots, 1), C.byref(self.deque))
         cfg = _abi.ExecCfg(rank=rank, world=world, max_batch=max_batch, steal_batch=steal_batch,
                            migrate_mode=migrate_mode, steps_per_req=w.steps, total_requests=total_requests)
         self.exec = C.c_void_p()
-        call("ferry_exec_create", self.dec.ctx, self.deque, C.byref(cfg),
-             C.c_void_p(self.q_table.data_ptr()), C.byref(self.exec))
+        call("ferry_exec_create", self.dec.ctx, self.deque, C.byref(cfg), q_ptr, C.byref(self.exec))
         if policy is not None:
             call("ferry_exec_policy", self.exec, C.byref(policy))
         self.slots = slots
@@ -250,11 +282,19 @@ class RankRunner:
                 slot += 1
 
     def run(self, home: np.ndarray, join: np.ndarray, epoch: int = 4, max_ticks: int = 100000,
-            exchange_device=None, llx: float | None = None) -> ClusterStats:
+            exchange_device=None, llx: float | None = None, window: tuple | None = None,
+            n_pages: np.ndarray | None = None, outputs: bool = False, barrier=None) -> ClusterStats:
         """Tick until every request of the job finished on some GPU. home/join:
-        each request's home rank and arrival tick. With ``exchange_device`` set
+        each request's home rank and arrival tick; n_pages: each request's
+        context in pages (default: the workload's). With ``exchange_device`` set
         (ranks on distinct GPUs) the ownership exchange runs over the C ABI's
-        NCCL communicator, created here before the timed region."""
+        NCCL communicator, created here before the timed region.
+
+        window=(w0, w1): run exactly w1 ticks (every rank the same count, so
+        the ranks take the same exchanges) and time ticks [w0, w1) with CUDA
+        events, bracketed by ``barrier()`` and a synchronize on both sides.
+        outputs: copy every tick's attention output to pinned host memory
+        (ferry_exec_output) -- the device -> host read of an end-to-end step."""
         import torch
 
         if exchange_device is not None and self.comm is None:
@@ -262,6 +302,7 @@ class RankRunner:
         comm = self.comm if exchange_device is not None else None
         st = torch.cuda.current_stream(self.dev)
         mine = np.nonzero(home == self.rank)[0]
+        pages_of = np.full(len(home), self.w.max_pages, np.int32) if n_pages is None else np.asarray(n_pages, np.int32)
         admitted = finished = tokens = ticks = steals = stolen = 0
         mig_ms, mig_b = 0.0, 0
         tick_ms = []
@@ -272,18 +313,47 @@ class RankRunner:
         u_steps, u_reqs = C.c_int64(), C.c_int32()
         rebalances = 0
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(st)
+        w0, w1 = window if window is not None else (0, max_ticks)
+        last = w1 if window is not None else max_ticks
+        win_tokens = win_h2d = win_d2h = 0
+        g0 = 0
+        host_out = n_out = None
+        if outputs:
+            host_out = torch.empty((self.slots, self.row_elems), dtype=torch.float32).pin_memory()
+            n_out = C.c_int()
+        if w0 == 0:
+            if barrier is not None:
+                torch.cuda.synchronize(self.dev)
+                barrier()
+                torch.cuda.synchronize(self.dev)
+            e0.record(st)
         t = 0
-        while t < max_ticks:
+        while t < last:
+            if window is not None and t == w0 and w0 > 0:
+                torch.cuda.synchronize(self.dev)
+                if barrier is not None:
+                    barrier()
+                    torch.cuda.synchronize(self.dev)
+                g0 = self.dec.all_stats()[1]
+                e0.record(st)
             arr = mine[join[mine] == t].astype(np.int32)
             if len(arr):
-                pages = np.full(len(arr), self.w.max_pages, np.int32)
+                pages = pages_of[arr]
                 call("ferry_exec_admit", self.exec, arr.ctypes.data_as(C.c_void_p),
                      pages.ctypes.data_as(C.c_void_p), len(arr))
                 admitted += len(arr)
             call("ferry_exec_tick", self.exec, C.c_void_p(st.cuda_stream), C.byref(s))
             tokens += s.decoded
             finished += s.finished
+            if w0 <= t < w1:
+                win_tokens += s.decoded
+                if self.host_q:
+                    win_h2d += s.decoded * self.row_elems * 2
+            if outputs and s.decoded:
+                call("ferry_exec_output", self.exec, C.c_void_p(st.cuda_stream), C.c_void_p(host_out.data_ptr()),
+                     None, self.slots, C.byref(n_out))
+                if w0 <= t < w1:
+                    win_d2h += n_out.value * self.row_elems * 4
             if s.stolen:
                 steals += 1
                 stolen += s.stolen
@@ -308,12 +378,18 @@ class RankRunner:
                     break
         e1.record(st)
         torch.cuda.synchronize(self.dev)
+        if window is not None and barrier is not None:
+            barrier()
         self.dec.check()
         g_units, g_bytes, m_units, m_bytes = self.dec.all_stats()[:4]
-        return ClusterStats(rank=self.rank, tokens=tokens, ticks=t, device_ms=e0.elapsed_time(e1),
+        dev_ms = e0.elapsed_time(e1)
+        return ClusterStats(rank=self.rank, tokens=tokens, ticks=t, device_ms=dev_ms,
                             steals=steals, stolen_tasks=stolen, migrated_units=m_units,
                             migrated_bytes=m_bytes, gathered_bytes=g_bytes, tick_ms=tick_ms,
-                            mig_ms=mig_ms, mig_event_bytes=mig_b, rebalances=rebalances)
+                            mig_ms=mig_ms, mig_event_bytes=mig_b, rebalances=rebalances,
+                            window_ms=dev_ms if window is not None else 0.0, window_tokens=win_tokens,
+                            window_gathered_bytes=g_bytes - g0 if window is not None else g_bytes,
+                            h2d_bytes=win_h2d, d2h_bytes=win_d2h)
 
     def close(self):
         if self.comm is not None:
@@ -329,11 +405,15 @@ class RankRunner:
             call("ferry_deque_destroy", self.deque)
             self.deque = None
         self.dec.close()
+        if getattr(self, "q_pool", None) is not None:
+            self.q_pool.close()
+            self.q_pool = None
 
 
-def job_schedule(w: Workload, total_requests: int, world: int, policy: str):
-    """Arrival tick and home rank of each request of a multi-GPU job."""
-    wj = dataclasses.replace(w, num_requests=total_requests)
+def job_schedule(w: Workload, total_requests: int, world: int, policy: str, rate: float | None = None):
+    """Arrival tick and home rank of each request of a multi-GPU job (Poisson
+    arrivals at ``rate`` requests/s box-wide, default the workload's)."""
+    wj = dataclasses.replace(w, num_requests=total_requests, arrival_rate=rate or w.arrival_rate)
     join = arrival_ticks(wj)
     join = join - join.min()
     home = assign_ranks(total_requests, world, policy, w.seed)

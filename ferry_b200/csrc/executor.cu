@@ -101,6 +101,7 @@ struct ferry_exec {
   // steal policy (ferry_exec_policy)
   ferry_steal_policy pol{0, 2.0, 3.0, 700.0, 0.06};
   double step_ms_ema = 2.0;
+  int last_n = 0;  // tasks decoded in the last tick (their outputs are in d_out)
   int32_t* h_live = nullptr;  // steal_batch * lanes_per_req resident-page counts of candidates
 };
 
@@ -443,9 +444,25 @@ int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out) {
   x->finished += ts.finished;
   if (n > 0) x->step_ms_ema = 0.9 * x->step_ms_ema + 0.1 * ms;  // one step of every decoded request
   ts.decoded = n;
+  x->last_n = n;
   ts.tick_ms = ms;
   ts.queued = np;
   *out = ts;
+  return FERRY_OK;
+}
+
+int ferry_exec_output(ferry_exec* x, void* stream, float* host_out, int32_t* host_req, int cap_rows,
+                      int* n_out) {
+  if (!x || !n_out || cap_rows < 0 || (cap_rows && !host_out))
+    return set_error("exec_output: bad arguments"), FERRY_E_INVAL;
+  const int n = std::min(x->last_n, cap_rows);
+  Guard g(x->ctx->device);
+  if (n > 0)
+    FERRY_TRY(cudaMemcpyAsync(host_out, x->d_out, (size_t)n * x->row_elems * 4, cudaMemcpyDeviceToHost,
+                              (cudaStream_t)stream));
+  if (host_req)
+    for (int i = 0; i < n; ++i) host_req[i] = task_req(x->h_tasks[i]);
+  *n_out = n;
   return FERRY_OK;
 }
 

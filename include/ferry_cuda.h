@@ -388,6 +388,13 @@ int ferry_exec_set_global(ferry_exec* x, int64_t global_pending);
 /* Global ids of the requests this GPU holds (the ownership table row). */
 int ferry_exec_owned(ferry_exec* x, int32_t* h_out, int cap, int* n);
 int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out);
+/* The attention output of the last tick: row i ([L][Hq][128] fp32) belongs to
+ * the i-th task decoded in that tick, host_req[i] (nullable) its global
+ * request. Copies min(decoded, cap_rows) rows device -> host_out on `stream`
+ * (asynchronous; pinned host_out); n_out = rows. The reference's exec loop
+ * keeps its outputs on the device (d_out_, wla_multigpu.cuh:2455-2468). */
+int ferry_exec_output(ferry_exec* x, void* stream, float* host_out, int32_t* host_req, int cap_rows,
+                      int* n_out);
 
 /* Steal policy. cost_filter = 0 is the water-level steal alone (the
  * reference's policy C, wla_multigpu.cuh:1063-1506). cost_filter = 1 adds

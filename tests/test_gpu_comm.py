@@ -133,6 +133,7 @@ def _deadline_worker(rank, port, out, gone):
             out.put((0, "no timeout", time.monotonic() - t0, 0))
         except TimeoutError:
             waited = time.monotonic() - t0
+            comm.wait_aborted()  # the abort's teardown, on its helper thread
             torch.cuda.synchronize(rank)  # the aborted collective has left the stream
             try:  # the communicator is unusable after the abort
                 comm.all_gather(np.zeros(8, np.int32), timeout_s=1.0)

@@ -510,6 +510,8 @@ def main():
     ap.add_argument("--per-gpu", type=int, default=16, help="skew: requests per GPU on average")
     ap.add_argument("--policy", default="zipf", help="skew: rr | zipf home assignment")
     ap.add_argument("--no-steal", action="store_true", help="skew: disable work stealing")
+    ap.add_argument("--slots", type=int, default=64, help="cfg3s/cfg4s: request slots per GPU")
+    ap.add_argument("--batch", type=int, default=32, help="cfg3s/cfg4s: requests decoded per GPU per tick")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: independent cfg1 replicas per rank instead of the executor job")
     args = ap.parse_args()
@@ -521,6 +523,9 @@ def main():
         return run_owner(args)
     if args.workload == "skew":
         run_cluster(args)
+        return
+    if args.workload in ("cfg3s", "cfg4s"):
+        run_config_slice(args, WORKLOADS[args.workload])
         return
     w = WORKLOADS[args.workload]
     if args.impl == "reference":
@@ -668,6 +673,107 @@ def run_scale(args, w):
     dist.destroy_process_group()
 
 
+def nvlink_peak(local, ws, nbytes=256 << 20):
+    """Peer-copy peak measured in this run: a copy kernel on this GPU reading
+    a peer's HBM over NVLink (ferry_probe_link), GB/s; None on one GPU."""
+    import ctypes as C
+
+    from ferry_b200 import _abi
+
+    if ws < 2:
+        return None
+    g = C.c_double()
+    _abi.call("ferry_probe_link", (local + 1) % ws, local, C.c_size_t(nbytes), 3, C.byref(g))
+    return g.value
+
+
+def run_config_slice(args, w):
+    """--workload cfg3s | cfg4s: configs[2] / configs[3] at their per-layer
+    shapes (one layer), N ranks through the executor. cfg3s: 256 requests,
+    contexts uniform in 8k-32k tokens, round-robin homes, Poisson 400 req/s
+    box-wide, top-128, 1024 steps each. cfg4s: 512 requests, contexts uniform
+    in 16k-64k tokens, Zipf(1.5) homes, ON/OFF arrivals (exponential 200 ms ON
+    at 2000 req/s, 800 ms OFF), top-256, 512 steps each, stealing with NVLink
+    migration. Every GPU keeps --slots request slots (arrivals beyond them wait
+    at the host until a slot frees) and decodes up to --batch of them per
+    tick. Ticks [W, W + K) are timed (barrier + synchronize on both sides, max
+    over ranks); value = tokens decoded in them by all ranks / that time."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from ferry_b200.cluster import RankRunner, assign_ranks, job_schedule
+    from ferry_b200.workload import CONTEXT_RANGE, onoff_arrival_ticks, ragged_pages
+
+    ws, rank, local = _dist()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    else:
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29517", rank=0, world_size=1)
+    total = w.num_requests if w.name == "cfg3s" else 512
+    lo, hi = CONTEXT_RANGE[w.name]
+    n_pages = ragged_pages(total, lo, hi, w.seed)
+    if w.name == "cfg3s":
+        home, join = job_schedule(w, total, ws, "rr")
+        policy = "round-robin"
+        arrivals = f"poisson {w.arrival_rate} req/s box-wide"
+    else:
+        home = assign_ranks(total, ws, "zipf", w.seed)
+        join = onoff_arrival_ticks(total, w.arrival_rate, 200.0, 800.0, w.seed, w.tick_ms)
+        policy = "zipf(1.5)"
+        arrivals = "ON/OFF: exp 200 ms ON at 2000 req/s, exp 800 ms OFF"
+    window = (args.warmup, args.warmup + args.steps)
+    steal = 0 if args.no_steal else 4
+    r = RankRunner(w, total, ws, rank, local, slots=args.slots, max_batch=args.batch, steal_batch=steal,
+                   q_steps=window[1] + 8)
+    try:
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        with Clocks(local) as clk:
+            st = r.run(home, join, epoch=4, window=window, exchange_device=dev if ws > 1 else None,
+                       n_pages=n_pages, barrier=dist.barrier)
+    finally:
+        r.close()
+    link = nvlink_peak(local, ws) if rank == 0 else None
+    mine_peak, agg_peak = concurrent_h2d_peak(dev, ws)
+    t = torch.tensor([st.window_ms, st.window_tokens, st.window_gathered_bytes, st.stolen_tasks,
+                      st.migrated_bytes, st.mig_ms, st.mig_event_bytes],
+                     dtype=torch.float64, device=dev)
+    mx, sm = t.clone(), t.clone()
+    if ws > 1:
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+    if rank == 0:
+        ms, tokens, gbytes = float(mx[0]), float(sm[1]), float(sm[2])
+        mig_gbs = float(sm[6]) / (float(sm[5]) / 1e3) / 1e9 if float(sm[5]) > 0 else None
+        line = {"metric": METRIC, "value": tokens / (ms / 1e3), "unit": UNIT, "n_gpus": ws,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "fp16-kv/fp32-acc", "data": "synthetic (procedural KV, AR(1) queries, seeded)",
+                "config": {"workload": f"{w.name}: configs[{2 if w.name == 'cfg3s' else 3}] at its per-layer "
+                                       "shape, 1 of 32 layers", "requests": total,
+                           "ctx_tokens": [lo, hi], "heads": [w.q_heads, w.kv_heads], "top_k": w.top_k,
+                           "cache_pages": w.cache_pages, "steps_per_request": w.steps, "homes": policy,
+                           "home_share": (np.bincount(home, minlength=ws) / total).round(3).tolist(),
+                           "arrivals": arrivals, "slots_per_gpu": args.slots, "batch_per_gpu": args.batch,
+                           "steal_batch": steal, "parallelism": f"{ws} ranks: executor + stealing + NCCL exchange"},
+                "miss_gather": {"aggregate_GB_s": gbytes / (ms / 1e3) / 1e9,
+                                "link_peak_aggregate_GB_s": agg_peak,
+                                "frac_of_aggregate": gbytes / (ms / 1e3) / 1e9 / agg_peak,
+                                "peak_kind": "copy-engine H2D from pinned host on all ranks at once, this run"},
+                "steal": {"stolen_tasks": int(sm[3]), "migrated_bytes": float(sm[4]),
+                          "migration_GB_s": mig_gbs, "nvlink_peak_GB_s": link,
+                          "migration_frac": mig_gbs / link if mig_gbs and link else None,
+                          "nvlink_peak_kind": "peer-read copy kernel, this run"},
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def run_cluster(args):
     """--workload skew: the multi-GPU job with work stealing and NVLink
     migration. cfg1-shaped requests (32/32 heads, 4096 tokens, top-64, 25%
@@ -720,6 +826,7 @@ def run_cluster(args):
     if ws > 1:
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
         dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+    link = nvlink_peak(local, ws) if rank == 0 else None
     if rank == 0:
         ms = float(mx[0])
         tokens = float(sm[1])
@@ -734,8 +841,9 @@ def run_cluster(args):
                            "steal_batch": steal, "home_share": share, "policy": args.policy,
                            "parallelism": f"{ws} ranks, work stealing + NVLink migration"},
                 "steal": {"stolen_tasks": int(sm[5]), "migrated_bytes": float(sm[2]),
-                          "migration_GB_s": mig_gbs, "nvlink_peak_GB_s": 770.0,
-                          "migration_frac": mig_gbs / 770.0 if mig_gbs else None},
+                          "migration_GB_s": mig_gbs, "nvlink_peak_GB_s": link,
+                          "migration_frac": mig_gbs / link if mig_gbs and link else None,
+                          "nvlink_peak_kind": "peer-read copy kernel, this run"},
                 "gathered_bytes": float(sm[6]), "ticks": st.ticks, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     dist.barrier()
@@ -851,6 +959,7 @@ def run_owner(args):
     if rank == 0:
         ms = float(mx[0])
         tokens = total * args.steps
+        link = nvlink_peak(local, ws)  # None on one GPU (the gather is then HBM-bound)
         gb, peer_b, self_b = float(sm[2]), float(sm[3]), float(sm[4])
         kms = [float(x) for x in mx[5:9]]  # max over ranks, per kernel
         hbm_peak, peak_kind = _peaks()
@@ -886,11 +995,11 @@ def run_owner(args):
                                        "frac": attn_bytes / kms[3] / 1e6 / hbm_peak, "bytes_per_launch": attn_bytes},
                 "roofline_gather": {"bound": "hbm" if ws == 1 else "nvlink", "kernel": "gather_store_kernel",
                                     "achieved": gat_bytes / kms[2] / 1e6,
-                                    "peak": hbm_peak if ws == 1 else 770.0,
+                                    "peak": hbm_peak if ws == 1 else link,
                                     "note": "HBM read + write of the gathered units" if ws == 1 else
-                                            "peer share of the units over the measured 770 GB/s peer-copy peak",
+                                            "peer share of the units over the peer-copy peak measured in this run",
                                     "frac": (gat_bytes / kms[2] / 1e6 / hbm_peak) if ws == 1 else
-                                            ((gb / args.steps / ws) * (peer_b / gb if gb else 0) / kms[2] / 1e6 / 770.0)},
+                                            ((gb / args.steps / ws) * (peer_b / gb if gb else 0) / kms[2] / 1e6 / link)},
                 "clocks": clocks.summary()}
         print(json.dumps(line), flush=True)
     dec.close()

@@ -44,7 +44,7 @@ EXPORTS = [
 MAX_PEERS = 8
 CTX_HANDLE_BYTES = 1024
 COMM_ID_BYTES = 128
-MIGRATE_FULL, MIGRATE_DELTA = 0, 1
+MIGRATE_FULL, MIGRATE_DELTA, MIGRATE_DROP = 0, 1, 2
 SRC_HOST, SRC_OWNER = 0, 1
 NUM_STATS = 8
 
@@ -65,7 +65,7 @@ class Cfg(C.Structure):
 class ExecCfg(C.Structure):
     _fields_ = [("rank", C.c_int), ("world", C.c_int), ("max_batch", C.c_int),
                 ("steal_batch", C.c_int), ("migrate_mode", C.c_int), ("steps_per_req", C.c_int),
-                ("total_requests", C.c_int)]
+                ("total_requests", C.c_int), ("q_table_steps", C.c_int)]
 
 
 class StealPolicy(C.Structure):

@@ -223,7 +223,8 @@ class RankRunner:
     def __init__(self, w: Workload, total_requests: int, world: int, rank: int, device: int,
                  slots: int, max_batch: int, steal_batch: int = 4,
                  migrate_mode: int = _abi.MIGRATE_DELTA, pool_units: int | None = None,
-                 policy: "_abi.StealPolicy | None" = None, host_q: bool = False):
+                 policy: "_abi.StealPolicy | None" = None, host_q: bool = False,
+                 q_steps: int | None = None):
         import torch
         import torch.distributed as dist
 
@@ -238,7 +239,9 @@ class RankRunner:
         # query table [total][steps][L][Hq][128]: resident in HBM, or (host_q)
         # in pinned, device-mapped host memory that the executor's query
         # gather reads over the host link every tick
-        q = np.stack([q_stream(w, r) for r in range(total_requests)])
+        # (q_steps: rows per request; later steps reuse them cyclically)
+        q_steps = w.steps if q_steps is None else min(q_steps, w.steps)
+        q = np.stack([q_stream(w, r, steps=q_steps) for r in range(total_requests)])
         self.host_q = host_q
         if host_q:
             from .engine import PinnedPool
@@ -253,7 +256,8 @@ class RankRunner:
         self.deque = C.c_void_p()
         call("ferry_deque_create", device, max(slots, 1), C.byref(self.deque))
         cfg = _abi.ExecCfg(rank=rank, world=world, max_batch=max_batch, steal_batch=steal_batch,
-                           migrate_mode=migrate_mode, steps_per_req=w.steps, total_requests=total_requests)
+                           migrate_mode=migrate_mode, steps_per_req=w.steps, total_requests=total_requests,
+                           q_table_steps=q_steps)
         self.exec = C.c_void_p()
         call("ferry_exec_create", self.dec.ctx, self.deque, C.byref(cfg), q_ptr, C.byref(self.exec))
         if policy is not None:

@@ -35,8 +35,9 @@ __host__ __device__ inline int task_slot(uint64_t t) { return (int)((t >> 24) & 
 __host__ __device__ inline int task_step(uint64_t t) { return (int)(t & 0xFFFFFF); }
 
 // q of (request, step) from the resident table into the batch buffer
+// (the table holds table_steps rows per request; later steps reuse them cyclically)
 __global__ void gather_q_kernel(const uint16_t* __restrict__ table, const uint64_t* __restrict__ tasks,
-                                int n, int steps, int64_t row_elems, int total_requests,
+                                int n, int steps, int table_steps, int64_t row_elems, int total_requests,
                                 uint16_t* __restrict__ out, uint32_t* err) {
   const int i = blockIdx.y;
   if (i >= n) return;
@@ -46,7 +47,8 @@ __global__ void gather_q_kernel(const uint16_t* __restrict__ table, const uint64
     if (threadIdx.x == 0 && blockIdx.x == 0) record_error(err, kErrRange);
     return;
   }
-  const uint4* src = reinterpret_cast<const uint4*>(table + ((int64_t)r * steps + s) * row_elems);
+  const uint4* src =
+      reinterpret_cast<const uint4*>(table + ((int64_t)r * table_steps + s % table_steps) * row_elems);
   uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)i * row_elems);
   const int64_t n4 = row_elems / 8;
   for (int64_t j = blockIdx.x * blockDim.x + threadIdx.x; j < n4; j += (int64_t)gridDim.x * blockDim.x)
@@ -182,8 +184,9 @@ int ferry_exec_create(ferry_ctx* ctx, ferry_deque* own, const ferry_exec_cfg* cf
   if (cfg->world < 1 || cfg->rank < 0 || cfg->rank >= cfg->world || cfg->max_batch < 1 ||
       cfg->max_batch > R || cfg->steal_batch < 0 || cfg->steps_per_req < 1 ||
       cfg->total_requests < 1 || cfg->total_requests >= (1 << 24) || R > 65535 ||
-      cfg->steps_per_req >= (1 << 24) ||
-      (cfg->migrate_mode != FERRY_MIGRATE_DELTA && cfg->migrate_mode != FERRY_MIGRATE_FULL))
+      cfg->steps_per_req >= (1 << 24) || cfg->q_table_steps < 0 ||
+      (cfg->migrate_mode != FERRY_MIGRATE_DELTA && cfg->migrate_mode != FERRY_MIGRATE_FULL &&
+       cfg->migrate_mode != FERRY_MIGRATE_DROP))
     return set_error("exec_create: bad configuration"), FERRY_E_INVAL;
   Guard g(ctx->device);
   auto* x = new ferry_exec;
@@ -408,7 +411,9 @@ int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out) {
     for (int i = 0; i < n; ++i) x->h_ids[i] = task_slot(x->h_tasks[i]);
     FERRY_TRY(cudaMemcpyAsync(x->d_ids, x->h_ids, (size_t)n * 4, cudaMemcpyHostToDevice, st));
     dim3 grid((unsigned)std::min<int64_t>(64, (x->row_elems / 8 + 255) / 256), (unsigned)n);
-    gather_q_kernel<<<grid, 256, 0, st>>>(x->q_table, x->d_tasks, n, x->cfg.steps_per_req, x->row_elems,
+    gather_q_kernel<<<grid, 256, 0, st>>>(x->q_table, x->d_tasks, n, x->cfg.steps_per_req,
+                                          x->cfg.q_table_steps > 0 ? x->cfg.q_table_steps : x->cfg.steps_per_req,
+                                          x->row_elems,
                                           x->cfg.total_requests, x->d_q, x->ctx->err);
     FERRY_TRY(cudaGetLastError());
     if ((rc = ferry_decode_step(x->ctx, st, x->d_q, x->d_ids, n, x->d_out))) return rc;

@@ -10,7 +10,9 @@
 //      resident pages, copy the request's context length;
 //   2. migrate_pages_kernel warp per 8 KiB page unit, 16 outstanding 16-byte
 //      peer loads per lane: the resident slots [0, size) of every lane
-//      (delta, the reference's kv-mode delta) or all slots (full);
+//      (delta, the reference's kv-mode delta) or all slots (full); none for
+//      drop (the reference's kv-mode drop, wla_multigpu.cuh:1314: the
+//      request's lanes start cold on the thief and refill by misses);
 //   3. release_kernel       marks the victim's request slot as migrated
 //      (system-scope release store) so the victim's host can reuse it.
 // The victim's memory is reached through a direct peer mapping (same process,
@@ -68,6 +70,7 @@ struct MigArgs {
   int C;
   int N;
   int full;
+  int drop;  // FERRY_MIGRATE_DROP: state only, the destination lanes start cold
   int unit_bytes;
   unsigned long long* stats;
   uint32_t* err;
@@ -93,7 +96,7 @@ __global__ void __launch_bounds__(256) migrate_meta_kernel(MigArgs A) {
     if (pg >= 0 && pg < A.N) ps[pg] = -1;
   }
   __syncwarp();
-  int ssz = A.p_size[sl];
+  int ssz = A.drop ? 0 : A.p_size[sl];
   if (ssz < 0 || ssz > A.C) {
     if (t == 0) record_error(A.err, kErrRange);
     ssz = 0;
@@ -290,7 +293,7 @@ int ferry_ctx_link(ferry_ctx* c, int peer_slot, ferry_ctx* peer) {
 int ferry_migrate_requests(ferry_ctx* c, void* stream, int peer_slot, const int32_t* d_src_req,
                            const int32_t* d_dst_req, int n, int mode) {
   if (!c || peer_slot < 0 || peer_slot >= FERRY_MAX_PEERS || n < 0 || (n && (!d_src_req || !d_dst_req)) ||
-      (mode != FERRY_MIGRATE_FULL && mode != FERRY_MIGRATE_DELTA))
+      (mode != FERRY_MIGRATE_FULL && mode != FERRY_MIGRATE_DELTA && mode != FERRY_MIGRATE_DROP))
     return set_error("migrate_requests: bad arguments"), FERRY_E_INVAL;
   const ferry_peer& p = c->peers[peer_slot];
   if (!p.cache) return set_error("migrate_requests: peer slot %d is not linked", peer_slot), FERRY_E_STATE;
@@ -319,6 +322,7 @@ int ferry_migrate_requests(ferry_ctx* c, void* stream, int peer_slot, const int3
   A.C = c->cfg.cache_pages;
   A.N = c->cfg.max_pages;
   A.full = mode == FERRY_MIGRATE_FULL;
+  A.drop = mode == FERRY_MIGRATE_DROP;
   A.unit_bytes = c->unit_bytes;
   A.stats = c->stats;
   A.err = c->err;
@@ -326,10 +330,12 @@ int ferry_migrate_requests(ferry_ctx* c, void* stream, int peer_slot, const int3
   const int lanes = n * c->lanes_per_req;
   migrate_meta_kernel<<<(lanes + 7) / 8, 256, 0, st>>>(A);
   FERRY_TRY(cudaGetLastError());
-  const int64_t items = (int64_t)lanes * A.C;
-  const int64_t blocks = std::min<int64_t>((items + 7) / 8, (int64_t)c->num_sms * 16);
-  migrate_pages_kernel<<<(unsigned)blocks, 256, 0, st>>>(A);
-  FERRY_TRY(cudaGetLastError());
+  if (!A.drop) {
+    const int64_t items = (int64_t)lanes * A.C;
+    const int64_t blocks = std::min<int64_t>((items + 7) / 8, (int64_t)c->num_sms * 16);
+    migrate_pages_kernel<<<(unsigned)blocks, 256, 0, st>>>(A);
+    FERRY_TRY(cudaGetLastError());
+  }
   release_kernel<<<(n + 127) / 128, 128, 0, st>>>(A);
   FERRY_TRY(cudaGetLastError());
   return FERRY_OK;

@@ -101,7 +101,24 @@ CFG5S_F16 = Workload(name="cfg5s_f16", num_requests=16, num_layers=2, q_heads=64
                      ctx_tokens=131072, top_k=512, cache_frac=0.15, steps=64, arrival_rate=50.0,
                      kv_dtype="f16")
 
-WORKLOADS = {"cfg1": CFG1, "cfg5s": CFG5S, "cfg5s_f16": CFG5S_F16}
+# configs[2] (steady balanced multi-GPU) cut to one of its 32 layers: 256
+# requests with contexts uniform in 8k-32k tokens (ragged, <= 2048 pages),
+# round-robin homes, Poisson 400 req/s box-wide, top-128, the cache at 30% of
+# the mean context (384 of its 1280 pages per lane), 1024 decode steps.
+CFG3S = Workload(name="cfg3s", num_requests=256, num_layers=1, q_heads=32, kv_heads=32,
+                 ctx_tokens=32768, top_k=128, cache_frac=0.3 * 20480 / 32768, steps=1024, arrival_rate=400.0)
+
+# configs[3] (skewed bursty) cut to one layer: contexts uniform in 16k-64k
+# tokens (<= 4096 pages), top-256, the cache at 30% of the mean context (768
+# of 2560 pages), Zipf(1.5) homes, ON/OFF arrivals (exponential ON periods of
+# mean 200 ms at 2000 req/s, exponential OFF periods of mean 800 ms); decode
+# steps as the config-2 model's (512).
+CFG4S = Workload(name="cfg4s", num_requests=256, num_layers=1, q_heads=32, kv_heads=32,
+                 ctx_tokens=65536, top_k=256, cache_frac=0.3 * 40960 / 65536, steps=512, arrival_rate=2000.0)
+
+CONTEXT_RANGE = {"cfg3s": (8192, 32768), "cfg4s": (16384, 65536)}
+
+WORKLOADS = {"cfg1": CFG1, "cfg5s": CFG5S, "cfg5s_f16": CFG5S_F16, "cfg3s": CFG3S, "cfg4s": CFG4S}
 
 
 def small(name: str = "tiny", **kw) -> Workload:
@@ -118,6 +135,31 @@ def arrival_ticks(w: Workload) -> np.ndarray:
     gaps = rng.exponential(1000.0 / w.arrival_rate, size=w.num_requests)
     t_ms = np.cumsum(gaps)
     return np.ceil(t_ms / w.tick_ms).astype(np.int64)
+
+
+def ragged_pages(n: int, lo_tokens: int, hi_tokens: int, seed: int) -> np.ndarray:
+    """Context of each request in pages: tokens uniform in [lo, hi], whole
+    pages (a ragged tail of < 16 tokens is not a page, as in the reference's
+    selector, tools/capture_miss_trace.py:131-133)."""
+    rng = np.random.default_rng([seed, 8191])
+    return (rng.integers(lo_tokens, hi_tokens + 1, size=n) // 16).astype(np.int32)
+
+
+def onoff_arrival_ticks(n: int, rate_on: float, on_ms: float, off_ms: float, seed: int,
+                        tick_ms: float = 20.0) -> np.ndarray:
+    """ON/OFF arrivals: alternating ON periods (exponential, mean on_ms) with
+    Poisson arrivals at rate_on req/s and silent OFF periods (exponential,
+    mean off_ms), starting ON at t = 0; the decode tick of each of n requests."""
+    rng = np.random.default_rng([seed, 2000])
+    t, out = 0.0, []
+    while len(out) < n:
+        end = t + rng.exponential(on_ms)
+        a = t + rng.exponential(1000.0 / rate_on)
+        while a < end and len(out) < n:
+            out.append(a)
+            a += rng.exponential(1000.0 / rate_on)
+        t = end + rng.exponential(off_ms)
+    return np.floor(np.asarray(out) / tick_ms).astype(np.int64)
 
 
 class Schedule:

@@ -248,12 +248,15 @@ int ferry_debug_read(ferry_ctx* ctx, int which, size_t offset, size_t bytes, voi
  * thief: it pulls each request's lane state (LRU order, slot table, page
  * table, context length) and its cache pages with 128-bit peer loads --
  * FERRY_MIGRATE_DELTA copies only resident slots (the reference's kv-mode
- * delta), FERRY_MIGRATE_FULL every slot -- then marks the victim's request
- * slot as migrated (ferry_slot_states reads those marks). */
+ * delta), FERRY_MIGRATE_FULL every slot, FERRY_MIGRATE_DROP none (context
+ * length and pool home only) -- then marks the victim's request slot as
+ * migrated (ferry_slot_states reads those marks). */
 #define FERRY_MAX_PEERS 8
 #define FERRY_CTX_HANDLE_BYTES 1024
 #define FERRY_MIGRATE_FULL 0
 #define FERRY_MIGRATE_DELTA 1
+#define FERRY_MIGRATE_DROP 2 /* no pages: the request's lanes start cold on the thief and refill by
+                                misses (the reference's kv-mode drop, wla_multigpu.cuh:129, 1314) */
 int ferry_ctx_export(ferry_ctx* ctx, void* handle /* FERRY_CTX_HANDLE_BYTES */);
 /* ---- page-owner stores
  * Pages sharded by page id across the GPUs of a job: rank `rank` of `world`
@@ -351,8 +354,9 @@ int ferry_exchange_ownership(ferry_comm* comm, void* stream, const int32_t* d_ro
  * share ceil(pending / world) -- steals min(steal_batch, size - fair,
  * size / 2 + 1) tasks from the peer deque with the largest excess and
  * migrates those requests over NVLink; then it runs ferry_decode_step on the
- * batch (queries gathered from d_q_table, [total_requests][steps][L][Hq][128]
- * fp16 on the ctx device) and pushes the next steps back. Request r's home in
+ * batch (queries gathered from d_q_table, [total_requests][q_table_steps][L][Hq]
+ * [128] fp16, device memory or pinned mapped host memory) and pushes the next
+ * steps back. Request r's home in
  * the host pool is r * L * Hkv * max_pages (every GPU registers a pool with
  * the same content). */
 typedef struct ferry_exec ferry_exec;
@@ -361,9 +365,11 @@ typedef struct ferry_exec_cfg {
   int world;          /* number of ranks */
   int max_batch;      /* tasks decoded per tick (<= ctx num_requests) */
   int steal_batch;    /* most tasks one steal takes (the reference's steal_batch, default 4) */
-  int migrate_mode;   /* FERRY_MIGRATE_DELTA or FERRY_MIGRATE_FULL */
+  int migrate_mode;   /* FERRY_MIGRATE_DELTA, FERRY_MIGRATE_FULL or FERRY_MIGRATE_DROP */
   int steps_per_req;  /* decode steps of every request */
   int total_requests; /* global request ids are [0, total_requests) */
+  int q_table_steps;  /* query-table rows per request (0 = steps_per_req); step s reads
+                         row s % q_table_steps */
 } ferry_exec_cfg;
 typedef struct ferry_tick_stats {
   int decoded;      /* tasks decoded this tick */

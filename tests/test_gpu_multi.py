@@ -225,6 +225,65 @@ def test_migrate_requests_bit_exact_then_same_decode(torch_cuda, devices, mode):
         src.close()
 
 
+@pytest.mark.parametrize("devices", [(0, 0), (0, 1)])
+def test_migrate_drop_starts_cold(torch_cuda, devices):
+    """FERRY_MIGRATE_DROP (the reference's kv-mode drop, wla_multigpu.cuh:1314):
+    no page moves; the thief's lanes are empty, the request keeps its context
+    length and pool home, and it decodes exactly as a cold restart of the
+    same request would (every selected page refilled by a miss)."""
+    from ferry_b200 import _abi
+    from ferry_b200.engine import Decoder
+
+    t = torch_cuda
+    if max(devices) >= t.cuda.device_count():
+        pytest.skip("needs two GPUs")
+    w = _workload()
+    src, dst, cold = Decoder(w, devices[0]), Decoder(w, devices[1]), Decoder(w, devices[1])
+    try:
+        d0, d1 = t.device("cuda", devices[0]), t.device("cuda", devices[1])
+        for dec, d in ((src, d0), (dst, d1), (cold, d1)):
+            dec.register_pool()
+            ids = t.arange(4, dtype=t.int32, device=d)
+            dec.begin(ids, t.full((4,), w.max_pages, dtype=t.int32, device=d))
+        _run_steps(t, src, w, [0, 1, 2, 3], range(3), d0)
+        _run_steps(t, dst, w, [0, 1, 2, 3], [7], d1)  # the thief's slots hold other state
+        _abi.call("ferry_ctx_link", dst.ctx, 0, src.ctx)
+        with t.cuda.device(d1):
+            s_ids = t.tensor([1, 3], dtype=t.int32, device=d1)
+            d_ids = t.tensor([0, 2], dtype=t.int32, device=d1)
+            _abi.call("ferry_migrate_requests", dst.ctx, C.c_void_p(t.cuda.current_stream(d1).cuda_stream),
+                      0, _p(s_ids), _p(d_ids), 2, _abi.MIGRATE_DROP)
+            t.cuda.synchronize(d1)
+        dst.check()
+        for dr in (0, 2):
+            for sz, _, ps, _ in _lane_state(dst, w, dr):
+                assert sz == 0 and (ps == -1).all()
+        states = np.zeros(w.num_requests, np.int32)
+        _abi.call("ferry_slot_states", src.ctx, states.ctypes.data_as(C.c_void_p), 1)
+        assert states.tolist() == [0, 2, 0, 2]
+        assert dst.all_stats()[2] == 0  # no page migrated
+        # slots 1 and 3 of `cold` start cold with requests 1 and 3's homes (default bases)
+        ids_t = t.tensor([0, 2], dtype=t.int32, device=d1)
+        ids_c = t.tensor([1, 3], dtype=t.int32, device=d1)
+        cold.begin(ids_c, t.full((2,), w.max_pages, dtype=t.int32, device=d1))
+        o = t.zeros((2, w.num_layers, w.q_heads, 128), dtype=t.float32, device=d1)
+        oc = t.zeros_like(o)
+        dst.all_stats(reset=True)
+        cold.all_stats(reset=True)
+        for s in (3, 4):
+            q = t.from_numpy(_q(w, [1, 3], s)).to(d1)
+            dst.step(q, ids_t, o)
+            cold.step(q, ids_c, oc)
+            t.cuda.synchronize(d1)
+            assert (o.cpu().numpy().view(np.uint32) == oc.cpu().numpy().view(np.uint32)).all()
+        assert dst.all_stats()[0] == cold.all_stats()[0] > 0
+        dst.check()
+    finally:
+        cold.close()
+        dst.close()
+        src.close()
+
+
 def _ipc_owner(conn, device):
     import torch
 

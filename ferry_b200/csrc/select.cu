@@ -27,12 +27,24 @@ namespace {
 constexpr int kSelThreads = 256;
 constexpr int kSelWarps = kSelThreads / 32;
 constexpr int kSelBatch = 8;  // pages per warp per stage
-constexpr int kStagePages = kSelWarps * kSelBatch;  // 64 summary rows per ring stage
 constexpr int kSelStages = 3;
-constexpr int kRowBytes = kHeadDim * 4;                        // 512
-constexpr int kStageBytes = kStagePages * kRowBytes;           // 32 KiB
-constexpr int kRingBytes = kSelStages * kStageBytes;           // 96 KiB
-static_assert(kMaxPages * 4 <= kRingBytes, "keys of a lane must fit the ring");
+constexpr int kRowBytes = kHeadDim * 4;  // 512
+
+// Ring geometry of a W-warp CTA: a stage holds 8 summary rows per warp.
+// W = 8 (long lanes, chunked): 64-row / 32 KiB stages, 96 KiB ring, 2 CTAs
+// per SM, block-level radix select. W = 4 (lanes of <= kSelSmallPages pages,
+// one CTA each): 32-row / 16 KiB stages, 48 KiB ring, 4 CTAs per SM -- the
+// whole batch in one wave with four lanes' loads in flight per SM -- and a
+// warp-level select, so no CTA holds the SM through block barriers.
+template <int W>
+struct SelGeom {
+  static constexpr int kThreads = W * 32;
+  static constexpr int kStagePages = W * kSelBatch;
+  static constexpr int kStageBytes = kStagePages * kRowBytes;
+  static constexpr int kRingBytes = kSelStages * kStageBytes;
+};
+constexpr int kSelSmallPages = 1024;
+static_assert(kMaxPages * 4 <= SelGeom<8>::kRingBytes, "keys of a lane must fit the ring");
 
 template <int G>
 struct SelShape {
@@ -179,6 +191,53 @@ __device__ __forceinline__ void topk_emit(const uint32_t* keys, int np, int k, i
   }
 }
 
+// Top-k of np > k order keys (np <= kSelSmallPages, shared memory) by one
+// warp, with the same result as topk_emit: the k-th largest key T is the
+// largest t with #(key >= t) >= k, built from the top bit down (32 counting
+// rounds over keys held in registers); then every key > T and the lowest-id
+// pages with key == T, emitted in ascending page order.
+__device__ __forceinline__ void warp_topk(const uint32_t* keys, int np, int k, int32_t* out) {
+  const int lane = threadIdx.x & 31;
+  constexpr int kPer = kSelSmallPages / 32;
+  uint32_t kr[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int p = j * 32 + lane;
+    kr[j] = p < np ? keys[p] : 0u;
+  }
+  const int nj = (np + 31) / 32;
+  uint32_t T = 0;
+#pragma unroll 1
+  for (int b = 31; b >= 0; --b) {
+    const uint32_t cand = T | (1u << b);
+    uint32_t c = 0;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j)
+      if (j < nj) c += (j * 32 + lane < np && kr[j] >= cand) ? 1u : 0u;
+    c = __reduce_add_sync(0xffffffffu, c);
+    if (c >= (uint32_t)k) T = cand;
+  }
+  uint32_t gt = 0;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j)
+    if (j < nj) gt += (j * 32 + lane < np && kr[j] > T) ? 1u : 0u;
+  gt = __reduce_add_sync(0xffffffffu, gt);
+  const uint32_t krem = (uint32_t)k - gt;  // keys equal to T that are taken
+  uint32_t pos = 0, eq_rank = 0;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    if (j >= nj) break;
+    const int p = j * 32 + lane;
+    const bool g = p < np && kr[j] > T, e = p < np && kr[j] == T;
+    const uint32_t meq = __ballot_sync(0xffffffffu, e);
+    const bool take = g || (e && eq_rank + __popc(meq & lanemask_lt(lane)) < krem);
+    const uint32_t mt = __ballot_sync(0xffffffffu, take);
+    if (take) out[pos + __popc(mt & lanemask_lt(lane))] = p;
+    pos += __popc(mt);
+    eq_rank += __popc(meq);
+  }
+}
+
 struct SelArgs {
   const uint16_t* q;
   const int32_t* req_ids;
@@ -195,13 +254,15 @@ struct SelArgs {
   uint32_t* err;
 };
 
-template <int G>
-__global__ void __launch_bounds__(kSelThreads, 2) select_kernel(SelArgs A) {
+template <int G, int W>
+__global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 4) select_kernel(SelArgs A) {
   using Sh = SelShape<G>;
+  using SG = SelGeom<W>;
+  constexpr int kThreads = SG::kThreads, kStagePages = SG::kStagePages, kStageBytes = SG::kStageBytes;
   // dynamic: the summary ring; keys after it (one chunk) or in it (after scoring)
   extern __shared__ __align__(128) uint8_t sel_smem[];
   uint8_t* ring = sel_smem;
-  uint32_t* keys = reinterpret_cast<uint32_t*>(sel_smem + (A.nchunks > 1 ? 0 : kRingBytes));
+  uint32_t* keys = reinterpret_cast<uint32_t*>(sel_smem + (A.nchunks > 1 ? 0 : SG::kRingBytes));
   __shared__ __align__(8) uint64_t bars[kSelStages];
   __shared__ TopkSmem tk;
   __shared__ uint32_t s_last;
@@ -216,7 +277,7 @@ __global__ void __launch_bounds__(kSelThreads, 2) select_kernel(SelArgs A) {
       record_error(A.err, kErrRange);
       A.n_sel_out[a] = 0;
     }
-    for (int j = tid; j < k; j += kSelThreads) out[j] = -1;
+    for (int j = tid; j < k; j += kThreads) out[j] = -1;
     return;
   }
   int np = A.ctx_pages[req];
@@ -328,17 +389,22 @@ __global__ void __launch_bounds__(kSelThreads, 2) select_kernel(SelArgs A) {
     if (!s_last) return;
     __threadfence();
     if (tid == 0) A.done[a] = 0;
-    for (int p = tid; p < np; p += kSelThreads) keys[p] = __ldcg(A.gkeys + (size_t)a * N + p);
+    for (int p = tid; p < np; p += kThreads) keys[p] = __ldcg(A.gkeys + (size_t)a * N + p);
   }
   __syncthreads();
 
   if (np <= k) {
-    for (int j = tid; j < k; j += kSelThreads) out[j] = j < np ? j : -1;
+    for (int j = tid; j < k; j += kThreads) out[j] = j < np ? j : -1;
     if (tid == 0) A.n_sel_out[a] = np;
     return;
   }
 
-  topk_emit(keys, np, k, out, tk);
+  if constexpr (W == 8) {
+    topk_emit(keys, np, k, out, tk);
+  } else {
+    if (warp != 0) return;
+    warp_topk(keys, np, k, out);
+  }
   if (tid == 0) A.n_sel_out[a] = k;
 }
 
@@ -516,14 +582,16 @@ int launch_select(const ferry_ctx* c, cudaStream_t st, const uint16_t* q,
     return FERRY_E_STATE;
   }
   const unsigned grid = (unsigned)((int64_t)n_req * c->lanes_per_req * A.nchunks);
-  const size_t smem = kRingBytes + (A.nchunks > 1 ? 0 : (size_t)A.N * sizeof(uint32_t));
+  const bool small = A.nchunks == 1 && A.N <= kSelSmallPages;
+  const size_t smem = (small ? SelGeom<4>::kRingBytes : SelGeom<8>::kRingBytes) +
+                      (A.nchunks > 1 ? 0 : (size_t)A.N * sizeof(uint32_t));
 #define FERRY_SEL_CASE(GG)                                                                    \
   case GG: {                                                                                  \
-    auto kern = select_kernel<GG>;                                                            \
+    auto kern = small ? select_kernel<GG, 4> : select_kernel<GG, 8>;                          \
     if (smem > 48 * 1024)                                                                     \
       FERRY_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,       \
                                      (int)smem));                                             \
-    kern<<<grid, kSelThreads, smem, st>>>(A);                                                 \
+    kern<<<grid, small ? 128 : 256, smem, st>>>(A);                                           \
     break;                                                                                    \
   }
   switch (c->group) {

@@ -155,6 +155,10 @@ def test_kvgen_and_summaries_bit_exact(torch_cuda):
     # long lanes: selection scores them in several chunks (one CTA each)
     dict(num_layers=1, q_heads=8, kv_heads=1, ctx_tokens=65536, top_k=64),  # N 4096, G 8
     dict(num_layers=1, q_heads=4, kv_heads=2, ctx_tokens=40000, top_k=48),  # N 2500, G 2
+    # the largest lanes of the 4-warp kernel (warp-level select over 1024 keys)
+    # and the smallest of the 8-warp one (one chunk of 2048 pages)
+    dict(num_layers=1, q_heads=4, kv_heads=4, ctx_tokens=16384, top_k=96),  # N 1024, G 1
+    dict(num_layers=1, q_heads=4, kv_heads=4, ctx_tokens=32768, top_k=128),  # N 2048, G 1
 ])
 def test_decode_steps_match_oracle(torch_cuda, shape):
     from ferry_b200.workload import small
@@ -217,10 +221,12 @@ def test_longest_lane(torch_cuda):
         h.close()
 
 
-@pytest.mark.parametrize("ctx_tokens", [2048, 65536])
+@pytest.mark.parametrize("ctx_tokens", [2048, 16384, 32768, 65536])
 def test_select_ties_and_signed_zeros(torch_cuda, ctx_tokens):
     """All-zero queries score every page +-0 (ties everywhere, and -0 < +0 in
-    key order); identical q heads tie the GQA maximum on every page."""
+    key order); identical q heads tie the GQA maximum on every page. Lanes of
+    128 and 1024 pages take the 4-warp kernel with the warp-level select,
+    2048 pages the 8-warp kernel in one chunk, 4096 pages several chunks."""
     from ferry_b200.workload import small
 
     t = torch_cuda

@@ -194,39 +194,37 @@ __device__ __forceinline__ void topk_emit(const uint32_t* keys, int np, int k, i
 // Top-k of np > k order keys (np <= kSelSmallPages, shared memory) by one
 // warp, with the same result as topk_emit: the k-th largest key T is the
 // largest t with #(key >= t) >= k, built from the top bit down (32 counting
-// rounds over keys held in registers); then every key > T and the lowest-id
-// pages with key == T, emitted in ascending page order.
+// rounds over the kPer keys per lane held in registers); then every key > T
+// and the lowest-id pages with key == T, emitted in ascending page order.
+// Keys are order_key() values, never 0 for a real score (a real key has its
+// top bit set or is the complement of a negative float's bits).
+template <int kPer>  // keys per lane: np <= 32 * kPer
 __device__ __forceinline__ void warp_topk(const uint32_t* keys, int np, int k, int32_t* out) {
   const int lane = threadIdx.x & 31;
-  constexpr int kPer = kSelSmallPages / 32;
   uint32_t kr[kPer];
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int p = j * 32 + lane;
-    kr[j] = p < np ? keys[p] : 0u;
+    kr[j] = p < np ? keys[p] : 0u;  // pages past np hold 0, below every real key
   }
-  const int nj = (np + 31) / 32;
   uint32_t T = 0;
 #pragma unroll 1
   for (int b = 31; b >= 0; --b) {
     const uint32_t cand = T | (1u << b);
     uint32_t c = 0;
 #pragma unroll
-    for (int j = 0; j < kPer; ++j)
-      if (j < nj) c += (j * 32 + lane < np && kr[j] >= cand) ? 1u : 0u;
+    for (int j = 0; j < kPer; ++j) c += kr[j] >= cand ? 1u : 0u;  // cand > 0: padding never counts
     c = __reduce_add_sync(0xffffffffu, c);
     if (c >= (uint32_t)k) T = cand;
   }
   uint32_t gt = 0;
 #pragma unroll
-  for (int j = 0; j < kPer; ++j)
-    if (j < nj) gt += (j * 32 + lane < np && kr[j] > T) ? 1u : 0u;
+  for (int j = 0; j < kPer; ++j) gt += kr[j] > T ? 1u : 0u;
   gt = __reduce_add_sync(0xffffffffu, gt);
   const uint32_t krem = (uint32_t)k - gt;  // keys equal to T that are taken
   uint32_t pos = 0, eq_rank = 0;
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
-    if (j >= nj) break;
     const int p = j * 32 + lane;
     const bool g = p < np && kr[j] > T, e = p < np && kr[j] == T;
     const uint32_t meq = __ballot_sync(0xffffffffu, e);
@@ -403,7 +401,12 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 4) select_kernel(SelArgs 
     topk_emit(keys, np, k, out, tk);
   } else {
     if (warp != 0) return;
-    warp_topk(keys, np, k, out);
+    if (np <= 256)
+      warp_topk<8>(keys, np, k, out);
+    else if (np <= 512)
+      warp_topk<16>(keys, np, k, out);
+    else
+      warp_topk<32>(keys, np, k, out);
   }
   if (tid == 0) A.n_sel_out[a] = k;
 }

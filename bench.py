@@ -177,7 +177,7 @@ def cpu_baseline(w, seconds: float = 15.0, threads: int | None = None, ticks: in
     per-tick [(ms, tokens, misses, output of the first `keep` ticks or None)]);
     the kept outputs let the caller check its own outputs of the same ticks."""
     import oracle
-    from ferry_b200.workload import Schedule, q_stream
+    from ferry_b200.workload import Schedule, pages_after, q_stream
 
     oracle.build()
     threads = threads or os.cpu_count() or 1
@@ -201,8 +201,10 @@ def cpu_baseline(w, seconds: float = 15.0, threads: int | None = None, ticks: in
         lanes = (active[:, None] * LH + np.arange(LH)[None]).ravel().astype(np.int32)
         reset = np.repeat((steps == 0).astype(np.uint8), LH)
         q = np.stack([qs[r][s] for r, s in zip(active, steps)]).view(np.uint16)
+        # the context at this step: decode appends grow it after every step
+        npg = np.repeat(pages_after(w.init_pages, steps, w.append, w.max_pages), LH).astype(np.int32)
         t0 = time.perf_counter()
-        out, misses = pipe.step(lanes, q.reshape(len(lanes), w.group, 128), reset=reset)
+        out, misses = pipe.step(lanes, q.reshape(len(lanes), w.group, 128), reset=reset, n_pages=npg)
         dt = time.perf_counter() - t0
         t_used += dt
         per_tick.append((dt * 1e3, len(active), misses, out if i <= keep else None))
@@ -299,7 +301,7 @@ def run_ferry(args, w):
                           ids=torch.from_numpy(active).to(dev),
                           qd=None if q is None else q.to(dev),
                           new=None if len(new) == 0 else torch.from_numpy(new).to(dev)))
-    n_pages = torch.full((w.num_requests,), w.max_pages, dtype=torch.int32, device=dev)
+    n_pages = torch.full((w.num_requests,), w.init_pages, dtype=torch.int32, device=dev)
     out = torch.empty((w.num_requests, w.num_layers, w.q_heads, 128), dtype=torch.float32, device=dev)
     st = torch.cuda.current_stream(dev)
 
@@ -321,6 +323,8 @@ def run_ferry(args, w):
         dec.gather(tk["ids"], stream=st)
         e[3].record(st)
         dec.attention(tk["qd"], tk["ids"], out[:n], stream=st)
+        if w.append:  # the decoded token joins the context (the fused step does this itself)
+            dec.append(tk["ids"], stream=st)
         e[4].record(st)
         evs.append((e, n))
         return n
@@ -459,7 +463,7 @@ def run_ferry(args, w):
             "config": {"workload": f"{w.name} (configs[0])", "requests": w.num_requests,
                        "ctx_tokens": w.ctx_tokens, "layers": w.num_layers,
                        "heads": [w.q_heads, w.kv_heads], "head_dim": 128, "page_tokens": 16,
-                       "top_k": w.top_k, "cache_pages": w.cache_pages,
+                       "top_k": w.top_k, "cache_pages": w.cache_pages, "append_tokens_per_step": w.append,
                        "arrivals": f"poisson {w.arrival_rate} req/s on a {w.tick_ms} ms tick",
                        "l2": "inputs larger than L2 (selected KV 256 MiB + summaries 64 MiB per full step)",
                        "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU"},
@@ -512,6 +516,8 @@ def main():
     ap.add_argument("--no-steal", action="store_true", help="skew: disable work stealing")
     ap.add_argument("--slots", type=int, default=64, help="cfg3s/cfg4s: request slots per GPU")
     ap.add_argument("--batch", type=int, default=32, help="cfg3s/cfg4s: requests decoded per GPU per tick")
+    ap.add_argument("--append", type=int, default=None,
+                    help="tokens each decode step appends to its context (default: the workload's)")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: independent cfg1 replicas per rank instead of the executor job")
     args = ap.parse_args()
@@ -528,6 +534,10 @@ def main():
         run_config_slice(args, WORKLOADS[args.workload])
         return
     w = WORKLOADS[args.workload]
+    if args.append is not None:
+        import dataclasses
+
+        w = dataclasses.replace(w, append=args.append)
     if args.impl == "reference":
         run_reference(args, w)
     elif _dist()[0] > 1 and args.workload == "cfg1" and not args.replicas:

@@ -306,7 +306,7 @@ class RankRunner:
         comm = self.comm if exchange_device is not None else None
         st = torch.cuda.current_stream(self.dev)
         mine = np.nonzero(home == self.rank)[0]
-        pages_of = np.full(len(home), self.w.max_pages, np.int32) if n_pages is None else np.asarray(n_pages, np.int32)
+        pages_of = np.full(len(home), self.w.init_pages, np.int32) if n_pages is None else np.asarray(n_pages, np.int32)
         admitted = finished = tokens = ticks = steals = stolen = 0
         mig_ms, mig_b = 0.0, 0
         tick_ms = []

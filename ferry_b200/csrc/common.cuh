@@ -214,7 +214,9 @@ struct ferry_ctx {
   uint8_t* cache = nullptr;  // lanes * C units
   alignas(64) unsigned char cache_map[128] = {};  // TMA tensor map of the e4m3 cache
   ferry_lru lru;             // page tables + LRU order, lanes x (C, N)
-  int32_t* ctx_pages = nullptr;  // R
+  int32_t* ctx_pages = nullptr;  // 2R: full pages of each request's context, then the tokens of
+                                 // its partial last page (0..15; decode appends)
+  int append_tokens = 0;         // tokens ferry_decode_step appends per request (0 = fixed context)
   int64_t* req_base = nullptr;   // R: pool unit of the request's (lane 0, page 0)
 
   // host pool
@@ -264,6 +266,9 @@ int launch_summary(cudaStream_t st, const uint8_t* pool, int64_t unit0, int64_t 
                    float* summ, int kv_dtype);
 int launch_select(const ferry_ctx* c, cudaStream_t st, const uint16_t* q, const int32_t* req_ids,
                   int n_req, int32_t* sel, int32_t* n_sel);
+// decode appends: grow each listed request's context by `tokens` tokens and
+// compute the summary of every page that becomes full (kvgen.cu)
+int launch_append(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, int n, int tokens);
 // Quest page bounds [kmin | kmax] of pool units (kvgen.cu)
 int launch_minmax(cudaStream_t st, const uint8_t* pool, int64_t unit0, int64_t n_units, float* mm,
                   int kv_dtype);

@@ -191,7 +191,7 @@ int ferry_ctx_create(int device, const ferry_cfg* cfg, ferry_ctx** out) {
   if (cfg->kv_dtype == FERRY_KV_E4M3 || c->group > 1) FERRY_CK(make_cache_tensor_map(c));
   FERRY_CK(alloc_lru_state(&c->lru, c->lanes, cfg->cache_pages, cfg->max_pages, c->err));
   c->lru.device = device;
-  FERRY_CK(dev_alloc(&c->ctx_pages, R, 0));
+  FERRY_CK(dev_alloc(&c->ctx_pages, 2 * R, 0));
   FERRY_CK(dev_alloc(&c->req_base, R, 0));
   {
     // default home of request slot r in the host pool: units r*L*Hkv*N onwards
@@ -398,7 +398,24 @@ int ferry_decode_step(ferry_ctx* c, void* stream, const uint16_t* d_q, const int
                        c->ws_islot, c->ws_mpage, c->ws_mslot, c->ws_nmiss)))
     return rc;
   if ((rc = launch_gather(c, st, d_req_ids, n_req, c->ws_mpage, c->ws_mslot, c->ws_nmiss))) return rc;
-  return launch_attention_any(c, st, d_q, d_req_ids, n_req, c->ws_islot, c->ws_nsel, d_out);
+  if ((rc = launch_attention_any(c, st, d_q, d_req_ids, n_req, c->ws_islot, c->ws_nsel, d_out))) return rc;
+  // the token decoded in this step joins its request's context
+  return c->append_tokens > 0 ? launch_append(c, st, d_req_ids, n_req, c->append_tokens) : FERRY_OK;
+}
+
+int ferry_requests_append(ferry_ctx* c, void* stream, const int32_t* d_req_ids, int n, int tokens) {
+  int rc = check_batch(c, d_req_ids, n);
+  if (rc) return rc;
+  if (tokens < 0) return set_error("requests_append: negative token count"), FERRY_E_INVAL;
+  if (!c->summ || !c->pool_dev) return set_error("no host pool registered"), FERRY_E_STATE;
+  DeviceGuard guard(c->device);
+  return launch_append(c, (cudaStream_t)stream, d_req_ids, n, tokens);
+}
+
+int ferry_decode_appends(ferry_ctx* c, int tokens_per_step) {
+  if (!c || tokens_per_step < 0) return set_error("decode_appends: bad arguments"), FERRY_E_INVAL;
+  c->append_tokens = tokens_per_step;
+  return FERRY_OK;
 }
 
 int ferry_wait_flag(ferry_ctx* c, void* stream, const uint32_t* d_flag, uint32_t value, uint32_t max_polls) {
@@ -429,7 +446,7 @@ int ferry_debug_read(ferry_ctx* c, int which, size_t offset, size_t bytes, void*
     case 2: base = (uint8_t*)c->lru.order; size = (size_t)c->lanes * c->cfg.cache_pages * 4; break;
     case 3: base = (uint8_t*)c->lru.size; size = (size_t)c->lanes * 4; break;
     case 4: base = (uint8_t*)c->summ; size = (size_t)c->pool_units * c->summ_row * 4; break;
-    case 5: base = (uint8_t*)c->ctx_pages; size = R * 4; break;
+    case 5: base = (uint8_t*)c->ctx_pages; size = 2 * R * 4; break;
     case 6: base = (uint8_t*)c->ws; size = R * LH * (4 * k + 2) * 4; break;
     case 7: base = (uint8_t*)c->req_base; size = R * 8; break;
     default: return set_error("debug_read: unknown buffer %d", which), FERRY_E_INVAL;

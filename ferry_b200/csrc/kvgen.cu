@@ -239,6 +239,133 @@ __global__ void __launch_bounds__(256) minmax_kernel(const uint8_t* __restrict__
     row[32 + lane] = make_float4(hi[0], hi[1], hi[2], hi[3]);
   }
 }
+
+// ---- decode appends
+// A decode step appends its token to the request's context. ctx_pages holds
+// the full pages of each request and, R entries later, the tokens of its
+// partial last page; a page joins the selectable context when its 16th token
+// arrives (the reference's selector scores whole pages only,
+// tools/capture_miss_trace.py:131-133), and its summary -- mean row or Quest
+// bounds -- is computed then from the pool unit that holds it (the caller has
+// written the page's K/V there). Warp per (request, lane) computes the new
+// pages' summaries; a second kernel advances the counters.
+struct AppendArgs {
+  const int32_t* req_ids;
+  int n, tokens, lanes_per_req, N, R;
+  int32_t* ctx_pages;
+  const int64_t* req_base;
+  const uint8_t* pool;
+  uint64_t pool_units;
+  float* summ;
+  int quest, f8;
+  uint32_t* err;
+};
+
+__device__ __forceinline__ void summary_unit(const uint8_t* pool, uint64_t u, float* summ, bool f8, int lane) {
+  float acc[4];
+  if (f8) {
+    const uint8_t* K = pool + (size_t)u * kUnitBytesF8;
+    const float ks = *reinterpret_cast<const float*>(K + 4096);
+#pragma unroll
+    for (int tt = 0; tt < kPageTokens; ++tt) {
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(K + tt * kHeadDim + lane * 4);
+      const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w & 0xFFFF), __NV_E4M3);
+      const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w >> 16), __NV_E4M3);
+      const float v[4] = {__half2float(__ushort_as_half(lo.x)), __half2float(__ushort_as_half(lo.y)),
+                          __half2float(__ushort_as_half(hi.x)), __half2float(__ushort_as_half(hi.y))};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float kv = __fmul_rn(v[j], ks);
+        acc[j] = tt == 0 ? kv : __fadd_rn(acc[j], kv);
+      }
+    }
+  } else {
+    const uint8_t* K = pool + (size_t)u * kUnitBytes;
+#pragma unroll
+    for (int tt = 0; tt < kPageTokens; ++tt) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(K + tt * kHeadDim * 2 + lane * 8);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+      const float v[4] = {a.x, a.y, b.x, b.y};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] = tt == 0 ? v[j] : __fadd_rn(acc[j], v[j]);
+    }
+  }
+  reinterpret_cast<float4*>(summ + (size_t)u * kHeadDim)[lane] =
+      make_float4(__fmul_rn(acc[0], 0.0625f), __fmul_rn(acc[1], 0.0625f), __fmul_rn(acc[2], 0.0625f),
+                  __fmul_rn(acc[3], 0.0625f));
+}
+
+__device__ __forceinline__ void minmax_unit(const uint8_t* pool, uint64_t u, float* mm, bool f8, int lane) {
+  float lo[4], hi[4];
+#pragma unroll
+  for (int tt = 0; tt < kPageTokens; ++tt) {
+    float v[4];
+    if (f8) {
+      const uint8_t* K = pool + (size_t)u * kUnitBytesF8;
+      const float ks = *reinterpret_cast<const float*>(K + 4096);
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(K + tt * kHeadDim + lane * 4);
+      const __half2_raw a = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w & 0xFFFF), __NV_E4M3);
+      const __half2_raw b = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w >> 16), __NV_E4M3);
+      v[0] = __fmul_rn(__half2float(__ushort_as_half(a.x)), ks);
+      v[1] = __fmul_rn(__half2float(__ushort_as_half(a.y)), ks);
+      v[2] = __fmul_rn(__half2float(__ushort_as_half(b.x)), ks);
+      v[3] = __fmul_rn(__half2float(__ushort_as_half(b.y)), ks);
+    } else {
+      const uint8_t* K = pool + (size_t)u * kUnitBytes;
+      const uint2 raw = *reinterpret_cast<const uint2*>(K + tt * kHeadDim * 2 + lane * 8);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+      v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      lo[j] = (tt == 0 || v[j] < lo[j]) ? v[j] : lo[j];
+      hi[j] = (tt == 0 || v[j] > hi[j]) ? v[j] : hi[j];
+    }
+  }
+  float4* row = reinterpret_cast<float4*>(mm + (size_t)u * 2 * kHeadDim);
+  row[lane] = make_float4(lo[0], lo[1], lo[2], lo[3]);
+  row[32 + lane] = make_float4(hi[0], hi[1], hi[2], hi[3]);
+}
+
+__global__ void __launch_bounds__(256) append_summary_kernel(AppendArgs A) {
+  const int t = threadIdx.x & 31;
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (w >= A.n * A.lanes_per_req) return;
+  const int i = w / A.lanes_per_req, l = w % A.lanes_per_req;
+  const int r = A.req_ids[i];
+  if (r < 0 || r >= A.R) {
+    if (t == 0 && l == 0) record_error(A.err, kErrRange);
+    return;
+  }
+  const int np = A.ctx_pages[r], tail = A.ctx_pages[A.R + r];
+  if (np < 0 || np > A.N || tail < 0 || tail >= kPageTokens) {
+    if (t == 0 && l == 0) record_error(A.err, kErrRange);
+    return;
+  }
+  const int64_t np2 = min((int64_t)A.N, (int64_t)np + ((int64_t)tail + A.tokens) / kPageTokens);
+  for (int64_t p = np; p < np2; ++p) {
+    const uint64_t u = (uint64_t)(A.req_base[r] + (int64_t)l * A.N + p) % A.pool_units;
+    if (A.quest)
+      minmax_unit(A.pool, u, A.summ, A.f8, t);
+    else
+      summary_unit(A.pool, u, A.summ, A.f8, t);
+  }
+}
+
+__global__ void append_state_kernel(AppendArgs A) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= A.n) return;
+  const int r = A.req_ids[i];
+  if (r < 0 || r >= A.R) return;
+  const int np = A.ctx_pages[r], tail = A.ctx_pages[A.R + r];
+  if (np < 0 || np > A.N || tail < 0 || tail >= kPageTokens) return;
+  const int64_t tot = (int64_t)tail + A.tokens;
+  const int64_t np2 = min((int64_t)A.N, (int64_t)np + tot / kPageTokens);
+  A.ctx_pages[r] = (int32_t)np2;
+  A.ctx_pages[A.R + r] = np2 >= A.N ? 0 : (int32_t)(tot % kPageTokens);  // a full context stops growing
+}
 }  // namespace
 
 int launch_kv_generate(cudaStream_t st, uint64_t seed, uint64_t unit0, int64_t n_units,
@@ -275,6 +402,31 @@ int launch_summary(cudaStream_t st, const uint8_t* pool, int64_t unit0, int64_t 
     summary_e4m3_kernel<<<(unsigned)blocks, 256, 0, st>>>(pool, unit0, n_units, summ);
   else
     summary_kernel<<<(unsigned)blocks, 256, 0, st>>>(pool, unit0, n_units, summ);
+  FERRY_TRY(cudaGetLastError());
+  return FERRY_OK;
+}
+
+int launch_append(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, int n, int tokens) {
+  if (n <= 0 || tokens <= 0) return FERRY_OK;
+  AppendArgs A{};
+  A.req_ids = req_ids;
+  A.n = n;
+  A.tokens = tokens;
+  A.lanes_per_req = c->lanes_per_req;
+  A.N = c->cfg.max_pages;
+  A.R = c->cfg.num_requests;
+  A.ctx_pages = c->ctx_pages;
+  A.req_base = c->req_base;
+  A.pool = c->pool_dev;
+  A.pool_units = c->pool_units;
+  A.summ = c->summ;
+  A.quest = c->select_mode == FERRY_SELECT_QUEST;
+  A.f8 = c->cfg.kv_dtype == FERRY_KV_E4M3;
+  A.err = c->err;
+  const int warps = n * c->lanes_per_req;
+  append_summary_kernel<<<(warps + 7) / 8, 256, 0, st>>>(A);
+  FERRY_TRY(cudaGetLastError());
+  append_state_kernel<<<(n + 127) / 128, 128, 0, st>>>(A);
   FERRY_TRY(cudaGetLastError());
   return FERRY_OK;
 }

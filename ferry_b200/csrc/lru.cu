@@ -417,14 +417,16 @@ __global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
   if (t == 0) A.n_miss[a] = nm;
 }
 
-// Empty every lane of the listed requests and record their context length.
+// Empty every lane of the listed requests and record their context length
+// (ctx_pages holds the full pages of each request, then, R entries later, the
+// tokens of its partial last page).
 __global__ void __launch_bounds__(256) lru_reset_kernel(int32_t* page_slot, int32_t* slot_page,
                                                         int32_t* size, int lanes, int cap, int ids,
                                                         const int32_t* req_ids, int n,
                                                         int lanes_per_req, const int32_t* n_pages,
                                                         int32_t* ctx_pages, int max_pages,
                                                         const int64_t* pool_base, int64_t* req_base,
-                                                        uint32_t* err) {
+                                                        int max_requests, uint32_t* err) {
   const int t = threadIdx.x & 31;
   const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (w >= n * lanes_per_req) return;
@@ -451,6 +453,7 @@ __global__ void __launch_bounds__(256) lru_reset_kernel(int32_t* page_slot, int3
         np = np < 0 ? 0 : max_pages;
       }
       ctx_pages[req_ids[i]] = np;
+      ctx_pages[max_requests + req_ids[i]] = 0;  // no partial page yet
       if (req_base)
         req_base[req_ids[i]] = pool_base ? pool_base[i]
                                          : (int64_t)req_ids[i] * lanes_per_req * (int64_t)max_pages;
@@ -519,7 +522,7 @@ int launch_lru_reset(const ferry_lru* L, cudaStream_t st, const int32_t* req_ids
   lru_reset_kernel<<<(warps + 7) / 8, 256, 0, st>>>(L->page_slot, L->slot_page, L->size, L->lanes,
                                                     L->cap, L->ids, req_ids, n, lanes_per_req,
                                                     n_pages, ctx_pages, L->ids, pool_base, req_base,
-                                                    L->err);
+                                                    L->lanes / lanes_per_req, L->err);
   FERRY_TRY(cudaGetLastError());
   return FERRY_OK;
 }

@@ -111,6 +111,7 @@ __global__ void __launch_bounds__(256) migrate_meta_kernel(MigArgs A) {
     A.size[dl] = ssz;
     if (l == 0) {
       A.ctx_pages[dr] = A.p_ctx_pages[sr];
+      A.ctx_pages[A.R + dr] = A.p_ctx_pages[A.R + sr];  // tokens of the partial last page
       A.req_base[dr] = A.p_req_base[sr];  // the request keeps its home in the host pool
     }
   }

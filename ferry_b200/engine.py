@@ -69,6 +69,8 @@ class Decoder:
         if select_mode != _abi.SELECT_MEAN:
             call("ferry_select_mode", h, select_mode)
         self.select_mode = select_mode
+        if w.append:
+            call("ferry_decode_appends", h, w.append)  # every fused step grows its requests' contexts
         self.pool: PinnedPool | None = None
         LH, k = w.lanes_per_req, w.top_k
         n = w.num_requests * LH
@@ -106,6 +108,12 @@ class Decoder:
         request's first unit in the host pool; default slot * L * Hkv * N."""
         call("ferry_requests_begin", self.ctx, _stream(stream), _ptr(req_ids), _ptr(n_pages),
              _ptr(pool_base), int(req_ids.numel()))
+
+    def append(self, req_ids: torch.Tensor, tokens: int | None = None, stream=None):
+        """Grow the requests' contexts by `tokens` tokens (default: the
+        workload's per-step append); pages that become full turn selectable."""
+        call("ferry_requests_append", self.ctx, _stream(stream), _ptr(req_ids), int(req_ids.numel()),
+             self.w.append if tokens is None else tokens)
 
     # ------------------------------------------------------------------ steps
     def select(self, q: torch.Tensor, req_ids: torch.Tensor, stream=None):
@@ -207,7 +215,7 @@ def run_miss_workload(dec: Decoder, ticks: int | None = None, stream=None) -> Wo
     qs = torch.from_numpy(np.stack([q_stream(w, r) for r in range(w.num_requests)])).to(dec.dev)
     out = torch.empty((w.num_requests, w.num_layers, w.q_heads, w.head_dim), dtype=torch.float32,
                       device=dec.dev)
-    n_pages = torch.full((w.num_requests,), w.max_pages, dtype=torch.int32, device=dec.dev)
+    n_pages = torch.full((w.num_requests,), w.init_pages, dtype=torch.int32, device=dec.dev)
     st = torch.cuda.current_stream(dec.dev) if stream is None else stream
     dec.stats(reset=True)
     evs = []

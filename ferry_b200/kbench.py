@@ -50,7 +50,7 @@ def migrate_bench(w, iters: int) -> dict:
             dec.register_pool()
             dd = torch.device("cuda", d)
             ids = torch.arange(R, dtype=torch.int32, device=dd)
-            dec.begin(ids, torch.full((R,), w.max_pages, dtype=torch.int32, device=dd))
+            dec.begin(ids, torch.full((R,), w.init_pages, dtype=torch.int32, device=dd))
         sd = torch.device("cuda", src_dev)
         ids = torch.arange(R, dtype=torch.int32, device=sd)
         out = torch.empty((R, w.num_layers, w.q_heads, 128), dtype=torch.float32, device=sd)
@@ -157,7 +157,7 @@ def main():
         dec.gather_source(_abi.SRC_OWNER)
     R = w.num_requests
     ids = torch.arange(R, dtype=torch.int32, device=dev)
-    dec.begin(ids, torch.full((R,), w.max_pages, dtype=torch.int32, device=dev))
+    dec.begin(ids, torch.full((R,), w.init_pages, dtype=torch.int32, device=dev))
     qs = [torch.from_numpy(np.stack([q_stream(w, r, steps=s + 1)[s] for r in range(R)])).to(dev)
           for s in range(4)]
     out = torch.empty((R, w.num_layers, w.q_heads, 128), dtype=torch.float32, device=dev)

@@ -36,6 +36,7 @@ class Workload:
     head_dim: int = 128
     page_tokens: int = 16
     kv_dtype: str = "f16"  # "f16" or "e4m3" (per-page fp32 scales)
+    append: int = 0  # tokens each decode step adds to its request's context (0: fixed contexts)
 
     @property
     def unit_bytes(self) -> int:
@@ -43,12 +44,20 @@ class Workload:
         return 8192 if self.kv_dtype == "f16" else 4112
 
     @property
-    def max_pages(self) -> int:
+    def init_pages(self) -> int:
+        """Whole pages of a request's context when it starts."""
         return self.ctx_tokens // self.page_tokens
 
     @property
+    def max_pages(self) -> int:
+        """Page-table size per lane: the starting context plus every page the
+        decode steps append."""
+        grow = (self.steps * self.append + self.page_tokens - 1) // self.page_tokens
+        return min(16384, self.init_pages + grow)
+
+    @property
     def cache_pages(self) -> int:
-        return max(self.top_k, int(round(self.cache_frac * self.max_pages)))
+        return max(self.top_k, int(round(self.cache_frac * self.init_pages)))
 
     @property
     def lanes_per_req(self) -> int:
@@ -104,17 +113,20 @@ CFG5S_F16 = Workload(name="cfg5s_f16", num_requests=16, num_layers=2, q_heads=64
 # configs[2] (steady balanced multi-GPU) cut to one of its 32 layers: 256
 # requests with contexts uniform in 8k-32k tokens (ragged, <= 2048 pages),
 # round-robin homes, Poisson 400 req/s box-wide, top-128, the cache at 30% of
-# the mean context (384 of its 1280 pages per lane), 1024 decode steps.
+# the mean context (384 of its 1280 pages per lane), 1024 decode steps, each
+# appending its token to the context.
 CFG3S = Workload(name="cfg3s", num_requests=256, num_layers=1, q_heads=32, kv_heads=32,
-                 ctx_tokens=32768, top_k=128, cache_frac=0.3 * 20480 / 32768, steps=1024, arrival_rate=400.0)
+                 ctx_tokens=32768, top_k=128, cache_frac=0.3 * 20480 / 32768, steps=1024, arrival_rate=400.0,
+                 append=1)
 
 # configs[3] (skewed bursty) cut to one layer: contexts uniform in 16k-64k
 # tokens (<= 4096 pages), top-256, the cache at 30% of the mean context (768
 # of 2560 pages), Zipf(1.5) homes, ON/OFF arrivals (exponential ON periods of
 # mean 200 ms at 2000 req/s, exponential OFF periods of mean 800 ms); decode
-# steps as the config-2 model's (512).
+# steps as the config-2 model's (512), each appending its token.
 CFG4S = Workload(name="cfg4s", num_requests=256, num_layers=1, q_heads=32, kv_heads=32,
-                 ctx_tokens=65536, top_k=256, cache_frac=0.3 * 40960 / 65536, steps=512, arrival_rate=2000.0)
+                 ctx_tokens=65536, top_k=256, cache_frac=0.3 * 40960 / 65536, steps=512, arrival_rate=2000.0,
+                 append=1)
 
 CONTEXT_RANGE = {"cfg3s": (8192, 32768), "cfg4s": (16384, 65536)}
 
@@ -135,6 +147,12 @@ def arrival_ticks(w: Workload) -> np.ndarray:
     gaps = rng.exponential(1000.0 / w.arrival_rate, size=w.num_requests)
     t_ms = np.cumsum(gaps)
     return np.ceil(t_ms / w.tick_ms).astype(np.int64)
+
+
+def pages_after(init_pages, steps_done, append: int, max_pages: int, page_tokens: int = 16):
+    """Whole pages of a context that started at init_pages whole pages after
+    steps_done decode steps of `append` tokens each (capped at max_pages)."""
+    return np.minimum(max_pages, np.asarray(init_pages) + (np.asarray(steps_done) * append) // page_tokens)
 
 
 def ragged_pages(n: int, lo_tokens: int, hi_tokens: int, seed: int) -> np.ndarray:

@@ -124,6 +124,21 @@ int ferry_page_summary_update(ferry_ctx* ctx, void* stream, int64_t unit0, int64
 int ferry_requests_begin(ferry_ctx* ctx, void* stream, const int32_t* d_req_ids,
                          const int32_t* d_n_pages, const int64_t* d_pool_base, int n);
 
+/* Decode appends: each decode step adds tokens to its request's context (the
+ * reference's history grows every step, src/workloads/missstream.cuh:119). A
+ * request's context is whole pages plus the tokens of a partial last page;
+ * a page becomes selectable when its 16th token arrives -- the reference's
+ * selector scores whole pages only (tools/capture_miss_trace.py:131-133) --
+ * and its summary (mean row, or Quest bounds) is then computed from the pool
+ * unit that holds it, which the caller must have written. A context that
+ * reaches max_pages stops growing. ferry_requests_append grows the listed
+ * (distinct) requests by `tokens` tokens, asynchronously on `stream`;
+ * ferry_decode_appends(ctx, t) makes every ferry_decode_step append t tokens
+ * to each request it decodes, after its attention (0, the default: fixed
+ * contexts). ferry_requests_begin starts a context at whole pages. */
+int ferry_requests_append(ferry_ctx* ctx, void* stream, const int32_t* d_req_ids, int n, int tokens);
+int ferry_decode_appends(ferry_ctx* ctx, int tokens_per_step);
+
 /* ---- the four hot-path steps --------------------------------------------- */
 
 /* Selection rule of the ctx (set before ferry_kv_register; FERRY_E_STATE after).
@@ -233,7 +248,7 @@ int ferry_wait_flag(ferry_ctx* ctx, void* stream, const uint32_t* d_flag, uint32
 
 /* Copy ctx device state to host for checking (synchronous).
  * which: 0 cache bytes, 1 page_slot, 2 lru order, 3 lru size, 4 summaries,
- * 5 ctx pages, 6 decode-step workspace (sel | item_slot | miss_page |
+ * 5 ctx pages (R full-page counts, then R partial-page token counts), 6 decode-step workspace (sel | item_slot | miss_page |
  * miss_slot | n_sel | n_miss, each sized for num_requests), 7 request pool
  * bases (int64). */
 int ferry_debug_read(ferry_ctx* ctx, int which, size_t offset, size_t bytes, void* host_dst);

@@ -94,7 +94,7 @@ def lib():
         L.orc_pipe_destroy.argtypes = [C.c_void_p]
         L.orc_pipe_step.restype = C.c_int64
         L.orc_pipe_step.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
-                                    C.c_float, C.c_void_p]
+                                    C.c_float, C.c_void_p, C.c_void_p]
         _LIB = L
     return _LIB
 
@@ -380,12 +380,16 @@ class CpuPipeline:
             lib().orc_pipe_destroy(self.h)
             self.h = None
 
-    def step(self, lane_ids, q_f16bits, reset=None, scale=128 ** -0.5):
+    def step(self, lane_ids, q_f16bits, reset=None, scale=128 ** -0.5, n_pages=None):
+        """One step of the lanes; n_pages (per lane, optional): whole pages of
+        each lane's context (default: all N)."""
         lane_ids = np.ascontiguousarray(lane_ids, np.int32)
         n = len(lane_ids)
         reset = np.zeros(n, np.uint8) if reset is None else np.ascontiguousarray(reset, np.uint8)
         q = _f16bits(q_f16bits)
         out = np.zeros((n, self.G, 128), np.float32)
+        npg = None if n_pages is None else np.ascontiguousarray(n_pages, np.int32)
         misses = lib().orc_pipe_step(self.h, n, lane_ids.ctypes.data, reset.ctypes.data,
-                                     q.ctypes.data, C.c_float(scale), out.ctypes.data)
+                                     q.ctypes.data, C.c_float(scale), out.ctypes.data,
+                                     None if npg is None else npg.ctypes.data)
         return out, int(misses)

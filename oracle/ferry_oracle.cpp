@@ -523,7 +523,7 @@ void orc_pipe_destroy(void* h) {
 // One decode step for n_active lanes: q is n_active x G x 128 fp16.
 // Returns miss count; out is n_active x G x 128.
 int64_t orc_pipe_step(void* h, int n_active, const int32_t* lane_ids, const uint8_t* reset,
-                      const uint16_t* q, float scale, float* out) {
+                      const uint16_t* q, float scale, float* out, const int32_t* n_pages) {
   auto* p = (OrcPipe*)h;
   std::atomic<int> next{0};
   std::atomic<int64_t> misses{0};
@@ -539,7 +539,8 @@ int64_t orc_pipe_step(void* h, int n_active, const int32_t* lane_ids, const uint
       const int lane = lane_ids[a];
       const uint16_t* qa = q + (size_t)a * G * kHeadDim;
       for (int j = 0; j < G * kHeadDim; ++j) qf[j] = h2f(qa[j]);
-      for (int pg = 0; pg < p->N; ++pg) {
+      const int np = n_pages ? std::max(0, std::min(p->N, n_pages[a])) : p->N;  // whole pages of the context
+      for (int pg = 0; pg < np; ++pg) {
         const float* s = p->summ + ((size_t)lane * p->N + pg) * kHeadDim;
         float best = score_dot(&qf[0], s);
         for (int g = 1; g < G; ++g) {
@@ -548,8 +549,8 @@ int64_t orc_pipe_step(void* h, int n_active, const int32_t* lane_ids, const uint
       }
         keys[pg] = {order_key(best), pg};
       }
-      const int kk = std::min(k, p->N);
-      std::partial_sort(keys.begin(), keys.begin() + kk, keys.end(),
+      const int kk = std::min(k, np);
+      std::partial_sort(keys.begin(), keys.begin() + kk, keys.begin() + np,
                         [](const auto& x, const auto& y) {
                           return x.first != y.first ? x.first > y.first : x.second < y.second;
                         });

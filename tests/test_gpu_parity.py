@@ -460,3 +460,40 @@ def test_empty_batch_and_bad_batch(torch_cuda):
         h.dec.check()
     finally:
         h.close()
+
+
+def test_lru_kernel_replays_prefix_group_lanes(torch_cuda):
+    """Prefix-group-shared LRU (the reference's kv_touch keyed by (GPU, prefix
+    group, layer), wla_multigpu.cuh:1937-1962, and its statistics replay
+    wla_recompute_stats, :376-417): every member of a group of 4 touches the
+    group's lane, members in request order, the first 8 steps of each member
+    being its group head's (wla_apply_prefix_sharing, :355-369). The device
+    LRU on group lanes reproduces the oracle's totals and the reference's
+    published hit rate 0.921 and 731.31 MB (results/wla_pathdep_20261018/
+    base_s42.log:12,14)."""
+    import oracle
+    from ferry_b200 import _abi
+
+    sp = oracle.miss_spec(prefix_group=4, prefix_steps=8)
+    R, L_, S, G, hot, pg = sp.num_requests, sp.num_layers, sp.steps, sp.sel_blocks, sp.hot_blocks, 4
+    blocks, _, _ = oracle.replay_miss_stream(sp)
+    shared, tot = oracle.prefix_share_stats(sp, blocks)
+    B = shared.reshape(R, S, L_, G).astype(np.int32)
+    ngrp, ids = R // pg, 64 + 8 * S
+    h = C.c_void_p()
+    _abi.call("ferry_lru_create", 0, ngrp * L_, hot, ids, C.byref(h))
+    try:
+        lanes = (np.arange(ngrp)[:, None] * L_ + np.arange(L_)[None]).ravel().astype(np.int32)
+        misses = 0
+        for m in range(pg):  # members in request order; a member runs all its steps
+            for s in range(S):
+                sel = B[np.arange(ngrp) * pg + m, s].reshape(ngrp * L_, G)
+                _, _, _, _, nm = _lru_touch(torch_cuda, h, lanes, sel)
+                misses += int(nm.sum())
+        assert misses == int(tot[1])
+        selects = R * S * L_ * G
+        c4 = 4 * 2 * sp.kv_heads * sp.head_dim * 2
+        assert round(1.0 - misses / selects, 3) == 0.921
+        assert round(misses * c4 / 1048576.0, 2) == 731.31
+    finally:
+        _abi.call("ferry_lru_destroy", h)

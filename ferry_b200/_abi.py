@@ -34,7 +34,7 @@ EXPORTS = [
     "ferry_deque_pop", "ferry_deque_steal", "ferry_deque_size", "ferry_deque_peek", "ferry_deque_export",
     "ferry_deque_import", "ferry_deque_peer_view", "ferry_deque_stress",
     "ferry_exec_create", "ferry_exec_destroy", "ferry_exec_link_peer", "ferry_exec_admit",
-    "ferry_exec_set_global", "ferry_exec_owned", "ferry_exec_tick", "ferry_exec_output", "ferry_exec_policy",
+    "ferry_exec_set_global", "ferry_exec_owned", "ferry_exec_tick", "ferry_exec_output", "ferry_exec_log", "ferry_exec_policy",
     "ferry_exec_usage", "ferry_exec_rebalance",
     "ferry_steal_filter",
     "ferry_comm_unique_id", "ferry_comm_create", "ferry_comm_destroy", "ferry_comm_abort",
@@ -138,6 +138,7 @@ _SIGS = {
     "ferry_exec_owned": (I, [V, V, I, C.POINTER(I)]),
     "ferry_exec_tick": (I, [V, V, C.POINTER(TickStats)]),
     "ferry_exec_output": (I, [V, V, V, V, I, V]),
+    "ferry_exec_log": (I, [V, C.c_char_p]),
     "ferry_exec_policy": (I, [V, C.POINTER(StealPolicy)]),
     "ferry_exec_usage": (I, [V, C.POINTER(C.c_int64), C.POINTER(C.c_int32)]),
     "ferry_exec_rebalance": (I, [V, I, I]),

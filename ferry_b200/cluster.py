@@ -224,7 +224,7 @@ class RankRunner:
                  slots: int, max_batch: int, steal_batch: int = 4,
                  migrate_mode: int = _abi.MIGRATE_DELTA, pool_units: int | None = None,
                  policy: "_abi.StealPolicy | None" = None, host_q: bool = False,
-                 q_steps: int | None = None):
+                 q_steps: int | None = None, log_path: str | None = None):
         import torch
         import torch.distributed as dist
 
@@ -262,6 +262,8 @@ class RankRunner:
         call("ferry_exec_create", self.dec.ctx, self.deque, C.byref(cfg), q_ptr, C.byref(self.exec))
         if policy is not None:
             call("ferry_exec_policy", self.exec, C.byref(policy))
+        if log_path is not None:  # one record per steal (ferry_b200.decisions reads it)
+            call("ferry_exec_log", self.exec, log_path.encode())
         self.slots = slots
         self.peer_deques = []
         self.comm = None

@@ -19,6 +19,8 @@
 //   5. push (request, slot, step + 1) back, or free the slot when done.
 // Everything on the data path runs on the GPU; the host only moves task ids.
 #include <chrono>
+#include <cstdio>
+#include <cstring>
 #include <vector>
 
 #include "common.cuh"
@@ -102,8 +104,15 @@ struct ferry_exec {
   uint64_t mig_bytes_seen = 0;
   // steal policy (ferry_exec_policy)
   ferry_steal_policy pol{0, 2.0, 3.0, 700.0, 0.06};
+  int64_t pending_fair = 0, pending_occ = 0, pending_vsize = 0;
+  int pending_victim = -1, pending_forced = 0, pending_planned = 0;
   double step_ms_ema = 2.0;
   int last_n = 0;  // tasks decoded in the last tick (their outputs are in d_out)
+  // decision log (ferry_exec_log): one record per steal, written at the tick's end
+  FILE* log = nullptr;
+  int64_t ticks = 0;
+  std::vector<uint8_t> rec;        // the pending record of this tick
+  std::vector<int32_t> h_res;      // resident units of the stolen requests' lanes
   int32_t* h_live = nullptr;  // steal_batch * lanes_per_req resident-page counts of candidates
 };
 
@@ -131,6 +140,7 @@ void free_exec(ferry_exec* x) {
   cudaFreeHost(x->h_begin); cudaFreeHost(x->h_base); cudaFreeHost(x->h_live);
   for (cudaEvent_t e : {x->ev0, x->ev1, x->ev2, x->ev3})
     if (e) cudaEventDestroy(e);
+  if (x->log) std::fclose(x->log);
   delete x;
 }
 
@@ -172,6 +182,55 @@ int admit_pending(ferry_exec* x, cudaStream_t st) {
   return ferry_deque_push(x->own, st, x->d_admit, n, x->d_cnt + 3);
 }
 
+}  // namespace
+
+// ---- decision log (ferry_exec_log): the B200 counterpart of the reference's
+// FERRY_WLA_SNAPSHOT decision records (src/runtime/wla_multigpu.cuh:667-788)
+// read by its offline counterfactual tool (src/tools/wla_counterfact.cpp).
+// Little-endian binary: a 64-byte header
+//   "FRYD" u32 version=1 | i32 rank, world, R, L, Hkv, N, C, k, unit_bytes,
+//   steps_per_req, migrate_mode, steal_batch, max_batch, cost_filter
+// then one record per steal:
+//   i64 tick | i32 victim, forced | i64 fair, own_occupancy, victim_size |
+//   i32 planned, got | f64 step_ms_ema | f32 mig_ms, pad | i64 mig_bytes |
+//   got x { i32 request, step, victim_slot, thief_slot | i64 resident_units }
+namespace {
+template <class T>
+void put(std::vector<uint8_t>& b, T v) {
+  const size_t o = b.size();
+  b.resize(o + sizeof(T));
+  std::memcpy(b.data() + o, &v, sizeof(T));
+}
+
+void write_decision(ferry_exec* x, const ferry_tick_stats& ts, int n) {
+  auto& b = x->rec;
+  b.clear();
+  const int got = ts.stolen, S = x->cfg.steal_batch, LH = x->ctx->lanes_per_req;
+  put<int64_t>(b, x->ticks);
+  put<int32_t>(b, x->pending_victim);
+  put<int32_t>(b, x->pending_forced);
+  put<int64_t>(b, x->pending_fair);
+  put<int64_t>(b, x->pending_occ);
+  put<int64_t>(b, x->pending_vsize);
+  put<int32_t>(b, x->pending_planned);
+  put<int32_t>(b, got);
+  put<double>(b, x->step_ms_ema);
+  put<float>(b, ts.mig_ms);
+  put<float>(b, 0.f);
+  put<int64_t>(b, ts.mig_bytes);
+  // the stolen tasks are the last `got` of the tick's batch (h_tasks, repacked with the thief slot)
+  for (int i = 0; i < got; ++i) {
+    const uint64_t t = x->h_tasks[n - got + i];
+    int64_t units = 0;
+    for (int l = 0; l < LH; ++l) units += std::max(0, x->h_res[(size_t)i * LH + l]);
+    put<int32_t>(b, task_req(t));
+    put<int32_t>(b, task_step(t));
+    put<int32_t>(b, x->h_mig[i]);
+    put<int32_t>(b, x->h_mig[S + i]);
+    put<int64_t>(b, units);
+  }
+  std::fwrite(b.data(), 1, b.size(), x->log);
+}
 }  // namespace
 
 extern "C" {
@@ -343,6 +402,12 @@ int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out) {
                               : std::min<int64_t>(x->cfg.steal_batch, std::min<int64_t>(cur - fair, cur / 2 + 1));
         take = std::min<int64_t>(take, B - n);
         take = std::min<int64_t>(take, (int64_t)x->free_slots.size());
+        x->pending_fair = fair;
+        x->pending_occ = occ;
+        x->pending_vsize = cur;
+        x->pending_victim = victim;
+        x->pending_forced = forced ? 1 : 0;
+        x->pending_planned = (int)take;
         const ferry_peer& vp = x->ctx->peers[x->peer_slot[victim]];
         if (take > 0 && !forced && x->pol.cost_filter && vp.size) {
           // price the tasks the steal would take: remaining steps x step time
@@ -387,6 +452,12 @@ int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out) {
             x->h_mig[i] = task_slot(t);
             x->h_mig[S + i] = s;
             x->h_tasks[n + i] = task_pack((uint64_t)task_req(t), (uint64_t)s, (uint64_t)task_step(t));
+          }
+          if (got && x->log) {  // resident pages of the stolen requests' lanes, before they move
+            const int LH = x->ctx->lanes_per_req;
+            for (int i = 0; i < got; ++i)
+              FERRY_TRY(cudaMemcpyAsync(x->h_res.data() + (size_t)i * LH, vp.size + (size_t)x->h_mig[i] * LH,
+                                        (size_t)LH * 4, cudaMemcpyDeviceToHost, st));
           }
           if (got) {
             FERRY_TRY(cudaMemcpyAsync(x->d_mig, x->h_mig, (size_t)2 * S * 4, cudaMemcpyHostToDevice, st));
@@ -447,12 +518,38 @@ int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out) {
     x->mig_bytes_seen = st4[3];
   }
   x->finished += ts.finished;
+  if (x->log && ts.stolen > 0) write_decision(x, ts, n);
+  ++x->ticks;
   if (n > 0) x->step_ms_ema = 0.9 * x->step_ms_ema + 0.1 * ms;  // one step of every decoded request
   ts.decoded = n;
   x->last_n = n;
   ts.tick_ms = ms;
   ts.queued = np;
   *out = ts;
+  return FERRY_OK;
+}
+
+int ferry_exec_log(ferry_exec* x, const char* path) {
+  if (!x) return set_error("exec_log: NULL executor"), FERRY_E_INVAL;
+  if (x->log) {
+    std::fclose(x->log);
+    x->log = nullptr;
+  }
+  if (!path) return FERRY_OK;
+  FILE* f = std::fopen(path, "wb");
+  if (!f) return set_error("exec_log: cannot open %s", path), FERRY_E_INVAL;
+  const ferry_cfg& c = x->ctx->cfg;
+  std::vector<uint8_t> h;
+  const char magic[4] = {'F', 'R', 'Y', 'D'};
+  h.insert(h.end(), magic, magic + 4);
+  put<uint32_t>(h, 1u);
+  for (int v : {x->cfg.rank, x->cfg.world, c.num_requests, c.num_layers, c.kv_heads, c.max_pages, c.cache_pages,
+                c.top_k, x->ctx->unit_bytes, x->cfg.steps_per_req, x->cfg.migrate_mode, x->cfg.steal_batch,
+                x->cfg.max_batch, x->pol.cost_filter})
+    put<int32_t>(h, v);
+  std::fwrite(h.data(), 1, h.size(), f);
+  x->log = f;
+  x->h_res.assign((size_t)std::max(1, x->cfg.steal_batch) * x->ctx->lanes_per_req, 0);
   return FERRY_OK;
 }
 

@@ -409,6 +409,16 @@ int ferry_exec_set_global(ferry_exec* x, int64_t global_pending);
 /* Global ids of the requests this GPU holds (the ownership table row). */
 int ferry_exec_owned(ferry_exec* x, int32_t* h_out, int cap, int* n);
 int ferry_exec_tick(ferry_exec* x, void* stream, ferry_tick_stats* out);
+/* Decision log: open (path) or close (NULL) a binary file receiving one
+ * record per steal this executor makes -- the tick, the water level seen
+ * (fair share, own and victim queue sizes), planned and taken tasks, the
+ * migration's bytes and device time, and per stolen request its step, slots
+ * and resident page units (what delta migration moves). The counterpart of the
+ * reference's FERRY_WLA_SNAPSHOT decision records (src/runtime/
+ * wla_multigpu.cuh:667-788) for its offline counterfactual tool
+ * (src/tools/wla_counterfact.cpp); ferry_b200/decisions.py reads the log and
+ * prices the alternatives. Layout in executor.cu. */
+int ferry_exec_log(ferry_exec* x, const char* path);
 /* The attention output of the last tick: row i ([L][Hq][128] fp32) belongs to
  * the i-th task decoded in that tick, host_req[i] (nullable) its global
  * request. Copies min(decoded, cap_rows) rows device -> host_out on `stream`

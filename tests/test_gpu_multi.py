@@ -349,7 +349,7 @@ def test_migrate_over_cuda_ipc(torch_cuda):
 # --------------------------------------------------------------------------- executor
 
 
-def _cluster_worker(rank, world, port, devices, out, policy=None, llx=None, nccl_exchange=False):
+def _cluster_worker(rank, world, port, devices, out, policy=None, llx=None, nccl_exchange=False, log_dir=None):
     import os
 
     import torch
@@ -371,14 +371,16 @@ def _cluster_worker(rank, world, port, devices, out, policy=None, llx=None, nccl
     # take the oldest tasks, which may not have run yet: DELTA could move 0)
     pol = None if policy is None else _abi.StealPolicy(cost_filter=1, margin=policy, cost_scale=3.0,
                                                         link_gbs=700.0, fixed_ms=0.06)
+    log = None if log_dir is None else os.path.join(log_dir, f"rank{rank}.log")
     runner = RankRunner(w, total, world, rank, devices[rank], slots=total + 4, max_batch=4,
-                        steal_batch=4, migrate_mode=_abi.MIGRATE_FULL, policy=pol)
+                        steal_batch=4, migrate_mode=_abi.MIGRATE_FULL, policy=pol, log_path=log)
     try:
         stats = runner.run(home, join, epoch=2, max_ticks=400, llx=llx,
                            exchange_device=devices[rank] if nccl_exchange else None)
     finally:
         runner.close()
-    out.put((rank, stats.tokens, stats.stolen_tasks, stats.migrated_units, stats.ticks, stats.rebalances))
+    out.put((rank, stats.tokens, stats.stolen_tasks, stats.migrated_units, stats.ticks, stats.rebalances,
+             stats.migrated_bytes))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -409,7 +411,7 @@ def test_executor_two_ranks_steal_and_migrate(torch_cuda, policy):
             p.join(timeout=120)
             if p.is_alive():
                 p.kill()
-    (r0, tok0, st0, mig0, ticks0, _), (r1, tok1, st1, mig1, ticks1, _) = res
+    (r0, tok0, st0, mig0, ticks0, _, _), (r1, tok1, st1, mig1, ticks1, _, _) = res
     assert tok0 + tok1 == 12 * 6
     if policy is not None and policy > 1e9:
         assert st0 == st1 == 0 and tok1 == 0 and mig1 == 0   # every candidate priced out
@@ -447,7 +449,7 @@ def test_executor_ownership_over_nccl_comm(torch_cuda):
             p.join(timeout=120)
             if p.is_alive():
                 p.kill()
-    (_, tok0, st0, _, ticks0, _), (_, tok1, st1, _, ticks1, _) = res
+    (_, tok0, st0, _, ticks0, _, _), (_, tok1, st1, _, ticks1, _, _) = res
     assert tok0 + tok1 == 12 * 6 and st1 > 0 and tok1 > 0
     assert ticks0 == ticks1
 
@@ -476,6 +478,54 @@ def test_executor_rebalance_orders_move_work(torch_cuda):
             p.join(timeout=120)
             if p.is_alive():
                 p.kill()
-    (r0, tok0, st0, mig0, ticks0, rb0), (r1, tok1, st1, mig1, ticks1, rb1) = res
+    (r0, tok0, st0, mig0, ticks0, rb0, _), (r1, tok1, st1, mig1, ticks1, rb1, _) = res
     assert tok0 + tok1 == 12 * 6
     assert rb1 > 0 and st1 > 0 and tok1 > 0 and rb0 == 0
+
+
+def test_executor_decision_log(torch_cuda, tmp_path):
+    """Both ranks log their steals (ferry_exec_log): the records add up to the
+    runner's stolen tasks and migrated bytes, every stolen request appears
+    with its step and slots, and ferry_b200.decisions prices each one under
+    a0 / delta / full / drop (full = the mode the job ran: its priced bytes
+    equal the measured ones)."""
+    import socket
+
+    from ferry_b200 import decisions
+
+    t = torch_cuda
+    devices = [0, 1] if t.cuda.device_count() > 1 else [0, 0]
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_cluster_worker, args=(r, 2, port, devices, q, None, None, False, str(tmp_path)))
+          for r in range(2)]
+    for p in ps:
+        p.start()
+    try:
+        res = sorted(q.get(timeout=300) for _ in ps)
+    finally:
+        for p in ps:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    w = _workload()
+    for rank, _, stolen, _, _, _, mig_bytes in res:
+        hdr, ds = decisions.read_log(str(tmp_path / f"rank{rank}.log"))
+        assert hdr["rank"] == rank and hdr["world"] == 2 and hdr["migrate_mode"] == 0
+        assert sum(d.taken for d in ds) == stolen
+        assert sum(d.mig_bytes for d in ds) == mig_bytes
+        for d in ds:
+            assert d.victim == 1 - rank and 0 < d.taken <= d.planned and len(d.tasks) == d.taken
+            for task in d.tasks:
+                assert 0 <= task.request < 12 and 0 <= task.step < 6
+                assert 0 <= task.resident_units <= w.lanes_per_req * w.cache_pages
+            rows = decisions.price(hdr, d, 700.0, 50.0)
+            full = sum(r[2] for r in rows if r[0] == "full")
+            assert full == d.mig_bytes  # FULL moves every slot of every lane
+    assert res[1][2] > 0  # the idle rank stole
+    csv = decisions.counterfactuals([str(tmp_path / "rank1.log")], 700.0, 50.0)
+    assert len(csv) == 1 + 4 * res[1][2]

@@ -306,27 +306,32 @@ def run_ferry(args, w):
     st = torch.cuda.current_stream(dev)
 
     def tick_run(tk, evs=None):
+        e = None
+        if evs is not None:
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+            e[0].record(st)  # the step on the device starts here (request starts included)
         if tk["new"] is not None:
             dec.begin(tk["new"], n_pages[: len(tk["new"])], stream=st)
         if tk["qd"] is None:
+            if e is not None:
+                evs.append((e, 0, False))
             return 0
         n = len(tk["active"])
         if evs is None:
             dec.step(tk["qd"], tk["ids"], out[:n], stream=st)
             return n
-        e = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
-        e[0].record(st)
-        dec.select(tk["qd"], tk["ids"], stream=st)
         e[1].record(st)
-        dec.detect(tk["ids"], stream=st)
+        dec.select(tk["qd"], tk["ids"], stream=st)
         e[2].record(st)
-        dec.gather(tk["ids"], stream=st)
+        dec.detect(tk["ids"], stream=st)
         e[3].record(st)
+        dec.gather(tk["ids"], stream=st)
+        e[4].record(st)
         dec.attention(tk["qd"], tk["ids"], out[:n], stream=st)
         if w.append:  # the decoded token joins the context (the fused step does this itself)
             dec.append(tk["ids"], stream=st)
-        e[4].record(st)
-        evs.append((e, n))
+        e[5].record(st)
+        evs.append((e, n, True))
         return n
 
     # ---------------------------------------------------------------- device-timed value
@@ -350,13 +355,14 @@ def run_ferry(args, w):
     elapsed_ms = t0.elapsed_time(t1)
     dec.check()
     units, gbytes = dec.stats(reset=True)
-    launches = len(evs) * 4 + sum(1 for i in range(args.warmup, n_ticks) if ticks[i]["new"] is not None)
+    full = [(e, n) for e, n, ok in evs if ok]
+    launches = len(full) * (4 + (2 if w.append else 0)) + sum(
+        1 for i in range(args.warmup, n_ticks) if ticks[i]["new"] is not None)
     k_ms = np.zeros(4)
-    step_ms = []
-    for e, n in evs:
-        d = [e[j].elapsed_time(e[j + 1]) for j in range(4)]
-        k_ms += d
-        step_ms.append(sum(d))
+    step_ms = []  # each tick's device time, first to last event (request starts included)
+    for e, n in full:
+        k_ms += [e[j].elapsed_time(e[j + 1]) for j in range(1, 5)]
+        step_ms.append(e[0].elapsed_time(e[5]))
     if ws > 1:
         t = torch.tensor([elapsed_ms, float(tokens), float(gbytes)], dtype=torch.float64, device=dev)
         mx = t.clone()
@@ -444,7 +450,7 @@ def run_ferry(args, w):
         nl = tokens * LH  # lanes processed by this rank
         attn_bytes = tokens * w.attn_bytes_per_token() + tokens * w.qo_bytes_per_token()
         sel_bytes = tokens * w.select_bytes_per_token()
-        n_launch = len(evs)
+        n_launch = len(full)
         attn_ms = k_ms[3] / max(1, n_launch)
         achieved = (attn_bytes / max(1, n_launch)) / (attn_ms / 1e3) / 1e9
         sel_ach = (sel_bytes / max(1, n_launch)) / (k_ms[0] / max(1, n_launch) / 1e3) / 1e9

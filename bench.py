@@ -475,7 +475,13 @@ def run_ferry(args, w):
                        "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU"},
             "miss_gather": {"GB_s": gather_gbs, "bytes": gbytes_all, "units": units,
                             "link_peak_GB_s": best, "frac": gather_gbs / best if best else None,
-                            "peak_kind": "measured H2D copy from pinned host, this run"},
+                            "peak_kind": "measured H2D copy from pinned host, this run",
+                            # host-link read bytes of one launch: ncu pcie__read_bytes of a full-batch
+                            # launch over its page bytes (profiles/ncu_traffic.json), times this run's
+                            # page bytes per launch
+                            "traffic": (traffic["gather_kernel"]["traffic_over_algorithmic"] * gbytes / max(1, n_launch)
+                                        if traffic else None),
+                            "bytes_per_launch": gbytes / max(1, n_launch)},
             "roofline": {"bound": "hbm", "kernel": "attn_kernel", "achieved": achieved,
                          "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                          "peak_kind": peak_kind,
@@ -483,7 +489,7 @@ def run_ferry(args, w):
                                  "(gather_kernel, ~96% of step time: see miss_gather.frac)",
                          # ncu DRAM bytes of a full-batch launch, scaled by this
                          # run's algorithmic bytes per launch (profiles/ncu_traffic.json)
-                         "traffic": (traffic["traffic_over_algorithmic"] * attn_bytes / max(1, n_launch)
+                         "traffic": (traffic["attn_kernel"]["traffic_over_algorithmic"] * attn_bytes / max(1, n_launch)
                                      if traffic else None),
                          "bytes_per_launch": attn_bytes / max(1, n_launch)},
             "roofline_select": {"bound": "hbm", "achieved": sel_ach, "peak": hbm_peak,

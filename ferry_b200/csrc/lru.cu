@@ -48,6 +48,7 @@ struct LruArgs {
 };
 
 constexpr int kLoadBatch = 8;
+constexpr int kLruCtaMinCap = 128;  // lanes with more slots take the CTA-per-lane kernel
 constexpr int kLruRounds = 8;  // fixpoint rounds before the serial replay takes over
 
 __global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
@@ -417,6 +418,421 @@ __global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
   if (t == 0) A.n_miss[a] = nm;
 }
 
+
+// ---------------------------------------------------------------------------
+// CTA-per-lane variant for distinct selections (the decode step) on lanes of
+// more than kLruCtaMinCap slots. The warp kernel above spends its time in one
+// warp's dependent chain of chunked ballot scans (~9k instructions per lane at
+// 1229 slots / 512 selected); here the lane's four warps share every loop:
+// each chunk of 128 items is ranked by one block-ordered scan (ballot counts
+// per warp through shared memory, one barrier), so the chain is ~4x shorter.
+// Same algorithm and same results as the warp kernel's parallel path, with
+// the same serial replay (thread 0) when it gives up.
+constexpr int kLruCtaWarps = 4;
+constexpr int kLruCtaThreads = kLruCtaWarps * 32;
+
+// Exclusive ranks of two flags over one chunk (item order = thread order) and
+// the chunk totals. One barrier; the double buffer lets the next call write
+// while no thread can still be reading the same half (it passed this barrier).
+__device__ __forceinline__ void cta_scan2(bool f0, bool f1, uint32_t (*buf)[2][kLruCtaWarps], int& par, int& r0,
+                                          int& r1, int& t0, int& t1) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t m0 = __ballot_sync(0xffffffffu, f0), m1 = __ballot_sync(0xffffffffu, f1);
+  if (lane == 0) {
+    buf[par][0][warp] = __popc(m0);
+    buf[par][1][warp] = __popc(m1);
+  }
+  __syncthreads();
+  int b0 = 0, b1 = 0;
+  t0 = t1 = 0;
+#pragma unroll
+  for (int w = 0; w < kLruCtaWarps; ++w) {
+    const int c0 = (int)buf[par][0][w], c1 = (int)buf[par][1][w];
+    if (w < warp) {
+      b0 += c0;
+      b1 += c1;
+    }
+    t0 += c0;
+    t1 += c1;
+  }
+  const uint32_t lt = (1u << lane) - 1u;
+  r0 = b0 + __popc(m0 & lt);
+  r1 = b1 + __popc(m1 & lt);
+  par ^= 1;
+}
+
+// Block sum and max (one barrier each, double-buffered like cta_scan2).
+__device__ __forceinline__ int cta_sum(int v, int (*buf)[kLruCtaWarps], int& par) {
+  v = __reduce_add_sync(0xffffffffu, v);
+  if ((threadIdx.x & 31) == 0) buf[par][threadIdx.x >> 5] = v;
+  __syncthreads();
+  int s = 0;
+#pragma unroll
+  for (int w = 0; w < kLruCtaWarps; ++w) s += buf[par][w];
+  par ^= 1;
+  return s;
+}
+__device__ __forceinline__ int cta_max(int v, int (*buf)[kLruCtaWarps], int& par) {
+  v = __reduce_max_sync(0xffffffffu, v);
+  if ((threadIdx.x & 31) == 0) buf[par][threadIdx.x >> 5] = v;
+  __syncthreads();
+  int s = buf[par][0];
+#pragma unroll
+  for (int w = 1; w < kLruCtaWarps; ++w) s = max(s, buf[par][w]);
+  par ^= 1;
+  return s;
+}
+
+__global__ void __launch_bounds__(kLruCtaThreads) lru_cta_kernel(LruArgs A) {
+  extern __shared__ int32_t smem_i[];
+  __shared__ uint32_t sbuf[2][2][kLruCtaWarps];
+  __shared__ int rbuf[2][kLruCtaWarps];
+  __shared__ int s_state[5];
+  const int tid = threadIdx.x, t = tid & 31;
+  const int a = blockIdx.x;
+  if (a >= A.n) return;
+  const int C = A.cap, k = A.k;
+  int32_t* old = smem_i;
+  int32_t* spg = old + C;
+  int32_t* seq = spg + C;
+  int32_t* sel_s = seq + C;
+  int32_t* islot = sel_s + k;
+  int32_t* prev = islot + k;
+  int32_t* newl = prev + k;
+  int32_t* evict = newl + k;
+  uint8_t* mflag = reinterpret_cast<uint8_t*>(evict + k);
+  int spar = 0, rpar = 0;
+
+  const int64_t lane = A.lane_ids ? (int64_t)A.lane_ids[a]
+                                  : (int64_t)A.req_ids[a / A.lanes_per_req] * A.lanes_per_req +
+                                        a % A.lanes_per_req;
+  const int n = A.n_sel[a];
+  if (lane < 0 || lane >= A.lanes || n < 0 || n > k) {
+    if (tid == 0) {
+      record_error(A.err, kErrRange);
+      A.n_miss[a] = 0;
+    }
+    for (int i = tid; i < k; i += kLruCtaThreads) {
+      A.item_slot[(size_t)a * k + i] = -1;
+      if (A.is_miss) A.is_miss[(size_t)a * k + i] = 0;
+    }
+    return;
+  }
+  int32_t* ps = A.page_slot + lane * A.ids;
+  int32_t* sp = A.slot_page + lane * C;
+  int32_t* od = A.order + lane * C;
+  int sz0 = A.size[lane];
+  if (sz0 < 0 || sz0 > C) {
+    if (tid == 0) record_error(A.err, kErrRange);
+    sz0 = 0;
+  }
+  const bool rst = A.reset && A.reset[a];
+
+  // the lane's tables, kLoadBatch loads per thread in flight
+  bool corrupt = false;
+  for (int j0 = tid; j0 < C; j0 += kLruCtaThreads * kLoadBatch) {
+    int vo[kLoadBatch], vs[kLoadBatch];
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int j = j0 + kLruCtaThreads * u;
+      vo[u] = j < sz0 ? __ldcg(od + j) : 0;
+      vs[u] = j < sz0 ? __ldcg(sp + j) : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int j = j0 + kLruCtaThreads * u;
+      if (j < C) {
+        if (j < sz0) {
+          if (vo[u] < 0 || vo[u] >= C) {
+            corrupt = true;
+            vo[u] = 0;
+          }
+          old[j] = vo[u];
+        }
+        spg[j] = vs[u];
+        seq[j] = -1;
+      }
+    }
+  }
+  if (__syncthreads_or(corrupt) && tid == 0) record_error(A.err, kErrRange);
+  if (rst) {
+    for (int s = tid; s < sz0; s += kLruCtaThreads) {
+      const int pg = spg[s];
+      if (pg >= 0 && pg < A.ids) ps[pg] = -1;
+      spg[s] = -1;
+    }
+    sz0 = 0;
+  }
+  __syncthreads();
+  bool bad = false;
+  for (int i0 = tid; i0 < n; i0 += kLruCtaThreads * kLoadBatch) {
+    int vx[kLoadBatch], vp[kLoadBatch];
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int i = i0 + kLruCtaThreads * u;
+      vx[u] = i < n ? __ldcg(A.sel + (size_t)a * k + i) : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int i = i0 + kLruCtaThreads * u;
+      if (i < n && (vx[u] < 0 || vx[u] >= A.ids)) {
+        bad = true;
+        vx[u] = -1;
+      }
+      vp[u] = (vx[u] >= 0 && !rst) ? __ldcg(ps + vx[u]) : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int i = i0 + kLruCtaThreads * u;
+      if (i < n) {
+        sel_s[i] = vx[u];
+        islot[i] = vp[u];
+      }
+    }
+  }
+  if (__syncthreads_or(bad) && tid == 0) record_error(A.err, kErrRange);
+
+  // ---- the parallel exact path (see lru_kernel); seq[s] = touch time of old
+  // slot s, -1 untouched, -(time + 2) in K
+  int p = 0, qn = 0, nn = 0, sz = sz0, ne = 0;
+  bool done = false;
+  int nv = 0;
+  for (int i0 = 0; i0 < n; i0 += kLruCtaThreads) {
+    const int i = i0 + tid;
+    const int x = i < n ? sel_s[i] : -1;
+    const int s = x >= 0 ? islot[i] : -1;
+    const bool valid = x >= 0, hit = valid && s >= 0 && s < C && spg[s] == x;
+    int rv, r1, tv, t1;
+    cta_scan2(valid, false, sbuf, spar, rv, r1, tv, t1);
+    if (i < n) {
+      if (!valid) islot[i] = -1;
+      if (hit) seq[s] = nv + rv;
+      mflag[i] = valid && !hit;
+    }
+    nv += tv;
+  }
+  __syncthreads();
+  const int f = max(0, C - sz0);
+  int nmiss = 0, E = 0, jlast = -1, kcount = 0;
+  bool ok = false;
+  for (int round = 0; round < kLruRounds; ++round) {
+    nmiss = 0;
+    int tvs = 0;
+    for (int i0 = 0; i0 < n; i0 += kLruCtaThreads) {
+      const int i = i0 + tid;
+      const bool valid = i < n && sel_s[i] >= 0;
+      const bool ism = valid && (mflag[i] || seq[islot[i]] <= -2);
+      int rv, rm, tv, tm;
+      cta_scan2(valid, ism, sbuf, spar, rv, rm, tv, tm);
+      if (ism) {
+        const int r = nmiss + rm;
+        prev[i] = r;
+        newl[r] = tvs + rv;
+      }
+      nmiss += tm;
+      tvs += tv;
+    }
+    __syncthreads();
+    E = max(0, nmiss - f);
+    int ucount = 0, kseen = 0, kadd = 0, kdrop = 0, jl = -1;
+    for (int j0 = 0; j0 < sz0 && ucount < E; j0 += kLruCtaThreads) {  // block-uniform
+      const int j = j0 + tid;
+      const int sl = j < sz0 ? old[j] : 0;
+      const int tt = j < sz0 ? seq[sl] : 0;
+      const bool cand = j < sz0 && (tt == -1 || tt <= -2);  // untouched or in K
+      int rc, r1, tc, t1;
+      cta_scan2(cand, false, sbuf, spar, rc, r1, tc, t1);
+      const int u = ucount + rc;  // evictions ahead of j
+      if (j < sz0 && u < E) {
+        const int me = newl[f + u];  // time of the miss making eviction u
+        if (cand) {
+          evict[u] = sl;
+          if (u == E - 1) jl = j;
+          if (tt <= -2) {
+            ++kseen;
+            if (-tt - 2 <= me) {  // touched before its eviction: a hit after all
+              seq[sl] = -tt - 2;
+              ++kdrop;
+            }
+          }
+        } else if (tt > me) {  // evicted before its touch: joins K
+          seq[sl] = -tt - 2;
+          ++kadd;
+        }
+      }
+      ucount += tc;
+    }
+    if (ucount < E) break;  // evictions would reach the touch list (block-uniform)
+    jlast = cta_max(jl, rbuf, rpar);
+    kseen = cta_sum(kseen, rbuf, rpar);
+    kadd = cta_sum(kadd, rbuf, rpar);
+    kdrop = cta_sum(kdrop, rbuf, rpar);
+    if (kseen < kcount) {  // K entries past the last eviction are not evicted
+      int d = 0;
+      for (int j = jlast + 1 + tid; j < sz0; j += kLruCtaThreads) {
+        const int sl = old[j], tt = seq[sl];
+        if (tt <= -2) {
+          seq[sl] = -tt - 2;
+          ++d;
+        }
+      }
+      kdrop += cta_sum(d, rbuf, rpar);
+    }
+    kcount += kadd - kdrop;
+    __syncthreads();
+    if (kadd == 0 && kdrop == 0) {
+      ok = true;
+      break;
+    }
+  }
+  __syncthreads();
+  if (ok) {
+    for (int i = tid; i < n; i += kLruCtaThreads)  // K pages miss at their touch
+      if (sel_s[i] >= 0 && !mflag[i] && seq[islot[i]] <= -2) mflag[i] = 1;
+    __syncthreads();
+    for (int i = tid; i < n; i += kLruCtaThreads)
+      if (mflag[i]) {
+        const int r = prev[i];
+        int sl;
+        if (r < f) {
+          sl = sz0 + r;
+        } else {
+          sl = evict[r - f];
+          evict[r - f] = spg[sl];
+        }
+        islot[i] = sl;
+      }
+    __syncthreads();
+    int nv2 = 0;
+    for (int i0 = 0; i0 < n; i0 += kLruCtaThreads) {  // touch list in selection order
+      const int i = i0 + tid;
+      const bool valid = i < n && sel_s[i] >= 0;
+      int rv, r1, tv, t1;
+      cta_scan2(valid, false, sbuf, spar, rv, r1, tv, t1);
+      if (valid) {
+        const int tr = nv2 + rv, sl = islot[i];
+        newl[tr] = sl;
+        seq[sl] = tr;
+        if (mflag[i]) spg[sl] = sel_s[i];
+      }
+      nv2 += tv;
+    }
+    p = E > 0 ? jlast + 1 : 0;
+    nn = nv;
+    sz = sz0 + min(nmiss, f);
+    ne = E;
+    done = true;
+  } else {
+    for (int i = tid; i < n; i += kLruCtaThreads)  // undo the hit marks for the serial replay
+      if (sel_s[i] >= 0 && !mflag[i]) seq[islot[i]] = -1;
+  }
+  __syncthreads();
+
+  // ---- sequential replay on shared memory (thread 0), as in lru_kernel
+  if (tid == 0 && !done) {
+    for (int i = 0; i < n; ++i) {
+      const int x = sel_s[i];
+      if (x < 0) {
+        islot[i] = -1;
+        mflag[i] = 0;
+        continue;
+      }
+      int s = islot[i];
+      const bool hit = s >= 0 && s < C && spg[s] == x;
+      if (hit) {
+        seq[s] = nn;
+        newl[nn++] = s;
+        islot[i] = s;
+        mflag[i] = 0;
+      } else {
+        if (sz >= C) {
+          while (p < sz0 && seq[old[p]] != -1) ++p;
+          if (p < sz0) {
+            s = old[p++];
+          } else {
+            while (qn < nn - 1 && seq[newl[qn]] != qn) ++qn;
+            s = newl[qn++];
+          }
+          evict[ne++] = spg[s];
+        } else {
+          s = sz++;
+        }
+        spg[s] = x;
+        seq[s] = nn;
+        newl[nn++] = s;
+        islot[i] = s;
+        mflag[i] = 1;
+      }
+    }
+  }
+  if (tid == 0) {
+    s_state[0] = p;
+    s_state[1] = qn;
+    s_state[2] = nn;
+    s_state[3] = sz;
+    s_state[4] = ne;
+  }
+  __syncthreads();
+  p = s_state[0];
+  qn = s_state[1];
+  nn = s_state[2];
+  sz = s_state[3];
+  ne = s_state[4];
+
+  // ---- new LRU order: live old entries, then live touch-list entries
+  int outp = 0;
+  for (int j0 = p; j0 < sz0; j0 += kLruCtaThreads) {
+    const int j = j0 + tid;
+    const bool live = j < sz0 && seq[old[j]] == -1;
+    int rl, r1, tl, t1;
+    cta_scan2(live, false, sbuf, spar, rl, r1, tl, t1);
+    if (live) od[outp + rl] = old[j];
+    outp += tl;
+  }
+  for (int j0 = qn; j0 < nn; j0 += kLruCtaThreads) {
+    const int j = j0 + tid;
+    const bool live = j < nn && seq[newl[j]] == j;
+    int rl, r1, tl, t1;
+    cta_scan2(live, false, sbuf, spar, rl, r1, tl, t1);
+    if (live) od[outp + rl] = newl[j];
+    outp += tl;
+  }
+  if (tid == 0) A.size[lane] = sz;
+  for (int i = tid; i < n; i += kLruCtaThreads)
+    if (mflag[i]) sp[islot[i]] = spg[islot[i]];
+  // page table: evictions first, then the final residents among the misses
+  for (int e = tid; e < ne; e += kLruCtaThreads) {
+    const int v = evict[e];
+    if (v >= 0 && v < A.ids) ps[v] = -1;
+  }
+  __syncthreads();
+  for (int i = tid; i < n; i += kLruCtaThreads)
+    if (mflag[i]) {
+      const int s = islot[i];
+      if (spg[s] == sel_s[i]) ps[sel_s[i]] = s;
+    }
+
+  // ---- outputs
+  int nm = 0;
+  for (int i0 = 0; i0 < n; i0 += kLruCtaThreads) {
+    const int i = i0 + tid;
+    const bool fl = i < n && mflag[i];
+    int rm, r1, tm, t1;
+    cta_scan2(fl, false, sbuf, spar, rm, r1, tm, t1);
+    if (fl) {
+      const int r = nm + rm;
+      A.miss_page[(size_t)a * k + r] = sel_s[i];
+      A.miss_slot[(size_t)a * k + r] = islot[i];
+    }
+    nm += tm;
+  }
+  for (int i = tid; i < k; i += kLruCtaThreads) {
+    A.item_slot[(size_t)a * k + i] = i < n ? islot[i] : -1;
+    if (A.is_miss) A.is_miss[(size_t)a * k + i] = i < n ? mflag[i] : 0;
+  }
+  if (tid == 0) A.n_miss[a] = nm;
+}
+
 // Empty every lane of the listed requests and record their context length
 // (ctx_pages holds the full pages of each request, then, R entries later, the
 // tokens of its partial last page).
@@ -498,6 +914,15 @@ int launch_lru(const ferry_lru* L, cudaStream_t st, const int32_t* lane_ids,
   // old, spg, seq (cap each) + sel, islot, prev, newl, evict (k each) + k flag bytes
   A.warp_ints = lru_lane_ints(L->cap, k);
   const size_t per_warp = (size_t)A.warp_ints * 4;
+  if (distinct && L->cap > kLruCtaMinCap && per_warp <= kLruLaneSmemMax) {
+    // a CTA per lane (decode steps on long lanes)
+    if (per_warp > 48 * 1024)
+      FERRY_TRY(cudaFuncSetAttribute(lru_cta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)per_warp));
+    lru_cta_kernel<<<(unsigned)n, kLruCtaThreads, per_warp, st>>>(A);
+    FERRY_TRY(cudaGetLastError());
+    return FERRY_OK;
+  }
   int warps = (int)std::min<size_t>(8, std::max<size_t>(1, (96 * 1024) / per_warp));
   const size_t smem = per_warp * warps;
   if (smem > kLruLaneSmemMax) {

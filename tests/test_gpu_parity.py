@@ -383,6 +383,11 @@ def test_lru_kernel_over_capacity_and_resets(torch_cuda):
     (16, 16, 60, 0.5),    # cache = k: touched pages at the LRU front, serial replay
     (24, 16, 40, 0.9),    # mixed: some steps each way
     (300, 128, 2000, 0.5),  # decode-step shape: touched pages interleave the evicted front
+    # lanes of more than 128 slots take the CTA-per-lane kernel: its parallel
+    # path, its serial replay (cache = k) and a mix
+    (400, 96, 3000, 0.7),
+    (160, 160, 400, 0.5),
+    (200, 128, 320, 0.9),
 ])
 def test_lru_distinct_selections_both_paths(torch_cuda, cap, k, ids, reuse):
     """Distinct ascending selections (the decode step's case) against the

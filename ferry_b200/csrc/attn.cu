@@ -34,16 +34,9 @@ namespace ferry {
 namespace {
 
 constexpr int kAttnWarps = 4;
-// The ring holds half pages: a page's K (4 KiB) and its V (4 KiB) are separate
-// stages, so K's stage is refilled as soon as the page's scores are done --
-// a quarter more bytes in flight per warp than whole-page stages in the same
-// 16 KiB.
-constexpr int kStages = 4;
-constexpr int kHalfBytes = kUnitBytes / 2;
+constexpr int kStages = 2;
 constexpr uint32_t kFull = 0xffffffffu;
-// per warp: the ring, its mbarriers, and p of 16 tokens + alpha for up to 8 heads
-constexpr int kPsmFloats = 8 * 16 + 8;
-constexpr size_t kAttnSmem = (size_t)kAttnWarps * (kStages * kHalfBytes + kStages * 8 + kPsmFloats * 4);
+constexpr size_t kAttnSmem = (size_t)kAttnWarps * (kStages * kUnitBytes + kStages * 8 + 64);
 
 struct AttnArgs {
   const uint16_t* q;
@@ -95,11 +88,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_kernel(AttnArgs A) {
   const int warp = threadIdx.x >> 5, t = threadIdx.x & 31;
   const int w = blockIdx.x * kAttnWarps + warp;
   if (w >= A.nw) return;
-  uint8_t* ring = smem + (size_t)warp * kStages * kHalfBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kAttnWarps * kStages * kHalfBytes) +
+  uint8_t* ring = smem + (size_t)warp * kStages * kUnitBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kAttnWarps * kStages * kUnitBytes) +
                    warp * kStages;
-  float* psm = reinterpret_cast<float*>(smem + (size_t)kAttnWarps * (kStages * kHalfBytes + kStages * 8)) +
-               warp * kPsmFloats;
+  float* psm = reinterpret_cast<float*>(smem + (size_t)kAttnWarps * (kStages * kUnitBytes + kStages * 8)) +
+               warp * 16;
   const int64_t x_lo = (int64_t)w * A.T / A.nw, x_hi = (int64_t)(w + 1) * A.T / A.nw;
   if (x_lo >= x_hi) return;
   if (t == 0) {
@@ -135,37 +128,25 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_kernel(AttnArgs A) {
   };
   lane_begin();
   uint32_t it_load = 0, it_use = 0;
-  // half-stage it_load: even = K of the next page in the warp's range, odd =
-  // V of that same page
-  bool lactive = false;
-  int lslot = 0;
   auto issue = [&]() {
-    if ((it_load & 1u) == 0) {
-      while ((int64_t)la * k < x_hi && lj >= lend) {
-        ++la;
-        if ((int64_t)la * k < x_hi) lane_begin();
-      }
-      lactive = (int64_t)la * k < x_hi;
-      if (!lactive) return;
-      if (t == 0) {
-        lslot = A.item_slot[(size_t)la * k + lj];
-        if (lslot < 0 || lslot >= A.C) {
-          record_error(A.err, kErrRange);
-          lslot = 0;
-        }
-      }
-      ++lj;
-    } else if (!lactive) {
-      return;
+    while ((int64_t)la * k < x_hi && lj >= lend) {
+      ++la;
+      if ((int64_t)la * k < x_hi) lane_begin();
     }
+    if ((int64_t)la * k >= x_hi) return;
     if (t == 0) {
+      int slot = A.item_slot[(size_t)la * k + lj];
+      if (slot < 0 || slot >= A.C) {
+        record_error(A.err, kErrRange);
+        slot = 0;
+      }
       const uint32_t s = it_load % kStages;
       fence_proxy_async_smem();
-      mbar_arrive_expect_tx(&bars[s], kHalfBytes);
-      bulk_load(ring + (size_t)s * kHalfBytes,
-                A.cache + (size_t)(lunit0 + lslot) * kUnitBytes + (it_load & 1u) * kHalfBytes, kHalfBytes,
-                &bars[s]);
+      mbar_arrive_expect_tx(&bars[s], kUnitBytes);
+      bulk_load(ring + (size_t)s * kUnitBytes, A.cache + (size_t)(lunit0 + slot) * kUnitBytes,
+                kUnitBytes, &bars[s]);
     }
+    ++lj;
     ++it_load;
   };
 #pragma unroll
@@ -192,13 +173,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_kernel(AttnArgs A) {
       ls[g] = 0.f;
     }
     for (int j = jlo; j < jhi; ++j) {
-      // K half: scores, running max, p and the rescale factor of every head
-      uint32_t s = it_use % kStages, par = (it_use / kStages) & 1u;
+      const uint32_t s = it_use % kStages, par = (it_use / kStages) & 1u;
       if (!mbar_wait(&bars[s], par, A.err)) {
         ok = false;
         break;
       }
-      const uint8_t* pk = ring + (size_t)s * kHalfBytes;
+      const uint8_t* pg = ring + (size_t)s * kUnitBytes;
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         float v[8];
@@ -206,7 +186,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_kernel(AttnArgs A) {
         for (int i = 0; i < 8; ++i) {
           const int tok = 2 * (i ^ m4) + h;
           float kf[8];
-          h8_to_f(*reinterpret_cast<const uint4*>(pk + tok * 256 + d0 * 2), kf);
+          h8_to_f(*reinterpret_cast<const uint4*>(pg + tok * 256 + d0 * 2), kf);
           float acc = qv[g][0] * kf[0];
 #pragma unroll
           for (int d = 1; d < 8; ++d) acc = fmaf(qv[g][d], kf[d], acc);
@@ -225,41 +205,26 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_kernel(AttnArgs A) {
         pm = fmaxf(pm, __shfl_xor_sync(kFull, pm, 8));
         pm = fmaxf(pm, __shfl_xor_sync(kFull, pm, 16));
         const float mn = fmaxf(mx[g], pm);
-        const float alpha = exp2f(mx[g] - mn);  // 0 on a segment's first page (warp-uniform)
+        const float alpha = exp2f(mx[g] - mn);  // 0 on a segment's first page
         const float p = exp2f(sc - mn);
         ls[g] = ls[g] * alpha + ((t & 1) ? 0.f : p);
         mx[g] = mn;
-        if (!(t & 1)) psm[g * 16 + h * 8 + m4] = p;  // slot of token 2*m4 + h
-        if (t == 0) psm[G * 16 + g] = alpha;
-      }
-      __syncwarp();  // K half consumed, p and alpha in psm
-      ++it_use;
-      issue();
-      // V half: o = o * alpha + p . V per head
-      s = it_use % kStages;
-      par = (it_use / kStages) & 1u;
-      if (!mbar_wait(&bars[s], par, A.err)) {
-        ok = false;
-        break;
-      }
-      const uint8_t* pvh = ring + (size_t)s * kHalfBytes;
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float4 pa = *reinterpret_cast<const float4*>(psm + g * 16 + h * 8);
-        const float4 pb = *reinterpret_cast<const float4*>(psm + g * 16 + h * 8 + 4);
+        if (!(t & 1)) psm[h * 8 + m4] = p;  // slot of token 2*m4 + h
+        __syncwarp();
+        const float4 pa = *reinterpret_cast<const float4*>(psm + h * 8);
+        const float4 pb = *reinterpret_cast<const float4*>(psm + h * 8 + 4);
         const float pt[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
-        const float alpha = psm[G * 16 + g];
 #pragma unroll
         for (int d = 0; d < 8; ++d) o[g][d] *= alpha;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           float vf[8];
-          h8_to_f(*reinterpret_cast<const uint4*>(pvh + (2 * i + h) * 256 + d0 * 2), vf);
+          h8_to_f(*reinterpret_cast<const uint4*>(pg + kUnitBytes / 2 + (2 * i + h) * 256 + d0 * 2), vf);
 #pragma unroll
           for (int d = 0; d < 8; ++d) o[g][d] = fmaf(pt[i], vf[d], o[g][d]);
         }
+        __syncwarp();  // psm reused by the next head / page
       }
-      __syncwarp();  // V half consumed; psm is rewritten by the next page
       ++it_use;
       issue();
     }

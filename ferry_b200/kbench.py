@@ -118,6 +118,7 @@ def main():
     ap.add_argument("--probe", action="store_true", help="topology and link peaks")
     ap.add_argument("--requests", type=int, default=0, help="override the batch (a smaller case to profile)")
     ap.add_argument("--only", default="", help="comma list of kernels to time (gather,attention,select,detect)")
+    ap.add_argument("--select", default="mean", help="selection rule: mean (the benchmark's) or quest")
     ap.add_argument("--store-world", type=int, default=0,
                     help="serve misses from page-owner stores of W ranks (rank r on GPU r mod count)")
     args = ap.parse_args()
@@ -135,7 +136,9 @@ def main():
     only = set(args.only.split(",")) if args.only else {"gather", "attention", "select", "detect"}
     torch.cuda.set_device(args.device)
     dev = torch.device("cuda", args.device)
-    dec = Decoder(w, args.device)
+    from . import _abi as _a
+
+    dec = Decoder(w, args.device, select_mode=_a.SELECT_QUEST if args.select == "quest" else _a.SELECT_MEAN)
     dec.register_pool()
     peers = []
     if args.store_world:
@@ -189,8 +192,9 @@ def main():
         res["attention"] = {"us": t, "bytes": b, "GB_s": b / t / 1e3}
     if "select" in only:
         t = _time(lambda: dec.select(q, ids), args.iters)
-        b = R * w.select_bytes_per_token()
-        res["select"] = {"us": t, "bytes": b, "GB_s": b / t / 1e3}
+        # summaries read: mean rows (512 B per page and lane) or Quest bounds (1 KiB)
+        b = R * w.select_bytes_per_token() * (2 if args.select == "quest" else 1)
+        res["select"] = {"us": t, "bytes": b, "GB_s": b / t / 1e3, "rule": args.select}
     if "detect" in only:
         # as in a decode step: each launch follows its step's selection (which
         # streams the summaries through L2) and sees that step's drift, so the

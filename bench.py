@@ -591,6 +591,65 @@ def concurrent_h2d_peak(dev, ws, nbytes=1 << 30, iters=3):
     return mine, agg
 
 
+def gather_pass(w, local, ws, rank, ticks=(6, 18)):
+    """The miss-gather kernel's own rate with every rank gathering at once: a
+    standalone decoder per rank runs ticks [0, ticks[1]) of the configs[0]
+    job as separate calls, a barrier before tick ticks[0], CUDA events around
+    each gather of the ticks after it. Returns (GB/s of this rank's gathers,
+    their bytes, their ms)."""
+    import dataclasses
+
+    import torch
+    import torch.distributed as dist
+
+    from ferry_b200.engine import Decoder
+    from ferry_b200.workload import Schedule, q_stream
+
+    dev = torch.device("cuda", local)
+    wr = dataclasses.replace(w, seed=w.seed + 1000 * rank)
+    dec = Decoder(wr, local)
+    try:
+        dec.register_pool()
+        sch = Schedule(wr)
+        qs = [torch.from_numpy(q_stream(wr, r)).to(dev) for r in range(wr.num_requests)]
+        n_pages = torch.full((wr.num_requests,), wr.init_pages, dtype=torch.int32, device=dev)
+        out = torch.empty((wr.num_requests, wr.num_layers, wr.q_heads, 128), dtype=torch.float32, device=dev)
+        st = torch.cuda.current_stream(dev)
+        evs, nbytes = [], 0
+        for i in range(ticks[1]):
+            if i == ticks[0]:
+                torch.cuda.synchronize(dev)
+                if ws > 1:
+                    dist.barrier()
+                dec.stats(reset=True)
+            active, steps, _ = sch.tick(i)
+            if len(active) == 0:
+                continue
+            ids = torch.from_numpy(active).to(dev)
+            new = active[steps == 0]
+            if len(new):
+                dec.begin(torch.from_numpy(new).to(dev), n_pages[: len(new)], stream=st)
+            q = torch.stack([qs[r][s] for r, s in zip(active, steps)])
+            dec.select(q, ids, stream=st)
+            dec.detect(ids, stream=st)
+            a = b = None
+            if i >= ticks[0]:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(st)
+            dec.gather(ids, stream=st)
+            if a is not None:
+                b.record(st)
+                evs.append((a, b))
+            dec.attention(q, ids, out[: len(active)], stream=st)
+        torch.cuda.synchronize(dev)
+        dec.check()
+        nbytes = dec.stats()[1]
+        ms = sum(x.elapsed_time(y) for x, y in evs)
+        return nbytes / (ms / 1e3) / 1e9, nbytes, ms
+    finally:
+        dec.close()
+
+
 def gpu_numa(local):
     """NUMA node of this GPU's PCI device and its local CPU list (sysfs)."""
     import torch
@@ -652,9 +711,11 @@ def run_scale(args, w):
         st = job(False)
     st2 = job(True)
     mine_peak, agg_peak = concurrent_h2d_peak(dev, ws)
+    g_gbs, g_bytes, g_ms = gather_pass(w, local, ws, rank)
     t = torch.tensor([st.window_ms, st.window_tokens, st.window_gathered_bytes, st.stolen_tasks,
                       st.migrated_bytes, st2.window_ms, st2.window_tokens, st2.h2d_bytes, st2.d2h_bytes,
-                      sum(st.tick_ms[window[0]:window[1]]), len(st.tick_ms[window[0]:window[1]])],
+                      sum(st.tick_ms[window[0]:window[1]]), len(st.tick_ms[window[0]:window[1]]),
+                      g_bytes, g_ms],
                      dtype=torch.float64, device=dev)
     mx, sm = t.clone(), t.clone()
     dist.all_reduce(mx, op=dist.ReduceOp.MAX)
@@ -678,7 +739,10 @@ def run_scale(args, w):
                                 "link_peak_aggregate_GB_s": agg_peak, "frac_of_aggregate": gather_agg / agg_peak,
                                 "link_peak_alone_GB_s": mine_peak,
                                 "peak_kind": "copy-engine H2D from pinned host on all ranks at once, this run",
-                                "note": "rate over the whole step (the gather is ~96% of it at N = 1)"},
+                                "note": "rate over the whole step (the gather is ~96% of it at N = 1)",
+                                # the gather kernel alone, every rank gathering at once
+                                "kernel_aggregate_GB_s": float(sm[11]) / (float(mx[12]) / 1e3) / 1e9,
+                                "kernel_frac_of_aggregate": float(sm[11]) / (float(mx[12]) / 1e3) / 1e9 / agg_peak},
                 "steal": {"stolen_tasks": int(sm[3]), "migrated_bytes": float(sm[4])},
                 # the executor's own device time per tick (pop .. push), slowest rank;
                 # ms_per_step above also holds the host's per-tick syncs and the exchange

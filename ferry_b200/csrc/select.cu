@@ -422,10 +422,16 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 4) select_kernel(SelArgs 
 // arithmetic (the oracle's): products rounded to fp32, a >= b ? a : b with
 // a = q*kmax, lane l sums dims 4l..4l+3 in order, the lanes combine by the
 // xor butterfly 16, 8, 4, 2, 1; heads kv-head major, the first wins ties.
-// A CTA scores kQuestChunk pages of one group lane, one page per warp at a
-// time (all Hkv x G bounds of that page); the last CTA of the group lane runs
-// topk_emit and copies the page set into the rows of all Hkv lanes.
-constexpr int kQuestChunk = 64;
+// A CTA scores a chunk of pages of one group lane, one page per warp at a
+// time (all Hkv x G bounds of that page, four kv heads' bounds in flight);
+// the last CTA of the group lane runs topk_emit and copies the page set into
+// the rows of all Hkv lanes. A chunk holds about kQuestChunkRows (page, kv
+// head) bound rows -- 16 pages at 32 kv heads, 64 at 8 -- so that many kv
+// heads still spread over many CTAs.
+constexpr int kQuestChunkRows = 512;
+__host__ __device__ constexpr int quest_chunk_pages(int kv_heads) {
+  return kQuestChunkRows / kv_heads < 8 ? 8 : (kQuestChunkRows / kv_heads > 64 ? 64 : kQuestChunkRows / kv_heads);
+}
 
 struct QuestArgs {
   const uint16_t* q;
@@ -475,26 +481,39 @@ __global__ void __launch_bounds__(kSelThreads) select_quest_kernel(QuestArgs A) 
   for (int x = tid; x < Hq * kHeadDim; x += kSelThreads)
     qs[x] = __half2float(__ushort_as_half(A.q[(size_t)ag * Hq * kHeadDim + x]));
   __syncthreads();
-  const int c0 = chunk * kQuestChunk, c1 = min(np, c0 + kQuestChunk);
+  const int cp = quest_chunk_pages(A.Hkv);
+  const int c0 = chunk * cp, c1 = min(np, c0 + cp);
   uint32_t* kd = A.gkeys + (size_t)ag * N;
   const int64_t lane0 = A.req_base[req] + (int64_t)layer * A.Hkv * N;  // pool unit of (h = 0, p = 0)
   for (int p = c0 + warp; p < c1; p += kSelWarps) {  // warp-uniform
     float best = 0.f;
 #pragma unroll 1
-    for (int h = 0; h < A.Hkv; ++h) {
-      const uint64_t unit = (uint64_t)(lane0 + (int64_t)h * N + p) % A.pool_units;
-      const float4 lo = __ldg(reinterpret_cast<const float4*>(A.mm + unit * 2 * kHeadDim) + lane);
-      const float4 hi = __ldg(reinterpret_cast<const float4*>(A.mm + unit * 2 * kHeadDim + kHeadDim) + lane);
-#pragma unroll 1
-      for (int g = 0; g < A.G; ++g) {
-        const float4 qv = reinterpret_cast<const float4*>(qs + (size_t)(h * A.G + g) * kHeadDim)[lane];
-        float v = quest_term(qv.x, lo.x, hi.x);
-        v = __fadd_rn(v, quest_term(qv.y, lo.y, hi.y));
-        v = __fadd_rn(v, quest_term(qv.z, lo.z, hi.z));
-        v = __fadd_rn(v, quest_term(qv.w, lo.w, hi.w));
+    for (int h0 = 0; h0 < A.Hkv; h0 += 4) {
+      // the bounds of 4 kv heads in flight, then their scores in head order
+      float4 lo[4], hi[4];
 #pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
-        if ((h == 0 && g == 0) || v > best) best = v;
+      for (int u = 0; u < 4; ++u) {
+        if (h0 + u < A.Hkv) {
+          const uint64_t unit = (uint64_t)(lane0 + (int64_t)(h0 + u) * N + p) % A.pool_units;
+          lo[u] = __ldg(reinterpret_cast<const float4*>(A.mm + unit * 2 * kHeadDim) + lane);
+          hi[u] = __ldg(reinterpret_cast<const float4*>(A.mm + unit * 2 * kHeadDim + kHeadDim) + lane);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int h = h0 + u;
+        if (h >= A.Hkv) break;
+#pragma unroll 1
+        for (int g = 0; g < A.G; ++g) {
+          const float4 qv = reinterpret_cast<const float4*>(qs + (size_t)(h * A.G + g) * kHeadDim)[lane];
+          float v = quest_term(qv.x, lo[u].x, hi[u].x);
+          v = __fadd_rn(v, quest_term(qv.y, lo[u].y, hi[u].y));
+          v = __fadd_rn(v, quest_term(qv.z, lo[u].z, hi[u].z));
+          v = __fadd_rn(v, quest_term(qv.w, lo[u].w, hi[u].w));
+#pragma unroll
+          for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+          if ((h == 0 && g == 0) || v > best) best = v;
+        }
       }
     }
     if (lane == 0) kd[p] = order_key(best);
@@ -538,7 +557,7 @@ static int launch_select_quest(const ferry_ctx* c, cudaStream_t st, const uint16
   A.N = c->cfg.max_pages;
   A.k = c->cfg.top_k;
   A.num_requests = c->cfg.num_requests;
-  A.nchunks = (A.N + kQuestChunk - 1) / kQuestChunk;
+  A.nchunks = (A.N + quest_chunk_pages(A.Hkv) - 1) / quest_chunk_pages(A.Hkv);
   A.gkeys = c->quest_keys;
   A.done = c->quest_done;
   A.sel_out = sel;

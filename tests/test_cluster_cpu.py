@@ -226,3 +226,29 @@ def test_exchange_over_a_communicator_merges_its_int32_rows():
     assert owner.tolist() == [0, 1, 0, -1, 1, 0, 1, -1]
     # loads 7 and 40, 3 requests each: mean 23.5, rank 0 pulls (40 - 23) // (23.5 // 3 + 1) = 2
     assert llx_plan(rows[:, 3], rows[:, 2], 0.25) == (1, 0, 2)
+
+
+def test_job_schedule_scales_the_box_rate_and_config_generators():
+    """The multi-GPU bench's job: homes round-robin, Poisson arrivals at N x the
+    single-GPU rate (each GPU sees the configs[0] rate); the configs[3] ON/OFF
+    generator puts its first requests in one ON period and then pauses; ragged
+    contexts are whole pages inside the configured token range."""
+    import numpy as np
+
+    from ferry_b200.cluster import job_schedule
+    from ferry_b200.workload import CFG1, onoff_arrival_ticks, pages_after, ragged_pages
+
+    home, join = job_schedule(CFG1, 64, 4, "rr", rate=CFG1.arrival_rate * 4)
+    assert (home == np.arange(64) % 4).all() and join.min() == 0
+    _, join1 = job_schedule(CFG1, 16, 1, "rr")
+    # four times the requests at four times the rate arrive over a similar span
+    assert 0.5 < join.max() / max(1, join1.max()) < 2.0
+    j = onoff_arrival_ticks(2000, 2000.0, 200.0, 800.0, seed=3)
+    assert (np.diff(j) >= 0).all() and j[0] == 0
+    gaps = np.diff(np.unique(j))
+    assert gaps.max() >= 10  # an OFF period of >= 200 ms on a 20 ms tick
+    per_tick = np.bincount(j)
+    assert per_tick.max() >= 30  # ~40 arrivals per 20 ms tick while ON
+    p = ragged_pages(1000, 8192, 32768, seed=1)
+    assert p.min() >= 512 and p.max() <= 2048
+    assert (pages_after(np.array([10, 2047]), 40, 1, 2048) == [12, 2048]).all()

@@ -698,7 +698,7 @@ def run_scale(args, w):
 
     def job(host_q):
         r = RankRunner(w, total, ws, rank, local, slots=slots_needed(home, ws, max_batch),
-                       max_batch=max_batch, steal_batch=4, host_q=host_q)
+                       max_batch=max_batch, steal_batch=4, host_q=host_q, q_steps=window[1] + 8)
         try:
             dist.barrier()
             torch.cuda.synchronize(dev)

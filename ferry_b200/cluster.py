@@ -327,12 +327,14 @@ class RankRunner:
         if outputs:
             host_out = torch.empty((self.slots, self.row_elems), dtype=torch.float32).pin_memory()
             n_out = C.c_int()
+        started = False
         if w0 == 0:
             if barrier is not None:
                 torch.cuda.synchronize(self.dev)
                 barrier()
                 torch.cuda.synchronize(self.dev)
             e0.record(st)
+            started = True
         t = 0
         while t < last:
             if window is not None and t == w0 and w0 > 0:
@@ -342,6 +344,7 @@ class RankRunner:
                     torch.cuda.synchronize(self.dev)
                 g0 = self.dec.all_stats()[1]
                 e0.record(st)
+                started = True
             arr = mine[join[mine] == t].astype(np.int32)
             if len(arr):
                 pages = pages_of[arr]
@@ -382,6 +385,11 @@ class RankRunner:
                         rebalances += 1
                 if fin_all >= self.total:
                     break
+        if not started:  # the job ended before the window opened: an empty window
+            e0.record(st)
+            if barrier is not None:  # the barrier the window's start would have taken
+                torch.cuda.synchronize(self.dev)
+                barrier()
         e1.record(st)
         torch.cuda.synchronize(self.dev)
         if window is not None and barrier is not None:

@@ -27,8 +27,11 @@ def _ptr(t: torch.Tensor | None):
     return None if t is None else C.c_void_p(t.data_ptr())
 
 
-def _stream(stream=None):
-    s = torch.cuda.current_stream() if stream is None else stream
+def _stream(stream=None, device=None):
+    """The stream handle for a call on `device`: the given stream, else that
+    device's current stream (never another device's: the library launches on
+    the ctx's device with the stream it is handed)."""
+    s = torch.cuda.current_stream(device) if stream is None else stream
     return C.c_void_p(s.cuda_stream)
 
 
@@ -92,9 +95,11 @@ class Decoder:
         w = self.w
         units = w.pool_units if units is None else units
         pool = PinnedPool(units * w.unit_bytes)
-        s = _stream()
-        call("ferry_kv_generate", s, C.c_uint64(w.seed if seed is None else seed), C.c_uint64(unit0),
-             C.c_int64(units), pool.ptr, self.kv_dtype)
+        s = _stream(None, self.dev)
+        # ferry_kv_generate runs on the current device: make it this ctx's
+        with torch.cuda.device(self.dev):
+            call("ferry_kv_generate", s, C.c_uint64(w.seed if seed is None else seed), C.c_uint64(unit0),
+                 C.c_int64(units), pool.ptr, self.kv_dtype)
         torch.cuda.synchronize(self.dev)
         call("ferry_kv_register", self.ctx, pool.ptr, C.c_size_t(pool.nbytes))
         call("ferry_page_summary_update", self.ctx, s, C.c_int64(0), C.c_int64(units))
@@ -106,36 +111,36 @@ class Decoder:
               pool_base: torch.Tensor | None = None):
         """Start requests (cold lanes). pool_base (int64, optional): each
         request's first unit in the host pool; default slot * L * Hkv * N."""
-        call("ferry_requests_begin", self.ctx, _stream(stream), _ptr(req_ids), _ptr(n_pages),
+        call("ferry_requests_begin", self.ctx, _stream(stream, self.dev), _ptr(req_ids), _ptr(n_pages),
              _ptr(pool_base), int(req_ids.numel()))
 
     def append(self, req_ids: torch.Tensor, tokens: int | None = None, stream=None):
         """Grow the requests' contexts by `tokens` tokens (default: the
         workload's per-step append); pages that become full turn selectable."""
-        call("ferry_requests_append", self.ctx, _stream(stream), _ptr(req_ids), int(req_ids.numel()),
+        call("ferry_requests_append", self.ctx, _stream(stream, self.dev), _ptr(req_ids), int(req_ids.numel()),
              self.w.append if tokens is None else tokens)
 
     # ------------------------------------------------------------------ steps
     def select(self, q: torch.Tensor, req_ids: torch.Tensor, stream=None):
-        call("ferry_select_topk", self.ctx, _stream(stream), _ptr(q), _ptr(req_ids),
+        call("ferry_select_topk", self.ctx, _stream(stream, self.dev), _ptr(q), _ptr(req_ids),
              int(req_ids.numel()), _ptr(self.sel), _ptr(self.n_sel))
 
     def detect(self, req_ids: torch.Tensor, stream=None):
-        call("ferry_detect_misses", self.ctx, _stream(stream), _ptr(req_ids), int(req_ids.numel()),
+        call("ferry_detect_misses", self.ctx, _stream(stream, self.dev), _ptr(req_ids), int(req_ids.numel()),
              _ptr(self.sel), _ptr(self.n_sel), _ptr(self.item_slot), _ptr(self.miss_page),
              _ptr(self.miss_slot), _ptr(self.n_miss), _ptr(self.is_miss))
 
     def gather(self, req_ids: torch.Tensor, stream=None):
-        call("ferry_gather_misses", self.ctx, _stream(stream), _ptr(req_ids), int(req_ids.numel()),
+        call("ferry_gather_misses", self.ctx, _stream(stream, self.dev), _ptr(req_ids), int(req_ids.numel()),
              _ptr(self.miss_page), _ptr(self.miss_slot), _ptr(self.n_miss))
 
     def attention(self, q: torch.Tensor, req_ids: torch.Tensor, out: torch.Tensor, stream=None):
-        call("ferry_sparse_decode", self.ctx, _stream(stream), _ptr(q), _ptr(req_ids),
+        call("ferry_sparse_decode", self.ctx, _stream(stream, self.dev), _ptr(q), _ptr(req_ids),
              int(req_ids.numel()), _ptr(self.item_slot), _ptr(self.n_sel), _ptr(out))
 
     def step(self, q: torch.Tensor, req_ids: torch.Tensor, out: torch.Tensor, stream=None):
         """Fused decode step on device-resident q / req_ids / out."""
-        call("ferry_decode_step", self.ctx, _stream(stream), _ptr(q), _ptr(req_ids),
+        call("ferry_decode_step", self.ctx, _stream(stream, self.dev), _ptr(q), _ptr(req_ids),
              int(req_ids.numel()), _ptr(out))
 
     # ------------------------------------------------------------------ inspection
@@ -166,7 +171,7 @@ class Decoder:
         (lane * N + p) mod pool_units (default: the registered pool's size)."""
         if pool_units is None:
             pool_units = self.pool.nbytes // self.w.unit_bytes if self.pool is not None else self.w.pool_units
-        call("ferry_store_fill", self.ctx, _stream(stream), C.c_uint64(self.w.seed if seed is None else seed),
+        call("ferry_store_fill", self.ctx, _stream(stream, self.dev), C.c_uint64(self.w.seed if seed is None else seed),
              C.c_uint64(pool_units))
 
     def gather_source(self, source: int):

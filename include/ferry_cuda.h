@@ -26,8 +26,9 @@
  *               src/runtime/wla_multigpu.cuh:323-332).
  *
  * Threading: one ferry_ctx per GPU, used from one host thread at a time. All
- * per-step calls are asynchronous on the caller's stream; pointers named d_*
- * are device pointers on the ctx's device.
+ * per-step calls are asynchronous on the caller's stream, which must be a
+ * stream of the ctx's device (calls switch to that device and restore the
+ * caller's); pointers named d_* are device pointers on the ctx's device.
  */
 #ifndef FERRY_CUDA_H
 #define FERRY_CUDA_H
@@ -100,8 +101,9 @@ int ferry_kv_register(ferry_ctx* ctx, void* host_pool, size_t bytes);
 /* Fill n_units page units starting at unit0 of dst (device or mapped host
  * memory) with the seeded procedural KV: Irwin-Hall N(0,1) values, rounded to
  * fp16 (FERRY_KV_F16) or quantised to e4m3 with per-page scale amax/448
- * (FERRY_KV_E4M3). Input generator for tests and benches; no reference
- * counterpart (the reference fills its slab from mt19937,
+ * (FERRY_KV_E4M3). Runs on the calling thread's current device, on `stream`
+ * (a stream of that device). Input generator for tests and benches; no
+ * reference counterpart (the reference fills its slab from mt19937,
  * src/runtime/wla_multigpu.cuh:535-543). */
 int ferry_kv_generate(void* stream, uint64_t seed, uint64_t unit0, int64_t n_units,
                       void* dst, int kv_dtype);

@@ -210,6 +210,7 @@ __global__ void stress_kernel(DequeHdr* h, unsigned long long* ring, int n_tasks
 struct ferry_deque {
   int device = -1;
   bool owned = true;  // false for an imported peer view
+  bool ipc = false;   // the view maps the owner through CUDA IPC (closed on destroy)
   ferry::DequeHdr* hdr = nullptr;
   unsigned long long* ring = nullptr;
   uint64_t cap = 0;
@@ -266,8 +267,9 @@ int ferry_deque_destroy(ferry_deque* q) {
   cudaDeviceSynchronize();
   if (q->owned)
     cudaFree(q->hdr);
-  else
+  else if (q->ipc)
     cudaIpcCloseMemHandle(q->hdr);
+  cudaGetLastError();  // teardown errors are not the caller's next launch's
   delete q;
   return FERRY_OK;
 }
@@ -331,6 +333,7 @@ int ferry_deque_import(int device, const void* handle64, uint64_t capacity, ferr
   auto* q = new ferry_deque;
   q->device = device;
   q->owned = false;
+  q->ipc = true;
   q->hdr = (DequeHdr*)p;
   q->ring = (unsigned long long*)((char*)p + sizeof(DequeHdr));
   q->cap = capacity;

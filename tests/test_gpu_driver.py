@@ -76,3 +76,24 @@ def test_cpp_driver_matches_python_path(torch_cuda, tmp_path, select):
     assert got.size == want.size
     assert (got.view(np.uint32) == want.view(np.uint32)).all()
     assert refill == units > 0
+
+
+@pytest.mark.parametrize("gpus,mode", [("0,0", "delta"), ("0,0", "drop"), ("0,1", "full")])
+def test_cpp_multigpu_driver_decodes_every_step_once(torch_cuda, gpus, mode):
+    """ferry_b200/drivers/run_wla_multigpu.cpp (the reference's
+    run_wla_multigpu counterpart): one host thread per GPU, peers linked in
+    process, 80% of the requests homed on the first GPU; the idle executor
+    steals and migrates, and every (request, step) is decoded exactly once."""
+    from ferry_b200 import build
+
+    t = torch_cuda
+    if max(int(g) for g in gpus.split(",")) >= t.cuda.device_count():
+        pytest.skip("needs two GPUs")
+    exe = [p for p in build.build_drivers() if p.endswith("run_wla_multigpu")][0]
+    res = subprocess.run([exe, "--gpus", gpus, "--requests-per-gpu", "8", "--steps", "12", "--ctx", "1024",
+                          "--heads", "4", "--top-k", "16", "--max-batch", "4", "--skew", "imbalanced",
+                          "--kv-mode", mode], capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "exactly_once=yes" in res.stdout
+    stolen = sum(int(m) for m in re.findall(r"stolen=(\d+)", res.stdout))
+    assert stolen > 0, res.stdout

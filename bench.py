@@ -236,6 +236,55 @@ def parity_vs_cpu(w, gpu_out, gpu_units, per_tick, rtol: float = 2e-3) -> dict:
             "against": "the oracle pipeline (cpu_baseline) on the same job ticks"}
 
 
+def owner_lane_parity(dec, w, q_np, out_np, slot: int, lanes, glane0: int, total_units: int,
+                      rtol: float = 2e-3) -> dict:
+    """Check sampled lanes of one request after an owner-gather step against
+    the oracle: its page summaries and top-k selection bit-exact, every
+    selected page's page-table entry pointing at the slot the attention read,
+    that slot holding the page's bytes, and the attention rows within rtol.
+    q_np / out_np: the step's queries [L][Hq][128] fp16 and outputs
+    [L][Hq][128] fp32 of request `slot`; glane0: its first global lane (the
+    procedural content of page p of lane l is unit (glane0 + l) * N + p)."""
+    import oracle
+
+    N, k, C, G, LH = w.max_pages, w.top_k, w.cache_pages, w.group, w.lanes_per_req
+    ub = w.unit_bytes
+    sel = dec.sel.cpu().numpy()
+    nsel = dec.n_sel.cpu().numpy()
+    islot = dec.item_slot.cpu().numpy()
+    worst, pages = 0.0, 0
+    bad = []
+    for l in lanes:
+        row = slot * LH + l
+        layer, h = divmod(l, w.kv_heads)
+        units = oracle.kv_gen_e4m3(w.seed, (glane0 + l) * N, N, threads=os.cpu_count() or 1)
+        summ_ref = oracle.page_summary_e4m3(units).reshape(N, 128)
+        summ = dec.debug_read(4, np.float32, N * 128, ((slot * LH + l) * N) * 128).reshape(N, 128)
+        if not np.array_equal(summ.view(np.uint32), summ_ref.view(np.uint32)):
+            bad.append(f"lane {l}: summaries")
+        qg = np.ascontiguousarray(q_np[layer, h * G:(h + 1) * G]).view(np.uint16)[None]
+        sel_ref, ns_ref = oracle.select_topk(qg, summ_ref[None], np.full(1, N, np.int32), k)
+        if int(nsel[row]) != int(ns_ref[0]) or not np.array_equal(sel[row, :k], sel_ref[0]):
+            bad.append(f"lane {l}: selection")
+        gl = slot * LH + l
+        cache = dec.debug_read(0, np.uint8, C * ub, gl * C * ub).reshape(C, ub)
+        ptab = dec.debug_read(1, np.int32, N, gl * N)
+        sl = islot[row, :k]
+        if (ptab[sel_ref[0]] != sl).any() or len(set(sl.tolist())) != k:
+            bad.append(f"lane {l}: page table")
+        if not np.array_equal(cache[sl], units[sel_ref[0]]):
+            bad.append(f"lane {l}: cached bytes")
+        pg = oracle.e4m3_dequant(units[sel_ref[0]]).reshape(1, k, 4096)
+        ref = oracle.sparse_decode_f32(qg, pg, ns_ref, 128 ** -0.5).reshape(G, 128)
+        got = out_np[layer, h * G:(h + 1) * G].astype(np.float64)
+        worst = max(worst, float((np.abs(got - ref).max(1) / np.abs(ref).max(1)).max()))
+        pages += k
+    ok = not bad and worst <= rtol
+    return {"status": "ok" if ok else "FAIL", "lanes": [int(x) for x in lanes], "request_slot": slot,
+            "pages_checked": pages, "attn_max_rel_err": worst, "tolerance": rtol, "mismatches": bad,
+            "against": "oracle summaries, top-k, page bytes and attention of the sampled lanes"}
+
+
 def run_reference(args, w):
     """--impl reference: the path's CPU implementation on the box's host cores."""
     ws, rank, _ = _dist()
@@ -530,6 +579,8 @@ def main():
     ap.add_argument("--batch", type=int, default=32, help="cfg3s/cfg4s: requests decoded per GPU per tick")
     ap.add_argument("--append", type=int, default=None,
                     help="tokens each decode step appends to its context (default: the workload's)")
+    ap.add_argument("--requests", type=int, default=None,
+                    help="cfg5 / cfg5s: requests of the job (default: the config's 32)")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: independent cfg1 replicas per rank instead of the executor job")
     args = ap.parse_args()
@@ -537,7 +588,7 @@ def main():
         ap.error("--warmup must be >= 3")
     from ferry_b200.workload import WORKLOADS
 
-    if args.workload == "cfg5s":
+    if args.workload in ("cfg5s", "cfg5"):
         return run_owner(args)
     if args.workload == "skew":
         run_cluster(args)
@@ -937,13 +988,16 @@ def run_cluster(args):
 
 
 def run_owner(args):
-    """configs[4] slice on N ranks with page ownership: fp8 e4m3 KV with
-    per-page scales, 64 q / 8 kv heads, 131072-token contexts (8192 pages),
-    top-512, cache 15%, 2 of the 80 layers. The 32 requests are split evenly
-    over the ranks; page p of every lane lives in the HBM store of rank
-    p % N and misses are gathered from the owner (NVLink for a peer). A step
-    decodes one token of every request (steady decode). Strong scaling: the
-    job is the same at every N."""
+    """configs[4] on N ranks with page ownership: fp8 e4m3 KV with per-page
+    scales, 64 q / 8 kv heads, 131072-token contexts (8192 pages), top-512,
+    cache 15%. ``cfg5s`` is a 2-of-80-layer slice whose KV also sits in each
+    rank's pinned host pool; ``cfg5`` is the full 80-layer job, whose 687 GB
+    of KV lives only in the owner stores (86 GB per GPU at N = 8; no host
+    pool, summaries read from the stores). The requests (32, or --requests)
+    are split evenly over the ranks; page p of every lane lives in the HBM
+    store of rank p % N and misses are gathered from the owner (NVLink for a
+    peer). A step decodes one token of every request (steady decode). Strong
+    scaling: the job is the same at every N."""
     import ctypes as C
     import dataclasses
     import datetime
@@ -953,32 +1007,40 @@ def run_owner(args):
 
     from ferry_b200 import _abi
     from ferry_b200.engine import Decoder
-    from ferry_b200.workload import CFG5S, q_stream
+    from ferry_b200.workload import CFG5, CFG5S, q_stream
 
     ws, rank, local = _dist()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     if ws > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    total = CFG5S.num_requests
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    full = args.workload == "cfg5"
+    base_w = CFG5 if full else CFG5S
+    total = args.requests or base_w.num_requests
     if total % ws:
-        raise SystemExit(f"cfg5s: {total} requests do not split over {ws} ranks")
+        raise SystemExit(f"{args.workload}: {total} requests do not split over {ws} ranks")
     R = total // ws
-    w = dataclasses.replace(CFG5S, num_requests=R)
+    w = dataclasses.replace(base_w, num_requests=R)
     LH, N = w.lanes_per_req, w.max_pages
     units = R * LH * N
     dec = Decoder(w, local)
-    # this rank's requests in the pinned pool (summaries, and misses of pages
-    # whose owner is unreachable): global request g = rank * R + slot
-    dec.register_pool(units=units, unit0=rank * units)
-    dec.store_create(ws, rank, total * LH)
+    t_setup = time.perf_counter()
+    if full:
+        # no host pool: the stores hold every page, summaries come from them
+        dec.store_create(ws, rank, total * LH)
+        dec.register_stores(units)
+    else:
+        # this rank's requests in the pinned pool (summaries, and misses of
+        # pages whose owner is unreachable): global request g = rank * R + slot
+        dec.register_pool(units=units, unit0=rank * units)
+        dec.store_create(ws, rank, total * LH)
     dec.store_fill(pool_units=total * LH * N)
     torch.cuda.synchronize(dev)
     if ws > 1:
         h = (C.c_uint8 * _abi.CTX_HANDLE_BYTES)()
         _abi.call("ferry_ctx_export", dec.ctx, h)
         allh = [None] * ws
-        dist.all_gather_object(allh, bytes(h))
+        dist.all_gather_object(allh, bytes(h))  # every rank's store is filled by now
         slot = 0
         for p in range(ws):
             if p != rank:
@@ -995,6 +1057,11 @@ def run_owner(args):
     out = torch.empty((R, w.num_layers, w.q_heads, 128), dtype=torch.float32, device=dev)
     st = torch.cuda.current_stream(dev)
     dec.begin(ids, torch.full((R,), N, dtype=torch.int32, device=dev), pool_base=base)
+    if full:
+        dec.summaries_from_stores(ids)
+        torch.cuda.synchronize(dev)
+        dec.check()
+    setup_s = time.perf_counter() - t_setup
     for s in range(args.warmup):
         dec.step(qs[s], ids, out)
     dec.all_stats(reset=True)
@@ -1036,6 +1103,12 @@ def run_owner(args):
     torch.cuda.synchronize(dev)
     dec.check()
     k_ms = np.mean([[e[j].elapsed_time(e[j + 1]) for j in range(4)] for e in kev], axis=0)
+    parity = None
+    if rank == 0:
+        # the last per-kernel step of request slot 0: first and last lane
+        s_last = n_steps + n_kb - 1
+        parity = owner_lane_parity(dec, w, qs[s_last, 0].cpu().numpy(), out[0].cpu().numpy(), 0,
+                                   [0, LH - 1], int(g_ids[0]) * LH, total * LH * N)
     t = torch.tensor([ms, float(np.percentile(step_ms, 99)), stats[1], stats[5], stats[7], *k_ms, host_ms],
                      dtype=torch.float64, device=dev)
     mx, sm = t.clone(), t.clone()
@@ -1058,7 +1131,8 @@ def run_owner(args):
                 "p99_step_ms": float(mx[1]), "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "e4m3-kv(per-page f32 scales)/fp32-acc",
                 "data": "synthetic (procedural KV, AR(1) queries, seeded)",
-                "config": {"workload": "configs[4] slice: 2 of 80 layers", "requests": total,
+                "config": {"workload": "configs[4]: all 80 layers, KV in the owner stores only" if full
+                           else "configs[4] slice: 2 of 80 layers", "layers": w.num_layers, "requests": total,
                            "requests_per_gpu": R, "ctx_tokens": w.ctx_tokens, "heads": [w.q_heads, w.kv_heads],
                            "top_k": w.top_k, "cache_pages": w.cache_pages, "kv_dtype": "e4m3",
                            "page_owner": f"page id mod {ws}", "parallelism": f"{ws} ranks, owner-store gathers"},
@@ -1086,6 +1160,11 @@ def run_owner(args):
                                             "peer share of the units over the peer-copy peak measured in this run",
                                     "frac": (gat_bytes / kms[2] / 1e6 / hbm_peak) if ws == 1 else
                                             ((gb / args.steps / ws) * (peer_b / gb if gb else 0) / kms[2] / 1e6 / link)},
+                "resident_GB_per_gpu": {"owner_store": total * LH * -(-N // ws) * w.unit_bytes / 1e9,
+                                        "cache": R * LH * w.cache_pages * w.unit_bytes / 1e9,
+                                        "summaries": units * 128 * 4 / 1e9,
+                                        "host_pool": 0.0 if full else units * w.unit_bytes / 1e9},
+                "setup_s": setup_s, "parity": parity,
                 "clocks": clocks.summary()}
         print(json.dumps(line), flush=True)
     dec.close()

@@ -29,6 +29,7 @@ EXPORTS = [
     "ferry_select_mode", "ferry_select_topk", "ferry_detect_misses", "ferry_gather_misses", "ferry_sparse_decode",
     "ferry_sparse_decode_noalloc", "ferry_sparse_decode_noalloc_status", "ferry_decode_step", "ferry_wait_flag", "ferry_stats_read", "ferry_debug_read",
     "ferry_ctx_export", "ferry_store_create", "ferry_store_fill", "ferry_gather_source",
+    "ferry_kv_register_stores", "ferry_page_summary_from_stores",
     "ferry_ctx_import", "ferry_ctx_link", "ferry_migrate_requests",
     "ferry_slot_states", "ferry_deque_create", "ferry_deque_destroy", "ferry_deque_push",
     "ferry_deque_pop", "ferry_deque_steal", "ferry_deque_size", "ferry_deque_peek", "ferry_deque_export",
@@ -115,6 +116,8 @@ _SIGS = {
     "ferry_store_create": (I, [V, I, I, C.c_int64]),
     "ferry_store_fill": (I, [V, V, C.c_uint64, C.c_uint64]),
     "ferry_gather_source": (I, [V, I]),
+    "ferry_kv_register_stores": (I, [V, C.c_uint64]),
+    "ferry_page_summary_from_stores": (I, [V, V, V, I]),
     "ferry_ctx_import": (I, [V, I, V]),
     "ferry_ctx_link": (I, [V, I, V]),
     "ferry_migrate_requests": (I, [V, V, I, V, V, I, I]),

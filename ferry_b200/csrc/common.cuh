@@ -220,6 +220,7 @@ struct ferry_ctx {
   int64_t* req_base = nullptr;   // R: pool unit of the request's (lane 0, page 0)
 
   // host pool
+  bool stores_only = false;       // summaries without a host pool; misses from owner stores only
   uint8_t* pool_dev = nullptr;  // device-visible address of the pinned pool
   uint64_t pool_units = 0;
   float* summ = nullptr;  // pool_units * summ_row: mean rows (128) or Quest [kmin | kmax] rows (256)
@@ -259,6 +260,14 @@ struct ferry_ctx {
 namespace ferry {
 constexpr int kPartStride = 132;  // o[128], m, l, pad -> 16-byte rows
 
+// Owner stores by rank (FERRY_SRC_OWNER) as a kernel argument; world == 0
+// means host only.
+struct OwnerMap {
+  const uint8_t* store[FERRY_MAX_PEERS + 1];
+  int world, self, own_np;
+  int64_t store_lanes;
+};
+
 // kernels' launchers (one per .cu)
 int launch_kv_generate(cudaStream_t st, uint64_t seed, uint64_t unit0, int64_t n_units, void* dst,
                        int kv_dtype);
@@ -269,6 +278,9 @@ int launch_select(const ferry_ctx* c, cudaStream_t st, const uint16_t* q, const 
 // decode appends: grow each listed request's context by `tokens` tokens and
 // compute the summary of every page that becomes full (kvgen.cu)
 int launch_append(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, int n, int tokens);
+// summaries (mean rows or Quest bounds) of every page of the listed
+// requests, read from the owner stores (kvgen.cu)
+int launch_store_summary(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, int n);
 // Quest page bounds [kmin | kmax] of pool units (kvgen.cu)
 int launch_minmax(cudaStream_t st, const uint8_t* pool, int64_t unit0, int64_t n_units, float* mm,
                   int kv_dtype);

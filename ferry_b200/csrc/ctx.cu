@@ -261,6 +261,7 @@ int ferry_host_free(void* p) {
 int ferry_kv_register(ferry_ctx* c, void* host_pool, size_t bytes) {
   if (!c || !host_pool || bytes < (size_t)c->unit_bytes || ((uintptr_t)host_pool & 15))
     return set_error("kv_register: need a 16-byte aligned pool of >= one page unit"), FERRY_E_INVAL;
+  if (c->stores_only) return set_error("kv_register: the ctx runs without a host pool"), FERRY_E_STATE;
   DeviceGuard guard(c->device);
   void* dev = nullptr;
   cudaError_t e = cudaHostGetDevicePointer(&dev, host_pool, 0);
@@ -278,6 +279,32 @@ int ferry_kv_register(ferry_ctx* c, void* host_pool, size_t bytes) {
   c->pool_dev = (uint8_t*)dev;
   c->pool_units = units;
   return FERRY_OK;
+}
+
+int ferry_kv_register_stores(ferry_ctx* c, uint64_t units) {
+  if (!c || units == 0) return set_error("kv_register_stores: bad arguments"), FERRY_E_INVAL;
+  if (!c->store) return set_error("kv_register_stores: create the owner store first"), FERRY_E_STATE;
+  if (c->pool_dev) return set_error("kv_register_stores: a host pool is registered"), FERRY_E_STATE;
+  DeviceGuard guard(c->device);
+  float* summ = nullptr;
+  int rc = dev_alloc(&summ, (size_t)units * c->summ_row, 0);
+  if (rc) return rc;
+  cudaFree(c->summ);
+  c->summ = summ;
+  c->pool_units = units;
+  c->stores_only = true;
+  c->gather_src = FERRY_SRC_OWNER;
+  return FERRY_OK;
+}
+
+static int check_batch(const ferry_ctx* c, const int32_t* req_ids, int n_req);
+
+int ferry_page_summary_from_stores(ferry_ctx* c, void* stream, const int32_t* d_req_ids, int n) {
+  int rc = check_batch(c, d_req_ids, n);
+  if (rc) return rc;
+  if (!c->store || !c->summ) return set_error("summary_from_stores: needs a store and summary rows"), FERRY_E_STATE;
+  DeviceGuard guard(c->device);
+  return launch_store_summary(c, (cudaStream_t)stream, d_req_ids, n);
 }
 
 int ferry_kv_generate(void* stream, uint64_t seed, uint64_t unit0, int64_t n_units, void* dst,
@@ -300,7 +327,8 @@ int ferry_select_mode(ferry_ctx* c, int mode) {
   if (!c) return set_error("ctx is NULL"), FERRY_E_INVAL;
   if (mode != FERRY_SELECT_MEAN && mode != FERRY_SELECT_QUEST)
     return set_error("select_mode: unknown mode %d", mode), FERRY_E_INVAL;
-  if (c->pool_dev) return set_error("select_mode: set it before ferry_kv_register"), FERRY_E_STATE;
+  if (c->pool_dev || c->stores_only)
+    return set_error("select_mode: set it before ferry_kv_register"), FERRY_E_STATE;
   if (mode == FERRY_SELECT_QUEST) {
     if (select_quest_smem(c->cfg.q_heads, c->cfg.max_pages) > 200 * 1024)
       return set_error("select_mode: %d q heads and %d pages exceed the Quest kernel's shared memory",
@@ -388,8 +416,10 @@ int ferry_decode_step(ferry_ctx* c, void* stream, const uint16_t* d_q, const int
                       int n_req, float* d_out) {
   int rc = check_batch(c, d_req_ids, n_req);
   if (rc) return rc;
-  if (!c->summ || !c->pool_dev) return set_error("no host pool registered"), FERRY_E_STATE;
+  if (!c->summ || !(c->pool_dev || c->stores_only)) return set_error("no host pool registered"), FERRY_E_STATE;
   if (n_req && (!d_q || !d_out)) return set_error("decode_step: NULL buffer"), FERRY_E_INVAL;
+  if (c->append_tokens > 0 && !c->pool_dev)
+    return set_error("decode_step: appends read the new pages from the host pool"), FERRY_E_STATE;
   DeviceGuard guard(c->device);
   cudaStream_t st = (cudaStream_t)stream;
   if ((rc = launch_select(c, st, d_q, d_req_ids, n_req, c->ws_sel, c->ws_nsel))) return rc;

@@ -14,13 +14,6 @@
 namespace ferry {
 namespace {
 
-// Owner stores by rank (FERRY_SRC_OWNER); world == 0 means host only.
-struct OwnerMap {
-  const uint8_t* store[FERRY_MAX_PEERS + 1];
-  int world, self, own_np;
-  int64_t store_lanes;
-};
-
 __global__ void __launch_bounds__(256) gather_kernel(
     const uint8_t* __restrict__ pool, uint64_t pool_units, uint8_t* __restrict__ cache, int N,
     int C, const int32_t* __restrict__ req_ids, int lanes_per_req, int64_t lanes_total,
@@ -58,7 +51,13 @@ __global__ void __launch_bounds__(256) gather_kernel(
           ++from_peer;
       }
     }
-    if (!src) src = pool + ((uint64_t)(home + page) % pool_units) * unit_bytes;
+    if (!src) {
+      if (!pool) {  // stores only: every owner must be mapped
+        if (t == 0) record_error(err, kErrRange);
+        continue;
+      }
+      src = pool + ((uint64_t)(home + page) % pool_units) * unit_bytes;
+    }
     uint8_t* dst = cache + ((uint64_t)gl * C + slot) * unit_bytes;
     warp_copy_unit(src, dst, unit_bytes, t);
     ++copied;
@@ -176,9 +175,12 @@ __global__ void __launch_bounds__(kGtMaxWarps * 32, 1) gather_store_kernel(
         pend_dst = dst;
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
-    } else {
+    } else if (pool) {
       const uint8_t* src = pool + ((uint64_t)(home + page) % pool_units) * unit_bytes;
       for (int v = t; v < (unit_bytes >> 4); v += 32) st_v4(dst + (size_t)v * 16, ld_nc_v4(src + (size_t)v * 16));
+    } else {  // stores only: every owner must be mapped
+      --copied;
+      if (t == 0) record_error(err, kErrRange);
     }
   }
   if (t == 0) {
@@ -208,8 +210,9 @@ __global__ void __launch_bounds__(kGtMaxWarps * 32, 1) gather_store_kernel(
 int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, int n_req,
                   const int32_t* miss_page, const int32_t* miss_slot, const int32_t* n_miss) {
   if (n_req <= 0) return FERRY_OK;
-  if (!c->pool_dev) {
-    set_error("gather: no host pool registered");
+  if (!c->pool_dev && !(c->stores_only && c->gather_src == FERRY_SRC_OWNER)) {
+    set_error(c->stores_only ? "gather: a ctx without a host pool gathers from owner stores only"
+                             : "gather: no host pool registered");
     return FERRY_E_STATE;
   }
   OwnerMap own{};

@@ -261,10 +261,11 @@ struct AppendArgs {
   uint32_t* err;
 };
 
-__device__ __forceinline__ void summary_unit(const uint8_t* pool, uint64_t u, float* summ, bool f8, int lane) {
+// Summary row of the page unit at K (mean of its 16 keys, as summary_kernel)
+// into row[128]; one warp, lane l owns dims 4l..4l+3.
+__device__ __forceinline__ void summary_unit(const uint8_t* K, float* row, bool f8, int lane) {
   float acc[4];
   if (f8) {
-    const uint8_t* K = pool + (size_t)u * kUnitBytesF8;
     const float ks = *reinterpret_cast<const float*>(K + 4096);
 #pragma unroll
     for (int tt = 0; tt < kPageTokens; ++tt) {
@@ -280,7 +281,6 @@ __device__ __forceinline__ void summary_unit(const uint8_t* pool, uint64_t u, fl
       }
     }
   } else {
-    const uint8_t* K = pool + (size_t)u * kUnitBytes;
 #pragma unroll
     for (int tt = 0; tt < kPageTokens; ++tt) {
       const uint2 raw = *reinterpret_cast<const uint2*>(K + tt * kHeadDim * 2 + lane * 8);
@@ -291,18 +291,18 @@ __device__ __forceinline__ void summary_unit(const uint8_t* pool, uint64_t u, fl
       for (int j = 0; j < 4; ++j) acc[j] = tt == 0 ? v[j] : __fadd_rn(acc[j], v[j]);
     }
   }
-  reinterpret_cast<float4*>(summ + (size_t)u * kHeadDim)[lane] =
+  reinterpret_cast<float4*>(row)[lane] =
       make_float4(__fmul_rn(acc[0], 0.0625f), __fmul_rn(acc[1], 0.0625f), __fmul_rn(acc[2], 0.0625f),
                   __fmul_rn(acc[3], 0.0625f));
 }
 
-__device__ __forceinline__ void minmax_unit(const uint8_t* pool, uint64_t u, float* mm, bool f8, int lane) {
+// Quest bounds of the page unit at K (as minmax_kernel) into row[256].
+__device__ __forceinline__ void minmax_unit(const uint8_t* K, float* row, bool f8, int lane) {
   float lo[4], hi[4];
 #pragma unroll
   for (int tt = 0; tt < kPageTokens; ++tt) {
     float v[4];
     if (f8) {
-      const uint8_t* K = pool + (size_t)u * kUnitBytesF8;
       const float ks = *reinterpret_cast<const float*>(K + 4096);
       const uint32_t w = *reinterpret_cast<const uint32_t*>(K + tt * kHeadDim + lane * 4);
       const __half2_raw a = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w & 0xFFFF), __NV_E4M3);
@@ -312,7 +312,6 @@ __device__ __forceinline__ void minmax_unit(const uint8_t* pool, uint64_t u, flo
       v[2] = __fmul_rn(__half2float(__ushort_as_half(b.x)), ks);
       v[3] = __fmul_rn(__half2float(__ushort_as_half(b.y)), ks);
     } else {
-      const uint8_t* K = pool + (size_t)u * kUnitBytes;
       const uint2 raw = *reinterpret_cast<const uint2*>(K + tt * kHeadDim * 2 + lane * 8);
       const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
       const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
@@ -324,9 +323,9 @@ __device__ __forceinline__ void minmax_unit(const uint8_t* pool, uint64_t u, flo
       hi[j] = (tt == 0 || v[j] > hi[j]) ? v[j] : hi[j];
     }
   }
-  float4* row = reinterpret_cast<float4*>(mm + (size_t)u * 2 * kHeadDim);
-  row[lane] = make_float4(lo[0], lo[1], lo[2], lo[3]);
-  row[32 + lane] = make_float4(hi[0], hi[1], hi[2], hi[3]);
+  float4* r4 = reinterpret_cast<float4*>(row);
+  r4[lane] = make_float4(lo[0], lo[1], lo[2], lo[3]);
+  r4[32 + lane] = make_float4(hi[0], hi[1], hi[2], hi[3]);
 }
 
 __global__ void __launch_bounds__(256) append_summary_kernel(AppendArgs A) {
@@ -347,10 +346,60 @@ __global__ void __launch_bounds__(256) append_summary_kernel(AppendArgs A) {
   const int64_t np2 = min((int64_t)A.N, (int64_t)np + ((int64_t)tail + A.tokens) / kPageTokens);
   for (int64_t p = np; p < np2; ++p) {
     const uint64_t u = (uint64_t)(A.req_base[r] + (int64_t)l * A.N + p) % A.pool_units;
+    const uint8_t* K = A.pool + (size_t)u * (A.f8 ? kUnitBytesF8 : kUnitBytes);
     if (A.quest)
-      minmax_unit(A.pool, u, A.summ, A.f8, t);
+      minmax_unit(K, A.summ + (size_t)u * 2 * kHeadDim, A.f8, t);
     else
-      summary_unit(A.pool, u, A.summ, A.f8, t);
+      summary_unit(K, A.summ + (size_t)u * kHeadDim, A.f8, t);
+  }
+}
+
+// ---- summaries read from the owner stores (no host pool)
+// Page p of request r's lane l lives in the store of rank p % world, at index
+// glane * own_np + p / world with glane = (req_base[r] + l * N) / N; its
+// summary row goes to pool unit (req_base[r] + l * N + p) mod pool_units, the
+// row ferry_page_summary_update would write from a host pool with the same
+// content. One warp per (request, lane, page); pages whose owner store is
+// not mapped are recorded as range errors and left alone.
+struct StoreSumArgs {
+  const int32_t* req_ids;
+  int n, lanes_per_req, N, R;
+  const int32_t* ctx_pages;
+  const int64_t* req_base;
+  OwnerMap own;
+  int unit_bytes;
+  uint64_t pool_units;
+  float* summ;
+  int quest, f8;
+  uint32_t* err;
+};
+
+__global__ void __launch_bounds__(256) store_summary_kernel(const __grid_constant__ StoreSumArgs A) {
+  const int t = threadIdx.x & 31;
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t total = (int64_t)A.n * A.lanes_per_req * A.N;
+  for (int64_t f = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); f < total; f += nw) {
+    const int p = (int)(f % A.N);
+    const int64_t a = f / A.N;
+    const int i = (int)(a / A.lanes_per_req), l = (int)(a % A.lanes_per_req);
+    const int r = A.req_ids[i];
+    if (r < 0 || r >= A.R) {
+      if (t == 0 && l == 0 && p == 0) record_error(A.err, kErrRange);
+      continue;
+    }
+    const int64_t home = A.req_base[r] + (int64_t)l * A.N;
+    const int64_t glane = home / A.N;
+    const int owner = p % A.own.world;
+    if (glane < 0 || glane >= A.own.store_lanes || !A.own.store[owner]) {
+      if (t == 0) record_error(A.err, kErrRange);
+      continue;
+    }
+    const uint8_t* K = A.own.store[owner] + ((size_t)glane * A.own.own_np + p / A.own.world) * A.unit_bytes;
+    const uint64_t u = (uint64_t)(home + p) % A.pool_units;
+    if (A.quest)
+      minmax_unit(K, A.summ + (size_t)u * 2 * kHeadDim, A.f8, t);
+    else
+      summary_unit(K, A.summ + (size_t)u * kHeadDim, A.f8, t);
   }
 }
 
@@ -427,6 +476,34 @@ int launch_append(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, i
   append_summary_kernel<<<(warps + 7) / 8, 256, 0, st>>>(A);
   FERRY_TRY(cudaGetLastError());
   append_state_kernel<<<(n + 127) / 128, 128, 0, st>>>(A);
+  FERRY_TRY(cudaGetLastError());
+  return FERRY_OK;
+}
+
+int launch_store_summary(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, int n) {
+  if (n <= 0) return FERRY_OK;
+  StoreSumArgs A{};
+  A.req_ids = req_ids;
+  A.n = n;
+  A.lanes_per_req = c->lanes_per_req;
+  A.N = c->cfg.max_pages;
+  A.R = c->cfg.num_requests;
+  A.ctx_pages = c->ctx_pages;
+  A.req_base = c->req_base;
+  A.own.world = c->own_world;
+  A.own.self = c->own_rank;
+  A.own.own_np = c->own_np;
+  A.own.store_lanes = c->store_lanes;
+  for (int r = 0; r <= FERRY_MAX_PEERS; ++r) A.own.store[r] = c->store_of[r];
+  A.unit_bytes = c->unit_bytes;
+  A.pool_units = c->pool_units;
+  A.summ = c->summ;
+  A.quest = c->select_mode == FERRY_SELECT_QUEST;
+  A.f8 = c->cfg.kv_dtype == FERRY_KV_E4M3;
+  A.err = c->err;
+  const int64_t warps = (int64_t)n * c->lanes_per_req * c->cfg.max_pages;
+  const int64_t blocks = std::min<int64_t>((warps + 7) / 8, (int64_t)c->num_sms * 16);
+  store_summary_kernel<<<(unsigned)blocks, 256, 0, st>>>(A);
   FERRY_TRY(cudaGetLastError());
   return FERRY_OK;
 }

@@ -70,6 +70,8 @@ int ferry_gather_source(ferry_ctx* c, int source) {
     return set_error("gather_source: bad arguments"), FERRY_E_INVAL;
   if (source == FERRY_SRC_OWNER && !c->store)
     return set_error("gather_source: owner gathers need ferry_store_create first"), FERRY_E_STATE;
+  if (source == FERRY_SRC_HOST && c->stores_only)
+    return set_error("gather_source: no host pool (ferry_kv_register_stores)"), FERRY_E_STATE;
   c->gather_src = source;
   return FERRY_OK;
 }

@@ -177,6 +177,17 @@ class Decoder:
     def gather_source(self, source: int):
         call("ferry_gather_source", self.ctx, source)
 
+    def register_stores(self, units: int):
+        """No host pool: summary rows for `units` pool units, misses from the
+        owner stores only (after store_create)."""
+        call("ferry_kv_register_stores", self.ctx, C.c_uint64(units))
+
+    def summaries_from_stores(self, req_ids: torch.Tensor, stream=None):
+        """Summaries of every page of the requests (after begin), read from
+        their owners' stores; every owner's store filled and linked first."""
+        call("ferry_page_summary_from_stores", self.ctx, _stream(stream, self.dev), _ptr(req_ids),
+             int(req_ids.numel()))
+
     def debug_read(self, which: int, dtype, count: int, offset_elems: int = 0) -> np.ndarray:
         out = np.empty(count, dtype)
         call("ferry_debug_read", self.ctx, which, C.c_size_t(offset_elems * out.itemsize),

@@ -104,6 +104,13 @@ CFG5S = Workload(name="cfg5s", num_requests=32, num_layers=2, q_heads=64, kv_hea
                  ctx_tokens=131072, top_k=512, cache_frac=0.15, steps=64, arrival_rate=50.0,
                  kv_dtype="e4m3")
 
+# configs[4] at full depth: all 80 layers (640 lanes per request). Its KV is
+# 687 GB of e4m3 units, 86 GB per GPU on 8 GPUs: it lives only in the
+# page-owner stores (no host pool; ferry_kv_register_stores).
+CFG5 = Workload(name="cfg5", num_requests=32, num_layers=80, q_heads=64, kv_heads=8,
+                ctx_tokens=131072, top_k=512, cache_frac=0.15, steps=64, arrival_rate=50.0,
+                kv_dtype="e4m3")
+
 # the same GQA shape with fp16 KV (16 requests, a 17 GB pinned pool): the
 # fp16 path of the tensor-core attention kernel at G = 8
 CFG5S_F16 = Workload(name="cfg5s_f16", num_requests=16, num_layers=2, q_heads=64, kv_heads=8,
@@ -130,7 +137,7 @@ CFG4S = Workload(name="cfg4s", num_requests=256, num_layers=1, q_heads=32, kv_he
 
 CONTEXT_RANGE = {"cfg3s": (8192, 32768), "cfg4s": (16384, 65536)}
 
-WORKLOADS = {"cfg1": CFG1, "cfg5s": CFG5S, "cfg5s_f16": CFG5S_F16, "cfg3s": CFG3S, "cfg4s": CFG4S}
+WORKLOADS = {"cfg1": CFG1, "cfg5": CFG5, "cfg5s": CFG5S, "cfg5s_f16": CFG5S_F16, "cfg3s": CFG3S, "cfg4s": CFG4S}
 
 
 def small(name: str = "tiny", **kw) -> Workload:

@@ -295,6 +295,23 @@ int ferry_ctx_export(ferry_ctx* ctx, void* handle /* FERRY_CTX_HANDLE_BYTES */);
 int ferry_store_create(ferry_ctx* ctx, int world, int rank, int64_t global_lanes);
 int ferry_store_fill(ferry_ctx* ctx, void* stream, uint64_t seed, uint64_t pool_units);
 int ferry_gather_source(ferry_ctx* ctx, int source);
+/* A job whose every page lives in an owner store needs no host pool
+ * (configs[4] at full depth: 687 GB of e4m3 KV, 86 GB per GPU at 8 GPUs, which
+ * fits the stores but not a pinned host pool). ferry_kv_register_stores takes
+ * the place of ferry_kv_register after ferry_store_create: it allocates the
+ * summary rows of `units` pool units (the same unit addressing, req_base +
+ * lane * N + p mod units) and switches the gather source to FERRY_SRC_OWNER.
+ * ferry_page_summary_from_stores then computes the summaries (mean rows, or
+ * Quest bounds) of every page of the listed requests (after
+ * ferry_requests_begin) from the bytes in their owners' stores -- this GPU's
+ * or a peer's over NVLink, so every rank's store must be filled and linked
+ * first; the rows equal what ferry_page_summary_update computes from a host
+ * pool with the same content. Without a pool, a page whose owner is not
+ * mapped is a range error (FERRY_E_RANGE from ferry_check_errors) and is not
+ * copied; FERRY_SRC_HOST, ferry_page_summary_update and appends return
+ * FERRY_E_STATE. */
+int ferry_kv_register_stores(ferry_ctx* ctx, uint64_t units);
+int ferry_page_summary_from_stores(ferry_ctx* ctx, void* stream, const int32_t* d_req_ids, int n);
 int ferry_ctx_import(ferry_ctx* ctx, int peer_slot, const void* handle);
 int ferry_ctx_link(ferry_ctx* ctx, int peer_slot, ferry_ctx* peer);
 int ferry_migrate_requests(ferry_ctx* ctx, void* stream, int peer_slot, const int32_t* d_src_req,

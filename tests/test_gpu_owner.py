@@ -170,3 +170,102 @@ def test_owner_gather_over_nvlink(torch_cuda):
         host.close()
         for d in decs:
             d.close()
+
+
+def _stores_only_job(t, world, kv_dtype, select_mode):
+    """The same job with no host pool: every rank's store filled and linked,
+    summaries from the stores."""
+    from ferry_b200 import _abi
+    from ferry_b200.engine import Decoder
+    from ferry_b200.workload import small
+
+    w = small(num_requests=4, num_layers=2, q_heads=8, kv_heads=2, ctx_tokens=2048, top_k=24,
+              kv_dtype=kv_dtype)
+    decs = [Decoder(w, 0, select_mode=select_mode) for _ in range(world)]
+    for r, d in enumerate(decs):
+        d.store_create(world, r)
+        d.register_stores(w.pool_units)
+        d.store_fill(pool_units=w.pool_units)
+    t.cuda.synchronize()
+    for r, d in enumerate(decs):
+        slot = 0
+        for p, e in enumerate(decs):
+            if p != r:
+                _abi.call("ferry_ctx_link", d.ctx, slot, e.ctx)
+                slot += 1
+    return w, decs
+
+
+@pytest.mark.parametrize("world,kv_dtype,mode", [(1, "e4m3", 0), (3, "e4m3", 0), (2, "f16", 1), (4, "f16", 0)])
+def test_stores_only_job_matches_host_pool(torch_cuda, world, kv_dtype, mode):
+    """ferry_kv_register_stores + ferry_page_summary_from_stores: summaries
+    (mean rows or Quest bounds), cache bytes and decode outputs bit-identical
+    to the host-pool path on the same content."""
+    from ferry_b200.engine import Decoder
+
+    t = torch_cuda
+    dev = t.device("cuda", 0)
+    w, decs = _stores_only_job(t, world, kv_dtype, mode)
+    host = Decoder(w, 0, select_mode=mode)
+    try:
+        host.register_pool()
+        reqs = list(range(w.num_requests))
+        ids = t.from_numpy(np.asarray(reqs, np.int32)).to(dev)
+        d = decs[0]
+        d.begin(ids, t.full((len(reqs),), w.max_pages, dtype=t.int32, device=dev))
+        d.summaries_from_stores(ids)
+        t.cuda.synchronize()
+        d.check()
+        row = 256 if mode == 1 else 128
+        sa = d.debug_read(4, np.float32, w.pool_units * row)
+        sb = host.debug_read(4, np.float32, w.pool_units * row)
+        assert (sa.view(np.uint32) == sb.view(np.uint32)).all()
+        d.all_stats(reset=True)
+        outs = []
+        for s in range(3):
+            out = t.zeros((len(reqs), w.num_layers, w.q_heads, 128), dtype=t.float32, device=dev)
+            d.step(t.from_numpy(_q(w, reqs, s)).to(dev), ids, out)
+            outs.append(out.cpu().numpy())
+        t.cuda.synchronize()
+        d.check()
+        ref = _run(t, host, w, reqs, 3, dev)
+        for x, y in zip(outs, ref):
+            assert (x.view(np.uint32) == y.view(np.uint32)).all()
+        n = w.num_requests * w.lanes_per_req * w.cache_pages * w.unit_bytes
+        assert (d.debug_read(0, np.uint8, n) == host.debug_read(0, np.uint8, n)).all()
+        st = d.all_stats()
+        assert st[0] > 0 and st[4] + st[6] == st[0]  # every miss from a store
+    finally:
+        host.close()
+        for x in decs:
+            x.close()
+
+
+def test_stores_only_rejects_host_paths_and_unmapped_owners(torch_cuda):
+    from ferry_b200 import _abi
+    from ferry_b200.engine import Decoder
+    from ferry_b200.workload import small
+
+    t = torch_cuda
+    dev = t.device("cuda", 0)
+    w = small(num_requests=2, ctx_tokens=1024, top_k=16)
+    d = Decoder(w, 0)
+    try:
+        with pytest.raises(_abi.FerryError):
+            d.register_stores(w.pool_units)               # no store yet
+        d.store_create(2, 0)                               # rank 1 is never linked
+        d.register_stores(w.pool_units)
+        d.store_fill(pool_units=w.pool_units)
+        with pytest.raises(_abi.FerryError):
+            d.gather_source(_abi.SRC_HOST)                # there is no host pool
+        with pytest.raises(_abi.FerryError):
+            d.register_pool()                             # nor can one be added
+        ids = t.tensor([0, 1], dtype=t.int32, device=dev)
+        d.begin(ids, t.full((2,), w.max_pages, dtype=t.int32, device=dev))
+        d.summaries_from_stores(ids)
+        t.cuda.synchronize()
+        with pytest.raises(_abi.FerryError) as e:         # the odd pages have no mapped owner
+            d.check()
+        assert e.value.code == _abi.E_RANGE
+    finally:
+        d.close()

@@ -83,7 +83,14 @@ def test_cpp_multigpu_driver_decodes_every_step_once(torch_cuda, gpus, mode):
     """ferry_b200/drivers/run_wla_multigpu.cpp (the reference's
     run_wla_multigpu counterpart): one host thread per GPU, peers linked in
     process, 80% of the requests homed on the first GPU; the idle executor
-    steals and migrates, and every (request, step) is decoded exactly once."""
+    steals and migrates, and every (request, step) is decoded exactly once.
+
+    The owner pops its deque LIFO (Chase-Lev), so it runs its newest batch to
+    completion while the older tasks wait; with a batch of 2 the homes (12 on
+    the first GPU, 4 on the second) leave the first GPU's deque above the
+    water level for whole ticks once the second GPU's work is done, so the
+    steal does not hinge on reading the deque between two of the owner's
+    ticks."""
     from ferry_b200 import build
 
     t = torch_cuda
@@ -91,7 +98,7 @@ def test_cpp_multigpu_driver_decodes_every_step_once(torch_cuda, gpus, mode):
         pytest.skip("needs two GPUs")
     exe = [p for p in build.build_drivers() if p.endswith("run_wla_multigpu")][0]
     res = subprocess.run([exe, "--gpus", gpus, "--requests-per-gpu", "8", "--steps", "12", "--ctx", "1024",
-                          "--heads", "4", "--top-k", "16", "--max-batch", "4", "--skew", "imbalanced",
+                          "--heads", "4", "--top-k", "16", "--max-batch", "2", "--skew", "imbalanced",
                           "--kv-mode", mode], capture_output=True, text=True, timeout=600)
     assert res.returncode == 0, res.stdout + res.stderr
     assert "exactly_once=yes" in res.stdout

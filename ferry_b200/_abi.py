@@ -42,11 +42,14 @@ EXPORTS = [
     "ferry_exchange_ownership",
     "ferry_trace_load", "ferry_probe_topology", "ferry_probe_link",
     "ferry_lru_create", "ferry_lru_destroy", "ferry_lru_touch", "ferry_lru_read",
+    "ferry_lru_group_enable", "ferry_lru_touch_owned", "ferry_lru_set_capacity", "ferry_lru_release",
+    "ferry_lru_count_owned", "ferry_lru_handoff", "ferry_lru_read_owned",
 ]
 MAX_PEERS = 8
 CTX_HANDLE_BYTES = 1024
 COMM_ID_BYTES = 128
 MIGRATE_FULL, MIGRATE_DELTA, MIGRATE_DROP = 0, 1, 2
+HANDOFF_DROP, HANDOFF_CARRY, HANDOFF_OWNED = 0, 1, 2
 SRC_HOST, SRC_OWNER = 0, 1
 NUM_STATS = 8
 
@@ -158,6 +161,13 @@ _SIGS = {
     "ferry_lru_destroy": (I, [V]),
     "ferry_lru_touch": (I, [V, V, V, V, I, V, I, V, I, V, V, V, V, V]),
     "ferry_lru_read": (I, [V, I, V, V, V]),
+    "ferry_lru_group_enable": (I, [V]),
+    "ferry_lru_touch_owned": (I, [V, V, V, V, I, V, I, V, I, V, V, V, V, V, V]),
+    "ferry_lru_set_capacity": (I, [V, V, V, V, I]),
+    "ferry_lru_release": (I, [V, V, V, I, C.c_uint32]),
+    "ferry_lru_count_owned": (I, [V, V, V, I, C.c_uint32, V]),
+    "ferry_lru_handoff": (I, [V, V, V, V, V, I, I, C.c_uint32]),
+    "ferry_lru_read_owned": (I, [V, I, V, V]),
 }
 
 

@@ -59,6 +59,34 @@ int cuda_status(cudaError_t e, const char* what);
     if (e__ != cudaSuccess) return ferry::cuda_status(e__, #call); \
   } while (0)
 
+// Switch to a device for the duration of a call and restore the caller's.
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = false;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    ok = cudaSetDevice(dev) == cudaSuccess;
+    if (!ok) set_error("cudaSetDevice(%d) failed", dev);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+// count elements of T on the current device, every byte set to fill_byte
+template <typename T>
+int dev_alloc(T** p, size_t count, int fill_byte) {
+  *p = nullptr;
+  if (count == 0) return FERRY_OK;
+  cudaError_t e = cudaMalloc((void**)p, count * sizeof(T));
+  if (e != cudaSuccess) {
+    *p = nullptr;
+    return cuda_status(e, "cudaMalloc");
+  }
+  FERRY_TRY(cudaMemset(*p, fill_byte, count * sizeof(T)));
+  return FERRY_OK;
+}
+
 // ---------------------------------------------------------------- device helpers
 __device__ __forceinline__ void record_error(uint32_t* err, uint32_t bit) {
   if (err) atomicOr(err, bit);
@@ -182,6 +210,10 @@ struct ferry_lru {
   int32_t* order = nullptr;      // lanes * cap, LRU order as slots (front first)
   int32_t* size = nullptr;       // lanes
   uint32_t* err = nullptr;       // device error record
+  // group lanes (group.cu): per-lane capacity and per-slot owner bits, null
+  // until ferry_lru_group_enable
+  int32_t* lane_cap = nullptr;   // lanes
+  uint32_t* mask = nullptr;      // lanes * cap
 };
 
 // Another GPU's ctx buffers as this ctx's device sees them (peer mapping or
@@ -289,7 +321,7 @@ size_t select_quest_smem(int q_heads, int max_pages);
 int launch_lru(const ferry_lru* L, cudaStream_t st, const int32_t* lane_ids, const int32_t* req_ids,
                int lanes_per_req, const uint8_t* reset, int n, const int32_t* sel, int k,
                const int32_t* n_sel, int distinct, uint8_t* is_miss, int32_t* item_slot,
-               int32_t* miss_page, int32_t* miss_slot, int32_t* n_miss);
+               int32_t* miss_page, int32_t* miss_slot, int32_t* n_miss, const uint32_t* bits = nullptr);
 int launch_lru_reset(const ferry_lru* L, cudaStream_t st, const int32_t* req_ids, int n,
                      int lanes_per_req, const int32_t* n_pages, int32_t* ctx_pages,
                      const int64_t* pool_base, int64_t* req_base);

@@ -51,39 +51,16 @@ __global__ void wait_flag_kernel(const uint32_t* flag, uint32_t value, uint32_t 
 }
 
 
-// Switch to a device for the duration of a call and restore the caller's.
-struct DeviceGuard {
-  int prev = -1;
-  bool ok = false;
-  explicit DeviceGuard(int dev) {
-    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-    ok = cudaSetDevice(dev) == cudaSuccess;
-    if (!ok) set_error("cudaSetDevice(%d) failed", dev);
-  }
-  ~DeviceGuard() {
-    if (prev >= 0) cudaSetDevice(prev);
-  }
-};
-
-template <typename T>
-int dev_alloc(T** p, size_t count, int fill_byte) {
-  *p = nullptr;
-  if (count == 0) return FERRY_OK;
-  cudaError_t e = cudaMalloc((void**)p, count * sizeof(T));
-  if (e != cudaSuccess) {
-    *p = nullptr;
-    return cuda_status(e, "cudaMalloc");
-  }
-  FERRY_TRY(cudaMemset(*p, fill_byte, count * sizeof(T)));
-  return FERRY_OK;
-}
 
 void free_lru_state(ferry_lru* L) {
   cudaFree(L->page_slot);
   cudaFree(L->slot_page);
   cudaFree(L->order);
   cudaFree(L->size);
-  L->page_slot = L->slot_page = L->order = L->size = nullptr;
+  cudaFree(L->lane_cap);
+  cudaFree(L->mask);
+  L->page_slot = L->slot_page = L->order = L->size = L->lane_cap = nullptr;
+  L->mask = nullptr;
 }
 
 int alloc_lru_state(ferry_lru* L, int64_t lanes, int cap, int ids, uint32_t* err) {

@@ -45,11 +45,33 @@ struct LruArgs {
   int32_t* n_miss;
   uint32_t* err;
   int warp_ints;  // shared-memory ints per warp
+  const int32_t* lane_cap;  // nullable: per-lane capacity (<= cap), group lanes
+  uint32_t* mask;           // nullable: per-slot owner bits, group lanes
+  const uint32_t* bits;     // nullable: the owner bit of each row's touches
 };
 
 constexpr int kLoadBatch = 8;
 constexpr int kLruCtaMinCap = 128;  // lanes with more slots take the CTA-per-lane kernel
 constexpr int kLruRounds = 8;  // fixpoint rounds before the serial replay takes over
+
+// Owner bits of a group lane after one row's touches (the reference's
+// own_ masks, wla_multigpu.cuh:1937-1962): a page the row inserted (its
+// latest insertion, the slot's final resident) owns `bit` alone -- the mask
+// of the page it evicted was dropped with it -- and a page it hit gains `bit`.
+// Every slot an eviction frees is refilled by the miss that caused it, so no
+// other slot changes. Threads th, th + nth, ... of the caller.
+__device__ __forceinline__ void update_owner_masks(uint32_t* mk, uint32_t bit, const int32_t* sel_s,
+                                                   const int32_t* islot, const uint8_t* mflag, const int32_t* spg,
+                                                   int n, int th, int nth) {
+  for (int i = th; i < n; i += nth)
+    if (mflag[i] && spg[islot[i]] == sel_s[i]) mk[islot[i]] = bit;
+  if (nth == 32)
+    __syncwarp();
+  else
+    __syncthreads();
+  for (int i = th; i < n; i += nth)
+    if (!mflag[i] && sel_s[i] >= 0 && islot[i] >= 0 && spg[islot[i]] == sel_s[i]) atomicOr(mk + islot[i], bit);
+}
 
 __global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
   extern __shared__ int32_t smem_i[];
@@ -86,8 +108,9 @@ __global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
   int32_t* ps = A.page_slot + lane * A.ids;
   int32_t* sp = A.slot_page + lane * C;
   int32_t* od = A.order + lane * C;
+  const int Ce = A.lane_cap ? min(max(A.lane_cap[lane], 1), C) : C;  // this lane's capacity
   int sz0 = A.size[lane];
-  if (sz0 < 0 || sz0 > C) {
+  if (sz0 < 0 || sz0 > Ce) {
     if (t == 0) record_error(A.err, kErrRange);
     sz0 = 0;
   }
@@ -127,6 +150,7 @@ __global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
       const int pg = spg[s];
       if (pg >= 0 && pg < A.ids) ps[pg] = -1;
       spg[s] = -1;
+      if (A.mask) A.mask[lane * C + s] = 0u;
     }
     sz0 = 0;
   }
@@ -208,7 +232,7 @@ __global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
       nv += __popc(mv);
     }
     __syncwarp();
-    const int f = max(0, C - sz0);
+    const int f = max(0, Ce - sz0);
     int nmiss = 0, E = 0, jlast = -1;  // jlast: old position of eviction E - 1
     int kcount = 0;                    // entries in K
     bool ok = false;
@@ -340,7 +364,7 @@ __global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
         islot[i] = s;
         mflag[i] = 0;
       } else {
-        if (sz >= C) {
+        if (sz >= Ce) {
           while (p < sz0 && seq[old[p]] != -1) ++p;
           if (p < sz0) {
             s = old[p++];
@@ -397,6 +421,7 @@ __global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
       const int s = islot[i];
       if (spg[s] == sel_s[i]) ps[sel_s[i]] = s;
     }
+  if (A.mask) update_owner_masks(A.mask + lane * C, A.bits ? A.bits[a] : 0u, sel_s, islot, mflag, spg, n, t, 32);
 
   // ---- outputs
   int nm = 0;
@@ -521,8 +546,9 @@ __global__ void __launch_bounds__(kLruCtaThreads) lru_cta_kernel(LruArgs A) {
   int32_t* ps = A.page_slot + lane * A.ids;
   int32_t* sp = A.slot_page + lane * C;
   int32_t* od = A.order + lane * C;
+  const int Ce = A.lane_cap ? min(max(A.lane_cap[lane], 1), C) : C;  // this lane's capacity
   int sz0 = A.size[lane];
-  if (sz0 < 0 || sz0 > C) {
+  if (sz0 < 0 || sz0 > Ce) {
     if (tid == 0) record_error(A.err, kErrRange);
     sz0 = 0;
   }
@@ -560,6 +586,7 @@ __global__ void __launch_bounds__(kLruCtaThreads) lru_cta_kernel(LruArgs A) {
       const int pg = spg[s];
       if (pg >= 0 && pg < A.ids) ps[pg] = -1;
       spg[s] = -1;
+      if (A.mask) A.mask[lane * C + s] = 0u;
     }
     sz0 = 0;
   }
@@ -612,7 +639,7 @@ __global__ void __launch_bounds__(kLruCtaThreads) lru_cta_kernel(LruArgs A) {
     nv += tv;
   }
   __syncthreads();
-  const int f = max(0, C - sz0);
+  const int f = max(0, Ce - sz0);
   int nmiss = 0, E = 0, jlast = -1, kcount = 0;
   bool ok = false;
   for (int round = 0; round < kLruRounds; ++round) {
@@ -745,7 +772,7 @@ __global__ void __launch_bounds__(kLruCtaThreads) lru_cta_kernel(LruArgs A) {
         islot[i] = s;
         mflag[i] = 0;
       } else {
-        if (sz >= C) {
+        if (sz >= Ce) {
           while (p < sz0 && seq[old[p]] != -1) ++p;
           if (p < sz0) {
             s = old[p++];
@@ -811,6 +838,8 @@ __global__ void __launch_bounds__(kLruCtaThreads) lru_cta_kernel(LruArgs A) {
       const int s = islot[i];
       if (spg[s] == sel_s[i]) ps[sel_s[i]] = s;
     }
+  if (A.mask) update_owner_masks(A.mask + lane * C, A.bits ? A.bits[a] : 0u, sel_s, islot, mflag, spg, n, tid,
+                                 kLruCtaThreads);
 
   // ---- outputs
   int nm = 0;
@@ -882,7 +911,8 @@ __global__ void __launch_bounds__(256) lru_reset_kernel(int32_t* page_slot, int3
 int launch_lru(const ferry_lru* L, cudaStream_t st, const int32_t* lane_ids,
                const int32_t* req_ids, int lanes_per_req, const uint8_t* reset, int n,
                const int32_t* sel, int k, const int32_t* n_sel, int distinct, uint8_t* is_miss,
-               int32_t* item_slot, int32_t* miss_page, int32_t* miss_slot, int32_t* n_miss) {
+               int32_t* item_slot, int32_t* miss_page, int32_t* miss_slot, int32_t* n_miss,
+               const uint32_t* bits) {
   if (n <= 0) return FERRY_OK;
   if (k <= 0 || !sel || !n_sel || !item_slot || !miss_page || !miss_slot || !n_miss) {
     set_error("lru: bad arguments");
@@ -911,6 +941,9 @@ int launch_lru(const ferry_lru* L, cudaStream_t st, const int32_t* lane_ids,
   A.miss_slot = miss_slot;
   A.n_miss = n_miss;
   A.err = L->err;
+  A.lane_cap = L->lane_cap;
+  A.mask = L->mask;
+  A.bits = bits;
   // old, spg, seq (cap each) + sel, islot, prev, newl, evict (k each) + k flag bytes
   A.warp_ints = lru_lane_ints(L->cap, k);
   const size_t per_warp = (size_t)A.warp_ints * 4;

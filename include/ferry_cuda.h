@@ -519,6 +519,63 @@ int ferry_lru_touch(ferry_lru* lru, void* stream, const int32_t* d_lane_ids,
 int ferry_lru_read(ferry_lru* lru, int lane, int32_t* page_slot, int32_t* lru_slots,
                    int32_t* size);
 
+/* ---- group lanes: the reference's prefix-group-shared LRU mirror ----------
+ * kv_touch keyed by (GPU, prefix group, layer) with cap_mode, ownership masks
+ * and steal-time handoff (src/runtime/wla_multigpu.cuh:1867-2015). A group
+ * lane is a ferry_lru lane that every member of a prefix group touches, in
+ * request order (one launch per member: a launch must list each lane once).
+ * ferry_lru_group_enable adds a capacity per lane (starting at the lru's
+ * capacity) and an owner mask per resident page (one bit per member, the
+ * reference's own_bit = 1 << (request % prefix_group), :1877-1879).
+ *   ferry_lru_touch_owned   ferry_lru_touch (same outputs) whose row i ORs
+ *                           d_bits[i] into the mask of every page it touches;
+ *                           a page it inserts owns d_bits[i] alone (the
+ *                           evicted page's mask is dropped: own_drop)
+ *   ferry_lru_set_capacity  new capacities (1..capacity) of the listed lanes;
+ *                           a lane above its new capacity is trimmed from its
+ *                           LRU front (grp_trim, :1923-1935, cap_mode 1:
+ *                           capacity = hot x resident members). Survivors at
+ *                           slots >= the new capacity move, in LRU order, into
+ *                           the freed slots below it, ascending, so the
+ *                           occupied slots stay [0, size)
+ *   ferry_lru_release       clear `bit` in every mask of the lanes (own_release)
+ *   ferry_lru_count_owned   d_count[i]: pages of lane i whose mask is exactly
+ *                           `bit` (kv_live_owned, :1912-1921)
+ *   ferry_lru_handoff       a steal's hot-set handoff from src lanes to the
+ *                           consumer's dst lanes (kv_handoff, :1970-1990):
+ *                           FERRY_HANDOFF_DROP empties the dst lanes (src
+ *                           unused); FERRY_HANDOFF_CARRY makes each dst lane a
+ *                           copy of its src lane (same capacity; a src lane
+ *                           larger than the dst lane's capacity is a range
+ *                           error); FERRY_HANDOFF_OWNED merges the src pages
+ *                           whose mask is exactly `bit` into the dst lane in
+ *                           src LRU order -- a page already resident there
+ *                           gains `bit` and keeps its place, otherwise the dst
+ *                           lane evicts its front while full and appends it
+ *                           (kv_handoff_owned, :1991-2015). src may live on a
+ *                           peer GPU (read over NVLink).
+ *   ferry_lru_read_owned    synchronous host copy of a lane's masks (capacity
+ *                           entries, by slot) and its capacity
+ * Range errors of these kernels are recorded in the lru's error word and
+ * returned by ferry_lru_read. */
+#define FERRY_HANDOFF_DROP 0
+#define FERRY_HANDOFF_CARRY 1
+#define FERRY_HANDOFF_OWNED 2
+int ferry_lru_group_enable(ferry_lru* lru);
+int ferry_lru_touch_owned(ferry_lru* lru, void* stream, const int32_t* d_lane_ids,
+                          const uint8_t* d_reset, int n, const int32_t* d_sel, int k,
+                          const int32_t* d_n_sel, int flags, const uint32_t* d_bits,
+                          uint8_t* d_is_miss, int32_t* d_item_slot, int32_t* d_miss_page,
+                          int32_t* d_miss_slot, int32_t* d_n_miss);
+int ferry_lru_set_capacity(ferry_lru* lru, void* stream, const int32_t* d_lane_ids,
+                           const int32_t* d_caps, int n);
+int ferry_lru_release(ferry_lru* lru, void* stream, const int32_t* d_lane_ids, int n, uint32_t bit);
+int ferry_lru_count_owned(ferry_lru* lru, void* stream, const int32_t* d_lane_ids, int n,
+                          uint32_t bit, int32_t* d_count);
+int ferry_lru_handoff(ferry_lru* dst, void* stream, const ferry_lru* src, const int32_t* d_src_lanes,
+                      const int32_t* d_dst_lanes, int n, int mode, uint32_t bit);
+int ferry_lru_read_owned(ferry_lru* lru, int lane, uint32_t* masks, int32_t* capacity);
+
 #ifdef __cplusplus
 }
 #endif

@@ -69,6 +69,15 @@ def lib():
         L.orc_lru_destroy.argtypes = [C.c_void_p]
         L.orc_lru_step.argtypes = [C.c_void_p, C.c_int] + [C.c_void_p] * 3 + [C.c_int] + [C.c_void_p] * 6
         L.orc_lru_state.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
+        L.orc_lru_group_enable.argtypes = [C.c_void_p]
+        L.orc_lru_touch_owned.argtypes = ([C.c_void_p, C.c_int] + [C.c_void_p] * 3 + [C.c_int]
+                                          + [C.c_void_p] * 7)
+        L.orc_lru_set_capacity.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
+        L.orc_lru_release.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_uint32]
+        L.orc_lru_count_owned.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_uint32, C.c_void_p]
+        L.orc_lru_handoff.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
+                                      C.c_uint32]
+        L.orc_lru_owned_state.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
         L.orc_kv_elem.restype = C.c_uint16
         L.orc_kv_elem.argtypes = [C.c_uint64, C.c_uint64, C.c_uint32]
         L.orc_kv_gen.argtypes = [C.c_uint64, C.c_uint64, C.c_int64, C.c_void_p]
@@ -220,6 +229,64 @@ class LruLanes:
         size = np.zeros(1, np.int32)
         lib().orc_lru_state(self.h, lane, ps.ctypes.data, order.ctypes.data, size.ctypes.data)
         return ps, order[: size[0]].copy(), int(size[0])
+
+    # ---- group lanes: the reference's kv_touch / grp_trim / own_* / kv_handoff
+    def group_enable(self):
+        lib().orc_lru_group_enable(self.h)
+
+    def step_owned(self, lane_ids, sel, bits, n_sel=None, reset=None):
+        lane_ids = np.ascontiguousarray(lane_ids, np.int32)
+        sel = np.ascontiguousarray(sel, np.int32)
+        bits = np.ascontiguousarray(bits, np.uint32)
+        n, k = sel.shape
+        n_sel = np.full(n, k, np.int32) if n_sel is None else np.ascontiguousarray(n_sel, np.int32)
+        reset = np.zeros(n, np.uint8) if reset is None else np.ascontiguousarray(reset, np.uint8)
+        is_miss = np.zeros((n, k), np.uint8)
+        item_slot = np.full((n, k), -1, np.int32)
+        mp = np.full((n, k), -1, np.int32)
+        ms = np.full((n, k), -1, np.int32)
+        nm = np.zeros(n, np.int32)
+        rc = lib().orc_lru_touch_owned(self.h, n, lane_ids.ctypes.data, reset.ctypes.data, sel.ctypes.data, k,
+                                       n_sel.ctypes.data, bits.ctypes.data, is_miss.ctypes.data,
+                                       item_slot.ctypes.data, mp.ctypes.data, ms.ctypes.data, nm.ctypes.data)
+        if rc != 0:
+            raise ValueError(f"orc_lru_touch_owned rc={rc}")
+        return is_miss, item_slot, mp, ms, nm
+
+    def set_capacity(self, lane_ids, caps):
+        lane_ids = np.ascontiguousarray(lane_ids, np.int32)
+        caps = np.ascontiguousarray(caps, np.int32)
+        rc = lib().orc_lru_set_capacity(self.h, len(lane_ids), lane_ids.ctypes.data, caps.ctypes.data)
+        if rc != 0:
+            raise ValueError(f"orc_lru_set_capacity rc={rc}")
+
+    def release(self, lane_ids, bit: int):
+        lane_ids = np.ascontiguousarray(lane_ids, np.int32)
+        if lib().orc_lru_release(self.h, len(lane_ids), lane_ids.ctypes.data, bit) != 0:
+            raise ValueError("orc_lru_release")
+
+    def count_owned(self, lane_ids, bit: int) -> np.ndarray:
+        lane_ids = np.ascontiguousarray(lane_ids, np.int32)
+        out = np.zeros(len(lane_ids), np.int32)
+        if lib().orc_lru_count_owned(self.h, len(lane_ids), lane_ids.ctypes.data, bit, out.ctypes.data) != 0:
+            raise ValueError("orc_lru_count_owned")
+        return out
+
+    def handoff(self, src: "LruLanes", src_lanes, dst_lanes, mode: int, bit: int = 0):
+        """mode 0 drop, 1 carry, 2 owned (into this object's dst lanes)."""
+        dst_lanes = np.ascontiguousarray(dst_lanes, np.int32)
+        src_lanes = np.ascontiguousarray(src_lanes if src_lanes is not None else dst_lanes, np.int32)
+        rc = lib().orc_lru_handoff(self.h, src.h, len(dst_lanes), src_lanes.ctypes.data, dst_lanes.ctypes.data,
+                                   mode, bit)
+        if rc != 0:
+            raise ValueError(f"orc_lru_handoff rc={rc}")
+
+    def owned_state(self, lane: int):
+        masks = np.zeros(self.cap, np.uint32)
+        cap = np.zeros(1, np.int32)
+        if lib().orc_lru_owned_state(self.h, lane, masks.ctypes.data, cap.ctypes.data) != 0:
+            raise ValueError("orc_lru_owned_state")
+        return masks, int(cap[0])
 
 
 # --------------------------------------------------------------------------- KV, selection, attention

@@ -31,6 +31,7 @@
 #include <deque>
 #include <random>
 #include <thread>
+#include <unordered_map>
 #include <unordered_set>
 #include <vector>
 
@@ -251,6 +252,11 @@ struct OrcLru {
   int lanes, cap, ids;
   std::vector<int32_t> page_slot;            // lanes*ids, -1 = absent
   std::vector<std::deque<int32_t>> order;    // LRU front .. MRU back (page ids)
+  // group lanes: capacity per lane and owner masks keyed by page id (the
+  // reference's own_ maps, src/runtime/wla_multigpu.cuh:1872-1916); empty
+  // until orc_lru_group_enable
+  std::vector<int> lane_cap;
+  std::vector<std::unordered_map<int32_t, uint32_t>> own;
 };
 
 void* orc_lru_create(int lanes, int capacity, int ids) {
@@ -268,19 +274,21 @@ void orc_lru_destroy(void* p) { delete (OrcLru*)p; }
 // items of row i are valid. reset[i] != 0 empties the lane first.
 // Outputs (n_active x k): is_miss, item_slot, miss_page/miss_slot compacted per
 // row in selection order, n_miss[i].
-int orc_lru_step(void* p, int n_active, const int32_t* lane_ids, const uint8_t* reset,
-                 const int32_t* sel, int k, const int32_t* n_sel, uint8_t* is_miss,
-                 int32_t* item_slot, int32_t* miss_page, int32_t* miss_slot,
-                 int32_t* n_miss) {
-  auto* h = (OrcLru*)p;
+static int lru_step(OrcLru* h, int n_active, const int32_t* lane_ids, const uint8_t* reset,
+                    const int32_t* sel, int k, const int32_t* n_sel, const uint32_t* bits,
+                    uint8_t* is_miss, int32_t* item_slot, int32_t* miss_page, int32_t* miss_slot,
+                    int32_t* n_miss) {
+  const bool group = !h->lane_cap.empty();
   for (int a = 0; a < n_active; ++a) {
     const int lane = lane_ids[a];
     if (lane < 0 || lane >= h->lanes) return -1;
     int32_t* ps = &h->page_slot[(size_t)lane * h->ids];
     auto& dq = h->order[lane];
+    const int cap = group ? h->lane_cap[lane] : h->cap;
     if (reset && reset[a]) {
       for (int32_t pg : dq) ps[pg] = -1;
       dq.clear();
+      if (group) h->own[lane].clear();
     }
     int nm = 0;
     for (int i = 0; i < n_sel[a]; ++i) {
@@ -292,11 +300,12 @@ int orc_lru_step(void* p, int n_active, const int32_t* lane_ids, const uint8_t* 
         dq.erase(std::find(dq.begin(), dq.end(), x));
         dq.push_back(x);
       } else {
-        if ((int)dq.size() >= h->cap) {
+        if ((int)dq.size() >= cap) {
           const int32_t v = dq.front();
           dq.pop_front();
           s = ps[v];
           ps[v] = -1;
+          if (group) h->own[lane].erase(v);  // own_drop
         } else {
           s = (int32_t)dq.size();
         }
@@ -308,9 +317,176 @@ int orc_lru_step(void* p, int n_active, const int32_t* lane_ids, const uint8_t* 
       }
       is_miss[(size_t)a * k + i] = hit ? 0 : 1;
       item_slot[(size_t)a * k + i] = s;
+      if (group && bits) h->own[lane][x] |= bits[a];  // kv_touch: the toucher needs it
     }
     n_miss[a] = nm;
   }
+  return 0;
+}
+
+int orc_lru_step(void* p, int n_active, const int32_t* lane_ids, const uint8_t* reset,
+                 const int32_t* sel, int k, const int32_t* n_sel, uint8_t* is_miss,
+                 int32_t* item_slot, int32_t* miss_page, int32_t* miss_slot,
+                 int32_t* n_miss) {
+  return lru_step((OrcLru*)p, n_active, lane_ids, reset, sel, k, n_sel, nullptr, is_miss, item_slot,
+                  miss_page, miss_slot, n_miss);
+}
+
+// ---- group lanes (kv_touch / grp_trim / own_* / kv_handoff of the reference,
+// src/runtime/wla_multigpu.cuh:1867-2015) with this build's slot rules:
+// occupied slots stay [0, size); a trim moves the survivors at slots >= the
+// new capacity, in LRU order, into the freed slots below it, ascending.
+int orc_lru_group_enable(void* p) {
+  auto* h = (OrcLru*)p;
+  if (h->lane_cap.empty()) {
+    h->lane_cap.assign(h->lanes, h->cap);
+    h->own.assign(h->lanes, {});
+  }
+  return 0;
+}
+
+int orc_lru_touch_owned(void* p, int n_active, const int32_t* lane_ids, const uint8_t* reset,
+                        const int32_t* sel, int k, const int32_t* n_sel, const uint32_t* bits,
+                        uint8_t* is_miss, int32_t* item_slot, int32_t* miss_page, int32_t* miss_slot,
+                        int32_t* n_miss) {
+  auto* h = (OrcLru*)p;
+  if (h->lane_cap.empty()) return -3;
+  return lru_step(h, n_active, lane_ids, reset, sel, k, n_sel, bits, is_miss, item_slot, miss_page,
+                  miss_slot, n_miss);
+}
+
+// grp_trim (:1923-1935) after a capacity change (cap_mode 1)
+int orc_lru_set_capacity(void* p, int n, const int32_t* lane_ids, const int32_t* caps) {
+  auto* h = (OrcLru*)p;
+  if (h->lane_cap.empty()) return -3;
+  for (int a = 0; a < n; ++a) {
+    const int lane = lane_ids[a], c = caps[a];
+    if (lane < 0 || lane >= h->lanes || c < 1 || c > h->cap) return -1;
+    h->lane_cap[lane] = c;
+    auto& dq = h->order[lane];
+    int32_t* ps = &h->page_slot[(size_t)lane * h->ids];
+    std::vector<char> freed(c, 0);
+    while ((int)dq.size() > c) {
+      const int32_t v = dq.front();
+      h->own[lane].erase(v);
+      if (ps[v] < c) freed[ps[v]] = 1;
+      ps[v] = -1;
+      dq.pop_front();
+    }
+    std::vector<int32_t> fr;
+    for (int s2 = 0; s2 < c; ++s2)
+      if (freed[s2]) fr.push_back(s2);
+    size_t r = 0;
+    for (int32_t pg : dq)
+      if (ps[pg] >= c) {
+        if (r >= fr.size()) return -4;
+        ps[pg] = fr[r++];
+      }
+  }
+  return 0;
+}
+
+// own_release (:1896-1911)
+int orc_lru_release(void* p, int n, const int32_t* lane_ids, uint32_t bit) {
+  auto* h = (OrcLru*)p;
+  if (h->lane_cap.empty()) return -3;
+  for (int a = 0; a < n; ++a) {
+    const int lane = lane_ids[a];
+    if (lane < 0 || lane >= h->lanes) return -1;
+    auto& m = h->own[lane];
+    for (auto it = m.begin(); it != m.end();) {
+      it->second &= ~bit;
+      if (it->second == 0)
+        it = m.erase(it);
+      else
+        ++it;
+    }
+  }
+  return 0;
+}
+
+// kv_live_owned (:1912-1921), per lane
+int orc_lru_count_owned(void* p, int n, const int32_t* lane_ids, uint32_t bit, int32_t* out) {
+  auto* h = (OrcLru*)p;
+  if (h->lane_cap.empty()) return -3;
+  for (int a = 0; a < n; ++a) {
+    const int lane = lane_ids[a];
+    if (lane < 0 || lane >= h->lanes) return -1;
+    int c = 0;
+    for (int32_t pg : h->order[lane]) {
+      auto it = h->own[lane].find(pg);
+      c += (it != h->own[lane].end() && it->second == bit);
+    }
+    out[a] = c;
+  }
+  return 0;
+}
+
+// kv_handoff (:1970-1990) and kv_handoff_owned (:1991-2015); mode 0 drop,
+// 1 carry, 2 owned
+int orc_lru_handoff(void* pd, void* psrc, int n, const int32_t* src_lanes, const int32_t* dst_lanes, int mode,
+                    uint32_t bit) {
+  auto* d = (OrcLru*)pd;
+  auto* sr = (OrcLru*)psrc;
+  if (d->lane_cap.empty() || (mode != 0 && sr->lane_cap.empty())) return -3;
+  for (int a = 0; a < n; ++a) {
+    const int dl = dst_lanes[a];
+    if (dl < 0 || dl >= d->lanes) return -1;
+    int32_t* dps = &d->page_slot[(size_t)dl * d->ids];
+    auto& ddq = d->order[dl];
+    if (mode == 0) {
+      for (int32_t pg : ddq) dps[pg] = -1;
+      ddq.clear();
+      d->own[dl].clear();
+      continue;
+    }
+    const int sl = src_lanes[a];
+    if (sl < 0 || sl >= sr->lanes) return -1;
+    const int32_t* sps = &sr->page_slot[(size_t)sl * sr->ids];
+    const auto& sdq = sr->order[sl];
+    if (mode == 1) {
+      if ((int)sdq.size() > d->lane_cap[dl]) return -5;
+      for (int32_t pg : ddq) dps[pg] = -1;
+      ddq = sdq;
+      for (int32_t pg : ddq) dps[pg] = sps[pg];
+      d->own[dl] = sr->own[sl];
+      continue;
+    }
+    const int cap = d->lane_cap[dl];
+    for (int32_t pg : sdq) {
+      auto it = sr->own[sl].find(pg);
+      if (it == sr->own[sl].end() || it->second != bit) continue;  // shared / dead: not moved
+      if (dps[pg] >= 0) {
+        d->own[dl][pg] |= bit;
+        continue;
+      }
+      int32_t slot;
+      if ((int)ddq.size() >= cap) {
+        const int32_t v = ddq.front();
+        ddq.pop_front();
+        d->own[dl].erase(v);
+        slot = dps[v];
+        dps[v] = -1;
+      } else {
+        slot = (int32_t)ddq.size();
+      }
+      ddq.push_back(pg);
+      dps[pg] = slot;
+      d->own[dl][pg] |= bit;
+    }
+  }
+  return 0;
+}
+
+// masks of one lane by slot (0 where no page or no owner) and its capacity
+int orc_lru_owned_state(void* p, int lane, uint32_t* masks, int32_t* capacity) {
+  auto* h = (OrcLru*)p;
+  if (h->lane_cap.empty() || lane < 0 || lane >= h->lanes) return -1;
+  const int32_t* ps = &h->page_slot[(size_t)lane * h->ids];
+  std::memset(masks, 0, sizeof(uint32_t) * h->cap);
+  for (const auto& kv : h->own[lane])
+    if (ps[kv.first] >= 0) masks[ps[kv.first]] = kv.second;
+  *capacity = h->lane_cap[lane];
   return 0;
 }
 

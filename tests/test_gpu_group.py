@@ -213,3 +213,46 @@ def test_group_handoff_drop_carry_and_errors(torch_cuda):
     finally:
         a.close()
         b.close()
+
+
+def test_group_lanes_replay_cap_mode_1(torch_cuda):
+    """The reference's prefix-shared block stream (prefix group 4, 8 shared
+    steps) on group lanes with cap_mode 1 capacities, hot x members
+    (wla_group_cap, src/workloads/missstream.cuh:91-94; wla_recompute_stats,
+    src/runtime/wla_multigpu.cuh:376-417): lanes allocated at twice that,
+    capacities set per lane; the device misses equal the oracle's totals,
+    and the larger group capacity hits more often than cap_mode 0."""
+    import oracle
+    from ferry_b200 import _abi
+
+    t = torch_cuda
+    pg = 4
+    sp1 = oracle.miss_spec(prefix_group=pg, prefix_steps=8, cap_mode=1)
+    sp0 = oracle.miss_spec(prefix_group=pg, prefix_steps=8, cap_mode=0)
+    R, L_, S, G, hot = sp1.num_requests, sp1.num_layers, sp1.steps, sp1.sel_blocks, sp1.hot_blocks
+    blocks, _, _ = oracle.replay_miss_stream(sp1)
+    shared, tot1 = oracle.prefix_share_stats(sp1, blocks.copy())
+    _, tot0 = oracle.prefix_share_stats(sp0, blocks.copy())
+    B = shared.reshape(R, S, L_, G).astype(np.int32)
+    ngrp, ids = R // pg, 64 + 8 * S
+    dev = DevLanes.__new__(DevLanes)
+    dev.t, dev.a, dev.dev, dev.ids, dev.cap = t, _abi, t.device("cuda", 0), ids, 2 * hot * pg
+    dev.h = C.c_void_p()
+    _abi.call("ferry_lru_create", 0, ngrp * L_, dev.cap, ids, C.byref(dev.h))
+    try:
+        _abi.call("ferry_lru_group_enable", dev.h)
+        lanes = (np.arange(ngrp)[:, None] * L_ + np.arange(L_)[None]).ravel().astype(np.int32)
+        dev.set_capacity(lanes, np.full(len(lanes), hot * pg, np.int32))
+        misses = 0
+        for m in range(pg):
+            for s in range(S):
+                sel = B[np.arange(ngrp) * pg + m, s].reshape(ngrp * L_, G)
+                *_, nm = dev.touch(lanes, sel, 1 << m, distinct=False)
+                misses += int(nm.sum())
+        assert misses == int(tot1[1]) and misses < int(tot0[1])
+        # every resident page was touched by some member
+        for lane in lanes[:4]:
+            ps, order, n, masks, cap = dev.state(int(lane))
+            assert cap == hot * pg and n <= cap and (masks[:n] != 0).all()
+    finally:
+        dev.close()

@@ -33,10 +33,22 @@
 namespace ferry {
 namespace {
 
-constexpr int kAttnWarps = 4;
-constexpr int kStages = 2;
+// warps per CTA and bulk-copy stages per warp (build-time tunables)
+#ifndef FERRY_ATTN_WARPS
+#define FERRY_ATTN_WARPS 4
+#endif
+#ifndef FERRY_ATTN_STAGES
+#define FERRY_ATTN_STAGES 2
+#endif
+constexpr int kAttnWarps = FERRY_ATTN_WARPS;
+constexpr int kStages = FERRY_ATTN_STAGES;
 constexpr uint32_t kFull = 0xffffffffu;
 constexpr size_t kAttnSmem = (size_t)kAttnWarps * (kStages * kUnitBytes + kStages * 8 + 64);
+// CTAs resident per SM: 228 KiB of shared memory per SM, 1 KiB reserved per CTA
+constexpr int kAttnCtasPerSm = (int)((228u * 1024u) / (kAttnSmem + 1024u)) < 8
+                                   ? (int)((228u * 1024u) / (kAttnSmem + 1024u))
+                                   : 8;
+static_assert(kAttnCtasPerSm >= 1, "attention ring does not fit an SM");
 
 struct AttnArgs {
   const uint16_t* q;
@@ -83,7 +95,7 @@ __device__ __forceinline__ int warp_of(int64_t x, int nw, int64_t T) {
 }
 
 template <int G>
-__global__ void __launch_bounds__(kAttnWarps * 32, 3) attn_kernel(AttnArgs A) {
+__global__ void __launch_bounds__(kAttnWarps * 32, kAttnCtasPerSm) attn_kernel(AttnArgs A) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, t = threadIdx.x & 31;
   const int w = blockIdx.x * kAttnWarps + warp;
@@ -329,7 +341,7 @@ int launch_attn(const AttnArgs& A, int group, cudaStream_t st) {
   }
 }
 
-int resident_warps(int sms) { return sms * 3 * kAttnWarps; }
+int resident_warps(int sms) { return sms * kAttnCtasPerSm * kAttnWarps; }
 
 }  // namespace
 

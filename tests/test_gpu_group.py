@@ -65,18 +65,20 @@ class DevLanes:
         t.cuda.synchronize(self.dev)
         return im.cpu().numpy(), isl.cpu().numpy(), mp.cpu().numpy(), ms.cpu().numpy(), nm.cpu().numpy()
 
+    # device copies are held in locals until the launch is queued: a temporary
+    # freed early hands its memory to the next copy, and two arguments alias
     def set_capacity(self, lanes, caps):
-        self.a.call("ferry_lru_set_capacity", self.h, self.stream(), self.p(self.d(lanes.astype(np.int32))),
-                    self.p(self.d(caps.astype(np.int32))), len(lanes))
+        l, c = self.d(lanes.astype(np.int32)), self.d(caps.astype(np.int32))
+        self.a.call("ferry_lru_set_capacity", self.h, self.stream(), self.p(l), self.p(c), len(lanes))
 
     def release(self, lanes, bit):
-        self.a.call("ferry_lru_release", self.h, self.stream(), self.p(self.d(lanes.astype(np.int32))), len(lanes),
-                    bit)
+        l = self.d(lanes.astype(np.int32))
+        self.a.call("ferry_lru_release", self.h, self.stream(), self.p(l), len(lanes), bit)
 
     def count_owned(self, lanes, bit):
         out = self.t.zeros(len(lanes), dtype=self.t.int32, device=self.dev)
-        self.a.call("ferry_lru_count_owned", self.h, self.stream(), self.p(self.d(lanes.astype(np.int32))),
-                    len(lanes), bit, self.p(out))
+        l = self.d(lanes.astype(np.int32))
+        self.a.call("ferry_lru_count_owned", self.h, self.stream(), self.p(l), len(lanes), bit, self.p(out))
         return out.cpu().numpy()
 
     def handoff(self, src, lanes, mode, bit):

@@ -579,6 +579,8 @@ def main():
     ap.add_argument("--batch", type=int, default=32, help="cfg3s/cfg4s: requests decoded per GPU per tick")
     ap.add_argument("--append", type=int, default=None,
                     help="tokens each decode step appends to its context (default: the workload's)")
+    ap.add_argument("--chunks", type=int, default=1,
+                    help="cfg5 / cfg5s: pipeline each step over this many request chunks (ferry_step_chunks)")
     ap.add_argument("--requests", type=int, default=None,
                     help="cfg5 / cfg5s: requests of the job (default: the config's 32)")
     ap.add_argument("--replicas", action="store_true",
@@ -1048,6 +1050,7 @@ def run_owner(args):
                           (C.c_uint8 * _abi.CTX_HANDLE_BYTES).from_buffer_copy(allh[p]))
                 slot += 1
     dec.gather_source(_abi.SRC_OWNER)
+    dec.step_chunks(max(1, min(args.chunks, R)))
     g_ids = np.arange(rank * R, (rank + 1) * R)
     ids = torch.arange(R, dtype=torch.int32, device=dev)
     base = torch.from_numpy(g_ids.astype(np.int64) * LH * N).to(dev)
@@ -1135,7 +1138,8 @@ def run_owner(args):
                            else "configs[4] slice: 2 of 80 layers", "layers": w.num_layers, "requests": total,
                            "requests_per_gpu": R, "ctx_tokens": w.ctx_tokens, "heads": [w.q_heads, w.kv_heads],
                            "top_k": w.top_k, "cache_pages": w.cache_pages, "kv_dtype": "e4m3",
-                           "page_owner": f"page id mod {ws}", "parallelism": f"{ws} ranks, owner-store gathers"},
+                           "page_owner": f"page id mod {ws}", "parallelism": f"{ws} ranks, owner-store gathers",
+                           "step_chunks": max(1, min(args.chunks, R))},
                 "miss_gather": {"bytes_per_step": gb / args.steps,
                                 "share_from_peer_gpus": peer_b / gb if gb else 0.0,
                                 "share_from_own_hbm": self_b / gb if gb else 0.0,

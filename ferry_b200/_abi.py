@@ -25,7 +25,7 @@ EXPORTS = [
     "ferry_last_error", "ferry_version", "ferry_ctx_create", "ferry_ctx_destroy",
     "ferry_ctx_check", "ferry_host_alloc", "ferry_host_free", "ferry_kv_register",
     "ferry_kv_generate", "ferry_page_summary_update", "ferry_requests_begin",
-    "ferry_requests_append", "ferry_decode_appends",
+    "ferry_requests_append", "ferry_decode_appends", "ferry_step_chunks",
     "ferry_select_mode", "ferry_select_topk", "ferry_detect_misses", "ferry_gather_misses", "ferry_sparse_decode",
     "ferry_sparse_decode_noalloc", "ferry_sparse_decode_noalloc_status", "ferry_decode_step", "ferry_wait_flag", "ferry_stats_read", "ferry_debug_read",
     "ferry_ctx_export", "ferry_store_create", "ferry_store_fill", "ferry_gather_source",
@@ -105,6 +105,7 @@ _SIGS = {
     "ferry_select_mode": (I, [V, I]),
     "ferry_requests_append": (I, [V, V, V, I, I]),
     "ferry_decode_appends": (I, [V, I]),
+    "ferry_step_chunks": (I, [V, I]),
     "ferry_select_topk": (I, [V, V, V, V, I, V, V]),
     "ferry_detect_misses": (I, [V, V, V, I, V, V, V, V, V, V, V]),
     "ferry_gather_misses": (I, [V, V, V, I, V, V, V]),

@@ -249,6 +249,13 @@ struct ferry_ctx {
   int32_t* ctx_pages = nullptr;  // 2R: full pages of each request's context, then the tokens of
                                  // its partial last page (0..15; decode appends)
   int append_tokens = 0;         // tokens ferry_decode_step appends per request (0 = fixed context)
+  // pipelined step (ferry_step_chunks): request chunks whose selection runs on
+  // the caller's stream while the previous chunk's detect / gather / attention
+  // run on `side`
+  int step_chunks = 1;
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+  cudaEvent_t ev_sel[16] = {};
   int64_t* req_base = nullptr;   // R: pool unit of the request's (lane 0, page 0)
 
   // host pool

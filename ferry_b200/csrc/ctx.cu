@@ -95,6 +95,11 @@ void destroy_ctx(ferry_ctx* c) {
   cudaFree(c->quest_done);
   cudaFree(c->err);
   cudaFree(c->stats);
+  for (cudaEvent_t& e : c->ev_sel)
+    if (e) cudaEventDestroy(e);
+  if (c->ev_fork) cudaEventDestroy(c->ev_fork);
+  if (c->ev_join) cudaEventDestroy(c->ev_join);
+  if (c->side) cudaStreamDestroy(c->side);
   delete c;
 }
 
@@ -399,15 +404,61 @@ int ferry_decode_step(ferry_ctx* c, void* stream, const uint16_t* d_q, const int
     return set_error("decode_step: appends read the new pages from the host pool"), FERRY_E_STATE;
   DeviceGuard guard(c->device);
   cudaStream_t st = (cudaStream_t)stream;
-  if ((rc = launch_select(c, st, d_q, d_req_ids, n_req, c->ws_sel, c->ws_nsel))) return rc;
-  if ((rc = launch_lru(&c->lru, st, nullptr, d_req_ids, c->lanes_per_req, nullptr,
-                       n_req * c->lanes_per_req, c->ws_sel, c->cfg.top_k, c->ws_nsel, 1, nullptr,
-                       c->ws_islot, c->ws_mpage, c->ws_mslot, c->ws_nmiss)))
-    return rc;
-  if ((rc = launch_gather(c, st, d_req_ids, n_req, c->ws_mpage, c->ws_mslot, c->ws_nmiss))) return rc;
-  if ((rc = launch_attention_any(c, st, d_q, d_req_ids, n_req, c->ws_islot, c->ws_nsel, d_out))) return rc;
+  const int LH = c->lanes_per_req, k = c->cfg.top_k;
+  const size_t qrow = (size_t)c->cfg.num_layers * c->cfg.q_heads * kHeadDim;  // q / out elements per request
+  // requests [s0, s0 + n) of the batch: detect, gather, attention on `ss`
+  auto rest = [&](cudaStream_t ss, int s0, int n) -> int {
+    const size_t l0 = (size_t)s0 * LH;
+    int r;
+    if ((r = launch_lru(&c->lru, ss, nullptr, d_req_ids + s0, LH, nullptr, n * LH, c->ws_sel + l0 * k, k,
+                        c->ws_nsel + l0, 1, nullptr, c->ws_islot + l0 * k, c->ws_mpage + l0 * k,
+                        c->ws_mslot + l0 * k, c->ws_nmiss + l0)))
+      return r;
+    if ((r = launch_gather(c, ss, d_req_ids + s0, n, c->ws_mpage + l0 * k, c->ws_mslot + l0 * k, c->ws_nmiss + l0)))
+      return r;
+    return launch_attention_any(c, ss, d_q + (size_t)s0 * qrow, d_req_ids + s0, n, c->ws_islot + l0 * k,
+                                c->ws_nsel + l0, d_out + (size_t)s0 * qrow);
+  };
+  const int nch = std::min(c->step_chunks, n_req);
+  if (nch <= 1 || !c->side) {
+    if ((rc = launch_select(c, st, d_q, d_req_ids, n_req, c->ws_sel, c->ws_nsel))) return rc;
+    if ((rc = rest(st, 0, n_req))) return rc;
+  } else {
+    // chunk i's selection (HBM-bound) overlaps chunk i-1's gather, which with
+    // owner stores on peers is NVLink-bound; every chunk keeps its own rows of
+    // the workspace, and kernels that share scratch stay on one stream each
+    // (selections on st; detect, gather, attention on side)
+    const int per = (n_req + nch - 1) / nch;
+    FERRY_TRY(cudaEventRecord(c->ev_fork, st));
+    FERRY_TRY(cudaStreamWaitEvent(c->side, c->ev_fork, 0));
+    for (int i = 0, s0 = 0; s0 < n_req; ++i, s0 += per) {
+      const int n = std::min(per, n_req - s0);
+      const size_t l0 = (size_t)s0 * LH;
+      if ((rc = launch_select(c, st, d_q + (size_t)s0 * qrow, d_req_ids + s0, n, c->ws_sel + l0 * k,
+                              c->ws_nsel + l0)))
+        return rc;
+      FERRY_TRY(cudaEventRecord(c->ev_sel[i], st));
+      FERRY_TRY(cudaStreamWaitEvent(c->side, c->ev_sel[i], 0));
+      if ((rc = rest(c->side, s0, n))) return rc;
+    }
+    FERRY_TRY(cudaEventRecord(c->ev_join, c->side));
+    FERRY_TRY(cudaStreamWaitEvent(st, c->ev_join, 0));
+  }
   // the token decoded in this step joins its request's context
   return c->append_tokens > 0 ? launch_append(c, st, d_req_ids, n_req, c->append_tokens) : FERRY_OK;
+}
+
+int ferry_step_chunks(ferry_ctx* c, int chunks) {
+  if (!c || chunks < 1 || chunks > 16) return set_error("step_chunks: 1..16 chunks"), FERRY_E_INVAL;
+  DeviceGuard guard(c->device);
+  if (chunks > 1 && !c->side) {
+    FERRY_TRY(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking));
+    FERRY_TRY(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming));
+    FERRY_TRY(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming));
+    for (cudaEvent_t& e : c->ev_sel) FERRY_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  }
+  c->step_chunks = chunks;
+  return FERRY_OK;
 }
 
 int ferry_requests_append(ferry_ctx* c, void* stream, const int32_t* d_req_ids, int n, int tokens) {

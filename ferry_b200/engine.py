@@ -177,6 +177,11 @@ class Decoder:
     def gather_source(self, source: int):
         call("ferry_gather_source", self.ctx, source)
 
+    def step_chunks(self, chunks: int):
+        """Pipeline step(): chunk i's selection overlaps chunk i-1's detect,
+        gather and attention (1 = no pipelining)."""
+        call("ferry_step_chunks", self.ctx, chunks)
+
     def register_stores(self, units: int):
         """No host pool: summary rows for `units` pool units, misses from the
         owner stores only (after store_create)."""

@@ -269,3 +269,37 @@ def test_stores_only_rejects_host_paths_and_unmapped_owners(torch_cuda):
         assert e.value.code == _abi.E_RANGE
     finally:
         d.close()
+
+
+@pytest.mark.parametrize("world,kv_dtype,chunks", [(2, "e4m3", 3), (3, "f16", 4), (1, "f16", 2)])
+def test_pipelined_step_matches_plain_step(torch_cuda, world, kv_dtype, chunks):
+    """ferry_step_chunks: each chunk's selection on the caller's stream
+    overlaps the previous chunk's detect / gather / attention on the ctx's
+    side stream; outputs, cache bytes and gather counts equal the plain
+    step's."""
+    from ferry_b200 import _abi
+    from ferry_b200.engine import Decoder
+
+    t = torch_cuda
+    dev = t.device("cuda", 0)
+    w, decs = _job(t, world, [0] * world, kv_dtype)
+    plain = Decoder(w, 0)
+    try:
+        plain.register_pool()
+        reqs = list(range(w.num_requests))
+        decs[0].gather_source(_abi.SRC_OWNER)
+        decs[0].step_chunks(chunks)
+        decs[0].all_stats(reset=True)
+        a = _run(t, decs[0], w, reqs, 4, dev)
+        b = _run(t, plain, w, reqs, 4, dev)
+        for x, y in zip(a, b):
+            assert (x.view(np.uint32) == y.view(np.uint32)).all()
+        n = w.num_requests * w.lanes_per_req * w.cache_pages * w.unit_bytes
+        assert (decs[0].debug_read(0, np.uint8, n) == plain.debug_read(0, np.uint8, n)).all()
+        assert decs[0].all_stats()[0] == plain.all_stats()[0] > 0
+        with pytest.raises(_abi.FerryError):
+            decs[0].step_chunks(17)
+    finally:
+        plain.close()
+        for d in decs:
+            d.close()

@@ -1,7 +1,7 @@
 """Build libferry_cuda.so in-tree for sm_100a (nvcc, no JIT cache).
 
-``python -m ferry_b200.build`` compiles every ``csrc/*.cu`` into
-``ferry_b200/libferry_cuda.so``. The library is git-ignored but travels with
+``python -m ferry_b200.build`` compiles every ``csrc/*.cu`` (one nvcc per
+file, in parallel) and links ``ferry_b200/libferry_cuda.so``. The library is git-ignored but travels with
 the working tree, so a GPU box runs exactly what was compiled here.
 """
 from __future__ import annotations
@@ -53,20 +53,38 @@ def build_drivers(force: bool = False) -> list[str]:
     return out
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and not _stale():
-        build_drivers()
-        return LIB
-    cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
-           "-I" + os.path.join(ROOT, "include"), "-I" + CSRC, "-o", LIB + ".tmp", *sources()]
+def _compile(src: str, obj: str, verbose: bool) -> str:
+    cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-c",
+           "-I" + os.path.join(ROOT, "include"), "-I" + CSRC, "-o", obj, src]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError("nvcc failed:\n" + " ".join(cmd) + "\n" + res.stdout + res.stderr)
+    return res.stdout + res.stderr
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    """Compile every csrc/*.cu to an object (in parallel, objects under
+    _build/), then link libferry_cuda.so."""
+    if not force and not _stale():
+        build_drivers()
+        return LIB
+    from concurrent.futures import ThreadPoolExecutor
+
+    objdir = os.path.join(HERE, "_build")
+    os.makedirs(objdir, exist_ok=True)
+    srcs = sources()
+    objs = [os.path.join(objdir, os.path.splitext(os.path.basename(p))[0] + ".o") for p in srcs]
+    with ThreadPoolExecutor(max_workers=min(len(srcs), os.cpu_count() or 4)) as ex:
+        logs = list(ex.map(lambda so: _compile(so[0], so[1], verbose), zip(srcs, objs)))
+    cmd = [NVCC, *ARCH, "-shared", "-o", LIB + ".tmp", *objs]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError("nvcc link failed:\n" + " ".join(cmd) + "\n" + res.stdout + res.stderr)
     os.replace(LIB + ".tmp", LIB)
     if verbose:
-        print(res.stdout + res.stderr)
+        print("".join(logs))
     build_drivers(force=True)
     return LIB
 

@@ -50,7 +50,7 @@ CTX_HANDLE_BYTES = 1024
 COMM_ID_BYTES = 128
 MIGRATE_FULL, MIGRATE_DELTA, MIGRATE_DROP = 0, 1, 2
 HANDOFF_DROP, HANDOFF_CARRY, HANDOFF_OWNED = 0, 1, 2
-SRC_HOST, SRC_OWNER = 0, 1
+SRC_HOST, SRC_OWNER, SRC_HOST_BULK = 0, 1, 2
 NUM_STATS = 8
 
 

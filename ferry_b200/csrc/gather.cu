@@ -83,7 +83,10 @@ __global__ void __launch_bounds__(256) gather_kernel(
 // cache slot), one unit's load in flight while the previous one is stored.
 // Units without a mapped owner fall back to a plain copy from the host pool
 // (one 16-byte chunk per lane at a time: few registers, so that more warps,
-// each an independent bulk-copy issuer, fit on an SM).
+// each an independent bulk-copy issuer, fit on an SM). With host_bulk
+// (FERRY_SRC_HOST_BULK, own.world == 0) the host-pool units take the bulk
+// ring too: the TMA engine reads each 8 KiB unit from the mapped pool as one
+// copy instead of 512 16-byte SM loads.
 constexpr int kGtMaxWarps = 16;
 constexpr int kGtSmemBudget = 200 * 1024;
 
@@ -107,7 +110,7 @@ __global__ void __launch_bounds__(kGtMaxWarps * 32, 1) gather_store_kernel(
     int C, const int32_t* __restrict__ req_ids, int lanes_per_req, int64_t lanes_total,
     int n_lanes, const int32_t* __restrict__ miss_page, const int32_t* __restrict__ miss_slot,
     const int32_t* __restrict__ n_miss, int k, const int64_t* __restrict__ req_base, int unit_bytes,
-    const __grid_constant__ OwnerMap own, unsigned long long* stats, uint32_t* err) {
+    const __grid_constant__ OwnerMap own, bool host_bulk, unsigned long long* stats, uint32_t* err) {
   extern __shared__ __align__(128) uint8_t gsm[];
   const int t = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int stride = gt_stride(unit_bytes);
@@ -147,16 +150,31 @@ __global__ void __launch_bounds__(kGtMaxWarps * 32, 1) gather_store_kernel(
       continue;
     }
     const int64_t home = req_base[req] + (int64_t)(a % lanes_per_req) * N;  // global lane * N
-    const int owner = page % own.world;
     const int64_t glane = home / N;
     uint8_t* dst = cache + ((uint64_t)gl * C + slot) * unit_bytes;
+    const uint8_t* src = nullptr;
+    bool bulk = false;
+    if (own.world > 0) {
+      const int owner = page % own.world;
+      if (glane >= 0 && glane < own.store_lanes && own.store[owner]) {
+        src = own.store[owner] + ((size_t)glane * own.own_np + page / own.world) * unit_bytes;
+        bulk = true;
+        if (owner == own.self)
+          ++from_self;
+        else
+          ++from_peer;
+      }
+    }
+    if (!src && pool) {
+      src = pool + ((uint64_t)(home + page) % pool_units) * unit_bytes;
+      bulk = host_bulk;
+    }
+    if (!src) {  // stores only: every owner must be mapped
+      if (t == 0) record_error(err, kErrRange);
+      continue;
+    }
     ++copied;
-    if (glane >= 0 && glane < own.store_lanes && own.store[owner]) {
-      const uint8_t* src = own.store[owner] + ((size_t)glane * own.own_np + page / own.world) * unit_bytes;
-      if (owner == own.self)
-        ++from_self;
-      else
-        ++from_peer;
+    if (bulk) {
       if (t == 0) {
         const int s = it & 1;
         bulk_wait_read();  // the store that last read stage s (the newest group) is done with it
@@ -175,12 +193,8 @@ __global__ void __launch_bounds__(kGtMaxWarps * 32, 1) gather_store_kernel(
         pend_dst = dst;
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
-    } else if (pool) {
-      const uint8_t* src = pool + ((uint64_t)(home + page) % pool_units) * unit_bytes;
+    } else {
       for (int v = t; v < (unit_bytes >> 4); v += 32) st_v4(dst + (size_t)v * 16, ld_nc_v4(src + (size_t)v * 16));
-    } else {  // stores only: every owner must be mapped
-      --copied;
-      if (t == 0) record_error(err, kErrRange);
     }
   }
   if (t == 0) {
@@ -225,7 +239,8 @@ int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, i
   }
   const int n_lanes = n_req * c->lanes_per_req;
   const int64_t items = (int64_t)n_lanes * c->cfg.top_k;
-  if (own.world > 0) {
+  const bool host_bulk = c->gather_src == FERRY_SRC_HOST_BULK;
+  if (own.world > 0 || host_bulk) {
     const int warps = std::max(1, std::min(kGtMaxWarps, kGtSmemBudget / gt_warp_smem(c->unit_bytes)));
     const int smem = warps * gt_warp_smem(c->unit_bytes);
     FERRY_TRY(cudaFuncSetAttribute(gather_store_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -233,7 +248,7 @@ int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, i
     gather_store_kernel<<<(unsigned)blocks, warps * 32, smem, st>>>(
         c->pool_dev, c->pool_units, c->cache, c->cfg.max_pages, c->cfg.cache_pages, req_ids,
         c->lanes_per_req, c->lanes, n_lanes, miss_page, miss_slot, n_miss, c->cfg.top_k, c->req_base,
-        c->unit_bytes, own, c->stats, c->err);
+        c->unit_bytes, own, host_bulk, c->stats, c->err);
     FERRY_TRY(cudaGetLastError());
     return FERRY_OK;
   }

@@ -66,11 +66,11 @@ int ferry_store_fill(ferry_ctx* c, void* stream, uint64_t seed, uint64_t pool_un
 }
 
 int ferry_gather_source(ferry_ctx* c, int source) {
-  if (!c || (source != FERRY_SRC_HOST && source != FERRY_SRC_OWNER))
+  if (!c || (source != FERRY_SRC_HOST && source != FERRY_SRC_OWNER && source != FERRY_SRC_HOST_BULK))
     return set_error("gather_source: bad arguments"), FERRY_E_INVAL;
   if (source == FERRY_SRC_OWNER && !c->store)
     return set_error("gather_source: owner gathers need ferry_store_create first"), FERRY_E_STATE;
-  if (source == FERRY_SRC_HOST && c->stores_only)
+  if (source != FERRY_SRC_OWNER && c->stores_only)
     return set_error("gather_source: no host pool (ferry_kv_register_stores)"), FERRY_E_STATE;
   c->gather_src = source;
   return FERRY_OK;

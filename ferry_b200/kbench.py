@@ -121,6 +121,8 @@ def main():
     ap.add_argument("--select", default="mean", help="selection rule: mean (the benchmark's) or quest")
     ap.add_argument("--store-world", type=int, default=0,
                     help="serve misses from page-owner stores of W ranks (rank r on GPU r mod count)")
+    ap.add_argument("--host-bulk", action="store_true",
+                    help="host-pool misses by TMA bulk copies (FERRY_SRC_HOST_BULK) instead of SM loads")
     args = ap.parse_args()
     if args.probe:
         print(json.dumps({"probe": probe()}))
@@ -158,6 +160,8 @@ def main():
         for d in range(ndev):
             torch.cuda.synchronize(d)
         dec.gather_source(_abi.SRC_OWNER)
+    elif args.host_bulk:
+        dec.gather_source(_a.SRC_HOST_BULK)
     R = w.num_requests
     ids = torch.arange(R, dtype=torch.int32, device=dev)
     dec.begin(ids, torch.full((R,), w.init_pages, dtype=torch.int32, device=dev))
@@ -183,7 +187,8 @@ def main():
         ub = w.unit_bytes
         st = dec.all_stats()
         res["gather"] = {"us": t, "units": units, "bytes": units * ub, "GB_s": units * ub / t / 1e3,
-                         "source": ("owner stores, world %d" % args.store_world) if args.store_world else "host pool",
+                         "source": ("owner stores, world %d" % args.store_world) if args.store_world else
+                         ("host pool, bulk copies" if args.host_bulk else "host pool, SM loads"),
                          "share_peer": st[4] / max(1, st[0]), "share_local_store": st[6] / max(1, st[0])}
     dec.gather(ids)
     if "attention" in only:

@@ -298,9 +298,14 @@ int ferry_ctx_export(ferry_ctx* ctx, void* handle /* FERRY_CTX_HANDLE_BYTES */);
  * ferry_ctx_import after the peer created its store; pages of unmapped owners
  * or of lanes outside the store come from the host pool). Stores are created
  * before ferry_ctx_export so that the handle carries them.
+ * FERRY_SRC_HOST_BULK reads the same host pool as FERRY_SRC_HOST with the
+ * TMA engine (one 1-D bulk copy per page unit into shared memory, then a bulk
+ * store into the slot) instead of 16-byte SM loads; the bytes moved are the
+ * same.
  * No counterpart in the reference (it has no page ownership). */
 #define FERRY_SRC_HOST 0
 #define FERRY_SRC_OWNER 1
+#define FERRY_SRC_HOST_BULK 2
 int ferry_store_create(ferry_ctx* ctx, int world, int rank, int64_t global_lanes);
 int ferry_store_fill(ferry_ctx* ctx, void* stream, uint64_t seed, uint64_t pool_units);
 int ferry_gather_source(ferry_ctx* ctx, int source);

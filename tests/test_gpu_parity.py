@@ -35,13 +35,15 @@ def _rel_err(gpu, ref):
 class Harness:
     """A Decoder plus the oracle state that mirrors it."""
 
-    def __init__(self, torch, w, n_pages=None):
+    def __init__(self, torch, w, n_pages=None, source=None):
         import oracle
         from ferry_b200.engine import Decoder
 
         self.t, self.w, self.o = torch, w, oracle
         self.dec = Decoder(w, 0)
         self.pool = self.dec.register_pool()
+        if source is not None:
+            self.dec.gather_source(source)
         U = w.pool_units
         self.units = self.pool.numpy(np.uint16).reshape(U, 4096)
         self.summ = oracle.page_summary(self.units)
@@ -179,6 +181,32 @@ def test_decode_steps_match_oracle(torch_cuda, shape):
         h.check_step(_q(w, reqs, 4, job=1), reqs)
         # a partial batch in a different order
         h.check_step(_q(w, [2, 0], 5), [2, 0])
+    finally:
+        h.close()
+
+
+@pytest.mark.parametrize("shape", [dict(), dict(q_heads=8, kv_heads=2, cache_frac=0.5)])
+def test_host_bulk_gather_matches_oracle(torch_cuda, shape):
+    """FERRY_SRC_HOST_BULK: host-pool misses moved by TMA bulk copies land the
+    same bytes in the same slots as the SM-load gather; every intermediate and
+    the attention match the oracle, cold and warm steps, restarts and a
+    partial batch."""
+    from ferry_b200 import _abi
+    from ferry_b200.workload import small
+
+    w = small(**shape)
+    reqs = list(range(w.num_requests))
+    h = Harness(torch_cuda, w, n_pages=[w.max_pages, w.max_pages - 5, w.top_k // 2, w.top_k][: w.num_requests],
+                source=_abi.SRC_HOST_BULK)
+    try:
+        h.begin(reqs)
+        total = 0
+        for s in range(3):
+            total += h.check_step(_q(w, reqs, s), reqs)[1]
+        h.begin([0, 2])
+        total += h.check_step(_q(w, reqs, 3, job=1), reqs)[1]
+        total += h.check_step(_q(w, [3, 1], 4), [3, 1])[1]
+        assert total > 0 and h.dec.all_stats()[0] == total
     finally:
         h.close()
 

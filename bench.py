@@ -20,6 +20,7 @@ e2e    the same through the fused public call ferry_decode_step with host
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import subprocess
@@ -328,8 +329,10 @@ def run_ferry(args, w):
     dev = torch.device("cuda", local)
     # replicas: same shape, per-rank seed
     w = dataclasses.replace(w, seed=w.seed + 1000 * rank)
+    chunks = max(1, min(args.chunks, w.num_requests))
     dec = Decoder(w, local)
     dec.register_pool()
+    dec.step_chunks(chunks)
     sch = Schedule(w)
     LH = w.lanes_per_req
     n_ticks = args.warmup + args.steps
@@ -354,7 +357,10 @@ def run_ferry(args, w):
     out = torch.empty((w.num_requests, w.num_layers, w.q_heads, 128), dtype=torch.float32, device=dev)
     st = torch.cuda.current_stream(dev)
 
-    def tick_run(tk, evs=None):
+    def tick_run(tk, evs=None, serial=True):
+        # serial: the four steps as separate calls with an event between each
+        # (the per-kernel breakdown); otherwise ferry_decode_step, pipelined
+        # over request chunks when chunks > 1, with events around the step
         e = None
         if evs is not None:
             e = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
@@ -366,8 +372,11 @@ def run_ferry(args, w):
                 evs.append((e, 0, False))
             return 0
         n = len(tk["active"])
-        if evs is None:
+        if evs is None or not serial:
             dec.step(tk["qd"], tk["ids"], out[:n], stream=st)
+            if e is not None:
+                e[5].record(st)
+                evs.append((e, n, True))
             return n
         e[1].record(st)
         dec.select(tk["qd"], tk["ids"], stream=st)
@@ -384,34 +393,50 @@ def run_ferry(args, w):
         return n
 
     # ---------------------------------------------------------------- device-timed value
-    for i in range(args.warmup):
-        tick_run(ticks[i], [])
-    torch.cuda.synchronize(dev)
-    dec.stats(reset=True)
-    if ws > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    evs = []
-    tokens = 0
-    with Clocks(local) as clk:
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record(st)
-        for i in range(args.warmup, n_ticks):
-            tokens += tick_run(ticks[i], evs)
-        t1.record(st)
+    def timed_pass(serial, clk=None):
+        for i in range(args.warmup):
+            tick_run(ticks[i], [], serial)
         torch.cuda.synchronize(dev)
-    elapsed_ms = t0.elapsed_time(t1)
-    dec.check()
+        dec.stats(reset=True)
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        evs = []
+        tokens = 0
+        with (clk if clk is not None else contextlib.nullcontext()):
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record(st)
+            for i in range(args.warmup, n_ticks):
+                tokens += tick_run(ticks[i], evs, serial)
+            t1.record(st)
+            torch.cuda.synchronize(dev)
+        dec.check()
+        return t0.elapsed_time(t1), tokens, evs
+
+    clk = Clocks(local)
+    elapsed_ms, tokens, evs = timed_pass(chunks == 1, clk)
     units, gbytes = dec.stats(reset=True)
     full = [(e, n) for e, n, ok in evs if ok]
-    launches = len(full) * (4 + (2 if w.append else 0)) + sum(
+    # request starts, then per decoded tick: select, detect, gather, attention
+    # (each once per chunk) and the appends' two
+    launches = len(full) * (4 * chunks + (2 if w.append else 0)) + sum(
         1 for i in range(args.warmup, n_ticks) if ticks[i]["new"] is not None)
+    step_ms = [e[0].elapsed_time(e[5]) for e, n in full]  # each tick's device time (request starts included)
+    if chunks > 1:
+        # the per-kernel breakdown: the same ticks again on a fresh job state,
+        # the four steps as separate calls
+        dec.close()
+        dec = Decoder(w, local)
+        dec.register_pool()
+        _, _, evs_k = timed_pass(True)
+        dec.stats(reset=True)
+        full_k = [(e, n) for e, n, ok in evs_k if ok]
+    else:
+        full_k = full
     k_ms = np.zeros(4)
-    step_ms = []  # each tick's device time, first to last event (request starts included)
-    for e, n in full:
+    for e, n in full_k:
         k_ms += [e[j].elapsed_time(e[j + 1]) for j in range(1, 5)]
-        step_ms.append(e[0].elapsed_time(e[5]))
     if ws > 1:
         t = torch.tensor([elapsed_ms, float(tokens), float(gbytes)], dtype=torch.float64, device=dev)
         mx = t.clone()
@@ -428,6 +453,7 @@ def run_ferry(args, w):
     dec.close()
     dec = Decoder(w, local)
     dec.register_pool()
+    dec.step_chunks(chunks)
     pin_q = [None if tk["q"] is None else tk["q"].pin_memory() for tk in ticks]
     pin_ids = [torch.from_numpy(tk["active"]).pin_memory() for tk in ticks]
     # one pinned output buffer per tick (the same bytes per step as a single
@@ -499,7 +525,7 @@ def run_ferry(args, w):
         nl = tokens * LH  # lanes processed by this rank
         attn_bytes = tokens * w.attn_bytes_per_token() + tokens * w.qo_bytes_per_token()
         sel_bytes = tokens * w.select_bytes_per_token()
-        n_launch = len(full)
+        n_launch = len(full_k)
         attn_ms = k_ms[3] / max(1, n_launch)
         achieved = (attn_bytes / max(1, n_launch)) / (attn_ms / 1e3) / 1e9
         sel_ach = (sel_bytes / max(1, n_launch)) / (k_ms[0] / max(1, n_launch) / 1e3) / 1e9
@@ -521,7 +547,8 @@ def run_ferry(args, w):
                        "top_k": w.top_k, "cache_pages": w.cache_pages, "append_tokens_per_step": w.append,
                        "arrivals": f"poisson {w.arrival_rate} req/s on a {w.tick_ms} ms tick",
                        "l2": "inputs larger than L2 (selected KV 256 MiB + summaries 64 MiB per full step)",
-                       "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU"},
+                       "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
+                       "step_chunks": chunks},
             "miss_gather": {"GB_s": gather_gbs, "bytes": gbytes_all, "units": units,
                             "link_peak_GB_s": best, "frac": gather_gbs / best if best else None,
                             "peak_kind": "measured H2D copy from pinned host, this run",
@@ -543,6 +570,9 @@ def run_ferry(args, w):
                          "bytes_per_launch": attn_bytes / max(1, n_launch)},
             "roofline_select": {"bound": "hbm", "achieved": sel_ach, "peak": hbm_peak,
                                 "unit": "GB/s", "frac": sel_ach / hbm_peak},
+            # per-kernel CUDA events of a serial pass over the same ticks (the
+            # four steps as separate calls); with step_chunks > 1 the value
+            # pass overlaps them across request chunks
             "kernel_ms_per_step": {k: float(v / max(1, n_launch)) for k, v in
                                    zip(["select", "detect", "gather", "attention"], k_ms)},
             "kernel_time_share": shares,
@@ -580,7 +610,7 @@ def main():
     ap.add_argument("--append", type=int, default=None,
                     help="tokens each decode step appends to its context (default: the workload's)")
     ap.add_argument("--chunks", type=int, default=1,
-                    help="cfg5 / cfg5s: pipeline each step over this many request chunks (ferry_step_chunks)")
+                    help="pipeline each decode step over this many request chunks (ferry_step_chunks)")
     ap.add_argument("--requests", type=int, default=None,
                     help="cfg5 / cfg5s: requests of the job (default: the config's 32)")
     ap.add_argument("--replicas", action="store_true",

@@ -249,13 +249,14 @@ struct ferry_ctx {
   int32_t* ctx_pages = nullptr;  // 2R: full pages of each request's context, then the tokens of
                                  // its partial last page (0..15; decode appends)
   int append_tokens = 0;         // tokens ferry_decode_step appends per request (0 = fixed context)
-  // pipelined step (ferry_step_chunks): request chunks whose selection runs on
-  // the caller's stream while the previous chunk's detect / gather / attention
-  // run on `side`
+  // pipelined step (ferry_step_chunks): request chunks whose selection and
+  // miss detection run on the caller's stream, gathers on `side`, attention
+  // on `side2`
   int step_chunks = 1;
-  cudaStream_t side = nullptr;
+  cudaStream_t side = nullptr, side2 = nullptr;
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
-  cudaEvent_t ev_sel[16] = {};
+  cudaEvent_t ev_sel[16] = {};  // chunk i's misses are known
+  cudaEvent_t ev_gat[16] = {};  // chunk i's pages are in their slots
   int64_t* req_base = nullptr;   // R: pool unit of the request's (lane 0, page 0)
 
   // host pool
@@ -332,8 +333,11 @@ int launch_lru(const ferry_lru* L, cudaStream_t st, const int32_t* lane_ids, con
 int launch_lru_reset(const ferry_lru* L, cudaStream_t st, const int32_t* req_ids, int n,
                      int lanes_per_req, const int32_t* n_pages, int32_t* ctx_pages,
                      const int64_t* pool_base, int64_t* req_base);
+// shared: the gather runs beside other kernels (a pipelined step), so its
+// grid leaves most of every SM to them
 int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, int n_req,
-                  const int32_t* miss_page, const int32_t* miss_slot, const int32_t* n_miss);
+                  const int32_t* miss_page, const int32_t* miss_slot, const int32_t* n_miss,
+                  bool shared = false);
 void close_all_peers(ferry_ctx* c);
 // owner store of rank `rank` of `world` (kvgen.cu)
 int launch_store_fill(cudaStream_t st, uint64_t seed, int world, int rank, int N, int own_np, int64_t n_units,

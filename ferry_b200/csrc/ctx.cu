@@ -97,9 +97,12 @@ void destroy_ctx(ferry_ctx* c) {
   cudaFree(c->stats);
   for (cudaEvent_t& e : c->ev_sel)
     if (e) cudaEventDestroy(e);
+  for (cudaEvent_t& e : c->ev_gat)
+    if (e) cudaEventDestroy(e);
   if (c->ev_fork) cudaEventDestroy(c->ev_fork);
   if (c->ev_join) cudaEventDestroy(c->ev_join);
   if (c->side) cudaStreamDestroy(c->side);
+  if (c->side2) cudaStreamDestroy(c->side2);
   delete c;
 }
 
@@ -406,42 +409,48 @@ int ferry_decode_step(ferry_ctx* c, void* stream, const uint16_t* d_q, const int
   cudaStream_t st = (cudaStream_t)stream;
   const int LH = c->lanes_per_req, k = c->cfg.top_k;
   const size_t qrow = (size_t)c->cfg.num_layers * c->cfg.q_heads * kHeadDim;  // q / out elements per request
-  // requests [s0, s0 + n) of the batch: detect, gather, attention on `ss`
-  auto rest = [&](cudaStream_t ss, int s0, int n) -> int {
-    const size_t l0 = (size_t)s0 * LH;
-    int r;
-    if ((r = launch_lru(&c->lru, ss, nullptr, d_req_ids + s0, LH, nullptr, n * LH, c->ws_sel + l0 * k, k,
-                        c->ws_nsel + l0, 1, nullptr, c->ws_islot + l0 * k, c->ws_mpage + l0 * k,
-                        c->ws_mslot + l0 * k, c->ws_nmiss + l0)))
-      return r;
-    if ((r = launch_gather(c, ss, d_req_ids + s0, n, c->ws_mpage + l0 * k, c->ws_mslot + l0 * k, c->ws_nmiss + l0)))
-      return r;
-    return launch_attention_any(c, ss, d_q + (size_t)s0 * qrow, d_req_ids + s0, n, c->ws_islot + l0 * k,
-                                c->ws_nsel + l0, d_out + (size_t)s0 * qrow);
-  };
   const int nch = std::min(c->step_chunks, n_req);
   if (nch <= 1 || !c->side) {
     if ((rc = launch_select(c, st, d_q, d_req_ids, n_req, c->ws_sel, c->ws_nsel))) return rc;
-    if ((rc = rest(st, 0, n_req))) return rc;
+    if ((rc = launch_lru(&c->lru, st, nullptr, d_req_ids, LH, nullptr, n_req * LH, c->ws_sel, k, c->ws_nsel, 1,
+                         nullptr, c->ws_islot, c->ws_mpage, c->ws_mslot, c->ws_nmiss)))
+      return rc;
+    if ((rc = launch_gather(c, st, d_req_ids, n_req, c->ws_mpage, c->ws_mslot, c->ws_nmiss))) return rc;
+    if ((rc = launch_attention_any(c, st, d_q, d_req_ids, n_req, c->ws_islot, c->ws_nsel, d_out))) return rc;
   } else {
-    // chunk i's selection (HBM-bound) overlaps chunk i-1's gather, which with
-    // owner stores on peers is NVLink-bound; every chunk keeps its own rows of
-    // the workspace, and kernels that share scratch stay on one stream each
-    // (selections on st; detect, gather, attention on side)
+    // Requests [s0, s0 + n) form chunk i. Chunk i's selection and miss
+    // detection (HBM- and latency-bound) run on the caller's stream while
+    // chunk i-1's gather (host- or NVLink-bound) runs on `side` and chunk
+    // i-2's attention on `side2`. Chunks own disjoint lanes and their own rows
+    // of the workspace; kernels of one kind, which share scratch (selection
+    // chunk keys, attention partials), stay on one stream each.
     const int per = (n_req + nch - 1) / nch;
     FERRY_TRY(cudaEventRecord(c->ev_fork, st));
     FERRY_TRY(cudaStreamWaitEvent(c->side, c->ev_fork, 0));
+    FERRY_TRY(cudaStreamWaitEvent(c->side2, c->ev_fork, 0));
     for (int i = 0, s0 = 0; s0 < n_req; ++i, s0 += per) {
       const int n = std::min(per, n_req - s0);
       const size_t l0 = (size_t)s0 * LH;
-      if ((rc = launch_select(c, st, d_q + (size_t)s0 * qrow, d_req_ids + s0, n, c->ws_sel + l0 * k,
-                              c->ws_nsel + l0)))
+      const int32_t* ids = d_req_ids + s0;
+      if ((rc = launch_select(c, st, d_q + (size_t)s0 * qrow, ids, n, c->ws_sel + l0 * k, c->ws_nsel + l0)))
+        return rc;
+      if ((rc = launch_lru(&c->lru, st, nullptr, ids, LH, nullptr, n * LH, c->ws_sel + l0 * k, k, c->ws_nsel + l0,
+                           1, nullptr, c->ws_islot + l0 * k, c->ws_mpage + l0 * k, c->ws_mslot + l0 * k,
+                           c->ws_nmiss + l0)))
         return rc;
       FERRY_TRY(cudaEventRecord(c->ev_sel[i], st));
       FERRY_TRY(cudaStreamWaitEvent(c->side, c->ev_sel[i], 0));
-      if ((rc = rest(c->side, s0, n))) return rc;
+      if ((rc = launch_gather(c, c->side, ids, n, c->ws_mpage + l0 * k, c->ws_mslot + l0 * k, c->ws_nmiss + l0,
+                              true)))
+        return rc;
+      FERRY_TRY(cudaEventRecord(c->ev_gat[i], c->side));
+      FERRY_TRY(cudaStreamWaitEvent(c->side2, c->ev_gat[i], 0));
+      if ((rc = launch_attention_any(c, c->side2, d_q + (size_t)s0 * qrow, ids, n, c->ws_islot + l0 * k,
+                                     c->ws_nsel + l0, d_out + (size_t)s0 * qrow)))
+        return rc;
     }
-    FERRY_TRY(cudaEventRecord(c->ev_join, c->side));
+    // side2's last attention follows side's last gather
+    FERRY_TRY(cudaEventRecord(c->ev_join, c->side2));
     FERRY_TRY(cudaStreamWaitEvent(st, c->ev_join, 0));
   }
   // the token decoded in this step joins its request's context
@@ -453,9 +462,11 @@ int ferry_step_chunks(ferry_ctx* c, int chunks) {
   DeviceGuard guard(c->device);
   if (chunks > 1 && !c->side) {
     FERRY_TRY(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking));
+    FERRY_TRY(cudaStreamCreateWithFlags(&c->side2, cudaStreamNonBlocking));
     FERRY_TRY(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming));
     FERRY_TRY(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming));
     for (cudaEvent_t& e : c->ev_sel) FERRY_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    for (cudaEvent_t& e : c->ev_gat) FERRY_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   }
   c->step_chunks = chunks;
   return FERRY_OK;

@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(kGtMaxWarps * 32, 1) gather_store_kernel(
 }  // namespace
 
 int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, int n_req,
-                  const int32_t* miss_page, const int32_t* miss_slot, const int32_t* n_miss) {
+                  const int32_t* miss_page, const int32_t* miss_slot, const int32_t* n_miss, bool shared) {
   if (n_req <= 0) return FERRY_OK;
   if (!c->pool_dev && !(c->stores_only && c->gather_src == FERRY_SRC_OWNER)) {
     set_error(c->stores_only ? "gather: a ctx without a host pool gathers from owner stores only"
@@ -241,7 +241,10 @@ int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, i
   const int64_t items = (int64_t)n_lanes * c->cfg.top_k;
   const bool host_bulk = c->gather_src == FERRY_SRC_HOST_BULK;
   if (own.world > 0 || host_bulk) {
-    const int warps = std::max(1, std::min(kGtMaxWarps, kGtSmemBudget / gt_warp_smem(c->unit_bytes)));
+    // shared: half the shared-memory budget, so that selection and attention
+    // CTAs fit beside the ring on every SM
+    const int budget = shared ? kGtSmemBudget / 2 : kGtSmemBudget;
+    const int warps = std::max(1, std::min(kGtMaxWarps, budget / gt_warp_smem(c->unit_bytes)));
     const int smem = warps * gt_warp_smem(c->unit_bytes);
     FERRY_TRY(cudaFuncSetAttribute(gather_store_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const int64_t blocks = std::min<int64_t>((items + warps - 1) / warps, (int64_t)c->num_sms);
@@ -252,8 +255,10 @@ int launch_gather(const ferry_ctx* c, cudaStream_t st, const int32_t* req_ids, i
     FERRY_TRY(cudaGetLastError());
     return FERRY_OK;
   }
-  // enough warps to keep the host link saturated, capped at 16 CTAs per SM
-  const int64_t blocks = std::min<int64_t>((items + 7) / 8, (int64_t)c->num_sms * 16);
+  // enough warps to keep the host link saturated, capped at 16 CTAs per SM;
+  // beside other kernels 2 per SM (16 warps, a unit each in flight: far more
+  // bytes in flight than the host link's latency needs)
+  const int64_t blocks = std::min<int64_t>((items + 7) / 8, (int64_t)c->num_sms * (shared ? 2 : 16));
   gather_kernel<<<(unsigned)blocks, 256, 0, st>>>(
       c->pool_dev, c->pool_units, c->cache, c->cfg.max_pages, c->cfg.cache_pages, req_ids,
       c->lanes_per_req, c->lanes, n_lanes, miss_page, miss_slot, n_miss, c->cfg.top_k, c->req_base,

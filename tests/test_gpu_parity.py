@@ -304,6 +304,75 @@ def test_fused_step_equals_separate_calls(torch_cuda):
         b.close()
 
 
+@pytest.mark.parametrize("shape,chunks", [(dict(), 2), (dict(), 4), (dict(q_heads=8, kv_heads=2, cache_frac=0.5), 3),
+                                          (dict(kv_dtype="e4m3", q_heads=8, kv_heads=1, ctx_tokens=2048, top_k=40), 2)])
+def test_pipelined_host_step_matches_oracle_checked_step(torch_cuda, shape, chunks):
+    """ferry_step_chunks with host-pool gathers: chunk i's selection and miss
+    detection on the caller's stream, chunk i-1's gather and chunk i-2's
+    attention on the ctx's two streams. Outputs, page tables, cache bytes and
+    gather counts equal those of a step whose every intermediate is checked
+    against the oracle (fp16), or of the plain fused step (e4m3); full,
+    partial and reordered batches, a restart in between."""
+    from ferry_b200.engine import Decoder
+    from ferry_b200.workload import small
+
+    t = torch_cuda
+    w = small(**shape)
+    dev = t.device("cuda", 0)
+    f16 = w.kv_dtype != "e4m3"
+    a = Decoder(w, 0)
+    b = Harness(t, w) if f16 else None
+    pb = None if f16 else Decoder(w, 0)
+    try:
+        a.register_pool()
+        a.step_chunks(chunks)
+        if pb is not None:
+            pb.register_pool()
+        ref_dec = b.dec if f16 else pb
+
+        def begin(reqs):
+            ids = t.from_numpy(np.asarray(reqs, np.int32)).to(dev)
+            a.begin(ids, t.full((len(reqs),), w.max_pages, dtype=t.int32, device=dev))
+            if f16:
+                b.begin(reqs)
+            else:
+                pb.begin(ids, t.full((len(reqs),), w.max_pages, dtype=t.int32, device=dev))
+
+        def step(q, reqs):
+            ids = t.from_numpy(np.asarray(reqs, np.int32)).to(dev)
+            qd = t.from_numpy(q).to(dev)
+            out = t.zeros((len(reqs), w.num_layers, w.q_heads, 128), dtype=t.float32, device=dev)
+            a.step(qd, ids, out)
+            if f16:
+                ref = b.check_step(q, reqs)[0]
+            else:
+                ro = t.zeros_like(out)
+                pb.step(qd, ids, ro)
+                ref = ro.cpu().numpy()
+            t.cuda.synchronize()
+            a.check()
+            assert (out.cpu().numpy().view(np.uint32) == ref.view(np.uint32)).all()
+
+        reqs = list(range(w.num_requests))
+        begin(reqs)
+        for s in range(3):
+            step(_q(w, reqs, s), reqs)
+        begin([1, 2])
+        step(_q(w, reqs, 3, job=1), reqs)
+        step(_q(w, [3, 0, 2], 4), [3, 0, 2])
+        nl = w.num_requests * w.lanes_per_req
+        assert (a.debug_read(1, np.int32, nl * w.max_pages) == ref_dec.debug_read(1, np.int32, nl * w.max_pages)).all()
+        n = nl * w.cache_pages * w.unit_bytes
+        assert (a.debug_read(0, np.uint8, n) == ref_dec.debug_read(0, np.uint8, n)).all()
+        assert a.stats()[0] == ref_dec.stats()[0] > 0
+    finally:
+        a.close()
+        if b is not None:
+            b.close()
+        if pb is not None:
+            pb.close()
+
+
 def _lru_touch(torch, L, lanes, sel, n_sel=None, reset=None, distinct=False):
     from ferry_b200 import _abi
 

@@ -141,13 +141,15 @@ int ferry_requests_begin(ferry_ctx* ctx, void* stream, const int32_t* d_req_ids,
 int ferry_requests_append(ferry_ctx* ctx, void* stream, const int32_t* d_req_ids, int n, int tokens);
 int ferry_decode_appends(ferry_ctx* ctx, int tokens_per_step);
 /* Pipelined ferry_decode_step: the batch is cut into `chunks` (1..16) runs of
- * requests; chunk i's selection runs on the caller's stream while chunk i-1's
- * miss detection, gather and attention run on a stream of the ctx, and the
- * caller's stream waits for all of it before the step returns control of it
- * (appends, if any, follow on the caller's stream). Selection is HBM-bound;
- * with owner stores on peers the gather is NVLink-bound, so the two overlap.
- * Results are identical to chunks = 1 (the default). Call it before any
- * stream capture: it creates the ctx's stream and events on first use. */
+ * requests; chunk i's selection and miss detection run on the caller's stream
+ * while chunk i-1's gather runs on one stream of the ctx and chunk i-2's
+ * attention on another, and the caller's stream waits for all of it before
+ * the step returns control of it (appends, if any, follow on the caller's
+ * stream). Selection and attention are HBM-bound, the gather host-link- or
+ * NVLink-bound, so they overlap. Results are identical to chunks = 1 (the
+ * default). Call it before any stream capture: it creates the ctx's streams
+ * and events on first use. No counterpart in the reference (its exec_step
+ * issues one request's layers at a time). */
 int ferry_step_chunks(ferry_ctx* ctx, int chunks);
 
 /* ---- the four hot-path steps --------------------------------------------- */

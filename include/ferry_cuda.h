@@ -148,8 +148,7 @@ int ferry_decode_appends(ferry_ctx* ctx, int tokens_per_step);
  * stream). Selection and attention are HBM-bound, the gather host-link- or
  * NVLink-bound, so they overlap. Results are identical to chunks = 1 (the
  * default). Call it before any stream capture: it creates the ctx's streams
- * and events on first use. No counterpart in the reference (its exec_step
- * issues one request's layers at a time). */
+ * and events on first use. No counterpart in the reference. */
 int ferry_step_chunks(ferry_ctx* ctx, int chunks);
 
 /* ---- the four hot-path steps --------------------------------------------- */

@@ -625,7 +625,7 @@ def main():
     if args.workload == "skew":
         run_cluster(args)
         return
-    if args.workload in ("cfg3s", "cfg4s"):
+    if args.workload in ("cfg2s", "cfg3s", "cfg4s"):
         run_config_slice(args, WORKLOADS[args.workload])
         return
     w = WORKLOADS[args.workload]
@@ -857,8 +857,10 @@ def nvlink_peak(local, ws, nbytes=256 << 20):
 
 
 def run_config_slice(args, w):
-    """--workload cfg3s | cfg4s: configs[2] / configs[3] at their per-layer
-    shapes (one layer), N ranks through the executor. cfg3s: 256 requests,
+    """--workload cfg2s | cfg3s | cfg4s: configs[1] / [2] / [3] sliced by layer,
+    N ranks through the executor. cfg2s: 64 requests per GPU of 32768 tokens,
+    8 of the 32 layers, top-128, cache at 30%, all present from the first tick
+    and decoded every tick, 512 steps each. cfg3s (one layer): 256 requests,
     contexts uniform in 8k-32k tokens, round-robin homes, Poisson 400 req/s
     box-wide, top-128, 1024 steps each. cfg4s: 512 requests, contexts uniform
     in 16k-64k tokens, Zipf(1.5) homes, ON/OFF arrivals (exponential 200 ms ON
@@ -882,10 +884,22 @@ def run_config_slice(args, w):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     else:
         dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29517", rank=0, world_size=1)
-    total = w.num_requests if w.name == "cfg3s" else 512
+    total = {"cfg2s": w.num_requests * ws, "cfg3s": w.num_requests}.get(w.name, 512)
     lo, hi = CONTEXT_RANGE[w.name]
     n_pages = ragged_pages(total, lo, hi, w.seed)
-    if w.name == "cfg3s":
+    slots, batch, pool_units = args.slots, args.batch, None
+    if w.name == "cfg2s":
+        # 64 concurrent requests per GPU, all decoding every tick,
+        # from the first tick on; a 17 GB pool (2^21 units, the reference's
+        # modulo slab addressing beyond it) keeps the 1 GB summary table
+        # larger than L2
+        home = np.arange(total, dtype=np.int64) % ws
+        join = np.zeros(total, np.int64)
+        policy = "round-robin"
+        arrivals = f"{w.num_requests} concurrent requests per GPU from the first tick"
+        slots = batch = w.num_requests
+        pool_units = 1 << 21
+    elif w.name == "cfg3s":
         home, join = job_schedule(w, total, ws, "rr")
         policy = "round-robin"
         arrivals = f"poisson {w.arrival_rate} req/s box-wide"
@@ -896,8 +910,8 @@ def run_config_slice(args, w):
         arrivals = "ON/OFF: exp 200 ms ON at 2000 req/s, exp 800 ms OFF"
     window = (args.warmup, args.warmup + args.steps)
     steal = 0 if args.no_steal else 4
-    r = RankRunner(w, total, ws, rank, local, slots=args.slots, max_batch=args.batch, steal_batch=steal,
-                   q_steps=window[1] + 8)
+    r = RankRunner(w, total, ws, rank, local, slots=slots, max_batch=batch, steal_batch=steal,
+                   q_steps=window[1] + 8, pool_units=pool_units)
     try:
         dist.barrier()
         torch.cuda.synchronize(dev)
@@ -922,12 +936,13 @@ def run_config_slice(args, w):
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "fp16-kv/fp32-acc", "data": "synthetic (procedural KV, AR(1) queries, seeded)",
-                "config": {"workload": f"{w.name}: configs[{2 if w.name == 'cfg3s' else 3}] at its per-layer "
-                                       "shape, 1 of 32 layers", "requests": total,
+                "config": {"workload": (f"{w.name}: configs[1], {w.num_layers} of 32 layers" if w.name == "cfg2s" else
+                                        f"{w.name}: configs[{2 if w.name == 'cfg3s' else 3}] at its per-layer "
+                                        "shape, 1 of 32 layers"), "requests": total, "layers": w.num_layers,
                            "ctx_tokens": [lo, hi], "heads": [w.q_heads, w.kv_heads], "top_k": w.top_k,
                            "cache_pages": w.cache_pages, "steps_per_request": w.steps, "homes": policy,
                            "home_share": (np.bincount(home, minlength=ws) / total).round(3).tolist(),
-                           "arrivals": arrivals, "slots_per_gpu": args.slots, "batch_per_gpu": args.batch,
+                           "arrivals": arrivals, "slots_per_gpu": slots, "batch_per_gpu": batch,
                            "steal_batch": steal, "parallelism": f"{ws} ranks: executor + stealing + NCCL exchange"},
                 "miss_gather": {"aggregate_GB_s": gbytes / (ms / 1e3) / 1e9,
                                 "link_peak_aggregate_GB_s": agg_peak,

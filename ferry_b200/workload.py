@@ -135,9 +135,19 @@ CFG4S = Workload(name="cfg4s", num_requests=256, num_layers=1, q_heads=32, kv_he
                  ctx_tokens=65536, top_k=256, cache_frac=0.3 * 40960 / 65536, steps=512, arrival_rate=2000.0,
                  append=1)
 
-CONTEXT_RANGE = {"cfg3s": (8192, 32768), "cfg4s": (16384, 65536)}
+# configs[1] (Llama-7B, 32 layers, 64 concurrent requests of 32768 tokens,
+# top-128, cache at 30% of the KV footprint, misses from pinned host memory,
+# 512 decode steps) cut to 8 of its 32 layers: the whole configuration's
+# cache (330 GB) exceeds one B200's HBM, 8 layers' (82 GB) fit. Every request
+# is present from the first tick; each step appends its token.
+CFG2S = Workload(name="cfg2s", num_requests=64, num_layers=8, q_heads=32, kv_heads=32,
+                 ctx_tokens=32768, top_k=128, cache_frac=0.3, steps=512, arrival_rate=1e9,
+                 append=1)
 
-WORKLOADS = {"cfg1": CFG1, "cfg5": CFG5, "cfg5s": CFG5S, "cfg5s_f16": CFG5S_F16, "cfg3s": CFG3S, "cfg4s": CFG4S}
+CONTEXT_RANGE = {"cfg2s": (32768, 32768), "cfg3s": (8192, 32768), "cfg4s": (16384, 65536)}
+
+WORKLOADS = {"cfg1": CFG1, "cfg2s": CFG2S, "cfg5": CFG5, "cfg5s": CFG5S, "cfg5s_f16": CFG5S_F16, "cfg3s": CFG3S,
+             "cfg4s": CFG4S}
 
 
 def small(name: str = "tiny", **kw) -> Workload:

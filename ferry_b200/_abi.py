@@ -44,6 +44,8 @@ EXPORTS = [
     "ferry_lru_create", "ferry_lru_destroy", "ferry_lru_touch", "ferry_lru_read",
     "ferry_lru_group_enable", "ferry_lru_touch_owned", "ferry_lru_set_capacity", "ferry_lru_release",
     "ferry_lru_count_owned", "ferry_lru_handoff", "ferry_lru_read_owned",
+    "ferry_taskb_generate", "ferry_taskb_create", "ferry_taskb_run", "ferry_taskb_results",
+    "ferry_taskb_reset", "ferry_taskb_destroy",
 ]
 MAX_PEERS = 8
 CTX_HANDLE_BYTES = 1024
@@ -78,6 +80,34 @@ class StealPolicy(C.Structure):
     1 = plus the value/cost filter (policy E)."""
     _fields_ = [("cost_filter", C.c_int), ("margin", C.c_double), ("cost_scale", C.c_double),
                 ("link_gbs", C.c_double), ("fixed_ms", C.c_double)]
+
+
+TASKB_STEADY, TASKB_BURSTY, TASKB_SKEWED, TASKB_TRACE = 0, 1, 2, 3
+TASKB_A, TASKB_B, TASKB_C = 0, 1, 2
+TASKB_P2P, TASKB_HOST_STAGED = 0, 1
+
+
+class TaskbSpec(C.Structure):
+    _fields_ = [("arrival", C.c_int), ("sparsity", C.c_int), ("imbalanced", C.c_int), ("num_gpus", C.c_int),
+                ("total", C.c_uint64), ("dest_hot_frac", C.c_double), ("dest_hot_cards", C.c_int),
+                ("pad", C.c_int)]
+
+
+class TaskbTask(C.Structure):
+    _fields_ = [("arrive_t", C.c_double), ("payload", C.c_uint64), ("work", C.c_int32), ("dest", C.c_int32)]
+
+
+class TaskbParams(C.Structure):
+    _fields_ = [("mode", C.c_int), ("transport", C.c_int), ("inner_scale", C.c_int), ("stride", C.c_int),
+                ("tick_ms", C.c_double), ("pending_ahead", C.c_uint64), ("adaptive", C.c_int),
+                ("overlap", C.c_int), ("min_mb", C.c_double), ("max_mb", C.c_double),
+                ("target_batches", C.c_double)]
+
+
+class TaskbStats(C.Structure):
+    _fields_ = [("makespan_ms", C.c_double), ("p50_ms", C.c_double), ("p99_ms", C.c_double),
+                ("throughput", C.c_double), ("backlog_max", C.c_double), ("arrival_span_ms", C.c_double),
+                ("migrated_bytes", C.c_uint64), ("migrations", C.c_uint64)]
 
 
 class TickStats(C.Structure):
@@ -169,6 +199,12 @@ _SIGS = {
     "ferry_lru_count_owned": (I, [V, V, V, I, C.c_uint32, V]),
     "ferry_lru_handoff": (I, [V, V, V, V, V, I, I, C.c_uint32]),
     "ferry_lru_read_owned": (I, [V, I, V, V]),
+    "ferry_taskb_generate": (I, [C.POINTER(TaskbSpec), C.c_uint64, V, V]),
+    "ferry_taskb_create": (I, [I, I, V, C.c_uint64, C.POINTER(V)]),
+    "ferry_taskb_run": (I, [V, C.POINTER(TaskbParams), C.POINTER(TaskbStats)]),
+    "ferry_taskb_results": (I, [V, V, C.c_uint64]),
+    "ferry_taskb_reset": (I, [V]),
+    "ferry_taskb_destroy": (I, [V]),
 }
 
 

@@ -591,6 +591,89 @@ int ferry_lru_handoff(ferry_lru* dst, void* stream, const ferry_lru* src, const 
                       const int32_t* d_dst_lanes, int n, int mode, uint32_t bit);
 int ferry_lru_read_owned(ferry_lru* lru, int lane, uint32_t* masks, int32_t* capacity);
 
+/* ---- Workload B: the reference's synthetic task stream and executors ------
+ * Tasks arrive open-loop with a payload on a source GPU and an FMA work count;
+ * an executor moves the payloads to the compute GPU and runs the task kernel
+ * (src/workloads/synthetic.cuh, src/workloads/baselines.cuh,
+ * src/runtime/redistribute.cuh). Not the decode path: kept so that the
+ * reference's Workload B drivers (src/benches/run_synthetic.cu) drop in.
+ *
+ * ferry_taskb_generate   generate_tasks (synthetic.cuh:83-173): the same
+ *                        mt19937_64 draws in the same order, so a seed gives
+ *                        the reference's stream; `trace_ticks` supplies the
+ *                        arrivals of FERRY_TASKB_TRACE (the reference reads
+ *                        them from FERRY_TRACE_CSV). `out` holds spec->total.
+ * ferry_taskb_create     payload pool (n * payload bytes, the reference's
+ *                        content: mt19937_64 seed 9, (rng() % 1000) / 8) on
+ *                        src_dev; moved payloads, outputs and works on
+ *                        dst_dev (make_ctx, baselines.cuh:82-111); peer
+ *                        access dst -> src when the devices differ. One
+ *                        payload size (a multiple of 16 bytes), ascending
+ *                        arrivals.
+ * ferry_taskb_run        one executor (run_baseline_a / run_baseline_b /
+ *                        run_ferry_abl, baselines.cuh:139-409) over the
+ *                        stream, arrivals replayed on the host clock at
+ *                        tick_ms per tick; synchronous; fills the reference's
+ *                        ExecStats. C's batches follow choose_batch
+ *                        (baselines.cuh:127-137) with adaptive, else the fixed
+ *                        max_mb; with overlap the kernel of a batch waits on
+ *                        its move's event and up to pending_ahead batches are
+ *                        in flight. Transports: FERRY_TASKB_P2P, a copy kernel
+ *                        on dst reading src's HBM (over NVLink, or local);
+ *                        FERRY_TASKB_HOST_STAGED, the reference's pinned ring
+ *                        (HostStagedChannel, host_staged_channel.cpp:43-87).
+ *                        The stats' timings are host milliseconds.
+ * ferry_taskb_results    synchronous copy of the first n_floats outputs
+ * ferry_taskb_reset      zero the moved payloads and outputs */
+#define FERRY_TASKB_STEADY 0
+#define FERRY_TASKB_BURSTY 1
+#define FERRY_TASKB_SKEWED 2
+#define FERRY_TASKB_TRACE 3
+#define FERRY_TASKB_A 0
+#define FERRY_TASKB_B 1
+#define FERRY_TASKB_C 2
+#define FERRY_TASKB_P2P 0
+#define FERRY_TASKB_HOST_STAGED 1
+typedef struct {
+  int arrival;          /* FERRY_TASKB_STEADY / BURSTY / SKEWED / TRACE */
+  int sparsity;         /* payload 0: 4 KB, 1: 16 KB, 2: 64 KB */
+  int imbalanced;       /* work 0: uniform 100..200; 1: 20 % of tasks x8 */
+  int num_gpus;         /* GPUs the dest field spreads over */
+  uint64_t total;       /* tasks */
+  double dest_hot_frac; /* the reference's default 0.8 */
+  int dest_hot_cards;   /* <= 0: max(1, num_gpus / 5) */
+  int pad;
+} ferry_taskb_spec;
+typedef struct {
+  double arrive_t; /* ticks */
+  uint64_t payload; /* bytes */
+  int32_t work;
+  int32_t dest;
+} ferry_taskb_task;
+typedef struct {
+  int mode;      /* FERRY_TASKB_A / B / C */
+  int transport; /* FERRY_TASKB_P2P / HOST_STAGED */
+  int inner_scale;
+  int stride;    /* B: tasks per segment (the reference's 64) */
+  double tick_ms;
+  uint64_t pending_ahead; /* C: batches in flight (4) */
+  int adaptive;  /* C: 1 = choose_batch, 0 = fixed max_mb */
+  int overlap;   /* C: 1 = kernels wait on events, 0 = move, compute, sync */
+  double min_mb, max_mb, target_batches; /* AdaptiveBatchPolicy */
+} ferry_taskb_params;
+typedef struct {
+  double makespan_ms, p50_ms, p99_ms, throughput, backlog_max, arrival_span_ms;
+  uint64_t migrated_bytes, migrations;
+} ferry_taskb_stats;
+typedef struct ferry_taskb ferry_taskb;
+int ferry_taskb_generate(const ferry_taskb_spec* spec, uint64_t seed, const double* trace_ticks,
+                         ferry_taskb_task* out);
+int ferry_taskb_create(int src_dev, int dst_dev, const ferry_taskb_task* tasks, uint64_t n, ferry_taskb** out);
+int ferry_taskb_run(ferry_taskb* tb, const ferry_taskb_params* params, ferry_taskb_stats* stats);
+int ferry_taskb_results(ferry_taskb* tb, float* host_out, uint64_t n_floats);
+int ferry_taskb_reset(ferry_taskb* tb);
+int ferry_taskb_destroy(ferry_taskb* tb);
+
 #ifdef __cplusplus
 }
 #endif

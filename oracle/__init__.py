@@ -104,6 +104,8 @@ def lib():
         L.orc_pipe_step.restype = C.c_int64
         L.orc_pipe_step.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.c_float, C.c_void_p, C.c_void_p]
+        L.orc_taskb_payload.argtypes = [C.c_uint64, C.c_void_p]
+        L.orc_taskb_compute.argtypes = [C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p, C.c_int]
         _LIB = L
     return _LIB
 
@@ -120,6 +122,8 @@ def ref_lib():
         R.ref_choose_mb.restype = C.c_double
         R.ref_choose_mb.argtypes = [C.c_double]
         R.ref_load_miss_trace.argtypes = [C.c_char_p] + [C.c_int] * 7 + [C.c_void_p] * 4
+        R.ref_generate_tasks.argtypes = ([C.c_char_p] * 3 + [C.c_uint64, C.c_int, C.c_double, C.c_int, C.c_uint64]
+                                         + [C.c_void_p] * 4)
         _REF = R
     return _REF
 
@@ -460,3 +464,47 @@ class CpuPipeline:
                                      q.ctypes.data, C.c_float(scale), out.ctypes.data,
                                      None if npg is None else npg.ctypes.data)
         return out, int(misses)
+
+
+# --------------------------------------------------------------------------- Workload B
+
+def taskb_payload(n_floats: int) -> np.ndarray:
+    """The reference's payload pool content (baselines.cuh:86-89)."""
+    out = np.empty(n_floats, np.float32)
+    lib().orc_taskb_payload(C.c_uint64(n_floats), out.ctypes.data_as(C.c_void_p))
+    return out
+
+
+def taskb_expected(tasks: np.ndarray, batches, inner: int) -> np.ndarray:
+    """Outputs an executor leaves: for a batch (off, cnt) the task kernel reads
+    the cnt floats from the batch's first payload float on, element j with
+    task off + j's work (baselines.cuh:40-48, 176-178, 220-223, 332-335)."""
+    payload = int(tasks["payload"][0])
+    pf = payload // 4
+    n_floats = len(tasks) * pf
+    pool = taskb_payload(n_floats)
+    works = np.ascontiguousarray(tasks["work"], np.int32)
+    out = np.zeros(n_floats, np.float32)
+    for off, cnt in batches:
+        seg = np.empty(cnt, np.float32)
+        lib().orc_taskb_compute(pool[off * pf:].ctypes.data_as(C.c_void_p), seg.ctypes.data_as(C.c_void_p),
+                                C.c_uint64(cnt), works[off:].ctypes.data_as(C.c_void_p), inner)
+        out[off * pf: off * pf + cnt] = seg
+    return out
+
+
+def ref_generate_tasks(arrival: str, sparsity: str, skew: str, total: int, num_gpus: int = 1,
+                       hot_frac: float = 0.8, hot_cards: int = 0, seed: int = 42):
+    """The reference's own generate_tasks (None when _ref is unavailable):
+    (arrive_t, payload, work, dest)."""
+    R = ref_lib()
+    if R is None:
+        return None
+    a = np.empty(total, np.float64)
+    p = np.empty(total, np.uint64)
+    w = np.empty(total, np.int32)
+    d = np.empty(total, np.int32)
+    R.ref_generate_tasks(arrival.encode(), sparsity.encode(), skew.encode(), C.c_uint64(total), num_gpus,
+                         hot_frac, hot_cards, C.c_uint64(seed), a.ctypes.data_as(C.c_void_p),
+                         p.ctypes.data_as(C.c_void_p), w.ctypes.data_as(C.c_void_p), d.ctypes.data_as(C.c_void_p))
+    return a, p, w, d

@@ -1000,6 +1000,25 @@ int orc_select_quest(const uint16_t* q, int Hkv, int G, const float* mm, int N,
   return 0;
 }
 
+// ---- Workload B (src/workloads/baselines.cuh) -----------------------------
+// The payload pool's content (baselines.cuh:86-89: mt19937_64 seed 9,
+// (rng() % 1000) / 8 as float) and the task kernel (baselines.cuh:40-48:
+// element i iterates v = fma(v, 1.0000001, 1e-7) works[i] * inner times) on
+// the CPU, one correctly rounded fmaf per step as on the GPU.
+void orc_taskb_payload(uint64_t n_floats, float* out) {
+  std::mt19937_64 rng(9);
+  for (uint64_t i = 0; i < n_floats; ++i) out[i] = (float)(rng() % 1000) / 8.0f;
+}
+
+void orc_taskb_compute(const float* in, float* out, uint64_t n, const int32_t* works, int inner) {
+  for (uint64_t i = 0; i < n; ++i) {
+    const int w = works[i] * inner;
+    float v = in[i];
+    for (int k = 0; k < w; ++k) v = std::fmaf(v, 1.0000001f, 1e-7f);
+    out[i] = v;
+  }
+}
+
 int orc_version(void) { return 2; }
 
 }  // extern "C"

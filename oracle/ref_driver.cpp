@@ -5,6 +5,7 @@
 //   workloads/missstream.cuh     replay_miss_stream  (missstream.cuh:104-170)
 //   workloads/miss_trace.cuh     load_miss_trace     (miss_trace.cuh:75-185)
 //   runtime/adaptive_batch.cuh   choose_mb           (adaptive_batch.cuh:31-36)
+//   workloads/synthetic.cuh      generate_tasks      (synthetic.cuh:83-173)
 // The output (oracle/_ref/libferry_ref.so and oracle/_ref/ref_trace_check) is
 // used only to validate the oracle restatement (ferry_oracle.cpp) and the GPU
 // miss-detect kernel against the reference's exact LRU.
@@ -18,6 +19,7 @@
 #include "runtime/adaptive_batch.cuh"
 #include "workloads/miss_trace.cuh"
 #include "workloads/missstream.cuh"
+#include "workloads/synthetic.cuh"
 
 namespace {
 ferry::MissSpec make_spec(int R, int L, int S, int sel, int hot, int kv, int d,
@@ -71,6 +73,29 @@ int ref_load_miss_trace(const char* path, int R, int L, int S, int sel, int hot,
 double ref_choose_mb(double pending_mb) {
   ferry::AdaptiveBatchPolicy pol;
   return pol.choose_mb(pending_mb);
+}
+
+// Workload B's task stream (arrival: steady | bursty | skewed; sparsity: low |
+// medium | high; skew: balanced | imbalanced).
+int ref_generate_tasks(const char* arrival, const char* sparsity, const char* skew, uint64_t total,
+                       int num_gpus, double hot_frac, int hot_cards, uint64_t seed, double* arrive_t,
+                       uint64_t* payload, int32_t* work, int32_t* dest) {
+  ferry::ArrivalSpec sp;
+  sp.arrival = arrival;
+  sp.sparsity = sparsity;
+  sp.load_skew = skew;
+  sp.total = total;
+  sp.num_gpus = num_gpus;
+  sp.dest_hot_frac = hot_frac;
+  sp.dest_hot_cards = hot_cards;
+  const std::vector<ferry::Task> t = ferry::generate_tasks(sp, seed);
+  for (size_t i = 0; i < t.size(); ++i) {
+    arrive_t[i] = t[i].arrive_t;
+    payload[i] = t[i].payload;
+    work[i] = t[i].work;
+    dest[i] = t[i].dest;
+  }
+  return 0;
 }
 
 }  // extern "C"

@@ -84,6 +84,89 @@ def migrate_bench(w, iters: int) -> dict:
         src.close()
 
 
+def migrate_many(w, iters: int, thieves: int) -> dict:
+    """Several thieves pulling from one victim at once (the skewed job's
+    steals: every idle GPU takes from the busiest): requests warmed on GPU 0,
+    GPU j (1..thieves) migrates its share [j-1 of thieves] of them with
+    ferry_migrate_requests (delta), all launched together; each thief's
+    calls timed with CUDA events on its own stream. Returns per-thief GB/s
+    and the victim's egress = all bytes / the slowest thief's time."""
+    import ctypes as C
+
+    from . import _abi
+
+    n = torch.cuda.device_count()
+    if n < thieves + 1:
+        raise SystemExit(f"needs {thieves + 1} GPUs")
+    R = w.num_requests
+    vic = Decoder(w, 0)
+    th = [Decoder(w, d) for d in range(1, thieves + 1)]
+    try:
+        for dec, d in [(vic, 0)] + [(t, i + 1) for i, t in enumerate(th)]:
+            dec.register_pool()
+            dd = torch.device("cuda", d)
+            ids = torch.arange(R, dtype=torch.int32, device=dd)
+            dec.begin(ids, torch.full((R,), w.init_pages, dtype=torch.int32, device=dd))
+        d0 = torch.device("cuda", 0)
+        ids = torch.arange(R, dtype=torch.int32, device=d0)
+        out = torch.empty((R, w.num_layers, w.q_heads, 128), dtype=torch.float32, device=d0)
+        for s in range(2):
+            q = torch.from_numpy(np.stack([q_stream(w, r, steps=s + 1)[s] for r in range(R)])).to(d0)
+            vic.step(q, ids, out)
+        torch.cuda.synchronize(d0)
+        vic.check()
+        share = R // thieves
+        calls = []
+        for j, t in enumerate(th):
+            dev = torch.device("cuda", j + 1)
+            _abi.call("ferry_ctx_link", t.ctx, 0, vic.ctx)
+            sub = torch.arange(j * share, (j + 1) * share, dtype=torch.int32, device=dev)
+            st = torch.cuda.Stream(dev)
+            calls.append((t, dev, sub, st))
+
+        def launch(t, dev, sub, st):
+            _abi.call("ferry_migrate_requests", t.ctx, C.c_void_p(st.cuda_stream), 0, C.c_void_p(sub.data_ptr()),
+                      C.c_void_p(sub.data_ptr()), share, _abi.MIGRATE_DELTA)
+
+        for c in calls:  # warm-up
+            for _ in range(2):
+                launch(*c)
+        for d in range(thieves + 1):
+            torch.cuda.synchronize(d)
+        for t, *_ in calls:
+            t.all_stats(reset=True)
+        evs = []
+        for t, dev, sub, st in calls:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.device(dev):
+                a.record(st)
+            evs.append((a, b))
+        for _ in range(iters):
+            for c in calls:
+                launch(*c)
+        for (t, dev, sub, st), (a, b) in zip(calls, evs):
+            with torch.cuda.device(dev):
+                b.record(st)
+        for d in range(thieves + 1):
+            torch.cuda.synchronize(d)
+        per, ms = [], []
+        for (t, *_), (a, b) in zip(calls, evs):
+            t.check()
+            per.append(t.all_stats()[3])
+            ms.append(a.elapsed_time(b))
+        g = C.c_double()
+        _abi.call("ferry_probe_link", 1, 0, C.c_size_t(256 << 20), 3, C.byref(g))
+        rates = [b_ / (m / 1e3) / 1e9 for b_, m in zip(per, ms)]
+        egress = sum(per) / (max(ms) / 1e3) / 1e9
+        return {"thieves": thieves, "requests_each": share, "bytes_each_per_call": per[0] / iters,
+                "thief_GB_s": rates, "victim_egress_GB_s": egress, "nvlink_peak_GB_s": g.value,
+                "thief_frac": [r / g.value for r in rates], "egress_frac": egress / g.value}
+    finally:
+        for t in th:
+            t.close()
+        vic.close()
+
+
 def probe() -> dict:
     """Devices, P2P access / native peer atomics, and the two link peaks the
     decode path uses (host -> device 0, and every peer -> device 0)."""
@@ -116,6 +199,8 @@ def main():
     ap.add_argument("--device", type=int, default=0)
     ap.add_argument("--migrate", action="store_true", help="time request migration over NVLink")
     ap.add_argument("--probe", action="store_true", help="topology and link peaks")
+    ap.add_argument("--thieves", type=int, default=0,
+                    help="with --migrate: this many GPUs pull from GPU 0 at once")
     ap.add_argument("--requests", type=int, default=0, help="override the batch (a smaller case to profile)")
     ap.add_argument("--only", default="", help="comma list of kernels to time (gather,attention,select,detect)")
     ap.add_argument("--select", default="mean", help="selection rule: mean (the benchmark's) or quest")
@@ -128,7 +213,15 @@ def main():
         print(json.dumps({"probe": probe()}))
         return
     if args.migrate:
-        print(json.dumps({"migrate": migrate_bench(WORKLOADS[args.workload], args.iters)}))
+        w = WORKLOADS[args.workload]
+        if args.requests:
+            import dataclasses
+
+            w = dataclasses.replace(w, num_requests=args.requests)
+        if args.thieves:
+            print(json.dumps({"migrate_many": migrate_many(w, args.iters, args.thieves)}))
+        else:
+            print(json.dumps({"migrate": migrate_bench(w, args.iters)}))
         return
     w = WORKLOADS[args.workload]
     if args.requests:

@@ -453,7 +453,10 @@ __global__ void __launch_bounds__(256) lru_kernel(LruArgs A) {
 // per warp through shared memory, one barrier), so the chain is ~4x shorter.
 // Same algorithm and same results as the warp kernel's parallel path, with
 // the same serial replay (thread 0) when it gives up.
-constexpr int kLruCtaWarps = 4;
+#ifndef FERRY_LRU_CTA_WARPS
+#define FERRY_LRU_CTA_WARPS 4
+#endif
+constexpr int kLruCtaWarps = FERRY_LRU_CTA_WARPS;  // warps sharing a lane (build-time tunable)
 constexpr int kLruCtaThreads = kLruCtaWarps * 32;
 
 // Exclusive ranks of two flags over one chunk (item order = thread order) and

@@ -420,7 +420,7 @@ def run_ferry(args, w):
     full = [(e, n) for e, n, ok in evs if ok]
     # request starts, then per decoded tick: select, detect, gather, attention
     # (each once per chunk) and the appends' two
-    launches = len(full) * (4 * chunks + (2 if w.append else 0)) + sum(
+    launches = sum(4 * min(chunks, n) + (2 if w.append else 0) for _, n in full) + sum(
         1 for i in range(args.warmup, n_ticks) if ticks[i]["new"] is not None)
     step_ms = [e[0].elapsed_time(e[5]) for e, n in full]  # each tick's device time (request starts included)
     if chunks > 1:
@@ -609,8 +609,9 @@ def main():
     ap.add_argument("--batch", type=int, default=32, help="cfg3s/cfg4s: requests decoded per GPU per tick")
     ap.add_argument("--append", type=int, default=None,
                     help="tokens each decode step appends to its context (default: the workload's)")
-    ap.add_argument("--chunks", type=int, default=1,
-                    help="pipeline each decode step over this many request chunks (ferry_step_chunks)")
+    ap.add_argument("--chunks", type=int, default=None,
+                    help="pipeline each decode step over this many request chunks (ferry_step_chunks); "
+                         "default 2 for cfg1 (the host-link gather overlaps the other kernels), else 1")
     ap.add_argument("--requests", type=int, default=None,
                     help="cfg5 / cfg5s: requests of the job (default: the config's 32)")
     ap.add_argument("--replicas", action="store_true",
@@ -620,6 +621,8 @@ def main():
         ap.error("--warmup must be >= 3")
     from ferry_b200.workload import WORKLOADS
 
+    if args.chunks is None:
+        args.chunks = 2 if args.workload == "cfg1" else 1
     if args.workload in ("cfg5s", "cfg5"):
         return run_owner(args)
     if args.workload == "skew":

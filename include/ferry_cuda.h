@@ -146,8 +146,11 @@ int ferry_decode_appends(ferry_ctx* ctx, int tokens_per_step);
  * attention on another, and the caller's stream waits for all of it before
  * the step returns control of it (appends, if any, follow on the caller's
  * stream). Selection and attention are HBM-bound, the gather host-link- or
- * NVLink-bound, so they overlap. Results are identical to chunks = 1 (the
- * default). Call it before any stream capture: it creates the ctx's streams
+ * NVLink-bound, so they overlap. Selections, miss lists, page tables and
+ * gathered bytes are identical to chunks = 1 (the default); the attention
+ * splits each chunk's pages over the GPU's warps by the chunk's size, so its
+ * outputs can differ from an unchunked step's in the last bits (both within
+ * the attention tolerance of the reference math). Call it before any stream capture: it creates the ctx's streams
  * and events on first use. No counterpart in the reference. */
 int ferry_step_chunks(ferry_ctx* ctx, int chunks);
 

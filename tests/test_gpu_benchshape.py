@@ -62,7 +62,11 @@ def _check_tables(dec, lru, w, gl):
 def test_cfg1_job_ticks_match_oracle(torch_cuda):
     """The bench's own job, ticks 0..T: every intermediate bit-exact and the
     attention within tolerance, with a fused-step decoder alongside that must
-    give bit-identical outputs (the bench times ferry_decode_step)."""
+    give bit-identical outputs, and a fused step pipelined over two request
+    chunks (ferry_step_chunks, what the bench times) whose selections, miss
+    lists and slots must be bit-identical and whose attention -- split over
+    warps by each chunk's own size, so rounded differently -- must meet the
+    same tolerance against the oracle."""
     import oracle
     from ferry_b200.engine import Decoder
     from ferry_b200.workload import WORKLOADS, Schedule, q_stream
@@ -71,10 +75,12 @@ def test_cfg1_job_ticks_match_oracle(torch_cuda):
     w = WORKLOADS["cfg1"]
     dev = t.device("cuda", 0)
     LH, N, k, C_, U = w.lanes_per_req, w.max_pages, w.top_k, w.cache_pages, w.pool_units
-    sep, fus = Decoder(w, 0), Decoder(w, 0)
+    sep, fus, pipe = Decoder(w, 0), Decoder(w, 0), Decoder(w, 0)
     try:
         pool = sep.register_pool()
         fus.register_pool()
+        pipe.register_pool()
+        pipe.step_chunks(2)
         units = pool.numpy(np.uint16).reshape(U, 4096)
         summ = oracle.page_summary(units)
         gpu_summ = sep.debug_read(4, np.float32, U * 128).reshape(U, 128)
@@ -94,7 +100,7 @@ def test_cfg1_job_ticks_match_oracle(torch_cuda):
             new = active[steps == 0]
             if len(new):
                 nid = t.from_numpy(new).to(dev)
-                for d in (sep, fus):
+                for d in (sep, fus, pipe):
                     d.begin(nid, n_pages[: len(new)])
                 gln = _glanes(new, LH).astype(np.int32)
                 lru.step(gln, np.zeros((len(gln), k), np.int32), n_sel=np.zeros(len(gln), np.int32),
@@ -105,14 +111,17 @@ def test_cfg1_job_ticks_match_oracle(torch_cuda):
             ids = t.from_numpy(active).to(dev)
             out = t.zeros((n, 1, w.q_heads, 128), dtype=t.float32, device=dev)
             out_f = t.zeros_like(out)
+            out_p = t.zeros_like(out)
             sep.select(q, ids)
             sep.detect(ids)
             sep.gather(ids)
             sep.attention(q, ids, out)
             fus.step(q, ids, out_f)
+            pipe.step(q, ids, out_p)
             t.cuda.synchronize()
             sep.check()
             fus.check()
+            pipe.check()
             assert (out.cpu().numpy().view(np.uint32) == out_f.cpu().numpy().view(np.uint32)).all()
             nl = n * LH
             gl = _glanes(active, LH)
@@ -121,6 +130,10 @@ def test_cfg1_job_ticks_match_oracle(torch_cuda):
                                                  np.full(nl, N, np.int32), k)
             assert (sep.n_sel[:nl].cpu().numpy() == ns_ref).all()
             assert (sep.sel[:nl].cpu().numpy() == sel_ref).all()
+            # the pipelined step's workspace (selections, slots, miss lists and
+            # counts of every lane) equals the plain fused step's
+            ws_words = w.num_requests * LH * (4 * k + 2)
+            assert (pipe.debug_read(6, np.int32, ws_words) == fus.debug_read(6, np.int32, ws_words)).all()
             im, islot, mp, ms, nm = lru.step(gl.astype(np.int32), sel_ref, n_sel=ns_ref)
             assert (sep.n_miss[:nl].cpu().numpy() == nm).all()
             assert (sep.is_miss[:nl].cpu().numpy() == im).all()
@@ -136,13 +149,19 @@ def test_cfg1_job_ticks_match_oracle(torch_cuda):
             ref = oracle.sparse_decode(qn.reshape(nl, 1, 128).view(np.uint16), pages, ns_ref, 128 ** -0.5)
             err = _rel_err(out.cpu().numpy(), ref)
             assert err <= ATTN_RTOL, (i, err)
+            err_p = _rel_err(out_p.cpu().numpy(), ref)
+            assert err_p <= ATTN_RTOL, (i, err_p)
             checked += 1
             total_miss += int(nm.sum())
             full_batches += int(n == w.num_requests)
         assert checked >= 3 and total_miss > 0
+        nlanes = w.num_requests * LH
+        for which, count in ((1, nlanes * N), (2, nlanes * C_), (3, nlanes)):
+            assert (pipe.debug_read(which, np.int32, count) == fus.debug_read(which, np.int32, count)).all()
     finally:
         sep.close()
         fus.close()
+        pipe.close()
 
 
 def test_cfg5s_requests_at_true_lane_shape_match_oracle(torch_cuda):

@@ -611,7 +611,7 @@ def main():
                     help="tokens each decode step appends to its context (default: the workload's)")
     ap.add_argument("--chunks", type=int, default=None,
                     help="pipeline each decode step over this many request chunks (ferry_step_chunks); "
-                         "default 2 for cfg1 (the host-link gather overlaps the other kernels), else 1")
+                         "default 3 for cfg1 (the host-link gather overlaps the other kernels), else 1")
     ap.add_argument("--requests", type=int, default=None,
                     help="cfg5 / cfg5s: requests of the job (default: the config's 32)")
     ap.add_argument("--replicas", action="store_true",
@@ -622,7 +622,7 @@ def main():
     from ferry_b200.workload import WORKLOADS
 
     if args.chunks is None:
-        args.chunks = 2 if args.workload == "cfg1" else 1
+        args.chunks = 3 if args.workload == "cfg1" else 1
     if args.workload in ("cfg5s", "cfg5"):
         return run_owner(args)
     if args.workload == "skew":

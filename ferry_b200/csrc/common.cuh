@@ -250,10 +250,10 @@ struct ferry_ctx {
                                  // its partial last page (0..15; decode appends)
   int append_tokens = 0;         // tokens ferry_decode_step appends per request (0 = fixed context)
   // pipelined step (ferry_step_chunks): request chunks whose selection and
-  // miss detection run on the caller's stream, gathers on `side`, attention
-  // on `side2`
+  // miss detection run on the caller's stream, gathers alternately on `side`
+  // and `side3`, attention on `side2`
   int step_chunks = 1;
-  cudaStream_t side = nullptr, side2 = nullptr;
+  cudaStream_t side = nullptr, side2 = nullptr, side3 = nullptr;
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   cudaEvent_t ev_sel[16] = {};  // chunk i's misses are known
   cudaEvent_t ev_gat[16] = {};  // chunk i's pages are in their slots

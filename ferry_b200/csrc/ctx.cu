@@ -103,6 +103,7 @@ void destroy_ctx(ferry_ctx* c) {
   if (c->ev_join) cudaEventDestroy(c->ev_join);
   if (c->side) cudaStreamDestroy(c->side);
   if (c->side2) cudaStreamDestroy(c->side2);
+  if (c->side3) cudaStreamDestroy(c->side3);
   delete c;
 }
 
@@ -420,14 +421,17 @@ int ferry_decode_step(ferry_ctx* c, void* stream, const uint16_t* d_q, const int
   } else {
     // Requests [s0, s0 + n) form chunk i. Chunk i's selection and miss
     // detection (HBM- and latency-bound) run on the caller's stream while
-    // chunk i-1's gather (host- or NVLink-bound) runs on `side` and chunk
-    // i-2's attention on `side2`. Chunks own disjoint lanes and their own rows
-    // of the workspace; kernels of one kind, which share scratch (selection
-    // chunk keys, attention partials), stay on one stream each.
+    // chunk i-1's gather (host- or NVLink-bound) runs on `side` or `side3`
+    // (alternating, so that a chunk's gather starts while the previous one
+    // drains and the link has no gap) and chunk i-2's attention on `side2`.
+    // Chunks own disjoint lanes and their own rows of the workspace; kernels
+    // of one kind that share scratch (selection chunk keys, attention
+    // partials) stay on one stream each; gathers share only atomic counters.
     const int per = (n_req + nch - 1) / nch;
     FERRY_TRY(cudaEventRecord(c->ev_fork, st));
     FERRY_TRY(cudaStreamWaitEvent(c->side, c->ev_fork, 0));
     FERRY_TRY(cudaStreamWaitEvent(c->side2, c->ev_fork, 0));
+    FERRY_TRY(cudaStreamWaitEvent(c->side3, c->ev_fork, 0));
     for (int i = 0, s0 = 0; s0 < n_req; ++i, s0 += per) {
       const int n = std::min(per, n_req - s0);
       const size_t l0 = (size_t)s0 * LH;
@@ -438,18 +442,19 @@ int ferry_decode_step(ferry_ctx* c, void* stream, const uint16_t* d_q, const int
                            1, nullptr, c->ws_islot + l0 * k, c->ws_mpage + l0 * k, c->ws_mslot + l0 * k,
                            c->ws_nmiss + l0)))
         return rc;
+      cudaStream_t gs = (i & 1) ? c->side3 : c->side;
       FERRY_TRY(cudaEventRecord(c->ev_sel[i], st));
-      FERRY_TRY(cudaStreamWaitEvent(c->side, c->ev_sel[i], 0));
-      if ((rc = launch_gather(c, c->side, ids, n, c->ws_mpage + l0 * k, c->ws_mslot + l0 * k, c->ws_nmiss + l0,
-                              true)))
+      FERRY_TRY(cudaStreamWaitEvent(gs, c->ev_sel[i], 0));
+      if ((rc = launch_gather(c, gs, ids, n, c->ws_mpage + l0 * k, c->ws_mslot + l0 * k, c->ws_nmiss + l0, true)))
         return rc;
-      FERRY_TRY(cudaEventRecord(c->ev_gat[i], c->side));
+      FERRY_TRY(cudaEventRecord(c->ev_gat[i], gs));
       FERRY_TRY(cudaStreamWaitEvent(c->side2, c->ev_gat[i], 0));
       if ((rc = launch_attention_any(c, c->side2, d_q + (size_t)s0 * qrow, ids, n, c->ws_islot + l0 * k,
                                      c->ws_nsel + l0, d_out + (size_t)s0 * qrow)))
         return rc;
     }
-    // side2's last attention follows side's last gather
+    // side2's last attention follows every chunk's gather (each attention
+    // waited for its own)
     FERRY_TRY(cudaEventRecord(c->ev_join, c->side2));
     FERRY_TRY(cudaStreamWaitEvent(st, c->ev_join, 0));
   }
@@ -463,6 +468,7 @@ int ferry_step_chunks(ferry_ctx* c, int chunks) {
   if (chunks > 1 && !c->side) {
     FERRY_TRY(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking));
     FERRY_TRY(cudaStreamCreateWithFlags(&c->side2, cudaStreamNonBlocking));
+    FERRY_TRY(cudaStreamCreateWithFlags(&c->side3, cudaStreamNonBlocking));
     FERRY_TRY(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming));
     FERRY_TRY(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming));
     for (cudaEvent_t& e : c->ev_sel) FERRY_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));

@@ -142,8 +142,9 @@ int ferry_requests_append(ferry_ctx* ctx, void* stream, const int32_t* d_req_ids
 int ferry_decode_appends(ferry_ctx* ctx, int tokens_per_step);
 /* Pipelined ferry_decode_step: the batch is cut into `chunks` (1..16) runs of
  * requests; chunk i's selection and miss detection run on the caller's stream
- * while chunk i-1's gather runs on one stream of the ctx and chunk i-2's
- * attention on another, and the caller's stream waits for all of it before
+ * while chunk i-1's gather runs on one of two streams of the ctx (alternating,
+ * so that consecutive gathers overlap at their ends) and chunk i-2's
+ * attention on a third, and the caller's stream waits for all of it before
  * the step returns control of it (appends, if any, follow on the caller's
  * stream). Selection and attention are HBM-bound, the gather host-link- or
  * NVLink-bound, so they overlap. Selections, miss lists, page tables and

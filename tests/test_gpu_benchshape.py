@@ -62,7 +62,7 @@ def _check_tables(dec, lru, w, gl):
 def test_cfg1_job_ticks_match_oracle(torch_cuda):
     """The bench's own job, ticks 0..T: every intermediate bit-exact and the
     attention within tolerance, with a fused-step decoder alongside that must
-    give bit-identical outputs, and a fused step pipelined over two request
+    give bit-identical outputs, and a fused step pipelined over three request
     chunks (ferry_step_chunks, what the bench times) whose selections, miss
     lists and slots must be bit-identical and whose attention -- split over
     warps by each chunk's own size, so rounded differently -- must meet the
@@ -80,7 +80,7 @@ def test_cfg1_job_ticks_match_oracle(torch_cuda):
         pool = sep.register_pool()
         fus.register_pool()
         pipe.register_pool()
-        pipe.step_chunks(2)
+        pipe.step_chunks(3)
         units = pool.numpy(np.uint16).reshape(U, 4096)
         summ = oracle.page_summary(units)
         gpu_summ = sep.debug_read(4, np.float32, U * 128).reshape(U, 128)

@@ -621,6 +621,7 @@ def main():
         ap.error("--warmup must be >= 3")
     from ferry_b200.workload import WORKLOADS
 
+    chunks_given = args.chunks is not None
     if args.chunks is None:
         args.chunks = 3 if args.workload == "cfg1" else 1
     if args.workload in ("cfg5s", "cfg5"):
@@ -639,6 +640,9 @@ def main():
     if args.impl == "reference":
         run_reference(args, w)
     elif _dist()[0] > 1 and args.workload == "cfg1" and not args.replicas:
+        # the executor job: 1 chunk unless asked (3 chunks measured the same at N = 2)
+        if not chunks_given:
+            args.chunks = 1
         run_scale(args, w)
     else:
         run_ferry(args, w)
@@ -784,7 +788,8 @@ def run_scale(args, w):
 
     def job(host_q):
         r = RankRunner(w, total, ws, rank, local, slots=slots_needed(home, ws, max_batch),
-                       max_batch=max_batch, steal_batch=4, host_q=host_q, q_steps=window[1] + 8)
+                       max_batch=max_batch, steal_batch=4, host_q=host_q, q_steps=window[1] + 8,
+                       step_chunks=args.chunks)
         try:
             dist.barrier()
             torch.cuda.synchronize(dev)
@@ -820,7 +825,8 @@ def run_scale(args, w):
                            "heads": [w.q_heads, w.kv_heads], "top_k": w.top_k, "cache_pages": w.cache_pages,
                            "homes": "round-robin", "arrivals": f"poisson {w.arrival_rate * ws} req/s box-wide",
                            "l2": "inputs larger than L2 (selected KV 256 MiB + summaries 64 MiB per GPU step)",
-                           "parallelism": f"{ws} ranks: executor + work stealing + NCCL ownership exchange"},
+                           "parallelism": f"{ws} ranks: executor + work stealing + NCCL ownership exchange",
+                           "step_chunks": args.chunks},
                 "miss_gather": {"aggregate_GB_s": gather_agg, "per_rank_GB_s": gather_agg / ws,
                                 "link_peak_aggregate_GB_s": agg_peak, "frac_of_aggregate": gather_agg / agg_peak,
                                 "link_peak_alone_GB_s": mine_peak,
@@ -833,9 +839,10 @@ def run_scale(args, w):
                 # the executor's own device time per tick (pop .. push), slowest rank;
                 # ms_per_step above also holds the host's per-tick syncs and the exchange
                 "tick_device_ms_mean": float(mx[9]) / max(1.0, float(mx[10])),
-                # per tick: deque pop + size, query gather, select, detect, gather,
-                # attention, push (steal attempts add size probes of the peers)
-                "gpu_launches": 8 * args.steps * ws,
+                # per tick: deque pop + size, query gather, push, and per request
+                # chunk select, detect, gather, attention (steal attempts add size
+                # probes of the peers)
+                "gpu_launches": (4 + 4 * args.chunks) * args.steps * ws,
                 "e2e": {"value": float(sm[6]) / (float(mx[5]) / 1e3), "unit": UNIT,
                         "h2d_bytes_per_step": float(sm[7]) / args.steps, "d2h_bytes_per_step": float(sm[8]) / args.steps,
                         "api": "ferry_exec_tick (query table in pinned host memory) + ferry_exec_output"},

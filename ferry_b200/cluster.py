@@ -224,7 +224,7 @@ class RankRunner:
                  slots: int, max_batch: int, steal_batch: int = 4,
                  migrate_mode: int = _abi.MIGRATE_DELTA, pool_units: int | None = None,
                  policy: "_abi.StealPolicy | None" = None, host_q: bool = False,
-                 q_steps: int | None = None, log_path: str | None = None):
+                 q_steps: int | None = None, log_path: str | None = None, step_chunks: int = 1):
         import torch
         import torch.distributed as dist
 
@@ -236,6 +236,8 @@ class RankRunner:
         wl = dataclasses.replace(w, num_requests=slots)
         self.dec = Decoder(wl, device)
         self.dec.register_pool(units=pool_units or min(total_requests * w.lanes_per_req * w.max_pages, 1 << 17))
+        # the executor's ferry_decode_step pipelined over request chunks (ferry_step_chunks)
+        self.dec.step_chunks(step_chunks)
         # query table [total][steps][L][Hq][128]: resident in HBM, or (host_q)
         # in pinned, device-mapped host memory that the executor's query
         # gather reads over the host link every tick

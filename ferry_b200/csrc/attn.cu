@@ -262,14 +262,17 @@ __global__ void __launch_bounds__(kAttnWarps * 32, kAttnCtasPerSm) attn_kernel(A
         pc[g * kPartStride + 129] = lsum;
       }
     }
-    __threadfence();
+    // the warp's partial stores, then one acq_rel count by lane 0: release
+    // publishes them at GPU scope, acquire (for the last warp) orders the
+    // other warps' partials before this warp's loads of them
     __syncwarp();
     uint32_t done = 0;
-    if (t == 0) done = atomicAdd(&A.lane_done[a], 1u);
+    if (t == 0)
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(done) : "l"(&A.lane_done[a]) : "memory");
     done = __shfl_sync(kFull, done, 0);
+    __syncwarp();
     if (done == (uint32_t)parts - 1) {
       // combine: lane j holds partial j's (m, l); the o loads are independent
-      __threadfence();
       const float* pl = A.part + ((size_t)a + wf) * G * kPartStride;
 #pragma unroll
       for (int g = 0; g < G; ++g) {

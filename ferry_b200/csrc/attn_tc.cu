@@ -559,13 +559,18 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
         pc[h * kPartStride + 128] = mv;
         pc[h * kPartStride + 129] = qred[wg * 4][t] + qred[wg * 4 + 1][t] + qred[wg * 4 + 2][t] + qred[wg * 4 + 3][t];
       }
-      __threadfence();
+      // partial stores ordered by the softmax barrier, then one acq_rel count
+      // by thread 0: release publishes them at GPU scope, acquire (for the
+      // last CTA of the lane) orders the other CTAs' partials before the loads
       softmax_bar_or(false);
-      if (tid == 0) s_flag = atomicAdd(&A.lane_done[a], 1u) == (uint32_t)(parts - 1);
+      if (tid == 0) {
+        uint32_t d;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(d) : "l"(&A.lane_done[a]) : "memory");
+        s_flag = d == (uint32_t)(parts - 1);
+      }
       softmax_bar_or(false);
       if (s_flag && wg_on) {
         // combine: thread t = dim t of this warpgroup's heads
-        __threadfence();
         const float* pl = A.part + ((size_t)a + cf) * G * kPartStride;
 #pragma unroll
         for (int hh = 0; hh < HG; ++hh) {

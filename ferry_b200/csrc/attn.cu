@@ -267,8 +267,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, kAttnCtasPerSm) attn_kernel(A
     // other warps' partials before this warp's loads of them
     __syncwarp();
     uint32_t done = 0;
-    if (t == 0)
-      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(done) : "l"(&A.lane_done[a]) : "memory");
+    if (t == 0) done = atom_add_acq_rel_gpu(&A.lane_done[a], 1u);
     done = __shfl_sync(kFull, done, 0);
     __syncwarp();
     if (done == (uint32_t)parts - 1) {

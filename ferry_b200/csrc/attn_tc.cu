@@ -563,11 +563,7 @@ __global__ void __launch_bounds__(kTcThreads, TcLayout<F8>::kCtasPerSm)
       // by thread 0: release publishes them at GPU scope, acquire (for the
       // last CTA of the lane) orders the other CTAs' partials before the loads
       softmax_bar_or(false);
-      if (tid == 0) {
-        uint32_t d;
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(d) : "l"(&A.lane_done[a]) : "memory");
-        s_flag = d == (uint32_t)(parts - 1);
-      }
+      if (tid == 0) s_flag = atom_add_acq_rel_gpu(&A.lane_done[a], 1u) == (uint32_t)(parts - 1);
       softmax_bar_or(false);
       if (s_flag && wg_on) {
         // combine: thread t = dim t of this warpgroup's heads

@@ -163,6 +163,17 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, 
 
 // 1-D bulk async copy global -> shared (TMA engine), completion signalled on
 // the mbarrier as transaction bytes. dst, src 16-byte aligned; bytes % 16 == 0.
+// Split-K / chunk completion count: one atomic add with acquire-release
+// semantics at GPU scope. Issued by one thread after a barrier over the
+// threads that stored the partials (the barrier orders their stores at CTA
+// scope, the release publishes them at GPU scope), its acquire orders the
+// other blocks' partials before the last block's loads of them.
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 __device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, uint32_t bytes,
                                           uint64_t* bar) {
   asm volatile(

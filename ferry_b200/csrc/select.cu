@@ -380,12 +380,10 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 4) select_kernel(SelArgs 
     }
   }
   if (A.nchunks > 1) {
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = atomicAdd(&A.done[a], 1u) == (uint32_t)(A.nchunks - 1);
+    __syncthreads();  // this chunk's keys are stored (CTA scope); the count publishes them
+    if (tid == 0) s_last = atom_add_acq_rel_gpu(&A.done[a], 1u) == (uint32_t)(A.nchunks - 1);
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
     if (tid == 0) A.done[a] = 0;
     for (int p = tid; p < np; p += kThreads) keys[p] = __ldcg(A.gkeys + (size_t)a * N + p);
   }
@@ -518,12 +516,10 @@ __global__ void __launch_bounds__(kSelThreads) select_quest_kernel(QuestArgs A) 
     }
     if (lane == 0) kd[p] = order_key(best);
   }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_last = atomicAdd(&A.done[ag], 1u) == (uint32_t)(A.nchunks - 1);
+  __syncthreads();  // this chunk's keys are stored (CTA scope); the count publishes them
+  if (tid == 0) s_last = atom_add_acq_rel_gpu(&A.done[ag], 1u) == (uint32_t)(A.nchunks - 1);
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   if (tid == 0) A.done[ag] = 0;
   for (int p = tid; p < np; p += kSelThreads) keys[p] = __ldcg(kd + p);
   __syncthreads();

@@ -165,16 +165,51 @@ __global__ void __launch_bounds__(kAttnWarps * 32, kAttnCtasPerSm) attn_kernel(A
   for (int s = 0; s < kStages; ++s) issue();
 
   bool ok = true;
-  for (int a = (int)(x_lo / k); (int64_t)a * k < x_hi && ok; ++a) {
-    int64_t unit0 = 0;
-    const int n = lane_pages(a, &unit0);
+  // the next segment's lane inputs (request id, n_sel and, for small groups,
+  // q) are loaded one segment ahead, so a segment starts without waiting on
+  // them
+  constexpr int kQPre = G <= 2 ? G : 1;
+  const int a_first = (int)(x_lo / k);
+  int nx_req = A.req_ids[a_first / A.lanes_per_req], nx_n = A.n_sel[a_first];
+  uint4 nx_q[kQPre];
+  if constexpr (G <= 2) {
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      nx_q[g] = *reinterpret_cast<const uint4*>(A.q + ((size_t)a_first * G + g) * kHeadDim + d0);
+  }
+  for (int a = a_first; (int64_t)a * k < x_hi && ok; ++a) {
+    const int req_a = nx_req, nsel_a = nx_n;
+    uint4 q_a[kQPre];
+#pragma unroll
+    for (int g = 0; g < kQPre; ++g) q_a[g] = nx_q[g];
+    if ((int64_t)(a + 1) * k < x_hi) {  // lane a + 1 < n_lanes
+      nx_req = A.req_ids[(a + 1) / A.lanes_per_req];
+      nx_n = A.n_sel[a + 1];
+      if constexpr (G <= 2) {
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+          nx_q[g] = *reinterpret_cast<const uint4*>(A.q + ((size_t)(a + 1) * G + g) * kHeadDim + d0);
+      }
+    }
+    int n = nsel_a;
+    {
+      const int64_t gl = (int64_t)req_a * A.lanes_per_req + a % A.lanes_per_req;
+      if (gl < 0 || gl >= A.lanes_total || n < 0 || n > k) {
+        if (t == 0) record_error(A.err, kErrRange);
+        n = 0;
+      }
+    }
     const int64_t base = (int64_t)a * k;
     const int jlo = (int)(max(x_lo, base) - base);
     const int jhi = seg_end(x_hi, base, k, n);
     float qv[G][8], mx[G], ls[G], o[G][8];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(A.q + ((size_t)a * G + g) * kHeadDim + d0);
+      uint4 raw;
+      if constexpr (G <= 2)
+        raw = q_a[g];
+      else
+        raw = *reinterpret_cast<const uint4*>(A.q + ((size_t)a * G + g) * kHeadDim + d0);
       h8_to_f(raw, qv[g]);
 #pragma unroll
       for (int d = 0; d < 8; ++d) {
